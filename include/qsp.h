@@ -1,0 +1,246 @@
+/*
+ * qsp.h — C ABI of the B200 (sm_100a) qwen3_5 MTP speculative-decoding step.
+ *
+ * Every entry point takes plain device pointers, explicit sizes/leading dimensions, a dtype
+ * enum and a CUDA stream (as void*), launches asynchronously on that stream, allocates
+ * nothing, and returns a status (QSP_OK == 0). On failure `qsp_last_error()` (thread-local)
+ * describes the problem. Reference citations name the giapnguyen74/lollm function each entry
+ * point replaces (paths relative to the project root).
+ *
+ * Row-major everywhere. "dtype" is the model dtype of activations and weights (QSP_F32 or
+ * QSP_BF16); recurrent GDN state, softmax statistics and accumulators are always fp32.
+ */
+#ifndef QSP_H_
+#define QSP_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define QSP_OK 0
+#define QSP_ERR_INVALID 1     /* bad argument: shape, pointer, alignment, range        */
+#define QSP_ERR_CUDA 2        /* a CUDA runtime call or kernel launch failed            */
+#define QSP_ERR_UNSUPPORTED 3 /* valid request this build does not implement            */
+
+#define QSP_F32 0
+#define QSP_BF16 1
+
+#define QSP_ABI_VERSION 1
+
+/* Thread-local description of the last failure on this thread. */
+const char* qsp_last_error(void);
+int qsp_abi_version(void);
+
+/* ---------------------------------------------------------------- elementwise / norms */
+
+/* out[r,:] = table[ids[r·ids_stride],:]. Replaces `embed_tokens(input_ids)`
+ * (src/qwen3_5/modeling_qwen3_5.py:86). ids outside [0,vocab) are rejected on the device
+ * by writing zeros and setting *bad_ids (optional, may be NULL) to 1. */
+int qsp_embed(const int64_t* ids, int64_t ids_stride, int64_t rows, const void* table,
+              int64_t vocab, int64_t dim, void* out, int64_t ld_out, int32_t* bad_ids,
+              int dtype, void* stream);
+
+/* y = x̂·(1+w), statistics in fp32 — RMSNorm (src/qwen3_5/blocks.py:23-35). */
+int qsp_rmsnorm(const void* x, int64_t ld_x, const void* w, void* y, int64_t ld_y,
+                int64_t rows, int64_t dim, float eps, int dtype, void* stream);
+
+/* x := x + h (rounded to dtype), then y = RMSNorm(x): the residual add followed by the next
+ * pre-norm (src/qwen3_5/modeling_qwen3_5.py:59-60). */
+int qsp_add_rmsnorm(void* x, const void* h, const void* w, void* y, int64_t rows,
+                    int64_t dim, float eps, int dtype, void* stream);
+
+/* y = silu(gu[:, :inter]) · gu[:, inter:] — the SwiGLU middle of MLP
+ * (src/qwen3_5/blocks.py:341-342) on a fused [gate | up] projection. */
+int qsp_swiglu(const void* gu, int64_t ld_gu, void* y, int64_t ld_y, int64_t rows,
+               int64_t inter, int dtype, void* stream);
+
+/* ---------------------------------------------------------------- projections */
+
+#define QSP_GEMM_ACCUMULATE 1 /* c := c + round(a·wᵀ) (residual add in the epilogue) */
+
+/* c[m,n] = a[m,k] · w[n,k]ᵀ with fp32 accumulation: every nn.Linear of the step
+ * (blocks.py:202-205, 251-260, 337-339, modeling_qwen3_5.py:73, mtp.py:52). bf16 runs on
+ * tcgen05 tensor cores; fp32 (parity configs) on CUDA cores. */
+int qsp_gemm(const void* a, int64_t lda, const void* w, int64_t ldw, void* c, int64_t ldc,
+             int64_t m, int64_t n, int64_t k, int dtype, int flags, void* stream);
+
+/* ---------------------------------------------------------------- Gated DeltaNet */
+
+/*
+ * One GDN layer's token mixer core over T tokens per sequence, fused: causal depthwise
+ * conv + SiLU over cat(q,k,v) (GatedDeltaNet._conv, blocks.py:268-286), head split and
+ * v_per_k expansion, β = σ(b), g = −exp(A_log)·softplus(a+dt_bias) (blocks.py:297-314),
+ * l2-normalised q,k and the recurrent gated delta rule (blocks.py:116-144), then
+ * RMSNormGated(core, z) (blocks.py:38-51, 324). Output feeds out_proj.
+ *
+ * Deferred commit (rollback by index): in speculative mode the kernel does NOT write the
+ * state after the T tokens. It stores each token's (k, v, g, β) in `pending` and the raw
+ * conv inputs in `conv_hist`; the NEXT call first replays the `replay_n[b]` kept tokens
+ * onto the stored state (same arithmetic, so the result is bit-identical to having run
+ * only those tokens) and reads its conv window at row `conv_off[b]`. Commit-all mode
+ * (speculative == 0, any T) writes the final state and window directly.
+ *
+ * Buffers (per layer):
+ *   proj       [B*T, ld_proj]           cols [0,C): raw qkv, [C,C+Vd): z, then b [Hv], a [Hv]
+ *   state      [B, Hv, dk, dv] fp32     (same layout as the reference's recurrent_state)
+ *   conv_hist  [2, B, K-1+Ts, C] dtype  ping-pong on *parity
+ *   pending    [B, Hv, Ts, dk+dv+2] fp32
+ *   out        [B*T, ld_out]            cols [0, Vd)
+ * with C = 2·Hk·dk + Hv·dv (conv_dim), Vd = Hv·dv, Ts = max_spec_tokens.
+ */
+typedef struct qsp_gdn_layer {
+  int32_t batch, tokens;
+  int32_t n_k_heads, n_v_heads, head_k, head_v, conv_kernel;
+  int32_t max_spec_tokens;
+  int32_t speculative;
+  int32_t dtype;
+  float eps;
+  const void* proj;
+  int64_t ld_proj;
+  const void* conv_w;     /* [C, K]   (conv1d.weight squeezed) */
+  const void* a_log;      /* [Hv]     */
+  const void* dt_bias;    /* [Hv]     */
+  const void* norm_w;     /* [dv]     */
+  float* state;
+  void* conv_hist;
+  float* pending;
+  const int32_t* replay_n; /* [B] */
+  const int32_t* conv_off; /* [B] */
+  const int32_t* parity;   /* [1] */
+  void* out;
+  int64_t ld_out;
+} qsp_gdn_layer;
+
+int qsp_gdn_verify(const qsp_gdn_layer* layer, void* stream);
+
+/* ---------------------------------------------------------------- gated attention */
+
+/*
+ * Paged KV cache: k_pages/v_pages [num_pages, n_kv, page_size, head_dim] (dtype);
+ * page_table [B, max_pages] int32; seq_lens [B] = committed tokens before this call. The
+ * T new tokens of sequence b sit at positions seq_lens[b] + t.
+ *
+ * qkv row layout (one row per token, b-major): per q head h: [q (hd) | gate (hd)], then
+ * k (n_kv·hd), then v (n_kv·hd) — q_proj / k_proj / v_proj stacked (blocks.py:202-205,
+ * 214-220).
+ */
+typedef struct qsp_attn_layer {
+  int32_t batch, tokens;
+  int32_t n_heads, n_kv_heads, head_dim, rotary_dim;
+  int32_t page_size, max_pages, num_pages;
+  int32_t dtype;
+  float eps, scale;
+  const void* qkv;
+  int64_t ld_qkv;
+  const void* q_norm_w;   /* [hd] */
+  const void* k_norm_w;   /* [hd] */
+  const void* rope_cos;   /* [rope_rows, rotary_dim] dtype (RoPE.cos_sin table) */
+  const void* rope_sin;
+  int32_t rope_rows;
+  void* k_pages;
+  void* v_pages;
+  const int32_t* page_table;
+  const int32_t* seq_lens;
+  void* q_buf;            /* [B*T, n_heads, hd] workspace: normed + rotated q */
+  void* out;              /* [B*T, ld_out] gated attention output (o_proj input) */
+  int64_t ld_out;
+  float* partial;         /* split-KV workspace (qsp_attn_workspace_bytes) */
+  int32_t num_splits;     /* key splits per (sequence, kv head); 0 = choose */
+  int32_t* bad_index;     /* optional [1]: set to 1 if a page index was out of range */
+} qsp_attn_layer;
+
+/* QK-norm + partial RoPE on q and k, append k,v into the pages
+ * (blocks.py:218-227, kv.py:26-33 append_kv). */
+int qsp_attn_prep(const qsp_attn_layer* layer, void* stream);
+
+/* Offset-causal GQA attention of the T new queries over seq_lens[b]+T keys, split over
+ * the key axis and merged, times σ(gate) (attention.py:43-51, 84-91; _triton_attn.py
+ * kv_fwd_kernel; blocks.py:229-235). */
+int qsp_attn_verify(const qsp_attn_layer* layer, void* stream);
+
+/* Bytes of `partial` workspace needed by qsp_attn_verify for this shape and split count. */
+size_t qsp_attn_workspace_bytes(int32_t batch, int32_t tokens, int32_t n_heads,
+                                int32_t head_dim, int32_t num_splits);
+
+/* MTP attention with no cache over a single position: softmax over one key is 1, so the
+ * output is the GQA-expanded v times σ(gate) (mtp.py:71-72 via blocks.py:226-235).
+ * gate of head h at gate[r·ld_gate + h·gate_head_stride + d] (2·hd for the q_proj
+ * [q|gate] layout, hd for a gate-only projection); v rows: n_kv·hd. */
+int qsp_mtp_single_token_attn(const void* gate, int64_t ld_gate, int64_t gate_head_stride,
+                              const void* v, int64_t ld_v, void* out, int64_t ld_out,
+                              int64_t rows, int32_t n_heads, int32_t n_kv_heads,
+                              int32_t head_dim, int dtype, void* stream);
+
+/* dst[b,:] = src[(b·tokens + index[b]),:] — the pre-norm hidden at each sequence's last
+ * kept position, handed to the MTP head (mtp.py:155 `hidden_last = hidden2[:, 1:2]`). */
+int qsp_select_rows(const void* src, int64_t ld_src, int32_t batch, int32_t tokens,
+                    const int32_t* index, void* dst, int64_t ld_dst, int64_t dim, int dtype,
+                    void* stream);
+
+/* ---------------------------------------------------------------- token selection */
+
+/* Row-wise argmax (first index of the maximum, like torch.argmax) over `vocab` logits. */
+int qsp_argmax_rows(const void* logits, int64_t ld, int64_t rows, int64_t vocab,
+                    int64_t* out, int64_t out_stride, int dtype, void* stream);
+
+/*
+ * Greedy verification (temperature 0): row i of sequence b scores the token after input i.
+ * accept_n[b] = number of leading drafts equal to argmax of their row; next_tok[b] = argmax
+ * of row accept_n[b]; draft i of sequence b is drafts[b·drafts_ld + i]. The exact-match rule of generate_mtp (src/qwen3_5/mtp.py:144-162)
+ * generalised to k = tokens-1 drafts. argmax_out [B*T] optional.
+ */
+int qsp_greedy_verify(const void* logits, int64_t ld, int32_t batch, int32_t tokens,
+                      int64_t vocab, const int64_t* drafts, int64_t drafts_ld, int32_t* accept_n,
+                      int64_t* next_tok, int64_t* argmax_out, float* workspace, int dtype,
+                      void* stream);
+
+/*
+ * Lossless speculative sampling (new behaviour; the reference has none): with
+ * p_i = softmax(target_logits[b,i]/temperature), q_i = softmax(draft_logits[b,i]/temperature),
+ * draft i is accepted iff u_accept[b,i]·q_i(d_i) < p_i(d_i); at the first rejection the token
+ * is drawn by inverse CDF at u_resample[b] from max(0, p_i − q_i); after k acceptances a
+ * bonus token is drawn from p_k. Writes accept_n[b], next_tok[b].
+ */
+int qsp_spec_sample(const void* target_logits, int64_t ld_t, const void* draft_logits,
+                    int64_t ld_d, int32_t batch, int32_t k, int64_t vocab, float temperature,
+                    const int64_t* drafts, int64_t drafts_ld, const float* u_accept,
+                    const float* u_resample, int32_t* accept_n, int64_t* next_tok,
+                    float* workspace, int dtype, void* stream);
+
+/* Categorical draw by inverse CDF of softmax(logits/temperature) at u[r] (temperature > 0),
+ * or argmax (temperature <= 0): the draw of sample_next (src/generate.py:25-37). */
+int qsp_sample_rows(const void* logits, int64_t ld, int64_t rows, int64_t vocab,
+                    float temperature, const float* u, int64_t* out, int64_t out_stride,
+                    float* workspace, int dtype, void* stream);
+
+/* Bytes of fp32 workspace the selection kernels need for `rows` rows of `vocab`. */
+size_t qsp_select_workspace_bytes(int64_t rows, int64_t vocab);
+
+/* ---------------------------------------------------------------- cache bookkeeping */
+
+/* After a forward of T tokens: seq_lens[b] += T; parity ^= 1; speculative → replay_n =
+ * conv_off = T (keep all unless qsp_cache_accept trims), commit-all → both 0. This is the
+ * reference's `advance(n)` (kv.py:46-47) for per-sequence lengths. */
+int qsp_cache_finalize(int32_t batch, int32_t tokens, int32_t speculative, int32_t* seq_lens,
+                       int32_t* replay_n, int32_t* conv_off, int32_t* parity, void* stream);
+
+/* Keep only keep[b] = accept_n[b] + 1 of the last speculative call's T tokens: the
+ * index rollback that replaces `past.clone()` + restore + recompute (mtp.py:141,156-162). */
+int qsp_cache_accept(int32_t batch, int32_t tokens, const int32_t* accept_n,
+                     int32_t* seq_lens, int32_t* replay_n, int32_t* conv_off, void* stream);
+
+/* Copy committed step tokens into per-sequence output streams: out[b, n_out[b] + j] =
+ * ids[b, j] for j <= accept_n[b] (capacity-checked), n_out[b] += accept_n[b]+1; then
+ * ids[b,0] := next_tok[b] (the next pending token). */
+int qsp_commit_tokens(int32_t batch, int32_t tokens, int64_t* ids, const int32_t* accept_n,
+                      const int64_t* next_tok, int64_t* out, int64_t out_cap, int32_t* n_out,
+                      void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QSP_H_ */

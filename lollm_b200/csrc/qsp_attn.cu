@@ -1,0 +1,291 @@
+// Gated full attention over the paged KV cache: prep (QK-norm, partial RoPE, KV append),
+// split-KV attention of the T new queries, and the merge of the splits with the σ(gate)
+// output gate.
+#include "qsp_common.cuh"
+
+namespace qsp {
+
+// ------------------------------------------------------------------ prep
+// One CTA per token row m = b*T + t; warps loop over the q and k heads.
+template <typename T>
+__global__ void attn_prep_kernel(const qsp_attn_layer L) {
+  extern __shared__ float sx[];  // [warps][hd]
+  const int m = blockIdx.x;
+  const int b = m / L.tokens, t = m % L.tokens;
+  const int hd = L.head_dim, rd = L.rotary_dim, half = rd / 2;
+  const int nh = L.n_heads, nkv = L.n_kv_heads;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const T* row = static_cast<const T*>(L.qkv) + (int64_t)m * L.ld_qkv;
+  const int pos = L.seq_lens[b] + t;
+  const int lp = pos / L.page_size, slot = pos % L.page_size;
+  int page = -1;
+  if (pos >= 0 && pos < L.rope_rows && lp < L.max_pages) page = L.page_table[(int64_t)b * L.max_pages + lp];
+  const bool ok = page >= 0 && page < L.num_pages;
+  if (!ok) {
+    if (threadIdx.x == 0 && L.bad_index != nullptr) *L.bad_index = 1;
+  }
+  const T* cosr = static_cast<const T*>(L.rope_cos) + (int64_t)(ok ? pos : 0) * rd;
+  const T* sinr = static_cast<const T*>(L.rope_sin) + (int64_t)(ok ? pos : 0) * rd;
+  float* xs = sx + warp * hd;
+  for (int hh = warp; hh < nh + nkv; hh += nw) {
+    const bool isq = hh < nh;
+    const T* src = isq ? row + (int64_t)hh * 2 * hd : row + (int64_t)nh * 2 * hd + (int64_t)(hh - nh) * hd;
+    const T* w = static_cast<const T*>(isq ? L.q_norm_w : L.k_norm_w);
+    float ss = 0.f;
+    for (int d = lane; d < hd; d += 32) {
+      const float v = dt<T>::to_f(src[d]);
+      xs[d] = v;
+      ss = fmaf(v, v, ss);
+    }
+    ss = warp_sum(ss);
+    const float inv = rsqrtf(ss / (float)hd + L.eps);
+    for (int d = lane; d < hd; d += 32) xs[d] = dt<T>::round(xs[d] * inv * (dt<T>::to_f(w[d]) + 1.0f));
+    __syncwarp();
+    T* dst;
+    if (isq) dst = static_cast<T*>(L.q_buf) + ((int64_t)m * nh + hh) * hd;
+    else dst = ok ? static_cast<T*>(L.k_pages) + (((int64_t)page * nkv + (hh - nh)) * L.page_size + slot) * hd : nullptr;
+    if (dst != nullptr) {
+      for (int d = lane; d < hd; d += 32) {
+        float v = xs[d];
+        if (d < rd) {
+          const float c = dt<T>::to_f(cosr[d]), s = dt<T>::to_f(sinr[d]);
+          const float r = d < half ? -xs[d + half] : xs[d - half];
+          v = dt<T>::round(dt<T>::round(v * c) + dt<T>::round(r * s));
+        }
+        dst[d] = dt<T>::from_f(v);
+      }
+    }
+    __syncwarp();
+  }
+  if (ok) {
+    const T* vsrc = row + (int64_t)nh * 2 * hd + (int64_t)nkv * hd;
+    for (int e = threadIdx.x; e < nkv * hd; e += blockDim.x) {
+      const int g = e / hd, d = e % hd;
+      static_cast<T*>(L.v_pages)[(((int64_t)page * nkv + g) * L.page_size + slot) * hd + d] = vsrc[e];
+    }
+  }
+}
+
+// ------------------------------------------------------------------ split-KV attention (CUDA cores)
+// CTA (split s, kv head g, sequence b × row group). Rows r of the group map to
+// (t = r / n_rep, q head g*n_rep + r % n_rep). Keys are staged 32 at a time; lane j scores key j.
+constexpr int AT_KT = 32;
+
+template <typename T, int HD, int RPW>
+__global__ void __launch_bounds__(128) attn_simt_kernel(const qsp_attn_layer L, int chunk,
+                                                        int n_row_groups) {
+  constexpr int DPL = HD / 32;
+  extern __shared__ float smem[];
+  const int s = blockIdx.x, g = blockIdx.y;
+  const int b = blockIdx.z / n_row_groups, rgp = blockIdx.z % n_row_groups;
+  const int nrep = L.n_heads / L.n_kv_heads;
+  const int rows_total = nrep * L.tokens;
+  const int row0 = rgp * 4 * RPW;
+  const int nrows = min(4 * RPW, rows_total - row0);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int base_len = L.seq_lens[b];
+  const int kv_len = base_len + L.tokens;
+  const int k_begin = s * chunk;
+  const int k_end = min(kv_len, k_begin + chunk);
+  // smem: Q [4*RPW][HD] fp32, K [32][HD+1] fp32, V [32][HD] fp32
+  float* Qs = smem;
+  float* Ks = Qs + 4 * RPW * HD;
+  float* Vs = Ks + AT_KT * (HD + 1);
+
+  const T* qb = static_cast<const T*>(L.q_buf);
+  for (int e = threadIdx.x; e < nrows * HD; e += blockDim.x) {
+    const int r = e / HD, d = e % HD;
+    const int rr = row0 + r, t = rr / nrep, hq = g * nrep + rr % nrep;
+    Qs[r * HD + d] = dt<T>::to_f(qb[(((int64_t)b * L.tokens + t) * L.n_heads + hq) * HD + d]);
+  }
+  float acc[RPW][DPL];
+  float mrow[RPW], lrow[RPW];
+#pragma unroll
+  for (int i = 0; i < RPW; ++i) {
+    mrow[i] = -INFINITY;
+    lrow[i] = 0.f;
+#pragma unroll
+    for (int j = 0; j < DPL; ++j) acc[i][j] = 0.f;
+  }
+  const T* kp = static_cast<const T*>(L.k_pages);
+  const T* vp = static_cast<const T*>(L.v_pages);
+  for (int k0 = k_begin; k0 < k_end; k0 += AT_KT) {
+    __syncthreads();
+    for (int e = threadIdx.x; e < AT_KT * HD; e += blockDim.x) {
+      const int j = e / HD, d = e % HD;
+      const int pos = k0 + j;
+      float kv = 0.f, vv = 0.f;
+      if (pos < k_end && pos / L.page_size < L.max_pages) {
+        const int page = L.page_table[(int64_t)b * L.max_pages + pos / L.page_size];
+        if (page >= 0 && page < L.num_pages) {
+          const int64_t off = (((int64_t)page * L.n_kv_heads + g) * L.page_size + pos % L.page_size) * HD + d;
+          kv = dt<T>::to_f(kp[off]);
+          vv = dt<T>::to_f(vp[off]);
+        }
+      }
+      Ks[j * (HD + 1) + d] = kv;
+      Vs[j * HD + d] = vv;
+    }
+    __syncthreads();
+    const int kpos = k0 + lane;
+#pragma unroll
+    for (int i = 0; i < RPW; ++i) {
+      const int r = warp + 4 * i;
+      if (r >= nrows) break;
+      const int rr = row0 + r;
+      const int qpos = base_len + rr / nrep;
+      float sc = 0.f;
+      const float* q = Qs + r * HD;
+      const float* kr = Ks + lane * (HD + 1);
+#pragma unroll 8
+      for (int d = 0; d < HD; ++d) sc = fmaf(q[d], kr[d], sc);
+      sc *= L.scale;
+      const bool vis = kpos < k_end && kpos <= qpos;
+      sc = vis ? sc : -INFINITY;
+      const float mt = warp_max(sc);
+      const float mnew = fmaxf(mrow[i], mt);
+      if (mnew == -INFINITY) continue;  // nothing visible yet for this row
+      const float alpha = expf(mrow[i] - mnew);
+      const float p = vis ? expf(sc - mnew) : 0.f;
+      lrow[i] = lrow[i] * alpha + warp_sum(p);
+      mrow[i] = mnew;
+#pragma unroll
+      for (int j = 0; j < DPL; ++j) acc[i][j] *= alpha;
+      for (int jj = 0; jj < AT_KT; ++jj) {
+        const float pj = __shfl_sync(0xffffffffu, p, jj);
+        if (pj != 0.f) {
+#pragma unroll
+          for (int j = 0; j < DPL; ++j) acc[i][j] = fmaf(pj, Vs[jj * HD + lane + 32 * j], acc[i][j]);
+        }
+      }
+    }
+  }
+  // write partials: o (unnormalised), m, l
+#pragma unroll
+  for (int i = 0; i < RPW; ++i) {
+    const int r = warp + 4 * i;
+    if (r >= nrows) break;
+    const int rr = row0 + r, t = rr / nrep, hq = g * nrep + rr % nrep;
+    const int64_t idx = (((int64_t)b * L.n_heads + hq) * L.tokens + t) * L.num_splits + s;
+    float* po = L.partial + idx * (HD + 2);
+#pragma unroll
+    for (int j = 0; j < DPL; ++j) po[lane + 32 * j] = acc[i][j];
+    if (lane == 0) {
+      po[HD] = mrow[i];
+      po[HD + 1] = lrow[i];
+    }
+  }
+}
+
+// ------------------------------------------------------------------ merge splits + gate
+template <typename T>
+__global__ void attn_combine_kernel(const qsp_attn_layer L) {
+  const int m = blockIdx.x, hq = blockIdx.y;
+  const int b = m / L.tokens, t = m % L.tokens;
+  const int hd = L.head_dim, ns = L.num_splits;
+  const float* base = L.partial + ((((int64_t)b * L.n_heads + hq) * L.tokens + t) * ns) * (hd + 2);
+  float M = -INFINITY;
+  for (int s = 0; s < ns; ++s) M = fmaxf(M, base[(int64_t)s * (hd + 2) + hd]);
+  const T* row = static_cast<const T*>(L.qkv) + (int64_t)m * L.ld_qkv;
+  T* o = static_cast<T*>(L.out) + (int64_t)m * L.ld_out + (int64_t)hq * hd;
+  for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+    float num = 0.f, den = 0.f;
+    if (M != -INFINITY) {
+      for (int s = 0; s < ns; ++s) {
+        const float* p = base + (int64_t)s * (hd + 2);
+        const float ms = p[hd];
+        if (ms == -INFINITY) continue;
+        const float w = expf(ms - M);
+        num = fmaf(w, p[d], num);
+        den = fmaf(w, p[hd + 1], den);
+      }
+    }
+    const float attn = dt<T>::round(den > 0.f ? num / den : 0.f);
+    const float gate = dt<T>::to_f(row[(int64_t)hq * 2 * hd + hd + d]);
+    o[d] = dt<T>::from_f(attn * dt<T>::round(sigmoidf_(gate)));
+  }
+}
+
+static int attn_chunk(const qsp_attn_layer& L) {
+  const int cap = L.max_pages * L.page_size;
+  int chunk = (cap + L.num_splits - 1) / L.num_splits;
+  chunk = ((chunk + AT_KT - 1) / AT_KT) * AT_KT;
+  return chunk;
+}
+
+template <typename T, int HD, int RPW>
+static int launch_attn_simt(const qsp_attn_layer& L, cudaStream_t st) {
+  const int rows_total = (L.n_heads / L.n_kv_heads) * L.tokens;
+  const int n_rg = (rows_total + 4 * RPW - 1) / (4 * RPW);
+  const size_t smem = (size_t)(4 * RPW * HD + AT_KT * (HD + 1) + AT_KT * HD) * sizeof(float);
+  auto kern = attn_simt_kernel<T, HD, RPW>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  dim3 grid(L.num_splits, L.n_kv_heads, L.batch * n_rg);
+  kern<<<grid, 128, smem, st>>>(L, attn_chunk(L), n_rg);
+  int rc = check_launch("qsp_attn_verify(simt)");
+  if (rc) return rc;
+  attn_combine_kernel<T><<<dim3(L.batch * L.tokens, L.n_heads), 128, 0, st>>>(L);
+  return check_launch("qsp_attn_verify(combine)");
+}
+
+}  // namespace qsp
+
+using namespace qsp;
+
+static int validate_attn(const qsp_attn_layer* p, bool need_ws) {
+  QSP_REQUIRE(p != nullptr, "qsp_attn: null layer");
+  const qsp_attn_layer& L = *p;
+  QSP_REQUIRE(L.qkv && L.q_norm_w && L.k_norm_w && L.rope_cos && L.rope_sin && L.k_pages &&
+                  L.v_pages && L.page_table && L.seq_lens && L.q_buf,
+              "qsp_attn: null pointer");
+  QSP_REQUIRE(L.batch > 0 && L.tokens > 0 && L.batch * L.tokens < (1 << 30), "qsp_attn: bad batch/tokens");
+  QSP_REQUIRE(L.n_heads > 0 && L.n_kv_heads > 0 && L.n_heads % L.n_kv_heads == 0,
+              "qsp_attn: n_heads must be a multiple of n_kv_heads");
+  QSP_REQUIRE(L.head_dim == 32 || L.head_dim == 64 || L.head_dim == 128 || L.head_dim == 256,
+              "qsp_attn: head_dim %d not built", L.head_dim);
+  QSP_REQUIRE(L.rotary_dim >= 0 && L.rotary_dim <= L.head_dim && L.rotary_dim % 2 == 0,
+              "qsp_attn: bad rotary_dim");
+  QSP_REQUIRE(L.page_size > 0 && L.max_pages > 0 && L.num_pages > 0, "qsp_attn: bad paging");
+  QSP_REQUIRE(L.ld_qkv >= 2ll * L.n_heads * L.head_dim + 2ll * L.n_kv_heads * L.head_dim,
+              "qsp_attn: ld_qkv too small");
+  if (need_ws) {
+    QSP_REQUIRE(L.out && L.partial && L.num_splits > 0 && L.ld_out >= (int64_t)L.n_heads * L.head_dim,
+                "qsp_attn_verify: missing output/workspace");
+  }
+  return QSP_OK;
+}
+
+extern "C" {
+
+int qsp_attn_prep(const qsp_attn_layer* layer, void* stream) {
+  int rc = validate_attn(layer, false);
+  if (rc) return rc;
+  const qsp_attn_layer& L = *layer;
+  const size_t smem = 4 * L.head_dim * sizeof(float);
+  QSP_DISPATCH_DTYPE(L.dtype, T, {
+    attn_prep_kernel<T><<<L.batch * L.tokens, 128, smem, as_stream(stream)>>>(L);
+  });
+  return check_launch("qsp_attn_prep");
+}
+
+int qsp_attn_verify(const qsp_attn_layer* layer, void* stream) {
+  int rc = validate_attn(layer, true);
+  if (rc) return rc;
+  const qsp_attn_layer& L = *layer;
+  cudaStream_t st = as_stream(stream);
+  QSP_DISPATCH_DTYPE(L.dtype, T, {
+    switch (L.head_dim) {
+      case 32: return launch_attn_simt<T, 32, 16>(L, st);
+      case 64: return launch_attn_simt<T, 64, 16>(L, st);
+      case 128: return launch_attn_simt<T, 128, 8>(L, st);
+      default: return launch_attn_simt<T, 256, 8>(L, st);
+    }
+  });
+}
+
+size_t qsp_attn_workspace_bytes(int32_t batch, int32_t tokens, int32_t n_heads, int32_t head_dim,
+                                int32_t num_splits) {
+  return (size_t)batch * tokens * n_heads * num_splits * (head_dim + 2) * sizeof(float);
+}
+
+}  // extern "C"

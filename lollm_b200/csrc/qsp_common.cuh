@@ -1,0 +1,89 @@
+// Shared helpers for the qsp (qwen3_5 speculative step) CUDA library, sm_100a.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <stdarg.h>
+
+#include "../../include/qsp.h"
+
+namespace qsp {
+
+// ---------------------------------------------------------------- errors
+int set_error(int code, const char* fmt, ...);
+int check_launch(const char* what);
+
+#define QSP_REQUIRE(cond, ...)                                   \
+  do {                                                           \
+    if (!(cond)) return ::qsp::set_error(QSP_ERR_INVALID, __VA_ARGS__); \
+  } while (0)
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+inline bool aligned(const void* p, size_t a) {
+  return (reinterpret_cast<uintptr_t>(p) % a) == 0;
+}
+
+// ---------------------------------------------------------------- dtype plumbing
+template <typename T> struct dt;
+template <> struct dt<float> {
+  static __device__ __forceinline__ float to_f(float x) { return x; }
+  static __device__ __forceinline__ float from_f(float x) { return x; }
+  // value after a round trip through the storage type (identity for fp32)
+  static __device__ __forceinline__ float round(float x) { return x; }
+};
+template <> struct dt<__nv_bfloat16> {
+  static __device__ __forceinline__ float to_f(__nv_bfloat16 x) { return __bfloat162float(x); }
+  static __device__ __forceinline__ __nv_bfloat16 from_f(float x) { return __float2bfloat16_rn(x); }
+  static __device__ __forceinline__ float round(float x) {
+    return __bfloat162float(__float2bfloat16_rn(x));
+  }
+};
+
+template <typename T> __device__ __forceinline__ float ld_f(const T* p) { return dt<T>::to_f(*p); }
+template <typename T> __device__ __forceinline__ void st_f(T* p, float v) { *p = dt<T>::from_f(v); }
+
+// ---------------------------------------------------------------- math
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + expf(-x)); }
+__device__ __forceinline__ float siluf_(float x) { return x / (1.0f + expf(-x)); }
+// torch.nn.functional.softplus(x) with its default threshold of 20
+__device__ __forceinline__ float softplusf_(float x) { return x > 20.0f ? x : log1pf(expf(x)); }
+
+// Block-wide sum for blockDim.x <= 1024 (multiple of 32); `red` holds >= 32 floats.
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+  v = warp_sum(v);
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float t = (lane < nw) ? red[lane] : 0.0f;
+  t = warp_sum(t);
+  return t;
+}
+
+}  // namespace qsp
+
+#define QSP_DISPATCH_DTYPE(dtype, T, ...)                                  \
+  do {                                                                     \
+    if ((dtype) == QSP_F32) {                                              \
+      using T = float;                                                     \
+      __VA_ARGS__                                                          \
+    } else if ((dtype) == QSP_BF16) {                                      \
+      using T = __nv_bfloat16;                                             \
+      __VA_ARGS__                                                          \
+    } else {                                                               \
+      return ::qsp::set_error(QSP_ERR_UNSUPPORTED, "unsupported dtype %d", (int)(dtype)); \
+    }                                                                      \
+  } while (0)

@@ -1,0 +1,209 @@
+"""Qwen3_5Model — the family forward, driven through the qsp C ABI on the GPU.
+
+Contract of the reference (src/qwen3_5/modeling_qwen3_5.py:82-102):
+    forward(input_ids, past=None, return_hidden=False) -> (logits, past[, hidden])
+with `past` the family cache object and `hidden` the pre-final-norm residual stream the MTP
+head consumes. Extensions, all keyword-only and off by default:
+    speculative=True   leave this call's GDN updates pending so the caller can keep a prefix
+                       of the T tokens by index (`past.accept(accept_n)`);
+    copy_outputs=False return views of the internal activation buffers (the speculative
+                       engine uses this; they are overwritten by the next call).
+
+Per layer (modeling_qwen3_5.py:47-61), every box a C-ABI launch:
+    RMSNorm → [GDN: in_proj(qkv|z|b|a) GEMM → qsp_gdn_verify → out_proj GEMM(+residual)]
+            | [attn: q|k|v GEMM → qsp_attn_prep → qsp_attn_verify → o_proj GEMM(+residual)]
+    RMSNorm → gate|up GEMM → SwiGLU → down GEMM(+residual)
+then the final RMSNorm and the lm_head GEMM. Projections of one input are concatenated into
+one weight so each reads the activation once.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+
+from .. import kernels as K
+from .. import _lib as L
+from .config import Qwen3_5Config
+from .kv import Qwen3_5Cache
+
+
+def rope_table(rotary_dim: int, theta: float, rows: int, dtype):
+    """cos/sin (rows, rotary_dim) for positions 0..rows-1, built exactly as the reference's
+    RoPE.cos_sin (blocks.py:166-173): fp32 inv_freq = 1/θ^(2i/rd), freqs = pos·inv_freq,
+    duplicated halves, cos/sin in fp32, cast to the model dtype. Computed once on the host."""
+    idx = torch.arange(0, rotary_dim, 2, dtype=torch.float32)
+    inv = 1.0 / (theta ** (idx / rotary_dim))
+    f = torch.arange(rows).float()[:, None] * inv[None, :]
+    f = torch.cat([f, f], dim=-1)
+    return f.cos().to(dtype), f.sin().to(dtype)
+
+
+class _Workspace:
+    """Activation buffers for one (batch, tokens) shape, reused across calls (and stable
+    under CUDA-graph capture)."""
+
+    def __init__(self, model: "Qwen3_5Model", B: int, T: int, num_splits: int):
+        cfg, dt, dev = model.cfg, model.dtype, model.device
+        M = B * T
+        H = cfg.hidden_size
+        n_in = cfg.conv_dim + cfg.value_dim + 2 * cfg.linear_num_value_heads
+        n_qkv = 2 * cfg.num_attention_heads * cfg.head_dim + 2 * cfg.num_key_value_heads * cfg.head_dim
+        e = lambda *s: torch.empty(*s, dtype=dt, device=dev)
+        self.x = e(M, H)
+        self.xn = e(M, H)
+        self.proj = e(M, max(n_in, n_qkv))
+        self.core = e(M, max(cfg.value_dim, cfg.num_attention_heads * cfg.head_dim))
+        self.q_buf = e(M, cfg.num_attention_heads * cfg.head_dim)
+        inter = cfg.intermediate_size if not cfg.is_moe else cfg.moe_intermediate_size
+        self.gu = e(M, 2 * max(inter, 1))
+        self.act = e(M, max(inter, 1))
+        self.logits = e(M, cfg.vocab_size)
+        self.num_splits = num_splits
+        ws = K.attn_workspace_bytes(B, T, cfg.num_attention_heads, cfg.head_dim, num_splits)
+        self.partial = torch.empty(max(ws // 4, 1), dtype=torch.float32, device=dev)
+
+
+class Qwen3_5Model:
+    def __init__(self, cfg: Qwen3_5Config, params: dict, *, dtype=torch.bfloat16, device="cuda",
+                 max_positions: int = 8192, page_size: int = 64, max_spec_tokens: int = 8):
+        L.load()
+        self.cfg, self.dtype, self.device = cfg, dtype, torch.device(device)
+        if self.device.type != "cuda":
+            raise RuntimeError("Qwen3_5Model runs on CUDA only (no CPU fallback)")
+        if cfg.is_moe:
+            raise NotImplementedError("qwen3_5_moe sparse FFN is not built yet")
+        self.page_size, self.max_spec_tokens = page_size, max_spec_tokens
+        self.max_positions = max_positions
+        dev = self.device
+        g = lambda n: params[n].to(device=dev, dtype=dtype).contiguous()
+        self.embed = g("model.embed_tokens.weight")
+        self.lm_head = self.embed if params["lm_head.weight"] is params["model.embed_tokens.weight"] \
+            else g("lm_head.weight")
+        self.final_norm = g("model.norm.weight")
+        self.layers = []
+        for i in range(cfg.num_hidden_layers):
+            p = f"model.layers.{i}."
+            lw = {"type": cfg.layer_type(i), "in_norm": g(p + "input_layernorm.weight"),
+                  "post_norm": g(p + "post_attention_layernorm.weight"),
+                  "w_gu": torch.cat([g(p + "mlp.gate_proj.weight"), g(p + "mlp.up_proj.weight")]).contiguous(),
+                  "down": g(p + "mlp.down_proj.weight")}
+            if lw["type"] == "full_attention":
+                a = p + "self_attn."
+                lw["w_qkv"] = torch.cat([g(a + "q_proj.weight"), g(a + "k_proj.weight"),
+                                         g(a + "v_proj.weight")]).contiguous()
+                lw["q_norm"], lw["k_norm"] = g(a + "q_norm.weight"), g(a + "k_norm.weight")
+                lw["o_proj"] = g(a + "o_proj.weight")
+            else:
+                a = p + "linear_attn."
+                lw["w_in"] = torch.cat([g(a + "in_proj_qkv.weight"), g(a + "in_proj_z.weight"),
+                                        g(a + "in_proj_b.weight"), g(a + "in_proj_a.weight")]).contiguous()
+                lw["conv_w"] = g(a + "conv1d.weight").reshape(cfg.conv_dim, cfg.linear_conv_kernel_dim).contiguous()
+                lw["a_log"], lw["dt_bias"] = g(a + "A_log"), g(a + "dt_bias")
+                lw["norm_w"], lw["out_proj"] = g(a + "norm.weight"), g(a + "out_proj.weight")
+            self.layers.append(lw)
+        cos, sin = rope_table(cfg.rotary_dim, cfg.rope_theta, max_positions, dtype)
+        self.rope_cos, self.rope_sin = cos.to(dev).contiguous(), sin.to(dev).contiguous()
+        self._ws = {}
+
+    # ------------------------------------------------------------------ helpers
+    def new_cache(self, batch: int, max_len: int | None = None, **kw) -> Qwen3_5Cache:
+        max_len = max_len or self.max_positions
+        if max_len > self.max_positions:
+            raise RuntimeError(f"max_len {max_len} exceeds the RoPE table ({self.max_positions})")
+        return Qwen3_5Cache(self.cfg, batch, max_len, dtype=self.dtype, device=self.device,
+                            page_size=kw.pop("page_size", self.page_size),
+                            max_spec_tokens=kw.pop("max_spec_tokens", self.max_spec_tokens), **kw)
+
+    def default_splits(self, B: int, cache: Qwen3_5Cache) -> int:
+        """Key splits per (sequence, kv head): ~512 keys per split, and enough CTAs to fill
+        the SMs twice over."""
+        n_seq_heads = B * self.cfg.num_key_value_heads
+        by_len = math.ceil(cache.capacity / 512)
+        by_fill = math.ceil(2 * 148 / max(n_seq_heads, 1))
+        return max(1, min(max(by_len, by_fill), math.ceil(cache.capacity / 32)))
+
+    def workspace(self, B: int, T: int, cache: Qwen3_5Cache) -> _Workspace:
+        key = (B, T, cache.capacity)
+        if key not in self._ws:
+            self._ws[key] = _Workspace(self, B, T, self.default_splits(B, cache))
+        return self._ws[key]
+
+    def attn_desc(self, lw, cache: Qwen3_5Cache, slot: int, ws: _Workspace, B: int, T: int):
+        cfg = self.cfg
+        d = L.AttnLayer()
+        d.batch, d.tokens = B, T
+        d.n_heads, d.n_kv_heads, d.head_dim, d.rotary_dim = (cfg.num_attention_heads, cfg.num_key_value_heads,
+                                                             cfg.head_dim, cfg.rotary_dim)
+        d.page_size, d.max_pages, d.num_pages = cache.page_size, cache.max_pages, cache.num_pages
+        d.dtype, d.eps, d.scale = L.dtype_code(self.dtype), cfg.rms_norm_eps, cfg.head_dim ** -0.5
+        d.qkv, d.ld_qkv = ws.proj.data_ptr(), ws.proj.stride(0)
+        d.q_norm_w, d.k_norm_w = lw["q_norm"].data_ptr(), lw["k_norm"].data_ptr()
+        d.rope_cos, d.rope_sin, d.rope_rows = self.rope_cos.data_ptr(), self.rope_sin.data_ptr(), self.max_positions
+        d.k_pages, d.v_pages = cache.k_pages[slot].data_ptr(), cache.v_pages[slot].data_ptr()
+        d.page_table, d.seq_lens = cache.page_table.data_ptr(), cache.seq_lens.data_ptr()
+        d.q_buf = ws.q_buf.data_ptr()
+        d.out, d.ld_out = ws.core.data_ptr(), ws.core.stride(0)
+        d.partial, d.num_splits = ws.partial.data_ptr(), ws.num_splits
+        d.bad_index = cache.bad_index.data_ptr()
+        return d
+
+    # ------------------------------------------------------------------ forward
+    @torch.no_grad()
+    def forward(self, input_ids: torch.Tensor, past: Qwen3_5Cache | None = None,
+                return_hidden: bool = False, *, speculative: bool = False,
+                copy_outputs: bool = True):
+        if input_ids.dim() != 2:
+            raise RuntimeError("input_ids must be (batch, tokens)")
+        B, T = input_ids.shape
+        ids = input_ids.to(device=self.device, dtype=torch.int64).contiguous()
+        cache = past if past is not None else self.new_cache(B)
+        if cache.batch != B:
+            raise RuntimeError(f"cache batch {cache.batch} != input batch {B}")
+        if speculative and T > cache.max_spec_tokens:
+            raise RuntimeError(f"speculative forward of {T} tokens > max_spec_tokens {cache.max_spec_tokens}")
+        self._forward_into(ids, cache, B, T, speculative)
+        ws = self.workspace(B, T, cache)
+        logits = ws.logits.view(B, T, -1)
+        hidden = ws.x.view(B, T, -1)
+        if copy_outputs:
+            logits, hidden = logits.clone(), hidden.clone()
+        if return_hidden:
+            return logits, cache, hidden
+        return logits, cache
+
+    __call__ = forward
+
+    def _forward_into(self, ids, cache: Qwen3_5Cache, B: int, T: int, speculative: bool):
+        cfg = self.cfg
+        ws = self.workspace(B, T, cache)
+        M = B * T
+        eps = cfg.rms_norm_eps
+        K.embed(ids, self.embed, ws.x, rows=M, bad=cache.bad_index)
+        for i, lw in enumerate(self.layers):
+            K.rmsnorm(ws.x, lw["in_norm"], ws.xn, eps, rows=M)
+            if lw["type"] == "full_attention":
+                slot = cache.attn_slot[i]
+                K.gemm(ws.xn, lw["w_qkv"], ws.proj, m=M)
+                d = self.attn_desc(lw, cache, slot, ws, B, T)
+                K.attn_prep(d)
+                K.attn_verify(d)
+                K.gemm(ws.core, lw["o_proj"], ws.x, accumulate=True, m=M)
+            else:
+                slot = cache.gdn_slot[i]
+                K.gemm(ws.xn, lw["w_in"], ws.proj, m=M)
+                d = cache.gdn_desc(slot, ws.proj, ws.proj.stride(0), T, lw["conv_w"], lw["a_log"],
+                                   lw["dt_bias"], lw["norm_w"], None, ws.core, speculative)
+                K.gdn_verify(d)
+                K.gemm(ws.core, lw["out_proj"], ws.x, accumulate=True, m=M)
+            K.rmsnorm(ws.x, lw["post_norm"], ws.xn, eps, rows=M)
+            inter = lw["down"].shape[1]
+            K.gemm(ws.xn, lw["w_gu"], ws.gu, m=M)
+            K.swiglu(ws.gu, ws.act, inter, rows=M)
+            K.gemm(ws.act, lw["down"], ws.x, accumulate=True, m=M)
+        K.rmsnorm(ws.x, self.final_norm, ws.xn, eps, rows=M)
+        K.gemm(ws.xn, self.lm_head, ws.logits, m=M)
+        K.cache_finalize(B, T, speculative, cache.seq_lens, cache.replay_n, cache.conv_off, cache.parity)
+        cache.last_tokens, cache.last_speculative = T, speculative
+        return ws

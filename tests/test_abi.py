@@ -1,0 +1,63 @@
+"""The C ABI library loads (no GPU needed) and exports every entry point include/qsp.h
+declares, with matching ctypes signatures; the product path refuses to run on the CPU."""
+
+import os
+import re
+
+import pytest
+import torch
+
+from lollm_b200 import _lib as L
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_symbols():
+    src = open(os.path.join(ROOT, "include", "qsp.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(qsp_\w+)\s*\(", src)))
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    lib = L.load()
+    names = declared_symbols()
+    assert len(names) >= 20
+    for n in names:
+        assert hasattr(lib, n), f"libqsp.so does not export {n}"
+        assert n in L.SIGNATURES, f"no ctypes signature for {n}"
+    assert lib.qsp_abi_version() == 1
+
+
+def test_struct_layouts_match_header():
+    # field counts mirror the C structs; sizes follow natural alignment on x86-64
+    assert L.GdnLayer.ld_out.offset + 8 == L.ctypes_sizeof(L.GdnLayer) if hasattr(L, "ctypes_sizeof") else True
+    import ctypes
+    assert ctypes.sizeof(L.GdnLayer) == 4 * 11 + 4 + 8 * 14
+    assert ctypes.sizeof(L.AttnLayer) % 8 == 0
+
+
+def test_argument_validation_without_gpu():
+    """Invalid arguments are rejected by the host-side checks before any launch."""
+    lib = L.load()
+    rc = lib.qsp_gemm(None, 1, None, 1, None, 1, 1, 1, 1, 0, 0, None)
+    assert rc == L.QSP_ERR_INVALID
+    assert b"null" in lib.qsp_last_error()
+    rc = lib.qsp_cache_finalize(0, 1, 0, None, None, None, None, None)
+    assert rc == L.QSP_ERR_INVALID
+
+
+def test_model_refuses_cpu():
+    from lollm_b200.qwen3_5.config import MICRO, Qwen3_5Config
+    from lollm_b200.qwen3_5 import Qwen3_5Model
+    from lollm_b200.qwen3_5.weights import load_checkpoint, random_init
+    cfg = Qwen3_5Config.from_hf(MICRO)
+    P = load_checkpoint(cfg, random_init(cfg, 0))
+    with pytest.raises(RuntimeError):
+        Qwen3_5Model(cfg, P, dtype=torch.float32, device="cpu")
+
+
+def test_kernel_wrappers_refuse_cpu_tensors():
+    from lollm_b200 import kernels as K
+    x = torch.zeros(2, 8)
+    with pytest.raises(RuntimeError):
+        K.rmsnorm(x, torch.zeros(8), x, 1e-6)
