@@ -1,0 +1,426 @@
+"""Benchmark: generated tok/s of the qwen3_5 MTP speculative-decoding step (2B shape, bf16,
+batch 64 per GPU, 2048-token prompts, k=3 recurrent MTP drafts, greedy), and the verify
+step's fraction of the HBM roofline.
+
+    python bench.py [--gpus N --steps K --warmup W]          # this implementation
+    python bench.py --impl reference [...]                   # the reference's algorithm on CPU
+
+One step = draft k tokens with the MTP head → verify [pending, d1..dk] through the 24-layer
+hybrid stack → accept → keep a prefix by index → emit, for all sequences of this GPU. The
+step runs as three CUDA graphs (draft / verify / accept+commit) so each phase is timed with
+CUDA events on its stream. Inputs are far larger than L2 (4 GB of weights, 2.4 GB of GDN
+state, 1.8 GB of KV per step), so no L2 flush is needed between steps.
+
+Multi-GPU (torchrun): one process per GPU, each its own replica and its own 64 sequences
+(weak scaling; sequences are independent, no collective on the data path). Rank 0 prints
+one JSON line; times are the max over ranks.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "generated tok/s (batch 64, k=3) at 1/2/4/8 B200; verify-step HBM % of peak"
+UNIT = "tok/s"
+
+
+# ─────────────────────────────────────────── helpers ───────────────────────────────────────────
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d["hbm_gbs"], d["bf16_tflops"], "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def dist_setup():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if ws > 1:
+        import datetime
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                             device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return ws, rank, local
+
+
+def barrier(ws):
+    if ws > 1:
+        torch.distributed.barrier()
+
+
+def reduce_max(x: float, ws: int) -> float:
+    if ws == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+def reduce_sum(x: float, ws: int) -> float:
+    if ws == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.SUM)
+    return float(t.item())
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled every 200 ms during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.idx = device_index
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.p = None
+
+    def start(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                       "-i", str(self.idx), "-lms", "200"], stdout=self.f,
+                                      stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+
+    def stop(self):
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.p.terminate()
+        try:
+            self.p.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.p.kill()
+        self.f.flush()
+        rows = [l.strip().split(", ") for l in open(self.f.name) if l.strip()]
+        sm = [float(r[1]) for r in rows if len(r) >= 9 and r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if len(r) >= 9 and r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows if len(r) >= 9 for i in range(4) if r[5 + i].strip() == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def verify_step_bytes(cfg, B, T, ctx_lens):
+    """Algorithmic HBM bytes of one verify forward (the minimum any implementation moves):
+    every weight except the embedding table once (lm_head counted once; the embedding gather
+    is B·T rows), the K/V of every visible key once plus the T new rows written, the fp32
+    GDN state read once and written once, the conv window read and written."""
+    from lollm_b200.qwen3_5.weights import param_specs
+    elt = 2
+    w = 0
+    for name, shape in param_specs(cfg, with_mtp=False):
+        if name == "model.embed_tokens.weight":
+            continue
+        w += math.prod(shape) * elt
+    if cfg.tie_word_embeddings:
+        w += cfg.vocab_size * cfg.hidden_size * elt
+    n_attn, n_gdn = len(cfg.attn_layers), len(cfg.gdn_layers)
+    kv_row = n_attn * cfg.num_key_value_heads * cfg.head_dim * 2 * elt
+    kv = sum(kv_row * (L + T) for L in ctx_lens) + kv_row * T * B
+    state = 2 * n_gdn * B * cfg.linear_num_value_heads * cfg.linear_key_head_dim * cfg.linear_value_head_dim * 4
+    conv = 2 * n_gdn * B * cfg.conv_dim * (cfg.linear_conv_kernel_dim - 1) * elt
+    return {"weights": w, "kv": kv, "gdn_state": state, "conv": conv, "total": w + kv + state + conv}
+
+
+# ─────────────────────────────────────────── CPU arm ───────────────────────────────────────────
+
+def cpu_reference_sample(cfg, batch, ctx, k, steps, warmup, seed=0, budget_s=None):
+    """The reference's own algorithm on the host cores (the oracle restatement of
+    generate_mtp generalised to k drafts: draft → clone → verify → exact-match accept →
+    restore + recompute on rejection), bf16, on a synthetic prefilled state of `ctx`
+    tokens per sequence. Returns (tok/s, tokens, seconds, steps_run, threads)."""
+    from oracle import loops as OL
+    from oracle import qwen35 as Q
+    from lollm_b200.qwen3_5.weights import load_checkpoint, random_init
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    torch.manual_seed(seed)
+    P = load_checkpoint(cfg, random_init(cfg, seed, dtype=torch.bfloat16, generator="torch"))
+    g = torch.Generator().manual_seed(seed + 1)
+    dt = torch.bfloat16
+    cache = Q.OracleCache(cfg.num_hidden_layers, lens=[ctx] * batch)
+    for i in cfg.attn_layers:
+        cache.kv[i] = [(torch.randn(cfg.num_key_value_heads, ctx, cfg.head_dim, generator=g).to(dt),
+                        torch.randn(cfg.num_key_value_heads, ctx, cfg.head_dim, generator=g).to(dt))
+                       for _ in range(batch)]
+    for i in cfg.gdn_layers:
+        cache.gdn[i] = ((torch.randn(batch, cfg.conv_dim, cfg.linear_conv_kernel_dim - 1, generator=g)).to(dt),
+                        torch.randn(batch, cfg.linear_num_value_heads, cfg.linear_key_head_dim,
+                                    cfg.linear_value_head_dim, generator=g) * 0.1)
+    hidden = torch.randn(batch, cfg.hidden_size, generator=g).to(dt)
+    pending = torch.randint(0, cfg.vocab_size, (batch,), generator=g)
+    with torch.no_grad():
+        for _ in range(warmup):
+            cache, hidden, pending, committed, acc, _ = OL.spec_step(P, cfg, cache, hidden, pending, k, scan="reference")
+        toks, t0, n = 0, time.perf_counter(), 0
+        for _ in range(steps):
+            cache, hidden, pending, committed, acc, _ = OL.spec_step(P, cfg, cache, hidden, pending, k, scan="reference")
+            toks += sum(len(c) for c in committed)
+            n += 1
+            if budget_s is not None and time.perf_counter() - t0 > budget_s:
+                break
+        dt_s = time.perf_counter() - t0
+    return toks / dt_s, toks, dt_s, n, threads
+
+
+def run_reference_arm(args, cfg, ws, rank):
+    if rank != 0:
+        return
+    batch, ctx = args.cpu_batch, args.prompt
+    tps, toks, secs, n, threads = cpu_reference_sample(cfg, batch, ctx, args.k, args.steps, args.warmup)
+    line = {"metric": METRIC, "value": tps, "unit": UNIT, "n_gpus": args.gpus, "steps": n,
+            "warmup": args.warmup, "ms_per_step": 1000 * secs / max(n, 1), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded random-init weights, random prefilled state)",
+            "impl": "reference",
+            "config": config_block(args, cfg),
+            "cpu_baseline": {"value": tps, "unit": UNIT, "cores": threads, "kind": "port",
+                             "sample": f"{n} speculative steps x {batch} sequences at context {ctx}, "
+                                       f"k={args.k}, the oracle restatement of the reference's generate_mtp "
+                                       f"(clone + verify + restore/recompute) in bf16 on {threads} threads"},
+            "e2e": {"value": tps, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def config_block(args, cfg):
+    return {"workload": "qwen3_5 2B-shape MTP speculative decode step (BASELINE configs[1])",
+            "batch_per_gpu": args.batch, "global_batch": args.batch * args.gpus,
+            "prompt_len": args.prompt, "k": args.k, "hidden": cfg.hidden_size,
+            "layers": cfg.num_hidden_layers, "vocab": cfg.vocab_size, "sampling": "greedy",
+            "parallelism": f"replicas x{args.gpus} (sequence-sharded, no collective)",
+            "l2": "inputs larger than L2 (weights 4 GB + GDN state 2.4 GB per step)"}
+
+
+# ─────────────────────────────────────────── GPU arm ───────────────────────────────────────────
+
+# kernels launched per C-ABI call (entry points that launch more than one kernel)
+LAUNCHES = {"qsp_attn_verify": 2, "qsp_greedy_verify": 2, "qsp_spec_sample": 3, "qsp_sample_rows": 2}
+
+
+def count_launches(fn):
+    from lollm_b200 import _lib as L
+    n = {"calls": 0, "launches": 0}
+    orig = L.call
+
+    def counting(name, *a):
+        n["calls"] += 1
+        n["launches"] += LAUNCHES.get(name, 1)
+        return orig(name, *a)
+
+    L.call = counting
+    try:
+        fn()
+    finally:
+        L.call = orig
+    return n["launches"]
+
+
+def run_gpu_arm(args, cfg, ws, rank, local):
+    from lollm_b200.qwen3_5 import MTP, Qwen3_5Model, SpecDecoder
+    from lollm_b200.qwen3_5.weights import load_checkpoint, random_init
+    dev = torch.device("cuda", local)
+    t_setup = time.perf_counter()
+    # identical replicas on every rank (same seed), generated on the device
+    w = random_init(cfg, 0, dtype=torch.bfloat16, device=dev, generator="torch")
+    params = load_checkpoint(cfg, w, device=dev)
+    n_steps_total = args.warmup + 2 * args.steps + 4
+    max_len = args.prompt + (n_steps_total + 2) * (args.k + 1) + 16
+    model = Qwen3_5Model(cfg, params, dtype=torch.bfloat16, device=dev, max_positions=max_len + 64)
+    mtp = MTP(model, params)
+    del w, params
+    dec = SpecDecoder(model, mtp, args.batch, args.k, max_len, out_capacity=n_steps_total * (args.k + 1) + 8)
+    g = torch.Generator(device=dev)
+    g.manual_seed(1000 + rank)
+    prompts = torch.randint(0, cfg.vocab_size, (args.batch, args.prompt), generator=g, device=dev)
+    torch.cuda.synchronize()
+    t_pf = time.perf_counter()
+    dec.prefill(prompts, chunk=args.prefill_chunk)
+    torch.cuda.synchronize()
+    prefill_s = time.perf_counter() - t_pf
+    launches_per_step = count_launches(dec.step)     # one eager step (also warms workspaces)
+    graphs = capture_split(dec)
+    stream = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        replay_split(graphs)
+    torch.cuda.synchronize()
+
+    # ---------------- timed region: device-resident inputs
+    n0 = int(dec.n_out.sum())
+    ctx_lens = dec.cache.seq_lens.tolist()
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+    clocks = ClockSampler(local)
+    barrier(ws)
+    torch.cuda.synchronize()
+    clocks.start()
+    time.sleep(0.3)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for s in range(args.steps):
+        replay_split(graphs, ev[s], stream)
+    end.record(stream)
+    torch.cuda.synchronize()
+    barrier(ws)
+    clk = clocks.stop()
+    elapsed_ms = start.elapsed_time(end)
+    tokens = int(dec.n_out.sum()) - n0
+    phase = {"draft": [], "verify": [], "accept": []}
+    for e in ev:
+        phase["draft"].append(e[0].elapsed_time(e[1]))
+        phase["verify"].append(e[1].elapsed_time(e[2]))
+        phase["accept"].append(e[2].elapsed_time(e[3]))
+    max_ms = reduce_max(elapsed_ms, ws)
+    tot_tokens = reduce_sum(tokens, ws)
+    value = tot_tokens / (max_ms / 1000.0)
+    verify_ms = statistics.mean(phase["verify"])
+
+    # ---------------- e2e: public API with host buffers (H2D pending ids, D2H committed tokens)
+    B, T = args.batch, args.k + 1
+    h_ids = torch.empty(B, T, dtype=torch.int64, pin_memory=True)
+    h_acc = torch.empty(B, dtype=torch.int32, pin_memory=True)
+    h_tok = torch.empty(B, T, dtype=torch.int64, pin_memory=True)
+    h_ids.copy_(dec.ids.cpu())
+    barrier(ws)
+    torch.cuda.synchronize()
+    e2e_tokens = 0
+    es, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    es.record(stream)
+    for _ in range(args.steps):
+        dec.ids[:, :1].copy_(h_ids[:, :1], non_blocking=True)
+        ids_before = dec.ids.clone()
+        replay_split(graphs)
+        h_acc.copy_(dec.accept_n, non_blocking=True)
+        h_tok.copy_(ids_before, non_blocking=True)
+        h_ids[:, :1].copy_(dec.ids[:, :1], non_blocking=True)
+        stream.synchronize()                      # the host now holds this step's tokens
+        e2e_tokens += int(h_acc.sum()) + B
+    ee.record(stream)
+    torch.cuda.synchronize()
+    barrier(ws)
+    e2e_ms = reduce_max(es.elapsed_time(ee), ws)
+    e2e_value = reduce_sum(e2e_tokens, ws) / (e2e_ms / 1000.0)
+    h2d = B * 1 * 8
+    d2h = B * 4 + B * T * 8 + B * 8
+
+    # ---------------- roofline of the verify step (HBM-bound): algorithmic bytes / time
+    hbm, tflops, src = peaks()
+    vb = verify_step_bytes(cfg, B, T, ctx_lens)
+    achieved = vb["total"] / (verify_ms / 1000.0) / 1e9
+    acc_rate = (tokens / (args.steps * B) - 1.0) / args.k
+    out = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": max_ms / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded random-init weights, uniform random prompt ids)",
+        "config": config_block(args, cfg), "clocks": clk,
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "gpu_launches": launches_per_step * args.steps,
+        "roofline": {"kernel": "verify step (24-layer forward, T=k+1)", "bound": "hbm",
+                     "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                     "peak_source": src, "traffic": None,
+                     "algorithmic_bytes": vb},
+        "phases_ms": {k: statistics.mean(v) for k, v in phase.items()},
+        "acceptance_rate": acc_rate, "tokens_per_step_per_seq": tokens / (args.steps * B),
+        "prefill_s": prefill_s, "setup_s": time.perf_counter() - t_setup,
+    }
+    return out
+
+
+def capture_split(dec):
+    """Three CUDA graphs for one step: MTP drafting, the speculative verify forward, and
+    accept + rollback-by-index + commit. Replayed back to back they are exactly dec.step()."""
+    from lollm_b200 import kernels as K
+    m, B, T, k = dec.model, dec.B, dec.T, dec.k
+
+    def draft():
+        dec.mtp.draft(dec.hidden_last, dec.ids, k)
+
+    def verify():
+        dec._ws = m._forward_into(dec.ids, dec.cache, B, T, True)
+
+    def accept():
+        ws = m.workspace(B, T, dec.cache)
+        K.greedy_verify(ws.logits, B, T, dec.ids[:, 1:], T, dec.accept_n, dec.next_tok, dec.amax)
+        dec.cache.accept(dec.accept_n)
+        K.select_rows(ws.x, B, T, dec.accept_n, dec.hidden_last)
+        K.commit_tokens(B, T, dec.ids, dec.accept_n, dec.next_tok, dec.out, dec.n_out)
+
+    graphs = []
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        draft(); verify(); accept()          # one eager warm-up step on the capture stream
+    torch.cuda.current_stream().wait_stream(s)
+    for fn in (draft, verify, accept):
+        gph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gph):
+            fn()
+        graphs.append(gph)
+    return graphs
+
+
+def replay_split(graphs, events=None, stream=None):
+    if events is not None:
+        events[0].record(stream)
+    for i, gph in enumerate(graphs):
+        gph.replay()
+        if events is not None:
+            events[i + 1].record(stream)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--prompt", type=int, default=2048)
+    ap.add_argument("--k", type=int, default=3)
+    ap.add_argument("--prefill-chunk", type=int, default=128)
+    ap.add_argument("--cpu-batch", type=int, default=2)
+    ap.add_argument("--cpu-steps", type=int, default=3)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    from lollm_b200.qwen3_5.config import QWEN35_2B, Qwen3_5Config
+    cfg = Qwen3_5Config.from_hf(QWEN35_2B)
+    if args.impl == "reference":
+        ws, rank = int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0"))
+        run_reference_arm(args, cfg, ws, rank)
+        return
+    ws, rank, local = dist_setup()
+    args.gpus = ws
+    out = run_gpu_arm(args, cfg, ws, rank, local)
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        tps, toks, secs, n, threads = cpu_reference_sample(cfg, args.cpu_batch, args.prompt, args.k,
+                                                           args.cpu_steps, 1, budget_s=30)
+        out["cpu_baseline"] = {"value": tps, "unit": UNIT, "cores": threads, "kind": "port",
+                               "sample": f"{n} speculative steps x {args.cpu_batch} sequences at context "
+                                         f"{args.prompt}, k={args.k}: the oracle restatement of the "
+                                         f"reference's generate_mtp in bf16 on {threads} host threads"}
+    if ws > 1:
+        torch.distributed.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -60,6 +60,10 @@ class _Workspace:
         self.gu = e(M, 2 * max(inter, 1))
         self.act = e(M, max(inter, 1))
         self.logits = e(M, cfg.vocab_size)
+        self.last_x = e(B, H)
+        self.last_xn = e(B, H)
+        self.last_logits = e(B, cfg.vocab_size)
+        self.last_idx = torch.full((B,), T - 1, dtype=torch.int32, device=dev)
         self.num_splits = num_splits
         ws = K.attn_workspace_bytes(B, T, cfg.num_attention_heads, cfg.head_dim, num_splits)
         self.partial = torch.empty(max(ws // 4, 1), dtype=torch.float32, device=dev)
@@ -175,7 +179,17 @@ class Qwen3_5Model:
 
     __call__ = forward
 
-    def _forward_into(self, ids, cache: Qwen3_5Cache, B: int, T: int, speculative: bool):
+    @torch.no_grad()
+    def prefill_last(self, input_ids: torch.Tensor, past: Qwen3_5Cache):
+        """Commit-all forward that computes logits only at each sequence's last position
+        (what a prompt prefill needs). Returns views (logits (B, V), hidden (B, H))."""
+        B, T = input_ids.shape
+        ids = input_ids.to(device=self.device, dtype=torch.int64).contiguous()
+        ws = self._forward_into(ids, past, B, T, False, last_only=True)
+        return ws.last_logits, ws.last_x
+
+    def _forward_into(self, ids, cache: Qwen3_5Cache, B: int, T: int, speculative: bool,
+                      last_only: bool = False):
         cfg = self.cfg
         ws = self.workspace(B, T, cache)
         M = B * T
@@ -202,8 +216,13 @@ class Qwen3_5Model:
             K.gemm(ws.xn, lw["w_gu"], ws.gu, m=M)
             K.swiglu(ws.gu, ws.act, inter, rows=M)
             K.gemm(ws.act, lw["down"], ws.x, accumulate=True, m=M)
-        K.rmsnorm(ws.x, self.final_norm, ws.xn, eps, rows=M)
-        K.gemm(ws.xn, self.lm_head, ws.logits, m=M)
+        if last_only:
+            K.select_rows(ws.x, B, T, ws.last_idx, ws.last_x)
+            K.rmsnorm(ws.last_x, self.final_norm, ws.last_xn, eps, rows=B)
+            K.gemm(ws.last_xn, self.lm_head, ws.last_logits, m=B)
+        else:
+            K.rmsnorm(ws.x, self.final_norm, ws.xn, eps, rows=M)
+            K.gemm(ws.xn, self.lm_head, ws.logits, m=M)
         K.cache_finalize(B, T, speculative, cache.seq_lens, cache.replay_n, cache.conv_off, cache.parity)
         cache.last_tokens, cache.last_speculative = T, speculative
         return ws

@@ -132,19 +132,13 @@ class SpecDecoder:
         B, P = prompts.shape
         assert B == self.B
         prompts = prompts.to(self.model.device).contiguous()
-        last = None
         for s in range(0, P, chunk):
-            part = prompts[:, s:s + chunk].contiguous()
-            logits, _, hidden = self.model.forward(part, self.cache, return_hidden=True, copy_outputs=False)
-            last = (logits, hidden, part.shape[1])
-        logits, hidden, t = last
-        lrow = logits[:, t - 1]
+            lrow, hid = self.model.prefill_last(prompts[:, s:s + chunk], self.cache)
         if self.temperature <= 0:
             K.argmax_rows(lrow, self.ids, rows=B, out_stride=self.T)
         else:
             K.sample_rows(lrow, self.temperature, u_first, self.ids, self.sel_ws, rows=B, out_stride=self.T)
-        idx = torch.full((B,), t - 1, dtype=torch.int32, device=self.model.device)
-        K.select_rows(hidden.reshape(B * t, -1), B, t, idx, self.hidden_last)
+        self.hidden_last.copy_(hid)
         self.n_out.zero_()
 
     # ------------------------------------------------------------------ one step
