@@ -1,0 +1,409 @@
+// bf16 GEMM on the 5th-generation tensor cores: c[m,n] = a[m,k]·w[n,k]ᵀ (+ c), fp32 accumulate.
+//
+// The step's projections are weight-streaming GEMMs: m = batch·(k+1) ≤ 256 token rows against
+// n·k weights read once from HBM. The weight tile is therefore the MMA "A" operand
+// (M_mma = 128 weight rows = 128 output columns) and the token rows are the "B" operand
+// (N_mma = MT ≤ 256), so one CTA holds D[128 × MT] fp32 in TMEM and streams its weight rows
+// once. Warp roles (192 threads): warp 0 issues TMA loads into a STAGES-deep ring of
+// 128B-swizzled tiles, warp 1 owns TMEM and issues tcgen05.mma (one thread), warps 2-5 drain
+// TMEM with tcgen05.ld and write bf16. When n/128 tiles cannot fill the SMs, the K range is
+// split; every split writes an fp32 partial and the last CTA of a tile (atomic ticket) sums
+// the partials in split order, so results do not depend on CTA scheduling.
+//
+// Every mbarrier wait is bounded; a wait that runs out records an error code in a device
+// flag (read by qsp_device_status) and the CTA finishes without hanging the GPU.
+#include "qsp_common.cuh"
+
+#include <cuda.h>
+
+#include <mutex>
+#include <unordered_map>
+
+namespace qsp {
+
+__device__ int g_qsp_dev_error = 0;
+
+constexpr int TC_BN = 128;          // weight rows per CTA (MMA M)
+constexpr int TC_BK = 64;           // K elements per stage (128 bytes of bf16: one swizzle row)
+constexpr int TC_THREADS = 192;
+constexpr uint32_t WAIT_LIMIT = 1u << 24;
+
+// ------------------------------------------------------------------ PTX helpers
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait: false (and the device error flag set to `code`) if the phase never completes.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int code) {
+  for (uint32_t i = 0; i < WAIT_LIMIT; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (i > 256) __nanosleep(64);
+  }
+  atomicExch(&g_qsp_dev_error, code);
+  return false;
+}
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          smem_u32(dst)),
+      "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// K-major operand tile written by TMA with 128-byte swizzling: rows of 128 B, 8-row groups
+// 1024 B apart (stride byte offset), descriptor version 1, layout SWIZZLE_128B.
+__device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
+  d |= (uint64_t)(16u >> 4) << 16;
+  d |= (uint64_t)(1024u >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+// kind::f16 instruction descriptor: D fp32, A and B bf16, both K-major, shape M x N.
+__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+template <int MT>
+struct TcCfg {
+  static constexpr int W_BYTES = TC_BN * TC_BK * 2;
+  static constexpr int X_BYTES = MT * TC_BK * 2;
+  static constexpr int STAGE_BYTES = W_BYTES + X_BYTES;
+  static constexpr int STAGES = (MT >= 256) ? 4 : (MT >= 128 ? 6 : 8);
+  static constexpr int TMEM_COLS = MT < 32 ? 32 : MT;
+  static constexpr size_t SMEM = (size_t)STAGES * STAGE_BYTES + 1024 + 256;
+};
+
+struct TcArgs {
+  __nv_bfloat16* c;
+  int64_t ldc;
+  int m, n, n_kb, kb_per_split, splits, accumulate;
+  float* partial;  // [splits][m_tiles*MT][n_tiles*128]
+  int* tickets;    // [m_tiles * n_tiles], zero between calls
+};
+
+template <int MT>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x, const TcArgs A) {
+  using C = TcCfg<MT>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
+  uint64_t* empty = full + C::STAGES;
+  uint64_t* accf = empty + C::STAGES;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(accf + 1);
+  int* last_flag = reinterpret_cast<int*>(tslot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int mb = blockIdx.x, nb = blockIdx.y, sp = blockIdx.z;
+  const int n_tiles = gridDim.y;
+  const int kb0 = sp * A.kb_per_split;
+  const int nk = min(A.n_kb, kb0 + A.kb_per_split) - kb0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accf, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tslot)),
+                 "r"((uint32_t)C::TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(&tm_w) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(&tm_x) : "memory");
+      for (int i = 0; i < nk; ++i) {
+        const int s = i % C::STAGES;
+        const uint32_t ph = (uint32_t)(i / C::STAGES) & 1u;
+        if (i >= C::STAGES && !mbar_wait(&empty[s], ph ^ 1u, 101)) break;
+        uint8_t* st = smem + s * C::STAGE_BYTES;
+        mbar_expect_tx(&full[s], C::STAGE_BYTES);
+        tma_load_2d(st, &tm_w, &full[s], (kb0 + i) * TC_BK, nb * TC_BN);
+        tma_load_2d(st + C::W_BYTES, &tm_x, &full[s], (kb0 + i) * TC_BK, mb * MT);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16(TC_BN, MT);
+      for (int i = 0; i < nk; ++i) {
+        const int s = i % C::STAGES;
+        const uint32_t ph = (uint32_t)(i / C::STAGES) & 1u;
+        if (!mbar_wait(&full[s], ph, 102)) break;
+        tc_fence_after();
+        const uint32_t a0 = smem_u32(smem + s * C::STAGE_BYTES);
+        const uint32_t b0 = a0 + C::W_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < TC_BK / 16; ++kk)
+          umma_bf16(tmem, sdesc_sw128(a0 + kk * 32), sdesc_sw128(b0 + kk * 32), idesc, (i > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&empty[s]);
+      }
+      umma_commit(accf);
+    }
+  } else {
+    // epilogue: warp w may read TMEM lanes 32*(w%4)..+31, i.e. output columns n of that quadrant
+    const int quad = warp & 3;
+    const int n = nb * TC_BN + quad * 32 + lane;
+    const bool ok = mbar_wait(accf, 0, 103);
+    tc_fence_after();
+    const uint32_t tbase = tmem + ((uint32_t)(quad * 32) << 16);
+    const bool split = A.splits > 1;
+    const int ldp = n_tiles * TC_BN;
+    const int64_t prow0 = ((int64_t)sp * gridDim.x + mb) * MT;
+    for (int c0 = 0; c0 < MT; c0 += 32) {
+      float v[32];
+      tmem_ld32(tbase + c0, v);
+      if (!ok) continue;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const int m = mb * MT + c0 + j;
+        if (split) {
+          A.partial[(prow0 + c0 + j) * ldp + n] = v[j];
+        } else if (m < A.m && n < A.n) {
+          __nv_bfloat16* p = A.c + (int64_t)m * A.ldc + n;
+          float r = dt<__nv_bfloat16>::round(v[j]);
+          if (A.accumulate) r += __bfloat162float(*p);
+          *p = __float2bfloat16_rn(r);
+        }
+      }
+    }
+    if (split) {
+      __threadfence();
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (threadIdx.x == 64) {
+        const int prev = atomicAdd(&A.tickets[mb * n_tiles + nb], 1);
+        *last_flag = (prev == A.splits - 1);
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (*last_flag) {
+        __threadfence();
+        for (int j = 0; j < MT; ++j) {
+          const int m = mb * MT + j;
+          if (m >= A.m || n >= A.n) continue;
+          float acc = 0.f;
+          for (int s = 0; s < A.splits; ++s)
+            acc += __ldcg(&A.partial[(((int64_t)s * gridDim.x + mb) * MT + j) * ldp + n]);
+          __nv_bfloat16* p = A.c + (int64_t)m * A.ldc + n;
+          float r = dt<__nv_bfloat16>::round(acc);
+          if (A.accumulate) r += __bfloat162float(*p);
+          *p = __float2bfloat16_rn(r);
+        }
+        if (threadIdx.x == 64) A.tickets[mb * n_tiles + nb] = 0;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)C::TMEM_COLS)
+                 : "memory");
+  }
+}
+
+// ------------------------------------------------------------------ host side
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiled get_encode() {
+  static EncodeTiled fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiled>(p);
+  });
+  return fn;
+}
+
+// 2-D bf16 row-major [rows, cols] with row stride ld (elements); box = [box_rows, 64 cols].
+static bool make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
+  EncodeTiled enc = get_encode();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+  cuuint32_t box[2] = {(cuuint32_t)TC_BK, (cuuint32_t)box_rows};
+  cuuint32_t es[2] = {1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+static int pick_mt(int64_t m) {
+  if (m <= 32) return 32;
+  if (m <= 64) return 64;
+  if (m <= 128) return 128;
+  return 256;
+}
+
+struct TcPlan {
+  int mt, m_tiles, n_tiles, n_kb, splits, kb_per_split;
+  size_t partial_bytes, ticket_bytes;
+};
+
+static TcPlan plan(int64_t m, int64_t n, int64_t k, int sm_count) {
+  TcPlan p{};
+  p.mt = pick_mt(m);
+  p.m_tiles = (int)((m + p.mt - 1) / p.mt);
+  p.n_tiles = (int)((n + TC_BN - 1) / TC_BN);
+  p.n_kb = (int)((k + TC_BK - 1) / TC_BK);
+  const int tiles = p.m_tiles * p.n_tiles;
+  int splits = 1;
+  if (tiles < sm_count) {
+    splits = (sm_count + tiles - 1) / tiles;
+    splits = std::min(splits, std::max(1, p.n_kb / 4));
+    splits = std::min(splits, 16);
+  }
+  p.kb_per_split = (p.n_kb + splits - 1) / splits;
+  p.splits = (p.n_kb + p.kb_per_split - 1) / p.kb_per_split;
+  p.partial_bytes = p.splits > 1 ? (size_t)p.splits * p.m_tiles * p.mt * p.n_tiles * TC_BN * sizeof(float) : 0;
+  p.ticket_bytes = (size_t)p.m_tiles * p.n_tiles * sizeof(int);
+  return p;
+}
+
+static int sm_count() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+template <int MT>
+static int launch_tc(const CUtensorMap& mw, const CUtensorMap& mx, const TcArgs& a, const TcPlan& p,
+                     cudaStream_t st) {
+  auto kern = gemm_tc_kernel<MT>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)TcCfg<MT>::SMEM) != cudaSuccess)
+      return set_error(QSP_ERR_CUDA, "qsp_gemm: cannot reserve %zu bytes of shared memory", TcCfg<MT>::SMEM);
+    attr_set = true;
+  }
+  dim3 grid(p.m_tiles, p.n_tiles, p.splits);
+  kern<<<grid, TC_THREADS, TcCfg<MT>::SMEM, st>>>(mw, mx, a);
+  return check_launch("qsp_gemm(tcgen05)");
+}
+
+static size_t ws_need(const TcPlan& p) {
+  return 256 + ((p.ticket_bytes + 255) / 256) * 256 + p.partial_bytes;
+}
+
+size_t gemm_tc_workspace(int64_t m, int64_t n, int64_t k) { return ws_need(plan(m, n, k, sm_count())); }
+
+// Returns QSP_ERR_UNSUPPORTED when the operands cannot go through TMA (alignment) or the
+// workspace is too small for the chosen split; the caller then uses the CUDA-core kernel.
+int gemm_tc(const void* a, int64_t lda, const void* w, int64_t ldw, void* c, int64_t ldc, int64_t m, int64_t n,
+            int64_t k, int flags, void* workspace, size_t ws_bytes, cudaStream_t st) {
+  if (!aligned(a, 16) || !aligned(w, 16) || (lda * 2) % 16 != 0 || (ldw * 2) % 16 != 0 || k % 8 != 0)
+    return QSP_ERR_UNSUPPORTED;
+  TcPlan p = plan(m, n, k, sm_count());
+  if (p.splits > 1) {
+    if (workspace == nullptr || ws_bytes < ws_need(p)) {
+      p.splits = 1;  // no room for partials: one K range per tile
+      p.kb_per_split = p.n_kb;
+      p.partial_bytes = 0;
+    }
+  }
+  if (p.splits > 1 && !aligned(workspace, 256)) return QSP_ERR_UNSUPPORTED;
+  CUtensorMap mw, mx;
+  if (!make_map(&mw, w, n, k, ldw, TC_BN) || !make_map(&mx, a, m, k, lda, p.mt)) return QSP_ERR_UNSUPPORTED;
+  TcArgs args{};
+  args.c = static_cast<__nv_bfloat16*>(c);
+  args.ldc = ldc;
+  args.m = (int)m;
+  args.n = (int)n;
+  args.n_kb = p.n_kb;
+  args.kb_per_split = p.kb_per_split;
+  args.splits = p.splits;
+  args.accumulate = (flags & QSP_GEMM_ACCUMULATE) ? 1 : 0;
+  if (p.splits > 1) {
+    args.tickets = reinterpret_cast<int*>(static_cast<char*>(workspace));
+    args.partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + 256 +
+                                            ((p.ticket_bytes + 255) / 256) * 256);
+  }
+  switch (p.mt) {
+    case 32: return launch_tc<32>(mw, mx, args, p, st);
+    case 64: return launch_tc<64>(mw, mx, args, p, st);
+    case 128: return launch_tc<128>(mw, mx, args, p, st);
+    default: return launch_tc<256>(mw, mx, args, p, st);
+  }
+}
+
+}  // namespace qsp
+
+extern "C" int qsp_device_status(int32_t* code, int32_t reset) {
+  QSP_REQUIRE(code != nullptr, "qsp_device_status: null pointer");
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, qsp::g_qsp_dev_error, sizeof(int));
+  if (e != cudaSuccess) return qsp::set_error(QSP_ERR_CUDA, "qsp_device_status: %s", cudaGetErrorString(e));
+  *code = v;
+  if (reset && v != 0) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(qsp::g_qsp_dev_error, &zero, sizeof(int));
+    if (e != cudaSuccess) return qsp::set_error(QSP_ERR_CUDA, "qsp_device_status: %s", cudaGetErrorString(e));
+  }
+  return QSP_OK;
+}

@@ -52,6 +52,18 @@ def swiglu(gu, y, inter, rows=None):
            L.dtype_code(gu.dtype), _s())
 
 
+_gemm_ws = {}
+
+
+def gemm_workspace(device) -> torch.Tensor:
+    """One zero-initialised split-K workspace per device, shared by every GEMM launched on
+    the (single) compute stream."""
+    key = str(device)
+    if key not in _gemm_ws:
+        _gemm_ws[key] = torch.zeros(64 << 20, dtype=torch.uint8, device=device)
+    return _gemm_ws[key]
+
+
 def gemm(a, w, c, accumulate=False, m=None):
     """c[:m] (+)= a[:m] @ w.T (w is [n, k], nn.Linear layout)."""
     _cuda(a, w, c)
@@ -59,9 +71,17 @@ def gemm(a, w, c, accumulate=False, m=None):
         raise RuntimeError("gemm operands must be row-major with unit inner stride")
     mm = a.shape[0] if m is None else m
     n, k = w.shape
+    ws = gemm_workspace(a.device)
     L.call("qsp_gemm", a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0), c.data_ptr(),
            c.stride(0), mm, n, k, L.dtype_code(a.dtype),
-           L.QSP_GEMM_ACCUMULATE if accumulate else 0, _s())
+           L.QSP_GEMM_ACCUMULATE if accumulate else 0, ws.data_ptr(), ws.numel(), _s())
+
+
+def device_status(reset=True) -> int:
+    import ctypes as C
+    v = C.c_int32(0)
+    L.call("qsp_device_status", C.byref(v), 1 if reset else 0)
+    return int(v.value)
 
 
 def gdn_verify(desc: L.GdnLayer):

@@ -29,8 +29,7 @@ def test_library_loads_and_exports_every_declared_symbol():
 
 
 def test_struct_layouts_match_header():
-    # field counts mirror the C structs; sizes follow natural alignment on x86-64
-    assert L.GdnLayer.ld_out.offset + 8 == L.ctypes_sizeof(L.GdnLayer) if hasattr(L, "ctypes_sizeof") else True
+    # sizes follow natural alignment on x86-64: 11 4-byte fields, padding, 14 8-byte fields
     import ctypes
     assert ctypes.sizeof(L.GdnLayer) == 4 * 11 + 4 + 8 * 14
     assert ctypes.sizeof(L.AttnLayer) % 8 == 0
@@ -39,7 +38,7 @@ def test_struct_layouts_match_header():
 def test_argument_validation_without_gpu():
     """Invalid arguments are rejected by the host-side checks before any launch."""
     lib = L.load()
-    rc = lib.qsp_gemm(None, 1, None, 1, None, 1, 1, 1, 1, 0, 0, None)
+    rc = lib.qsp_gemm(None, 1, None, 1, None, 1, 1, 1, 1, 0, 0, None, 0, None)
     assert rc == L.QSP_ERR_INVALID
     assert b"null" in lib.qsp_last_error()
     rc = lib.qsp_cache_finalize(0, 1, 0, None, None, None, None, None)
