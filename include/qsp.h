@@ -64,9 +64,8 @@ int qsp_swiglu(const void* gu, int64_t ld_gu, void* y, int64_t ld_y, int64_t row
 /* c[m,n] = a[m,k] · w[n,k]ᵀ with fp32 accumulation: every nn.Linear of the step
  * (blocks.py:202-205, 251-260, 337-339, modeling_qwen3_5.py:73, mtp.py:52). bf16 runs on
  * tcgen05 tensor cores (TMA-fed, TMEM accumulators); fp32 (parity configs) on CUDA cores.
- * `workspace` (may be NULL) holds split-K partials and per-tile tickets: it must be zeroed
- * once when allocated (the kernel leaves the tickets at zero again) and must not be shared
- * by two GEMMs running concurrently. With too little workspace the GEMM runs unsplit. */
+ * `workspace` (may be NULL, 16-byte aligned) holds split-K partials; it must not be shared by
+ * two GEMMs running concurrently. With too little workspace the GEMM runs unsplit. */
 int qsp_gemm(const void* a, int64_t lda, const void* w, int64_t ldw, void* c, int64_t ldc,
              int64_t m, int64_t n, int64_t k, int dtype, int flags, void* workspace,
              size_t workspace_bytes, void* stream);

@@ -5,6 +5,8 @@
 
 namespace qsp {
 
+int launch_attn_mma(const qsp_attn_layer& L, cudaStream_t st);
+
 // ------------------------------------------------------------------ prep
 // One CTA per token row m = b*T + t; warps loop over the q and k heads.
 template <typename T>
@@ -213,6 +215,12 @@ static int attn_chunk(const qsp_attn_layer& L) {
   return chunk;
 }
 
+template <typename T>
+static int launch_combine(const qsp_attn_layer& L, cudaStream_t st) {
+  attn_combine_kernel<T><<<dim3(L.batch * L.tokens, L.n_heads), 128, 0, st>>>(L);
+  return check_launch("qsp_attn_verify(combine)");
+}
+
 template <typename T, int HD, int RPW>
 static int launch_attn_simt(const qsp_attn_layer& L, cudaStream_t st) {
   const int rows_total = (L.n_heads / L.n_kv_heads) * L.tokens;
@@ -273,6 +281,12 @@ int qsp_attn_verify(const qsp_attn_layer* layer, void* stream) {
   if (rc) return rc;
   const qsp_attn_layer& L = *layer;
   cudaStream_t st = as_stream(stream);
+  if (L.dtype == QSP_BF16) {
+    // tensor-core path (head_dim 64/128/256); other shapes use the CUDA-core kernel below
+    int rc2 = launch_attn_mma(L, st);
+    if (rc2 == QSP_OK) return launch_combine<__nv_bfloat16>(L, st);
+    if (rc2 != QSP_ERR_UNSUPPORTED) return rc2;
+  }
   QSP_DISPATCH_DTYPE(L.dtype, T, {
     switch (L.head_dim) {
       case 32: return launch_attn_simt<T, 32, 16>(L, st);

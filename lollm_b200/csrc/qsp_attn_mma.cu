@@ -1,0 +1,327 @@
+// bf16 split-KV verify attention on tensor cores (warp-level mma.sync m16n8k16).
+//
+// CTA = (key split s, kv head g, sequence b × row group). A row group is 32 query rows
+// (t, q head) = n_rep heads × tokens sharing this kv head, so K/V are read from HBM once per
+// (sequence, kv head, split) for all of them (GQA without materialising the expansion).
+// Keys stream through a 2-stage cp.async ring of 64-key tiles in padded shared memory (row
+// pitch hd+8 elements: ldmatrix without bank conflicts). Warp w computes rows 16·(w&1)..+15
+// against keys 32·(w>>1)..+31 of every tile: S = QKᵀ in fp32, online softmax in registers
+// (exp2 with the scale folded in), P·V with P taken straight from the S accumulators. The two
+// key-half warps of a row tile merge through shared memory at the end and write one
+// unnormalised partial (o, m, l) per row; attn_combine_kernel merges the splits and applies
+// the output gate.
+#include "qsp_common.cuh"
+
+namespace qsp {
+
+constexpr int AM_KT = 64;        // keys per tile
+constexpr int AM_ROWS = 32;      // query rows per CTA
+constexpr int AM_THREADS = 128;
+
+__device__ __forceinline__ uint32_t su32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+
+__device__ __forceinline__ void cp16(void* dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(su32(dst)), "l"(src), "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(su32(p)));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(su32(p)));
+}
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+template <int HD>
+struct AmSmem {
+  static constexpr int PITCH = HD + 8;  // elements
+  static constexpr int TILE = AM_KT * PITCH;
+  static constexpr size_t BYTES = (size_t)(AM_ROWS * PITCH + 4 * TILE) * 2;
+};
+
+template <int HD>
+__global__ void __launch_bounds__(AM_THREADS, 1)
+attn_mma_kernel(const qsp_attn_layer L, int n_row_groups) {
+  using SM = AmSmem<HD>;
+  constexpr int P = SM::PITCH;
+  constexpr int NKS = HD / 16;   // k-steps over head_dim
+  constexpr int NNT = HD / 8;    // n-tiles of O
+  extern __shared__ __align__(16) __nv_bfloat16 sm[];
+  __nv_bfloat16* sQ = sm;
+  __nv_bfloat16* sK[2] = {sm + AM_ROWS * P, sm + AM_ROWS * P + SM::TILE};
+  __nv_bfloat16* sV[2] = {sm + AM_ROWS * P + 2 * SM::TILE, sm + AM_ROWS * P + 3 * SM::TILE};
+
+  const int s = blockIdx.x, g = blockIdx.y;
+  const int b = blockIdx.z / n_row_groups, rgp = blockIdx.z % n_row_groups;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int nrep = L.n_heads / L.n_kv_heads;
+  const int rows_total = nrep * L.tokens;
+  const int row0 = rgp * AM_ROWS;
+  const int nrows = min(AM_ROWS, rows_total - row0);
+  const int base_len = L.seq_lens[b];
+  const int kv_len = base_len + L.tokens;
+  // this split's key range, even across splits and aligned to whole tiles
+  int chunk = (kv_len + L.num_splits - 1) / L.num_splits;
+  chunk = ((chunk + AM_KT - 1) / AM_KT) * AM_KT;
+  const int k_begin = s * chunk;
+  const int k_end = min(kv_len, k_begin + chunk);
+  const int64_t idx0 = ((int64_t)b * L.n_heads) * L.tokens;
+
+  if (k_begin >= k_end) {  // empty split: an all-masked partial
+    for (int r = tid; r < nrows; r += AM_THREADS) {
+      const int rr = row0 + r, t = rr / nrep, hq = g * nrep + rr % nrep;
+      float* po = L.partial + ((idx0 + (int64_t)hq * L.tokens + t) * L.num_splits + s) * (HD + 2);
+      po[HD] = -INFINITY;
+      po[HD + 1] = 0.f;
+    }
+    return;
+  }
+
+  const __nv_bfloat16* kp = static_cast<const __nv_bfloat16*>(L.k_pages);
+  const __nv_bfloat16* vp = static_cast<const __nv_bfloat16*>(L.v_pages);
+  const __nv_bfloat16* qb = static_cast<const __nv_bfloat16*>(L.q_buf);
+
+  // Q rows of this group (rows beyond nrows zero-filled)
+  for (int e = tid; e < AM_ROWS * (HD / 8); e += AM_THREADS) {
+    const int r = e / (HD / 8), c = e % (HD / 8);
+    const int rr = row0 + r;
+    const bool ok = r < nrows;
+    const int t = ok ? rr / nrep : 0, hq = ok ? g * nrep + rr % nrep : 0;
+    const __nv_bfloat16* src = qb + (((int64_t)b * L.tokens + t) * L.n_heads + hq) * HD + c * 8;
+    cp16(sQ + r * P + c * 8, ok ? src : qb, ok);
+  }
+  auto load_tile = [&](int k0, int st) {
+    for (int e = tid; e < AM_KT * (HD / 8); e += AM_THREADS) {
+      const int j = e / (HD / 8), c = e % (HD / 8);
+      const int pos = k0 + j;
+      bool ok = pos < k_end;
+      int64_t off = 0;
+      if (ok) {
+        const int lp = pos / L.page_size;
+        const int page = lp < L.max_pages ? L.page_table[(int64_t)b * L.max_pages + lp] : -1;
+        ok = page >= 0 && page < L.num_pages;
+        if (ok) off = (((int64_t)page * L.n_kv_heads + g) * L.page_size + pos % L.page_size) * HD + c * 8;
+      }
+      cp16(sK[st] + j * P + c * 8, ok ? kp + off : kp, ok);
+      cp16(sV[st] + j * P + c * 8, ok ? vp + off : vp, ok);
+    }
+  };
+
+  const int n_tiles = (k_end - k_begin + AM_KT - 1) / AM_KT;
+  load_tile(k_begin, 0);
+  cp_commit();
+
+  const int mt = warp & 1, kh = warp >> 1;       // row tile, key half
+  const int gq = lane >> 2, tq = lane & 3;
+  const float sl2 = L.scale * 1.4426950408889634f;  // scale in log2 units
+  // rows of this thread: mt*16 + gq and +8 → absolute query positions
+  int qpos[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int r = mt * 16 + gq + 8 * h;
+    qpos[h] = (r < nrows) ? base_len + (row0 + r) / nrep : -1;
+  }
+  float o[NNT][4];
+#pragma unroll
+  for (int i = 0; i < NNT; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
+
+  for (int it = 0; it < n_tiles; ++it) {
+    const int st = it & 1;
+    if (it + 1 < n_tiles) {
+      load_tile(k_begin + (it + 1) * AM_KT, st ^ 1);
+      cp_commit();
+      cp_wait<1>();
+    } else {
+      cp_wait<0>();
+    }
+    __syncthreads();
+    const int k0 = k_begin + it * AM_KT;
+    // S = Q Kᵀ for 16 rows x 32 keys
+    float sacc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) sacc[i][0] = sacc[i][1] = sacc[i][2] = sacc[i][3] = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < NKS; ++ks) {
+      uint32_t a[4];
+      ldsm_x4(a, sQ + (mt * 16 + (lane & 7) + 8 * ((lane >> 3) & 1)) * P + ks * 16 + 8 * (lane >> 4));
+#pragma unroll
+      for (int np = 0; np < 2; ++np) {
+        uint32_t bb[4];
+        const int key = kh * 32 + np * 16 + (lane & 7) + 8 * (lane >> 4);
+        ldsm_x4(bb, sK[st] + key * P + ks * 16 + 8 * ((lane >> 3) & 1));
+        mma16816(sacc[2 * np], a, bb[0], bb[1]);
+        mma16816(sacc[2 * np + 1], a, bb[2], bb[3]);
+      }
+    }
+    // mask (causal over the new tokens, and the split end), scale, online softmax
+    float tmax[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int h = e >> 1;
+        const int key = k0 + kh * 32 + nt * 8 + 2 * tq + (e & 1);
+        const bool vis = key < k_end && key <= qpos[h];
+        const float v = vis ? sacc[nt][e] * sl2 : -INFINITY;
+        sacc[nt][e] = v;
+        tmax[h] = fmaxf(tmax[h], v);
+      }
+    }
+    float alpha[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      tmax[h] = fmaxf(tmax[h], __shfl_xor_sync(0xffffffffu, tmax[h], 1));
+      tmax[h] = fmaxf(tmax[h], __shfl_xor_sync(0xffffffffu, tmax[h], 2));
+      const float mnew = fmaxf(mrow[h], tmax[h]);
+      alpha[h] = (mnew == -INFINITY) ? 1.f : exp2f(mrow[h] - mnew);
+      mrow[h] = mnew;
+    }
+    float psum[2] = {0.f, 0.f};
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int h = e >> 1;
+        const float p = (mrow[h] == -INFINITY) ? 0.f : exp2f(sacc[nt][e] - mrow[h]);
+        sacc[nt][e] = p;
+        psum[h] += p;
+      }
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) lrow[h] = lrow[h] * alpha[h] + psum[h];
+#pragma unroll
+    for (int i = 0; i < NNT; ++i) {
+      o[i][0] *= alpha[0];
+      o[i][1] *= alpha[0];
+      o[i][2] *= alpha[1];
+      o[i][3] *= alpha[1];
+    }
+    // O += P V over this warp's 32 keys (two k-steps of 16)
+#pragma unroll
+    for (int kk = 0; kk < 2; ++kk) {
+      uint32_t pa[4];
+      pa[0] = pack_bf16(sacc[2 * kk][0], sacc[2 * kk][1]);
+      pa[1] = pack_bf16(sacc[2 * kk][2], sacc[2 * kk][3]);
+      pa[2] = pack_bf16(sacc[2 * kk + 1][0], sacc[2 * kk + 1][1]);
+      pa[3] = pack_bf16(sacc[2 * kk + 1][2], sacc[2 * kk + 1][3]);
+      const int keyr = kh * 32 + kk * 16 + (lane & 7) + 8 * ((lane >> 3) & 1);
+#pragma unroll
+      for (int dp = 0; dp < NNT / 2; ++dp) {
+        uint32_t vb[4];
+        ldsm_x4_t(vb, sV[st] + keyr * P + dp * 16 + 8 * (lane >> 4));
+        mma16816(o[2 * dp], pa, vb[0], vb[1]);
+        mma16816(o[2 * dp + 1], pa, vb[2], vb[3]);
+      }
+    }
+    __syncthreads();  // the stage is refilled next iteration
+  }
+
+  // row sums over the 4 threads of a row
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    lrow[h] += __shfl_xor_sync(0xffffffffu, lrow[h], 1);
+    lrow[h] += __shfl_xor_sync(0xffffffffu, lrow[h], 2);
+  }
+  // merge the two key halves of each row tile through shared memory (reusing the K/V ring)
+  float* xo = reinterpret_cast<float*>(sK[0]);            // [2 row tiles][16][HD]
+  float* xm = xo + 2 * 16 * HD;                           // [2][16] m, then l
+  if (kh == 1) {
+#pragma unroll
+    for (int i = 0; i < NNT; ++i) {
+      const int d = i * 8 + 2 * tq;
+      float* r0 = xo + ((mt * 16) + gq) * HD + d;
+      float* r1 = xo + ((mt * 16) + gq + 8) * HD + d;
+      r0[0] = o[i][0]; r0[1] = o[i][1];
+      r1[0] = o[i][2]; r1[1] = o[i][3];
+    }
+    if (tq == 0) {
+      xm[mt * 16 + gq] = mrow[0];
+      xm[mt * 16 + gq + 8] = mrow[1];
+      xm[32 + mt * 16 + gq] = lrow[0];
+      xm[32 + mt * 16 + gq + 8] = lrow[1];
+    }
+  }
+  __syncthreads();
+  if (kh == 0) {
+    float f0[2], f1[2], mm[2], ll[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int r = mt * 16 + gq + 8 * h;
+      const float m2 = xm[r], l2 = xm[32 + r];
+      const float M = fmaxf(mrow[h], m2);
+      f0[h] = (mrow[h] == -INFINITY) ? 0.f : exp2f(mrow[h] - M);
+      f1[h] = (m2 == -INFINITY) ? 0.f : exp2f(m2 - M);
+      mm[h] = M;
+      ll[h] = lrow[h] * f0[h] + l2 * f1[h];
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int r = mt * 16 + gq + 8 * h;
+      if (r >= nrows) continue;
+      const int rr = row0 + r, t = rr / nrep, hq = g * nrep + rr % nrep;
+      float* po = L.partial + ((idx0 + (int64_t)hq * L.tokens + t) * L.num_splits + s) * (HD + 2);
+      const float* x = xo + r * HD;
+#pragma unroll
+      for (int i = 0; i < NNT; ++i) {
+        const int d = i * 8 + 2 * tq;
+        po[d] = o[i][2 * h] * f0[h] + x[d] * f1[h];
+        po[d + 1] = o[i][2 * h + 1] * f0[h] + x[d + 1] * f1[h];
+      }
+      if (tq == 0) {
+        po[HD] = mm[h] * 0.6931471805599453f;  // log2 units → natural log (attn_combine_kernel)
+        po[HD + 1] = ll[h];
+      }
+    }
+  }
+}
+
+int launch_attn_mma(const qsp_attn_layer& L, cudaStream_t st);
+
+int launch_attn_mma(const qsp_attn_layer& L, cudaStream_t st) {
+  const int rows_total = (L.n_heads / L.n_kv_heads) * L.tokens;
+  const int n_rg = (rows_total + AM_ROWS - 1) / AM_ROWS;
+  dim3 grid(L.num_splits, L.n_kv_heads, L.batch * n_rg);
+#define QSP_AM_CASE(HDV)                                                                     \
+  case HDV: {                                                                                \
+    auto kern = attn_mma_kernel<HDV>;                                                        \
+    const size_t smem = AmSmem<HDV>::BYTES;                                                  \
+    static bool set = false;                                                                 \
+    if (!set) {                                                                              \
+      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) \
+          != cudaSuccess)                                                                    \
+        return set_error(QSP_ERR_CUDA, "qsp_attn_verify: cannot reserve shared memory");     \
+      set = true;                                                                            \
+    }                                                                                        \
+    kern<<<grid, AM_THREADS, smem, st>>>(L, n_rg);                                           \
+    return check_launch("qsp_attn_verify(mma)");                                             \
+  }
+  switch (L.head_dim) {
+    QSP_AM_CASE(64)
+    QSP_AM_CASE(128)
+    QSP_AM_CASE(256)
+    default:
+      return QSP_ERR_UNSUPPORTED;
+  }
+#undef QSP_AM_CASE
+}
+
+}  // namespace qsp

@@ -7,8 +7,8 @@
 // once. Warp roles (192 threads): warp 0 issues TMA loads into a STAGES-deep ring of
 // 128B-swizzled tiles, warp 1 owns TMEM and issues tcgen05.mma (one thread), warps 2-5 drain
 // TMEM with tcgen05.ld and write bf16. When n/128 tiles cannot fill the SMs, the K range is
-// split; every split writes an fp32 partial and the last CTA of a tile (atomic ticket) sums
-// the partials in split order, so results do not depend on CTA scheduling.
+// split; every split writes an fp32 partial and a second, fully parallel kernel sums the
+// partials in split order (results do not depend on CTA scheduling).
 //
 // Every mbarrier wait is bounded; a wait that runs out records an error code in a device
 // flag (read by qsp_device_status) and the CTA finishes without hanging the GPU.
@@ -126,8 +126,33 @@ struct TcArgs {
   int64_t ldc;
   int m, n, n_kb, kb_per_split, splits, accumulate;
   float* partial;  // [splits][m_tiles*MT][n_tiles*128]
-  int* tickets;    // [m_tiles * n_tiles], zero between calls
 };
+
+// Split-K merge: c = round(Σ_s partial[s]) (+ c), summed in split order (deterministic).
+// Each thread owns 4 consecutive output columns of one row.
+__global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restrict__ partial, int splits,
+                                                            int64_t split_stride, int ldp,
+                                                            __nv_bfloat16* __restrict__ c, int64_t ldc,
+                                                            int m, int n, int accumulate) {
+  const int row = blockIdx.y;
+  const int col = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
+  if (col >= n) return;
+  const float* p = partial + (int64_t)row * ldp + col;
+  float4 acc = __ldcg(reinterpret_cast<const float4*>(p));
+  for (int s = 1; s < splits; ++s) {
+    const float4 v = __ldcg(reinterpret_cast<const float4*>(p + s * split_stride));
+    acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+  }
+  const float a4[4] = {acc.x, acc.y, acc.z, acc.w};
+  __nv_bfloat16* o = c + (int64_t)row * ldc + col;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    if (col + j >= n) break;
+    float r = dt<__nv_bfloat16>::round(a4[j]);
+    if (accumulate) r += __bfloat162float(o[j]);
+    o[j] = __float2bfloat16_rn(r);
+  }
+}
 
 template <int MT>
 __global__ void __launch_bounds__(TC_THREADS, 1)
@@ -139,7 +164,6 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
   uint64_t* empty = full + C::STAGES;
   uint64_t* accf = empty + C::STAGES;
   uint32_t* tslot = reinterpret_cast<uint32_t*>(accf + 1);
-  int* last_flag = reinterpret_cast<int*>(tslot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int mb = blockIdx.x, nb = blockIdx.y, sp = blockIdx.z;
@@ -224,30 +248,6 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
         }
       }
     }
-    if (split) {
-      __threadfence();
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (threadIdx.x == 64) {
-        const int prev = atomicAdd(&A.tickets[mb * n_tiles + nb], 1);
-        *last_flag = (prev == A.splits - 1);
-      }
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (*last_flag) {
-        __threadfence();
-        for (int j = 0; j < MT; ++j) {
-          const int m = mb * MT + j;
-          if (m >= A.m || n >= A.n) continue;
-          float acc = 0.f;
-          for (int s = 0; s < A.splits; ++s)
-            acc += __ldcg(&A.partial[(((int64_t)s * gridDim.x + mb) * MT + j) * ldp + n]);
-          __nv_bfloat16* p = A.c + (int64_t)m * A.ldc + n;
-          float r = dt<__nv_bfloat16>::round(acc);
-          if (A.accumulate) r += __bfloat162float(*p);
-          *p = __float2bfloat16_rn(r);
-        }
-        if (threadIdx.x == 64) A.tickets[mb * n_tiles + nb] = 0;
-      }
-    }
   }
   tc_fence_before();
   __syncthreads();
@@ -298,7 +298,7 @@ static int pick_mt(int64_t m) {
 
 struct TcPlan {
   int mt, m_tiles, n_tiles, n_kb, splits, kb_per_split;
-  size_t partial_bytes, ticket_bytes;
+  size_t partial_bytes;
 };
 
 static TcPlan plan(int64_t m, int64_t n, int64_t k, int sm_count) {
@@ -317,7 +317,6 @@ static TcPlan plan(int64_t m, int64_t n, int64_t k, int sm_count) {
   p.kb_per_split = (p.n_kb + splits - 1) / splits;
   p.splits = (p.n_kb + p.kb_per_split - 1) / p.kb_per_split;
   p.partial_bytes = p.splits > 1 ? (size_t)p.splits * p.m_tiles * p.mt * p.n_tiles * TC_BN * sizeof(float) : 0;
-  p.ticket_bytes = (size_t)p.m_tiles * p.n_tiles * sizeof(int);
   return p;
 }
 
@@ -344,12 +343,17 @@ static int launch_tc(const CUtensorMap& mw, const CUtensorMap& mx, const TcArgs&
   }
   dim3 grid(p.m_tiles, p.n_tiles, p.splits);
   kern<<<grid, TC_THREADS, TcCfg<MT>::SMEM, st>>>(mw, mx, a);
-  return check_launch("qsp_gemm(tcgen05)");
+  int rc = check_launch("qsp_gemm(tcgen05)");
+  if (rc || p.splits == 1) return rc;
+  const int ldp = p.n_tiles * TC_BN;
+  const int64_t split_stride = (int64_t)p.m_tiles * MT * ldp;
+  dim3 rgrid((unsigned)((a.n / 4 + 255) / 256 + 1), (unsigned)a.m);
+  splitk_reduce_kernel<<<rgrid, 256, 0, st>>>(a.partial, p.splits, split_stride, ldp, a.c, a.ldc, a.m, a.n,
+                                              a.accumulate);
+  return check_launch("qsp_gemm(split-k reduce)");
 }
 
-static size_t ws_need(const TcPlan& p) {
-  return 256 + ((p.ticket_bytes + 255) / 256) * 256 + p.partial_bytes;
-}
+static size_t ws_need(const TcPlan& p) { return p.partial_bytes; }
 
 size_t gemm_tc_workspace(int64_t m, int64_t n, int64_t k) { return ws_need(plan(m, n, k, sm_count())); }
 
@@ -379,11 +383,7 @@ int gemm_tc(const void* a, int64_t lda, const void* w, int64_t ldw, void* c, int
   args.kb_per_split = p.kb_per_split;
   args.splits = p.splits;
   args.accumulate = (flags & QSP_GEMM_ACCUMULATE) ? 1 : 0;
-  if (p.splits > 1) {
-    args.tickets = reinterpret_cast<int*>(static_cast<char*>(workspace));
-    args.partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + 256 +
-                                            ((p.ticket_bytes + 255) / 256) * 256);
-  }
+  if (p.splits > 1) args.partial = static_cast<float*>(workspace);
   switch (p.mt) {
     case 32: return launch_tc<32>(mw, mx, args, p, st);
     case 64: return launch_tc<64>(mw, mx, args, p, st);

@@ -248,7 +248,7 @@ def test_gdn_replay_bitwise_equals_fresh_forward(dt):
 
 # ─────────────────────────────────────────── attention ───────────────────────────────────────────
 
-def _attn_case(dt, B, T, nh, nkv, hd, rd, lens, page_size=16, seed=4, shuffle_pages=True):
+def _attn_case(dt, B, T, nh, nkv, hd, rd, lens, page_size=16, seed=4, shuffle_pages=True, splits=3):
     from lollm_b200 import _lib as L
     from lollm_b200.qwen3_5.modeling_qwen3_5 import rope_table
     g = gen(seed)
@@ -270,7 +270,6 @@ def _attn_case(dt, B, T, nh, nkv, hd, rd, lens, page_size=16, seed=4, shuffle_pa
              pt=dev(page_table), lens=dev(torch.tensor(lens, dtype=torch.int32)))
     D["q_buf"] = torch.empty(B * T, nh * hd, dtype=dt, device=DEV)
     D["out"] = torch.empty(B * T, nh * hd, dtype=dt, device=DEV)
-    splits = 3
     from lollm_b200 import kernels
     D["partial"] = torch.empty(kernels.attn_workspace_bytes(B, T, nh, hd, splits) // 4, device=DEV)
     D["bad"] = torch.zeros(1, dtype=torch.int32, device=DEV)
@@ -289,11 +288,13 @@ def _attn_case(dt, B, T, nh, nkv, hd, rd, lens, page_size=16, seed=4, shuffle_pa
 
 
 @pytest.mark.parametrize("dt", DTS)
-@pytest.mark.parametrize("shape", [(2, 4, 4, 2, 32, 8, [5, 17]), (3, 4, 16, 2, 256, 64, [40, 1, 77]),
-                                   (2, 1, 8, 2, 64, 16, [100, 3]), (1, 9, 4, 1, 128, 32, [0])])
+@pytest.mark.parametrize("shape", [(2, 4, 4, 2, 32, 8, [5, 17], 16, 3), (3, 4, 16, 2, 256, 64, [40, 1, 77], 16, 3),
+                                   (2, 1, 8, 2, 64, 16, [100, 3], 16, 3), (1, 9, 4, 1, 128, 32, [0], 16, 3),
+                                   (3, 4, 16, 2, 256, 64, [700, 1500, 64], 64, 4),
+                                   (2, 16, 4, 2, 64, 16, [300, 129], 64, 2)])
 def test_attention_matches_oracle(dt, shape):
-    B, T, nh, nkv, hd, rd, lens = shape
-    d, D, H = _attn_case(dt, B, T, nh, nkv, hd, rd, lens)
+    B, T, nh, nkv, hd, rd, lens, ps, splits = shape
+    d, D, H = _attn_case(dt, B, T, nh, nkv, hd, rd, lens, page_size=ps, splits=splits)
     K().attn_prep(d)
     K().attn_verify(d)
     assert int(D["bad"]) == 0
