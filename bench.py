@@ -273,11 +273,15 @@ def run_gpu_arm(args, cfg, ws, rank, local):
     clocks.start()
     time.sleep(0.3)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if args.profile:
+        torch.cuda.profiler.start()       # ncu --profile-from-start off: only the timed steps
     start.record(stream)
     for s in range(args.steps):
         replay_split(graphs, ev[s], stream)
     end.record(stream)
     torch.cuda.synchronize()
+    if args.profile:
+        torch.cuda.profiler.stop()
     barrier(ws)
     clk = clocks.stop()
     elapsed_ms = start.elapsed_time(end)
@@ -399,6 +403,8 @@ def main():
     ap.add_argument("--cpu-batch", type=int, default=2)
     ap.add_argument("--cpu-steps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", action="store_true",
+                    help="bracket the timed steps with cudaProfilerStart/Stop (for ncu --profile-from-start off)")
     args = ap.parse_args()
     from lollm_b200.qwen3_5.config import QWEN35_2B, Qwen3_5Config
     cfg = Qwen3_5Config.from_hf(QWEN35_2B)

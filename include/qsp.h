@@ -97,9 +97,10 @@ int qsp_device_status(int32_t* code, int32_t reset);
  *   proj       [B*T, ld_proj]           cols [0,C): raw qkv, [C,C+Vd): z, then b [Hv], a [Hv]
  *   state      [B, Hv, dk, dv] fp32     (same layout as the reference's recurrent_state)
  *   conv_hist  [2, B, K-1+Ts, C] dtype  ping-pong on *parity
- *   pending    [B, Hv, Ts, dk+dv+2] fp32
+ *   pending    [B, Hv, Ts, dk+dv+4] fp32  (k | v | g | β | 2 pad)
  *   out        [B*T, ld_out]            cols [0, Vd)
- * with C = 2·Hk·dk + Hv·dv (conv_dim), Vd = Hv·dv, Ts = max_spec_tokens.
+ * with C = 2·Hk·dk + Hv·dv (conv_dim), Vd = Hv·dv, Ts = max_spec_tokens ≤ 8, conv kernel ≤ 4;
+ * proj, state, pending and conv_hist 16-byte aligned, ld_proj a multiple of 16 bytes.
  */
 typedef struct qsp_gdn_layer {
   int32_t batch, tokens;

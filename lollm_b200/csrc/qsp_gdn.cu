@@ -12,19 +12,9 @@
 
 namespace qsp {
 
-constexpr int GDN_TB = 4;  // tokens per prologue block
+constexpr int GDN_TB = 8;    // tokens per block (a whole verify step)
+constexpr int GDN_KMAX = 4;  // largest conv kernel
 
-template <typename T, int DK, int DV>
-struct __align__(16) GdnSmem {
-  float q[GDN_TB][DK];
-  float k[GDN_TB][DK];
-  float v[GDN_TB][DV];
-  float z[GDN_TB][DV];
-  float o[GDN_TB][DV];
-  float g[GDN_TB];
-  float beta[GDN_TB];
-  float red[32];
-};
 
 // One state update S ← S·e^g; δ = (v − Sᵀk)·β; S ← S + k δᵀ. Explicit _rn intrinsics keep
 // the arithmetic identical wherever it is inlined (the replay of kept tokens must reproduce
@@ -105,12 +95,46 @@ __device__ __forceinline__ void warp_l2norm(float* x, float post_scale, int lane
   for (int i = lane; i < DK; i += 32) x[i] = dt<T>::round(x[i] * r) * post_scale;
 }
 
+// 16-byte vector of T converted to floats
+template <typename T>
+__device__ __forceinline__ void load16_as_float(const T* src, float* dst) {
+  const uint4 u = *reinterpret_cast<const uint4*>(src);
+  if constexpr (sizeof(T) == 4) {
+    dst[0] = __uint_as_float(u.x); dst[1] = __uint_as_float(u.y);
+    dst[2] = __uint_as_float(u.z); dst[3] = __uint_as_float(u.w);
+  } else {
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      dst[2 * i] = __uint_as_float(w[i] << 16);
+      dst[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+    }
+  }
+}
+
+template <int DK, int DV>
+struct __align__(16) GdnSmem {
+  static constexpr int NCH = 2 * DK + DV;   // q, k, v conv channels of one value head
+  float xin[GDN_KMAX - 1 + GDN_TB][NCH];    // conv inputs: window rows, then this block's tokens
+  float cw[GDN_KMAX][NCH];                  // conv weights, tap-major
+  float q[GDN_TB][DK];
+  float k[GDN_TB][DK];
+  float v[GDN_TB][DV];
+  float z[GDN_TB][DV];
+  float o[GDN_TB][DV];
+  float g[GDN_TB];
+  float beta[GDN_TB];
+  float ab[GDN_TB][2];                      // raw a, b of this head
+};
+
 template <typename T, int DK, int DV>
 __global__ void __launch_bounds__(DV, (DV >= 128 ? 3 : 4))
 gdn_verify_kernel(const qsp_gdn_layer L) {
   constexpr int RPT = DK / 4;
   constexpr int NT = DV;
-  __shared__ GdnSmem<T, DK, DV> sm;
+  constexpr int NCH = GdnSmem<DK, DV>::NCH;
+  constexpr int EPV = 16 / (int)sizeof(T);   // elements per 16-byte vector
+  __shared__ GdnSmem<DK, DV> sm;
 
   const int h = blockIdx.x, b = blockIdx.y;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -120,7 +144,6 @@ gdn_verify_kernel(const qsp_gdn_layer L) {
   const int key_dim = Hk * DK, conv_dim = 2 * key_dim + Hv * DV, value_dim = Hv * DV;
   const bool spec = L.speculative != 0;
   const T* proj = static_cast<const T*>(L.proj);
-  const T* cw = static_cast<const T*>(L.conv_w);
   T* hist = static_cast<T*>(L.conv_hist);
   T* out = static_cast<T*>(L.out);
   const int par = L.parity[0];
@@ -131,63 +154,83 @@ gdn_verify_kernel(const qsp_gdn_layer L) {
   const int hist_rows = K - 1 + Ts;
   const T* hist_in = hist + ((int64_t)par * L.batch + b) * hist_rows * conv_dim;
   T* hist_out = hist + ((int64_t)(par ^ 1) * L.batch + b) * hist_rows * conv_dim;
-  const int pstride = DK + DV + 2;
-  float* pend = L.pending + (((int64_t)b * Hv + h) * Ts) * pstride;
+  constexpr int PS = DK + DV + 4;   // pending row: k | v | g | beta | pad (16-byte rows)
+  float* pend = L.pending + (((int64_t)b * Hv + h) * Ts) * PS;
   float* state = L.state + ((int64_t)b * Hv + h) * DK * DV;
+  // global channel of local conv channel c: q | k | v segments of this head
+  auto gch = [&](int c) -> int {
+    return c < DK ? kh * DK + c : (c < 2 * DK ? key_dim + kh * DK + (c - DK) : 2 * key_dim + h * DV + (c - 2 * DK));
+  };
 
-  // 1. the state of this head into registers (issued first; latency overlaps the replay load)
+  // 1. the state of this head into registers
   float4 S[RPT];
 #pragma unroll
   for (int i = 0; i < RPT; ++i)
     S[i] = *reinterpret_cast<const float4*>(state + (int64_t)(4 * i + rg) * DV + 4 * cg);
 
-  // 2. replay the kept tokens of the previous speculative call
-  for (int j0 = 0; j0 < R; j0 += GDN_TB) {
-    const int nj = min(GDN_TB, R - j0);
-    __syncthreads();
-    for (int e = tid; e < nj * pstride; e += NT) {
-      const int j = e / pstride, c = e % pstride;
-      const float val = pend[(int64_t)(j0 + j) * pstride + c];
-      if (c < DK) sm.k[j][c] = val;
-      else if (c < DK + DV) sm.v[j][c - DK] = val;
-      else if (c == DK + DV) sm.g[j] = val;
-      else sm.beta[j] = val;
+  // 2. one bulk load phase (all independent, vectorised): pending replay rows, conv weights,
+  //    the conv window, the first token block's raw q/k/v rows, z rows, a and b
+  for (int e = tid; e < R * (PS / 4); e += NT) {
+    const int j = e / (PS / 4), c4 = (e % (PS / 4)) * 4;
+    const float4 v4 = *reinterpret_cast<const float4*>(pend + (int64_t)j * PS + c4);
+    const float vv[4] = {v4.x, v4.y, v4.z, v4.w};
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int c = c4 + u;
+      if (c < DK) sm.k[j][c] = vv[u];
+      else if (c < DK + DV) sm.v[j][c - DK] = vv[u];
+      else if (c == DK + DV) sm.g[j] = vv[u];
+      else if (c == DK + DV + 1) sm.beta[j] = vv[u];
     }
-    __syncthreads();
-    for (int j = 0; j < nj; ++j) gdn_update<RPT>(S, sm.k[j], sm.v[j], sm.g[j], sm.beta[j], rg, cg);
   }
+  {
+    const T* cw = static_cast<const T*>(L.conv_w);
+    for (int e = tid; e < NCH * K; e += NT) {
+      const int c = e / K, j = e % K;
+      sm.cw[j][c] = dt<T>::to_f(cw[(int64_t)gch(c) * K + j]);
+    }
+  }
+  auto load_tokens = [&](int t0, int nt, int row_base) {
+    // raw q/k/v of tokens t0..t0+nt-1 into xin rows row_base.., z rows, a/b
+    for (int e = tid; e < nt * (NCH / EPV); e += NT) {
+      const int t = e / (NCH / EPV), c = (e % (NCH / EPV)) * EPV;
+      load16_as_float<T>(proj + (int64_t)(b * T_ + t0 + t) * L.ld_proj + gch(c), &sm.xin[row_base + t][c]);
+    }
+    for (int e = tid; e < nt * (DV / EPV); e += NT) {
+      const int t = e / (DV / EPV), c = (e % (DV / EPV)) * EPV;
+      load16_as_float<T>(proj + (int64_t)(b * T_ + t0 + t) * L.ld_proj + conv_dim + h * DV + c, &sm.z[t][c]);
+    }
+    if (tid < 2 * nt) {
+      const int t = tid >> 1, w = tid & 1;   // w = 0: b, 1: a
+      sm.ab[t][w] = dt<T>::to_f(proj[(int64_t)(b * T_ + t0 + t) * L.ld_proj + conv_dim + value_dim + w * Hv + h]);
+    }
+  };
+  for (int e = tid; e < (K - 1) * (NCH / EPV); e += NT) {
+    const int i = e / (NCH / EPV), c = (e % (NCH / EPV)) * EPV;
+    load16_as_float<T>(hist_in + (int64_t)(coff + i) * conv_dim + gch(c), &sm.xin[i][c]);
+  }
+  load_tokens(0, min(GDN_TB, T_), K - 1);
+  __syncthreads();
+
+  // 3. replay the kept tokens of the previous speculative call
+  for (int j = 0; j < R; ++j) gdn_update<RPT>(S, sm.k[j], sm.v[j], sm.g[j], sm.beta[j], rg, cg);
   if (R > 0 && spec) {
 #pragma unroll
     for (int i = 0; i < RPT; ++i)
       *reinterpret_cast<float4*>(state + (int64_t)(4 * i + rg) * DV + 4 * cg) = S[i];
   }
 
-  // conv input x(c, i) over the combined sequence [window (K-1 rows) | raw tokens]
-  auto xin = [&](int c, int i) -> float {
-    if (i < K - 1) return dt<T>::to_f(hist_in[(int64_t)(coff + i) * conv_dim + c]);
-    return dt<T>::to_f(proj[(int64_t)(b * T_ + (i - (K - 1))) * L.ld_proj + c]);
-  };
-  // channels this CTA owns for the conv history: its v channels, and the q/k channels of its
-  // k head when it is the first v head of the group
+  // conv-history ownership: every head writes its v channels; the first v head of a k-head
+  // group also writes that group's q and k channels
   const bool own_qk = (h % vpk) == 0;
-  const int n_own = DV + (own_qk ? 2 * DK : 0);
-  auto own_channel = [&](int e) -> int {
-    if (e < DV) return 2 * key_dim + h * DV + e;
-    e -= DV;
-    if (e < DK) return kh * DK + e;
-    return key_dim + kh * DK + (e - DK);
+  auto write_hist_rows = [&](int src_row0, int n_rows) {
+    for (int e = tid; e < n_rows * NCH; e += NT) {
+      const int i = e / NCH, c = e % NCH;
+      if (c < 2 * DK && !own_qk) continue;
+      hist_out[(int64_t)i * conv_dim + gch(c)] = dt<T>::from_f(sm.xin[src_row0 + i][c]);
+    }
   };
-  if (spec) {
-    for (int e = tid; e < n_own * (K - 1 + T_); e += NT) {
-      const int i = e / n_own, c = own_channel(e % n_own);
-      hist_out[(int64_t)i * conv_dim + c] = dt<T>::from_f(xin(c, i));
-    }
-  } else {
-    for (int e = tid; e < n_own * (K - 1); e += NT) {
-      const int i = e / n_own, c = own_channel(e % n_own);
-      hist_out[(int64_t)i * conv_dim + c] = dt<T>::from_f(xin(c, T_ + i));
-    }
-  }
+  if (T_ == 0) write_hist_rows(0, K - 1);
 
   const float qscale = (float)(1.0 / sqrt((double)DK));  // dk^-0.5 rounded once to fp32
   const float A = -expf(dt<T>::to_f(static_cast<const T*>(L.a_log)[h]));
@@ -196,61 +239,49 @@ gdn_verify_kernel(const qsp_gdn_layer L) {
 
   for (int t0 = 0; t0 < T_; t0 += GDN_TB) {
     const int nt = min(GDN_TB, T_ - t0);
-    __syncthreads();
-    // 3. prologue: conv + SiLU for q, k, v channels; z, β, g
-    for (int e = tid; e < nt * (2 * DK + 2 * DV); e += NT) {
-      const int t = e / (2 * DK + 2 * DV);
-      int c = e % (2 * DK + 2 * DV);
-      const int tok = t0 + t;
-      const T* prow = proj + (int64_t)(b * T_ + tok) * L.ld_proj;
-      if (c < 2 * DK + DV) {
-        int ch;
-        float* dst;
-        if (c < DK) { ch = kh * DK + c; dst = &sm.q[t][c]; }
-        else if (c < 2 * DK) { ch = key_dim + kh * DK + (c - DK); dst = &sm.k[t][c - DK]; }
-        else { ch = 2 * key_dim + h * DV + (c - 2 * DK); dst = &sm.v[t][c - 2 * DK]; }
-        float acc = 0.f;
-        for (int j = 0; j < K; ++j) acc = fmaf(dt<T>::to_f(cw[(int64_t)ch * K + j]), xin(ch, tok + j), acc);
-        *dst = dt<T>::round(siluf_(dt<T>::round(acc)));
-      } else {
-        c -= 2 * DK + DV;
-        sm.z[t][c] = dt<T>::to_f(prow[conv_dim + h * DV + c]);
-      }
+    __syncthreads();   // replay / previous block done with the k, v, q, o arrays
+    // 4. conv + SiLU (fp32 accumulate, rounded like F.conv1d then F.silu), gates
+    for (int e = tid; e < nt * NCH; e += NT) {
+      const int t = e / NCH, c = e % NCH;
+      float acc = 0.f;
+      for (int j = 0; j < K; ++j) acc = fmaf(sm.cw[j][c], sm.xin[t + j][c], acc);
+      const float a = dt<T>::round(siluf_(dt<T>::round(acc)));
+      if (c < DK) sm.q[t][c] = a;
+      else if (c < 2 * DK) sm.k[t][c - DK] = a;
+      else sm.v[t][c - 2 * DK] = a;
     }
     if (tid < nt) {
-      const T* prow = proj + (int64_t)(b * T_ + t0 + tid) * L.ld_proj;
-      const float bb = dt<T>::to_f(prow[conv_dim + value_dim + h]);
-      const float aa = dt<T>::to_f(prow[conv_dim + value_dim + Hv + h]);
-      sm.beta[tid] = dt<T>::round(sigmoidf_(bb));
-      sm.g[tid] = A * softplusf_(aa + dtb);
+      sm.beta[tid] = dt<T>::round(sigmoidf_(sm.ab[tid][0]));
+      sm.g[tid] = A * softplusf_(sm.ab[tid][1] + dtb);
     }
+    if (spec && t0 == 0) write_hist_rows(0, K - 1 + nt);
     __syncthreads();
-    // l2norm of q (with the dk^-0.5 scale applied after, in fp32) and k: one warp per vector
     for (int vidx = warp; vidx < 2 * nt; vidx += NT / 32) {
       const int t = vidx >> 1;
       if (vidx & 1) warp_l2norm<T, DK>(sm.k[t], 1.0f, lane);
       else warp_l2norm<T, DK>(sm.q[t], qscale, lane);
     }
     __syncthreads();
-    // 4. recurrence + readout; pending (k, v, g, β) for the next call's replay
+    // 5. recurrence + readout; pending (k, v, g, β) for the next call's replay
     for (int t = 0; t < nt; ++t) {
       gdn_update<RPT>(S, sm.k[t], sm.v[t], sm.g[t], sm.beta[t], rg, cg);
       const float4 o = gdn_readout<RPT>(S, sm.q[t], rg);
       if (rg == 0) *reinterpret_cast<float4*>(&sm.o[t][4 * cg]) = o;
     }
     if (spec) {
-      for (int e = tid; e < nt * pstride; e += NT) {
-        const int t = e / pstride, c = e % pstride;
-        float val;
-        if (c < DK) val = sm.k[t][c];
-        else if (c < DK + DV) val = sm.v[t][c - DK];
-        else if (c == DK + DV) val = sm.g[t];
-        else val = sm.beta[t];
-        pend[(int64_t)(t0 + t) * pstride + c] = val;
+      for (int e = tid; e < nt * (PS / 4); e += NT) {
+        const int t = e / (PS / 4), c4 = (e % (PS / 4)) * 4;
+        float vv[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int c = c4 + u;
+          vv[u] = c < DK ? sm.k[t][c] : (c < DK + DV ? sm.v[t][c - DK] : (c == DK + DV ? sm.g[t] : (c == DK + DV + 1 ? sm.beta[t] : 0.f)));
+        }
+        *reinterpret_cast<float4*>(pend + (int64_t)(t0 + t) * PS + c4) = make_float4(vv[0], vv[1], vv[2], vv[3]);
       }
     }
     __syncthreads();
-    // 5. RMSNormGated over dv per token: w·round(x̂) · silu(z), x = round(core)
+    // 6. RMSNormGated over dv per token: w·round(x̂) · silu(z), x = round(core)
     for (int t = warp; t < nt; t += NT / 32) {
       float ss = 0.f;
       for (int c = lane; c < DV; c += 32) {
@@ -265,6 +296,29 @@ gdn_verify_kernel(const qsp_gdn_layer L) {
         const float wx = dt<T>::round(dt<T>::to_f(normw[c]) * xh);
         orow[c] = dt<T>::from_f(wx * siluf_(sm.z[t][c]));
       }
+    }
+    const bool last = t0 + nt >= T_;
+    if (last) {
+      if (!spec) write_hist_rows(nt, K - 1);   // the window after the last token
+    } else {
+      // slide the window (last K-1 combined rows to the front) and load the next block
+      // (source and destination rows may overlap: read everything, barrier, then write)
+      constexpr int SLIDE = ((GDN_KMAX - 1) * NCH + NT - 1) / NT;
+      float keep[SLIDE];
+      __syncthreads();
+#pragma unroll
+      for (int u = 0; u < SLIDE; ++u) {
+        const int e = tid + u * NT;
+        keep[u] = e < (K - 1) * NCH ? sm.xin[nt + e / NCH][e % NCH] : 0.f;
+      }
+      __syncthreads();
+#pragma unroll
+      for (int u = 0; u < SLIDE; ++u) {
+        const int e = tid + u * NT;
+        if (e < (K - 1) * NCH) sm.xin[e / NCH][e % NCH] = keep[u];
+      }
+      __syncthreads();
+      load_tokens(t0 + nt, min(GDN_TB, T_ - t0 - nt), K - 1);
     }
   }
 
@@ -304,8 +358,10 @@ extern "C" int qsp_gdn_verify(const qsp_gdn_layer* layer, void* stream) {
   QSP_REQUIRE(L.batch > 0 && L.batch <= 65535 && L.tokens >= 0, "qsp_gdn_verify: bad batch/tokens");
   QSP_REQUIRE(L.n_k_heads > 0 && L.n_v_heads > 0 && L.n_v_heads % L.n_k_heads == 0,
               "qsp_gdn_verify: v heads must be a multiple of k heads");
-  QSP_REQUIRE(L.conv_kernel >= 2 && L.conv_kernel <= 8, "qsp_gdn_verify: conv kernel %d", L.conv_kernel);
-  QSP_REQUIRE(L.max_spec_tokens >= 1, "qsp_gdn_verify: max_spec_tokens must be >= 1");
+  QSP_REQUIRE(L.conv_kernel >= 2 && L.conv_kernel <= GDN_KMAX, "qsp_gdn_verify: conv kernel %d (max %d)",
+              L.conv_kernel, GDN_KMAX);
+  QSP_REQUIRE(L.max_spec_tokens >= 1 && L.max_spec_tokens <= GDN_TB,
+              "qsp_gdn_verify: max_spec_tokens must be in [1, %d]", GDN_TB);
   QSP_REQUIRE(!L.speculative || (L.tokens >= 1 && L.tokens <= L.max_spec_tokens),
               "qsp_gdn_verify: speculative call with %d tokens > max_spec_tokens %d", L.tokens,
               L.max_spec_tokens);
@@ -313,6 +369,9 @@ extern "C" int qsp_gdn_verify(const qsp_gdn_layer* layer, void* stream) {
   QSP_REQUIRE(L.ld_proj >= conv_dim + (int64_t)L.n_v_heads * L.head_v + 2 * L.n_v_heads,
               "qsp_gdn_verify: ld_proj too small");
   QSP_REQUIRE(L.ld_out >= (int64_t)L.n_v_heads * L.head_v, "qsp_gdn_verify: ld_out too small");
-  QSP_REQUIRE(aligned(L.state, 16) && aligned(L.pending, 16), "qsp_gdn_verify: state/pending must be 16-byte aligned");
+  QSP_REQUIRE(aligned(L.state, 16) && aligned(L.pending, 16) && aligned(L.proj, 16) && aligned(L.conv_hist, 16),
+              "qsp_gdn_verify: state/pending/proj/conv_hist must be 16-byte aligned");
+  const int esz = L.dtype == QSP_F32 ? 4 : 2;
+  QSP_REQUIRE((L.ld_proj * esz) % 16 == 0, "qsp_gdn_verify: ld_proj must be a multiple of 16 bytes");
   QSP_DISPATCH_DTYPE(L.dtype, T, { return launch_gdn<T>(L, as_stream(stream)); });
 }

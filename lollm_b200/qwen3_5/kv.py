@@ -59,7 +59,7 @@ class Qwen3_5Cache:
         self.state = torch.zeros(n_gdn, batch, Hv, dk, dv, dtype=torch.float32, device=dev)
         self.conv_hist = torch.zeros(n_gdn, 2, batch, Kc - 1 + max_spec_tokens, cfg.conv_dim,
                                      dtype=dtype, device=dev)
-        self.pending = torch.zeros(n_gdn, batch, Hv, max_spec_tokens, dk + dv + 2,
+        self.pending = torch.zeros(n_gdn, batch, Hv, max_spec_tokens, dk + dv + 4,
                                    dtype=torch.float32, device=dev)
         self.replay_n = torch.zeros(batch, dtype=torch.int32, device=dev)
         self.conv_off = torch.zeros(batch, dtype=torch.int32, device=dev)

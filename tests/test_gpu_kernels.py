@@ -116,7 +116,7 @@ class GdnCase:
         self.g = g
         self.state = torch.zeros(B, Hv, d, d, device=DEV)
         self.hist = torch.zeros(2, B, Kc - 1 + Ts, self.C, dtype=dt, device=DEV)
-        self.pending = torch.zeros(B, Hv, Ts, 2 * d + 2, device=DEV)
+        self.pending = torch.zeros(B, Hv, Ts, 2 * d + 4, device=DEV)
         self.replay = torch.zeros(B, dtype=torch.int32, device=DEV)
         self.coff = torch.zeros(B, dtype=torch.int32, device=DEV)
         self.parity = torch.zeros(1, dtype=torch.int32, device=DEV)
@@ -171,7 +171,7 @@ def test_gdn_commit_all_matches_oracle(dt, d):
     c = GdnCase(dt, d=d, seed=d)
     conv = torch.zeros(c.B, c.C, c.Kc - 1, dtype=dt)
     rec = torch.zeros(c.B, c.Hv, d, d)
-    for T in (6, 1, 3):
+    for T in (6, 1, 19, 3):
         proj = c.random_proj(T)
         got = c.run(proj, speculative=False)
         want, conv, rec = c.oracle(proj, conv, rec)
