@@ -390,6 +390,148 @@ def replay_split(graphs, events=None, stream=None):
             events[i + 1].record(stream)
 
 
+# ─────────────────────────────────────── isolated kernels ───────────────────────────────────────
+
+def timed_loop(fn, steps, warmup, stream, between=None):
+    """CUDA-event time of `steps` calls of fn (after `warmup`), per call in ms; `between`
+    (not timed) runs before each call."""
+    for _ in range(warmup):
+        if between: between()
+        fn()
+    torch.cuda.synchronize()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for a, b in evs:
+        if between: between()
+        a.record(stream)
+        fn()
+        b.record(stream)
+    torch.cuda.synchronize()
+    return [a.elapsed_time(b) for a, b in evs]
+
+
+def run_gdn_workload(args):
+    """one GDN verify update over T=4 tokens for 64 sequences x 32 value
+    heads (16 key heads), fp32 128x128 state per head, then a rollback to a random kept prefix
+    by index. Units: one launch updates 64x32 head states."""
+    from lollm_b200 import _lib as L
+    from lollm_b200 import kernels as K
+    dev = torch.device("cuda", 0)
+    B, Hk, Hv, d, Kc, T = 64, 16, 32, 128, 4, 4
+    C, Vd = 2 * Hk * d + Hv * d, Hv * d
+    g = torch.Generator(device=dev); g.manual_seed(0)
+    rnd = lambda *s: torch.randn(*s, generator=g, device=dev)
+    state = rnd(B, Hv, d, d) * 0.1
+    hist = torch.zeros(2, B, Kc - 1 + 8, C, dtype=torch.bfloat16, device=dev)
+    pending = torch.zeros(B, Hv, 8, 2 * d + 4, device=dev)
+    replay = torch.zeros(B, dtype=torch.int32, device=dev)
+    coff = torch.zeros(B, dtype=torch.int32, device=dev)
+    parity = torch.zeros(1, dtype=torch.int32, device=dev)
+    lens = torch.zeros(B, dtype=torch.int32, device=dev)
+    proj = rnd(B * T, C + Vd + 2 * Hv).to(torch.bfloat16)
+    # decay exp(-softplus(a + dt_bias) * A), A ~ U[1, 16]: A_log = log(A)
+    a_log = torch.log(1 + 15 * torch.rand(Hv, generator=g, device=dev)).to(torch.bfloat16)
+    dt_bias = torch.zeros(Hv, dtype=torch.bfloat16, device=dev)
+    conv_w = (rnd(C, Kc) * 0.5).to(torch.bfloat16)
+    norm_w = torch.ones(d, dtype=torch.bfloat16, device=dev)
+    out = torch.empty(B * T, Vd, dtype=torch.bfloat16, device=dev)
+    desc = L.GdnLayer()
+    desc.batch, desc.tokens, desc.n_k_heads, desc.n_v_heads, desc.head_k, desc.head_v = B, T, Hk, Hv, d, d
+    desc.conv_kernel, desc.max_spec_tokens, desc.speculative, desc.dtype, desc.eps = Kc, 8, 1, L.QSP_BF16, 1e-6
+    desc.proj, desc.ld_proj = proj.data_ptr(), proj.stride(0)
+    desc.conv_w, desc.a_log, desc.dt_bias, desc.norm_w = conv_w.data_ptr(), a_log.data_ptr(), dt_bias.data_ptr(), norm_w.data_ptr()
+    desc.state, desc.conv_hist, desc.pending = state.data_ptr(), hist.data_ptr(), pending.data_ptr()
+    desc.replay_n, desc.conv_off, desc.parity = replay.data_ptr(), coff.data_ptr(), parity.data_ptr()
+    desc.out, desc.ld_out = out.data_ptr(), out.stride(0)
+    acc_all = torch.randint(0, T, (args.warmup + args.steps + 1, B), generator=g, device=dev, dtype=torch.int32)
+    it = {"i": 0}
+
+    def between():   # rollback of the previous step to a random kept prefix (index only)
+        K.cache_accept(B, T, acc_all[it["i"]], lens, replay, coff)
+        it["i"] += 1
+
+    def step():
+        K.gdn_verify(desc)
+        K.cache_finalize(B, T, True, lens, replay, coff, parity)
+
+    stream = torch.cuda.current_stream()
+    if args.profile:
+        torch.cuda.profiler.start()
+    ms = timed_loop(step, args.steps, args.warmup, stream, between)
+    if args.profile:
+        torch.cuda.profiler.stop()
+    # kernel-only time (finalize is a 2 µs bookkeeping launch): time the GDN launch alone too
+    ms_k = timed_loop(lambda: K.gdn_verify(desc), args.steps, 1, stream)
+    hbm, _, src = peaks()
+    algo = 2 * B * Hv * d * d * 4 + 2 * B * C * (Kc - 1) * 2 + B * T * (C + Vd) * 2 + B * T * Vd * 2
+    t = statistics.mean(ms_k) / 1000
+    return {"metric": "GDN verify update (64 seq x 32 heads, T=4) state GB/s", "value": algo / t / 1e9,
+            "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": statistics.mean(ms), "higher_is_better": True, "dtype": "f32 state, bf16 io",
+            "data": "synthetic (BASELINE configs[3] shapes)", "config": {"workload": "gdn (BASELINE configs[3])"},
+            "roofline": {"kernel": "gdn_verify_kernel", "bound": "hbm", "achieved": algo / t / 1e9, "peak": hbm,
+                         "unit": "GB/s", "frac": algo / t / 1e9 / hbm, "peak_source": src, "traffic": None,
+                         "algorithmic_bytes_per_launch": algo}}
+
+
+def run_attn_workload(args):
+    """verify attention of T=4 queries x 16 heads (2 kv heads, hd 256)
+    for 64 sequences with per-sequence context L ~ U[1024, 32768] over a paged bf16 cache."""
+    from lollm_b200 import _lib as L
+    from lollm_b200 import kernels as K
+    from lollm_b200.qwen3_5.modeling_qwen3_5 import rope_table
+    dev = torch.device("cuda", 0)
+    B, T, nh, nkv, hd, rd, ps = 64, 4, 16, 2, 256, 64, 64
+    g = torch.Generator(device=dev); g.manual_seed(0)
+    lens = torch.randint(1024, 32768 + 1 - T, (B,), generator=g, device=dev, dtype=torch.int32)
+    max_pages = (32768 + ps - 1) // ps
+    # only the pages each sequence uses are allocated, in shuffled order (a paged pool)
+    need = [(int(l) + T + ps - 1) // ps for l in lens.tolist()]
+    num_pages = sum(need)
+    perm = torch.randperm(num_pages, generator=g, device=dev).to(torch.int32)
+    page_table = torch.zeros(B, max_pages, dtype=torch.int32, device=dev)
+    o = 0
+    for b, n in enumerate(need):
+        page_table[b, :n] = perm[o:o + n]
+        o += n
+    kp = torch.empty(num_pages, nkv, ps, hd, dtype=torch.bfloat16, device=dev).normal_(generator=g)
+    vp = torch.empty_like(kp).normal_(generator=g)
+    qkv = torch.randn(B * T, 2 * nh * hd + 2 * nkv * hd, generator=g, device=dev).to(torch.bfloat16)
+    qn = torch.zeros(hd, dtype=torch.bfloat16, device=dev); kn = torch.zeros_like(qn)
+    cos, sin = rope_table(rd, 1e7, 32768 + 8, torch.bfloat16)
+    cos, sin = cos.to(dev), sin.to(dev)
+    splits = max(1, (32768 + 511) // 512)
+    q_buf = torch.empty(B * T, nh * hd, dtype=torch.bfloat16, device=dev)
+    out = torch.empty(B * T, nh * hd, dtype=torch.bfloat16, device=dev)
+    part = torch.empty(K.attn_workspace_bytes(B, T, nh, hd, splits) // 4, device=dev)
+    d = L.AttnLayer()
+    d.batch, d.tokens, d.n_heads, d.n_kv_heads, d.head_dim, d.rotary_dim = B, T, nh, nkv, hd, rd
+    d.page_size, d.max_pages, d.num_pages, d.dtype, d.eps, d.scale = ps, max_pages, num_pages, L.QSP_BF16, 1e-6, 1 / 16
+    d.qkv, d.ld_qkv, d.q_norm_w, d.k_norm_w = qkv.data_ptr(), qkv.stride(0), qn.data_ptr(), kn.data_ptr()
+    d.rope_cos, d.rope_sin, d.rope_rows = cos.data_ptr(), sin.data_ptr(), 32768 + 8
+    d.k_pages, d.v_pages, d.page_table, d.seq_lens = kp.data_ptr(), vp.data_ptr(), page_table.data_ptr(), lens.data_ptr()
+    d.q_buf, d.out, d.ld_out, d.partial, d.num_splits, d.bad_index = (q_buf.data_ptr(), out.data_ptr(), out.stride(0),
+                                                                     part.data_ptr(), splits, 0)
+    K.attn_prep(d)
+    stream = torch.cuda.current_stream()
+    if args.profile:
+        torch.cuda.profiler.start()
+    ms = timed_loop(lambda: K.attn_verify(d), args.steps, args.warmup, stream)
+    if args.profile:
+        torch.cuda.profiler.stop()
+    hbm, _, src = peaks()
+    Ls = lens.tolist()
+    algo = sum((l + T) * nkv * hd * 2 * 2 for l in Ls)
+    t = statistics.mean(ms) / 1000
+    return {"metric": "verify attention (64 seq, T=4, L~U[1024,32768]) KV GB/s", "value": algo / t / 1e9,
+            "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": statistics.mean(ms), "higher_is_better": True, "dtype": "bf16",
+            "data": "synthetic (BASELINE configs[2] shapes)",
+            "config": {"workload": "attn (BASELINE configs[2])", "mean_L": sum(Ls) / B, "splits": splits},
+            "roofline": {"kernel": "attn_mma_kernel + attn_combine_kernel", "bound": "hbm", "achieved": algo / t / 1e9,
+                         "peak": hbm, "unit": "GB/s", "frac": algo / t / 1e9 / hbm, "peak_source": src,
+                         "traffic": None, "algorithmic_bytes_per_launch": algo}}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -405,9 +547,16 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", action="store_true",
                     help="bracket the timed steps with cudaProfilerStart/Stop (for ncu --profile-from-start off)")
+    ap.add_argument("--workload", choices=["step", "gdn", "attn"], default="step",
+                    help="step: the speculative step (headline); gdn / attn: BASELINE configs[3] / [2] kernels alone")
     args = ap.parse_args()
     from lollm_b200.qwen3_5.config import QWEN35_2B, Qwen3_5Config
     cfg = Qwen3_5Config.from_hf(QWEN35_2B)
+    if args.workload != "step":
+        torch.cuda.set_device(0)
+        out = run_gdn_workload(args) if args.workload == "gdn" else run_attn_workload(args)
+        print(json.dumps(out), flush=True)
+        return
     if args.impl == "reference":
         ws, rank = int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0"))
         run_reference_arm(args, cfg, ws, rank)
