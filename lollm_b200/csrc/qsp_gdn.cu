@@ -10,6 +10,8 @@
 // Rollback by index: see the qsp_gdn_layer comment in include/qsp.h.
 #include "qsp_common.cuh"
 
+#include <algorithm>
+
 namespace qsp {
 
 constexpr int GDN_TB = 8;    // tokens per block (a whole verify step)
@@ -113,8 +115,9 @@ __device__ __forceinline__ void load16_as_float(const T* src, float* dst) {
 }
 
 template <int DK, int DV>
-struct __align__(16) GdnSmem {
+struct __align__(128) GdnSmem {
   static constexpr int NCH = 2 * DK + DV;   // q, k, v conv channels of one value head
+  float sst[DK * DV];                       // next head's state (TMA bulk prefetch target)
   float xin[GDN_KMAX - 1 + GDN_TB][NCH];    // conv inputs: window rows, then this block's tokens
   float cw[GDN_KMAX][NCH];                  // conv weights, tap-major
   float q[GDN_TB][DK];
@@ -125,224 +128,303 @@ struct __align__(16) GdnSmem {
   float g[GDN_TB];
   float beta[GDN_TB];
   float ab[GDN_TB][2];                      // raw a, b of this head
+  uint64_t bar;                             // state prefetch barrier
 };
 
+__device__ int g_gdn_error = 0;
+
+__device__ __forceinline__ uint32_t gsm(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+
+__device__ __forceinline__ bool gdn_wait(uint64_t* bar, uint32_t parity) {
+  for (uint32_t i = 0; i < (1u << 24); ++i) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok) : "r"(gsm(bar)), "r"(parity) : "memory");
+    if (ok) return true;
+    if (i > 256) __nanosleep(64);
+  }
+  atomicExch(&g_gdn_error, 201);
+  return false;
+}
+
+// Prefetch one head's fp32 state (contiguous DK*DV floats) into shared memory with a single
+// bulk copy that completes on `bar`.
+__device__ __forceinline__ void gdn_prefetch_state(float* dst, const float* src, uint64_t* bar, uint32_t bytes) {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(gsm(bar)), "r"(bytes) : "memory");
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(gsm(dst)),
+               "l"(src), "r"(bytes), "r"(gsm(bar))
+               : "memory");
+}
+
+// Persistent: CTA c handles (sequence, value head) units c, c+G, c+2G, ... . While a unit is
+// computed from registers, the next unit's state streams into shared memory, so the HBM
+// traffic of the recurrence (one state read and one write per head) overlaps the math.
 template <typename T, int DK, int DV>
-__global__ void __launch_bounds__(DV, (DV >= 128 ? 3 : 4))
+__global__ void __launch_bounds__(DV, 2)
 gdn_verify_kernel(const qsp_gdn_layer L) {
   constexpr int RPT = DK / 4;
   constexpr int NT = DV;
   constexpr int NCH = GdnSmem<DK, DV>::NCH;
   constexpr int EPV = 16 / (int)sizeof(T);   // elements per 16-byte vector
-  __shared__ GdnSmem<DK, DV> sm;
+  constexpr int PS = DK + DV + 4;            // pending row: k | v | g | beta | pad (16-byte rows)
+  extern __shared__ __align__(128) uint8_t gdn_smem_raw[];
+  GdnSmem<DK, DV>& sm = *reinterpret_cast<GdnSmem<DK, DV>*>(gdn_smem_raw);
 
-  const int h = blockIdx.x, b = blockIdx.y;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int cg = warp * 8 + (lane & 7), rg = lane >> 3;
   const int T_ = L.tokens, K = L.conv_kernel, Ts = L.max_spec_tokens;
-  const int Hv = L.n_v_heads, Hk = L.n_k_heads, vpk = Hv / Hk, kh = h / vpk;
+  const int Hv = L.n_v_heads, Hk = L.n_k_heads, vpk = Hv / Hk;
   const int key_dim = Hk * DK, conv_dim = 2 * key_dim + Hv * DV, value_dim = Hv * DV;
   const bool spec = L.speculative != 0;
   const T* proj = static_cast<const T*>(L.proj);
   T* hist = static_cast<T*>(L.conv_hist);
   T* out = static_cast<T*>(L.out);
   const int par = L.parity[0];
-  // device-side counters are clamped to the buffers they index (they are produced by
-  // qsp_cache_finalize / qsp_cache_accept and never exceed max_spec_tokens)
-  const int R = min(max(L.replay_n[b], 0), Ts);
-  const int coff = min(max(L.conv_off[b], 0), Ts);
   const int hist_rows = K - 1 + Ts;
-  const T* hist_in = hist + ((int64_t)par * L.batch + b) * hist_rows * conv_dim;
-  T* hist_out = hist + ((int64_t)(par ^ 1) * L.batch + b) * hist_rows * conv_dim;
-  constexpr int PS = DK + DV + 4;   // pending row: k | v | g | beta | pad (16-byte rows)
-  float* pend = L.pending + (((int64_t)b * Hv + h) * Ts) * PS;
-  float* state = L.state + ((int64_t)b * Hv + h) * DK * DV;
-  // global channel of local conv channel c: q | k | v segments of this head
-  auto gch = [&](int c) -> int {
-    return c < DK ? kh * DK + c : (c < 2 * DK ? key_dim + kh * DK + (c - DK) : 2 * key_dim + h * DV + (c - 2 * DK));
-  };
-
-  // 1. the state of this head into registers
-  float4 S[RPT];
-#pragma unroll
-  for (int i = 0; i < RPT; ++i)
-    S[i] = *reinterpret_cast<const float4*>(state + (int64_t)(4 * i + rg) * DV + 4 * cg);
-
-  // 2. one bulk load phase (all independent, vectorised): pending replay rows, conv weights,
-  //    the conv window, the first token block's raw q/k/v rows, z rows, a and b
-  for (int e = tid; e < R * (PS / 4); e += NT) {
-    const int j = e / (PS / 4), c4 = (e % (PS / 4)) * 4;
-    const float4 v4 = *reinterpret_cast<const float4*>(pend + (int64_t)j * PS + c4);
-    const float vv[4] = {v4.x, v4.y, v4.z, v4.w};
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int c = c4 + u;
-      if (c < DK) sm.k[j][c] = vv[u];
-      else if (c < DK + DV) sm.v[j][c - DK] = vv[u];
-      else if (c == DK + DV) sm.g[j] = vv[u];
-      else if (c == DK + DV + 1) sm.beta[j] = vv[u];
-    }
-  }
-  {
-    const T* cw = static_cast<const T*>(L.conv_w);
-    for (int e = tid; e < NCH * K; e += NT) {
-      const int c = e / K, j = e % K;
-      sm.cw[j][c] = dt<T>::to_f(cw[(int64_t)gch(c) * K + j]);
-    }
-  }
-  auto load_tokens = [&](int t0, int nt, int row_base) {
-    // raw q/k/v of tokens t0..t0+nt-1 into xin rows row_base.., z rows, a/b
-    for (int e = tid; e < nt * (NCH / EPV); e += NT) {
-      const int t = e / (NCH / EPV), c = (e % (NCH / EPV)) * EPV;
-      load16_as_float<T>(proj + (int64_t)(b * T_ + t0 + t) * L.ld_proj + gch(c), &sm.xin[row_base + t][c]);
-    }
-    for (int e = tid; e < nt * (DV / EPV); e += NT) {
-      const int t = e / (DV / EPV), c = (e % (DV / EPV)) * EPV;
-      load16_as_float<T>(proj + (int64_t)(b * T_ + t0 + t) * L.ld_proj + conv_dim + h * DV + c, &sm.z[t][c]);
-    }
-    if (tid < 2 * nt) {
-      const int t = tid >> 1, w = tid & 1;   // w = 0: b, 1: a
-      sm.ab[t][w] = dt<T>::to_f(proj[(int64_t)(b * T_ + t0 + t) * L.ld_proj + conv_dim + value_dim + w * Hv + h]);
-    }
-  };
-  for (int e = tid; e < (K - 1) * (NCH / EPV); e += NT) {
-    const int i = e / (NCH / EPV), c = (e % (NCH / EPV)) * EPV;
-    load16_as_float<T>(hist_in + (int64_t)(coff + i) * conv_dim + gch(c), &sm.xin[i][c]);
-  }
-  load_tokens(0, min(GDN_TB, T_), K - 1);
-  __syncthreads();
-
-  // 3. replay the kept tokens of the previous speculative call
-  for (int j = 0; j < R; ++j) gdn_update<RPT>(S, sm.k[j], sm.v[j], sm.g[j], sm.beta[j], rg, cg);
-  if (R > 0 && spec) {
-#pragma unroll
-    for (int i = 0; i < RPT; ++i)
-      *reinterpret_cast<float4*>(state + (int64_t)(4 * i + rg) * DV + 4 * cg) = S[i];
-  }
-
-  // conv-history ownership: every head writes its v channels; the first v head of a k-head
-  // group also writes that group's q and k channels
-  const bool own_qk = (h % vpk) == 0;
-  auto write_hist_rows = [&](int src_row0, int n_rows) {
-    for (int e = tid; e < n_rows * NCH; e += NT) {
-      const int i = e / NCH, c = e % NCH;
-      if (c < 2 * DK && !own_qk) continue;
-      hist_out[(int64_t)i * conv_dim + gch(c)] = dt<T>::from_f(sm.xin[src_row0 + i][c]);
-    }
-  };
-  if (T_ == 0) write_hist_rows(0, K - 1);
-
+  const int units = L.batch * Hv;
   const float qscale = (float)(1.0 / sqrt((double)DK));  // dk^-0.5 rounded once to fp32
-  const float A = -expf(dt<T>::to_f(static_cast<const T*>(L.a_log)[h]));
-  const float dtb = dt<T>::to_f(static_cast<const T*>(L.dt_bias)[h]);
   const T* normw = static_cast<const T*>(L.norm_w);
+  constexpr uint32_t SBYTES = DK * DV * 4;
 
-  for (int t0 = 0; t0 < T_; t0 += GDN_TB) {
-    const int nt = min(GDN_TB, T_ - t0);
-    __syncthreads();   // replay / previous block done with the k, v, q, o arrays
-    // 4. conv + SiLU (fp32 accumulate, rounded like F.conv1d then F.silu), gates
-    for (int e = tid; e < nt * NCH; e += NT) {
-      const int t = e / NCH, c = e % NCH;
-      float acc = 0.f;
-      for (int j = 0; j < K; ++j) acc = fmaf(sm.cw[j][c], sm.xin[t + j][c], acc);
-      const float a = dt<T>::round(siluf_(dt<T>::round(acc)));
-      if (c < DK) sm.q[t][c] = a;
-      else if (c < 2 * DK) sm.k[t][c - DK] = a;
-      else sm.v[t][c - 2 * DK] = a;
-    }
-    if (tid < nt) {
-      sm.beta[tid] = dt<T>::round(sigmoidf_(sm.ab[tid][0]));
-      sm.g[tid] = A * softplusf_(sm.ab[tid][1] + dtb);
-    }
-    if (spec && t0 == 0) write_hist_rows(0, K - 1 + nt);
-    __syncthreads();
-    for (int vidx = warp; vidx < 2 * nt; vidx += NT / 32) {
-      const int t = vidx >> 1;
-      if (vidx & 1) warp_l2norm<T, DK>(sm.k[t], 1.0f, lane);
-      else warp_l2norm<T, DK>(sm.q[t], qscale, lane);
-    }
-    __syncthreads();
-    // 5. recurrence + readout; pending (k, v, g, β) for the next call's replay
-    for (int t = 0; t < nt; ++t) {
-      gdn_update<RPT>(S, sm.k[t], sm.v[t], sm.g[t], sm.beta[t], rg, cg);
-      const float4 o = gdn_readout<RPT>(S, sm.q[t], rg);
-      if (rg == 0) *reinterpret_cast<float4*>(&sm.o[t][4 * cg]) = o;
-    }
-    if (spec) {
-      for (int e = tid; e < nt * (PS / 4); e += NT) {
-        const int t = e / (PS / 4), c4 = (e % (PS / 4)) * 4;
-        float vv[4];
+  if (tid == 0) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(gsm(&sm.bar)) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  if (tid == 0 && blockIdx.x < units)
+    gdn_prefetch_state(sm.sst, L.state + (int64_t)blockIdx.x * DK * DV, &sm.bar, SBYTES);
+  // conv weights are shared by every unit of a head; loaded per unit (head changes)
+
+  uint32_t it = 0;
+  for (int u = blockIdx.x; u < units; u += gridDim.x, ++it) {
+    const int b = u / Hv, h = u % Hv, kh = h / vpk;
+    // device-side counters are clamped to the buffers they index (they are produced by
+    // qsp_cache_finalize / qsp_cache_accept and never exceed max_spec_tokens)
+    const int R = min(max(L.replay_n[b], 0), Ts);
+    const int coff = min(max(L.conv_off[b], 0), Ts);
+    const T* hist_in = hist + ((int64_t)par * L.batch + b) * hist_rows * conv_dim;
+    T* hist_out = hist + ((int64_t)(par ^ 1) * L.batch + b) * hist_rows * conv_dim;
+    float* pend = L.pending + (((int64_t)b * Hv + h) * Ts) * PS;
+    float* state = L.state + ((int64_t)b * Hv + h) * DK * DV;
+    auto gch = [&](int c) -> int {
+      return c < DK ? kh * DK + c : (c < 2 * DK ? key_dim + kh * DK + (c - DK) : 2 * key_dim + h * DV + (c - 2 * DK));
+    };
+
+    // 1. this unit's small inputs → shared memory (vectorised, all independent)
+    for (int e = tid; e < R * (PS / 4); e += NT) {
+      const int j = e / (PS / 4), c4 = (e % (PS / 4)) * 4;
+      const float4 v4 = *reinterpret_cast<const float4*>(pend + (int64_t)j * PS + c4);
+      const float vv[4] = {v4.x, v4.y, v4.z, v4.w};
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int c = c4 + u;
-          vv[u] = c < DK ? sm.k[t][c] : (c < DK + DV ? sm.v[t][c - DK] : (c == DK + DV ? sm.g[t] : (c == DK + DV + 1 ? sm.beta[t] : 0.f)));
+      for (int q4 = 0; q4 < 4; ++q4) {
+        const int c = c4 + q4;
+        if (c < DK) sm.k[j][c] = vv[q4];
+        else if (c < DK + DV) sm.v[j][c - DK] = vv[q4];
+        else if (c == DK + DV) sm.g[j] = vv[q4];
+        else if (c == DK + DV + 1) sm.beta[j] = vv[q4];
+      }
+    }
+    {
+      const T* cw = static_cast<const T*>(L.conv_w);
+      for (int e = tid; e < NCH * K; e += NT) {
+        const int c = e / K, j = e % K;
+        sm.cw[j][c] = dt<T>::to_f(cw[(int64_t)gch(c) * K + j]);
+      }
+    }
+    auto load_tokens = [&](int t0, int nt, int row_base) {
+      for (int e = tid; e < nt * (NCH / EPV); e += NT) {
+        const int t = e / (NCH / EPV), c = (e % (NCH / EPV)) * EPV;
+        load16_as_float<T>(proj + (int64_t)(b * T_ + t0 + t) * L.ld_proj + gch(c), &sm.xin[row_base + t][c]);
+      }
+      for (int e = tid; e < nt * (DV / EPV); e += NT) {
+        const int t = e / (DV / EPV), c = (e % (DV / EPV)) * EPV;
+        load16_as_float<T>(proj + (int64_t)(b * T_ + t0 + t) * L.ld_proj + conv_dim + h * DV + c, &sm.z[t][c]);
+      }
+      if (tid < 2 * nt) {
+        const int t = tid >> 1, w = tid & 1;   // w = 0: b, 1: a
+        sm.ab[t][w] = dt<T>::to_f(proj[(int64_t)(b * T_ + t0 + t) * L.ld_proj + conv_dim + value_dim + w * Hv + h]);
+      }
+    };
+    for (int e = tid; e < (K - 1) * (NCH / EPV); e += NT) {
+      const int i = e / (NCH / EPV), c = (e % (NCH / EPV)) * EPV;
+      load16_as_float<T>(hist_in + (int64_t)(coff + i) * conv_dim + gch(c), &sm.xin[i][c]);
+    }
+    load_tokens(0, min(GDN_TB, T_), K - 1);
+
+    // 2. this unit's state: prefetched into shared memory → registers
+    gdn_wait(&sm.bar, it & 1u);
+    float4 S[RPT];
+#pragma unroll
+    for (int i = 0; i < RPT; ++i) S[i] = *reinterpret_cast<const float4*>(&sm.sst[(4 * i + rg) * DV + 4 * cg]);
+    __syncthreads();   // inputs staged; every thread holds its state slice
+    // 3. prefetch the next unit's state while this one computes
+    if (tid == 0 && u + (int)gridDim.x < units)
+      gdn_prefetch_state(sm.sst, L.state + (int64_t)(u + gridDim.x) * DK * DV, &sm.bar, SBYTES);
+
+    // 4. replay the kept tokens of the previous speculative call
+    for (int j = 0; j < R; ++j) gdn_update<RPT>(S, sm.k[j], sm.v[j], sm.g[j], sm.beta[j], rg, cg);
+    if (R > 0 && spec) {
+#pragma unroll
+      for (int i = 0; i < RPT; ++i)
+        *reinterpret_cast<float4*>(state + (int64_t)(4 * i + rg) * DV + 4 * cg) = S[i];
+    }
+
+    // conv-history ownership: every head writes its v channels; the first v head of a k-head
+    // group also writes that group's q and k channels
+    const bool own_qk = (h % vpk) == 0;
+    auto write_hist_rows = [&](int src_row0, int n_rows) {
+      for (int e = tid; e < n_rows * NCH; e += NT) {
+        const int i = e / NCH, c = e % NCH;
+        if (c < 2 * DK && !own_qk) continue;
+        hist_out[(int64_t)i * conv_dim + gch(c)] = dt<T>::from_f(sm.xin[src_row0 + i][c]);
+      }
+    };
+    if (T_ == 0) write_hist_rows(0, K - 1);
+
+    const float A = -expf(dt<T>::to_f(static_cast<const T*>(L.a_log)[h]));
+    const float dtb = dt<T>::to_f(static_cast<const T*>(L.dt_bias)[h]);
+
+    for (int t0 = 0; t0 < T_; t0 += GDN_TB) {
+      const int nt = min(GDN_TB, T_ - t0);
+      __syncthreads();   // replay / previous block done with the k, v, q, o arrays
+      // 5. conv + SiLU (fp32 accumulate, rounded like F.conv1d then F.silu), gates
+      for (int e = tid; e < nt * NCH; e += NT) {
+        const int t = e / NCH, c = e % NCH;
+        float acc = 0.f;
+        for (int j = 0; j < K; ++j) acc = fmaf(sm.cw[j][c], sm.xin[t + j][c], acc);
+        const float a = dt<T>::round(siluf_(dt<T>::round(acc)));
+        if (c < DK) sm.q[t][c] = a;
+        else if (c < 2 * DK) sm.k[t][c - DK] = a;
+        else sm.v[t][c - 2 * DK] = a;
+      }
+      if (tid < nt) {
+        sm.beta[tid] = dt<T>::round(sigmoidf_(sm.ab[tid][0]));
+        sm.g[tid] = A * softplusf_(sm.ab[tid][1] + dtb);
+      }
+      if (spec && t0 == 0) write_hist_rows(0, K - 1 + nt);
+      __syncthreads();
+      for (int vidx = warp; vidx < 2 * nt; vidx += NT / 32) {
+        const int t = vidx >> 1;
+        if (vidx & 1) warp_l2norm<T, DK>(sm.k[t], 1.0f, lane);
+        else warp_l2norm<T, DK>(sm.q[t], qscale, lane);
+      }
+      __syncthreads();
+      // 6. recurrence + readout; pending (k, v, g, β) for the next call's replay
+      for (int t = 0; t < nt; ++t) {
+        gdn_update<RPT>(S, sm.k[t], sm.v[t], sm.g[t], sm.beta[t], rg, cg);
+        const float4 o = gdn_readout<RPT>(S, sm.q[t], rg);
+        if (rg == 0) *reinterpret_cast<float4*>(&sm.o[t][4 * cg]) = o;
+      }
+      if (spec) {
+        for (int e = tid; e < nt * (PS / 4); e += NT) {
+          const int t = e / (PS / 4), c4 = (e % (PS / 4)) * 4;
+          float vv[4];
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4) {
+            const int c = c4 + q4;
+            vv[q4] = c < DK ? sm.k[t][c]
+                            : (c < DK + DV ? sm.v[t][c - DK]
+                                           : (c == DK + DV ? sm.g[t] : (c == DK + DV + 1 ? sm.beta[t] : 0.f)));
+          }
+          *reinterpret_cast<float4*>(pend + (int64_t)(t0 + t) * PS + c4) = make_float4(vv[0], vv[1], vv[2], vv[3]);
         }
-        *reinterpret_cast<float4*>(pend + (int64_t)(t0 + t) * PS + c4) = make_float4(vv[0], vv[1], vv[2], vv[3]);
       }
-    }
-    __syncthreads();
-    // 6. RMSNormGated over dv per token: w·round(x̂) · silu(z), x = round(core)
-    for (int t = warp; t < nt; t += NT / 32) {
-      float ss = 0.f;
-      for (int c = lane; c < DV; c += 32) {
-        const float x = dt<T>::round(sm.o[t][c]);
-        ss = fmaf(x, x, ss);
-      }
-      ss = warp_sum(ss);
-      const float inv = rsqrtf(ss / (float)DV + L.eps);
-      T* orow = out + (int64_t)(b * T_ + t0 + t) * L.ld_out + h * DV;
-      for (int c = lane; c < DV; c += 32) {
-        const float xh = dt<T>::round(dt<T>::round(sm.o[t][c]) * inv);
-        const float wx = dt<T>::round(dt<T>::to_f(normw[c]) * xh);
-        orow[c] = dt<T>::from_f(wx * siluf_(sm.z[t][c]));
-      }
-    }
-    const bool last = t0 + nt >= T_;
-    if (last) {
-      if (!spec) write_hist_rows(nt, K - 1);   // the window after the last token
-    } else {
-      // slide the window (last K-1 combined rows to the front) and load the next block
-      // (source and destination rows may overlap: read everything, barrier, then write)
-      constexpr int SLIDE = ((GDN_KMAX - 1) * NCH + NT - 1) / NT;
-      float keep[SLIDE];
       __syncthreads();
+      // 7. RMSNormGated over dv per token: w·round(x̂) · silu(z), x = round(core)
+      for (int t = warp; t < nt; t += NT / 32) {
+        float ss = 0.f;
+        for (int c = lane; c < DV; c += 32) {
+          const float x = dt<T>::round(sm.o[t][c]);
+          ss = fmaf(x, x, ss);
+        }
+        ss = warp_sum(ss);
+        const float inv = rsqrtf(ss / (float)DV + L.eps);
+        T* orow = out + (int64_t)(b * T_ + t0 + t) * L.ld_out + h * DV;
+        for (int c = lane; c < DV; c += 32) {
+          const float xh = dt<T>::round(dt<T>::round(sm.o[t][c]) * inv);
+          const float wx = dt<T>::round(dt<T>::to_f(normw[c]) * xh);
+          orow[c] = dt<T>::from_f(wx * siluf_(sm.z[t][c]));
+        }
+      }
+      const bool last = t0 + nt >= T_;
+      if (last) {
+        if (!spec) write_hist_rows(nt, K - 1);   // the window after the last token
+      } else {
+        // slide the window (last K-1 combined rows to the front) and load the next block;
+        // source and destination rows may overlap: read everything, barrier, then write
+        constexpr int SLIDE = ((GDN_KMAX - 1) * NCH + NT - 1) / NT;
+        float keep[SLIDE];
+        __syncthreads();
 #pragma unroll
-      for (int u = 0; u < SLIDE; ++u) {
-        const int e = tid + u * NT;
-        keep[u] = e < (K - 1) * NCH ? sm.xin[nt + e / NCH][e % NCH] : 0.f;
-      }
-      __syncthreads();
+        for (int q4 = 0; q4 < SLIDE; ++q4) {
+          const int e = tid + q4 * NT;
+          keep[q4] = e < (K - 1) * NCH ? sm.xin[nt + e / NCH][e % NCH] : 0.f;
+        }
+        __syncthreads();
 #pragma unroll
-      for (int u = 0; u < SLIDE; ++u) {
-        const int e = tid + u * NT;
-        if (e < (K - 1) * NCH) sm.xin[e / NCH][e % NCH] = keep[u];
+        for (int q4 = 0; q4 < SLIDE; ++q4) {
+          const int e = tid + q4 * NT;
+          if (e < (K - 1) * NCH) sm.xin[e / NCH][e % NCH] = keep[q4];
+        }
+        __syncthreads();
+        load_tokens(t0 + nt, min(GDN_TB, T_ - t0 - nt), K - 1);
       }
-      __syncthreads();
-      load_tokens(t0 + nt, min(GDN_TB, T_ - t0 - nt), K - 1);
     }
-  }
 
-  if (!spec) {
+    if (!spec) {
 #pragma unroll
-    for (int i = 0; i < RPT; ++i)
-      *reinterpret_cast<float4*>(state + (int64_t)(4 * i + rg) * DV + 4 * cg) = S[i];
+      for (int i = 0; i < RPT; ++i)
+        *reinterpret_cast<float4*>(state + (int64_t)(4 * i + rg) * DV + 4 * cg) = S[i];
+    }
+    __syncthreads();   // next unit's loads overwrite the staged inputs
   }
+}
+
+static int sm_count_gdn() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+template <typename T, int DK, int DV>
+static int launch_gdn_dims(const qsp_gdn_layer& L, cudaStream_t st) {
+  auto kern = gdn_verify_kernel<T, DK, DV>;
+  const size_t smem = sizeof(GdnSmem<DK, DV>);
+  static bool set = false;
+  if (!set) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+      return set_error(QSP_ERR_CUDA, "qsp_gdn_verify: cannot reserve %zu bytes of shared memory", smem);
+    set = true;
+  }
+  const int units = L.batch * L.n_v_heads;
+  const int grid = std::min(units, 2 * sm_count_gdn());
+  kern<<<grid, DV, smem, st>>>(L);
+  return check_launch("qsp_gdn_verify");
 }
 
 template <typename T>
 static int launch_gdn(const qsp_gdn_layer& L, cudaStream_t st) {
-  dim3 grid(L.n_v_heads, L.batch);
-#define QSP_GDN_CASE(DKV)                                                    \
-  if (L.head_k == DKV && L.head_v == DKV) {                                  \
-    gdn_verify_kernel<T, DKV, DKV><<<grid, DKV, 0, st>>>(L);                 \
-    return check_launch("qsp_gdn_verify");                                   \
+  if (L.head_k == 32 && L.head_v == 32) return launch_gdn_dims<T, 32, 32>(L, st);
+  if (L.head_k == 64 && L.head_v == 64) return launch_gdn_dims<T, 64, 64>(L, st);
+  if (L.head_k == 128 && L.head_v == 128) return launch_gdn_dims<T, 128, 128>(L, st);
+  return set_error(QSP_ERR_UNSUPPORTED, "qsp_gdn_verify: head dims %d/%d not built", L.head_k, L.head_v);
+}
+
+int gdn_device_error(int reset) {
+  int v = 0;
+  cudaMemcpyFromSymbol(&v, g_gdn_error, sizeof(int));
+  if (reset && v) {
+    const int z = 0;
+    cudaMemcpyToSymbol(g_gdn_error, &z, sizeof(int));
   }
-  QSP_GDN_CASE(32)
-  QSP_GDN_CASE(64)
-  QSP_GDN_CASE(128)
-#undef QSP_GDN_CASE
-  return set_error(QSP_ERR_UNSUPPORTED, "qsp_gdn_verify: head dims %d/%d not built", L.head_k,
-                   L.head_v);
+  return v;
 }
 
 }  // namespace qsp
