@@ -114,26 +114,32 @@ __device__ __forceinline__ void load16_as_float(const T* src, float* dst) {
   }
 }
 
-template <int DK, int DV>
+template <typename T, int DK, int DV>
 struct __align__(128) GdnSmem {
   static constexpr int NCH = 2 * DK + DV;   // q, k, v conv channels of one value head
+  static constexpr int PS = DK + DV + 4;    // pending row: k | v | g | beta | pad
   float sst[DK * DV];                       // next head's state (TMA bulk prefetch target)
-  float xin[GDN_KMAX - 1 + GDN_TB][NCH];    // conv inputs: window rows, then this block's tokens
-  float cw[GDN_KMAX][NCH];                  // conv weights, tap-major
+  T xr[GDN_KMAX - 1 + GDN_TB][NCH];         // raw conv inputs: window rows, then tokens
+  T zr[GDN_TB][DV];                         // raw output gate z
+  T cwr[NCH][GDN_KMAX];                     // conv weights of this head's channels
+  float pr[GDN_TB][PS];                     // pending rows to replay
   float q[GDN_TB][DK];
   float k[GDN_TB][DK];
   float v[GDN_TB][DV];
-  float z[GDN_TB][DV];
   float o[GDN_TB][DV];
   float g[GDN_TB];
   float beta[GDN_TB];
-  float ab[GDN_TB][2];                      // raw a, b of this head
+  float ab[GDN_TB][2];                      // a, b of this head
   uint64_t bar;                             // state prefetch barrier
 };
 
 __device__ int g_gdn_error = 0;
 
 __device__ __forceinline__ uint32_t gsm(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+
+__device__ __forceinline__ void gcp16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(gsm(dst)), "l"(src) : "memory");
+}
 
 __device__ __forceinline__ bool gdn_wait(uint64_t* bar, uint32_t parity) {
   for (uint32_t i = 0; i < (1u << 24); ++i) {
@@ -160,17 +166,20 @@ __device__ __forceinline__ void gdn_prefetch_state(float* dst, const float* src,
 
 // Persistent: CTA c handles (sequence, value head) units c, c+G, c+2G, ... . While a unit is
 // computed from registers, the next unit's state streams into shared memory, so the HBM
-// traffic of the recurrence (one state read and one write per head) overlaps the math.
+// traffic of the recurrence (one state read and one write per head) overlaps the math. A
+// unit's small inputs (conv window, token rows, z, weights, pending rows) are staged with
+// cp.async (all in flight at once, raw in shared memory).
 template <typename T, int DK, int DV>
 __global__ void __launch_bounds__(DV, 2)
 gdn_verify_kernel(const qsp_gdn_layer L) {
+  using SMT = GdnSmem<T, DK, DV>;
   constexpr int RPT = DK / 4;
   constexpr int NT = DV;
-  constexpr int NCH = GdnSmem<DK, DV>::NCH;
+  constexpr int NCH = SMT::NCH;
+  constexpr int PS = SMT::PS;
   constexpr int EPV = 16 / (int)sizeof(T);   // elements per 16-byte vector
-  constexpr int PS = DK + DV + 4;            // pending row: k | v | g | beta | pad (16-byte rows)
   extern __shared__ __align__(128) uint8_t gdn_smem_raw[];
-  GdnSmem<DK, DV>& sm = *reinterpret_cast<GdnSmem<DK, DV>*>(gdn_smem_raw);
+  SMT& sm = *reinterpret_cast<SMT*>(gdn_smem_raw);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int cg = warp * 8 + (lane & 7), rg = lane >> 3;
@@ -179,6 +188,7 @@ gdn_verify_kernel(const qsp_gdn_layer L) {
   const int key_dim = Hk * DK, conv_dim = 2 * key_dim + Hv * DV, value_dim = Hv * DV;
   const bool spec = L.speculative != 0;
   const T* proj = static_cast<const T*>(L.proj);
+  const T* cw = static_cast<const T*>(L.conv_w);
   T* hist = static_cast<T*>(L.conv_hist);
   T* out = static_cast<T*>(L.out);
   const int par = L.parity[0];
@@ -195,7 +205,6 @@ gdn_verify_kernel(const qsp_gdn_layer L) {
   __syncthreads();
   if (tid == 0 && blockIdx.x < units)
     gdn_prefetch_state(sm.sst, L.state + (int64_t)blockIdx.x * DK * DV, &sm.bar, SBYTES);
-  // conv weights are shared by every unit of a head; loaded per unit (head changes)
 
   uint32_t it = 0;
   for (int u = blockIdx.x; u < units; u += gridDim.x, ++it) {
@@ -208,63 +217,49 @@ gdn_verify_kernel(const qsp_gdn_layer L) {
     T* hist_out = hist + ((int64_t)(par ^ 1) * L.batch + b) * hist_rows * conv_dim;
     float* pend = L.pending + (((int64_t)b * Hv + h) * Ts) * PS;
     float* state = L.state + ((int64_t)b * Hv + h) * DK * DV;
-    auto gch = [&](int c) -> int {
-      return c < DK ? kh * DK + c : (c < 2 * DK ? key_dim + kh * DK + (c - DK) : 2 * key_dim + h * DV + (c - 2 * DK));
-    };
+    // global channel of local conv channel c (q | k | v segments of this head)
+    const int seg0 = kh * DK, seg1 = key_dim + kh * DK - DK, seg2 = 2 * key_dim + h * DV - 2 * DK;
+    auto gch = [&](int c) -> int { return c + (c < DK ? seg0 : (c < 2 * DK ? seg1 : seg2)); };
 
-    // 1. this unit's small inputs → shared memory (vectorised, all independent)
-    for (int e = tid; e < R * (PS / 4); e += NT) {
-      const int j = e / (PS / 4), c4 = (e % (PS / 4)) * 4;
-      const float4 v4 = *reinterpret_cast<const float4*>(pend + (int64_t)j * PS + c4);
-      const float vv[4] = {v4.x, v4.y, v4.z, v4.w};
-#pragma unroll
-      for (int q4 = 0; q4 < 4; ++q4) {
-        const int c = c4 + q4;
-        if (c < DK) sm.k[j][c] = vv[q4];
-        else if (c < DK + DV) sm.v[j][c - DK] = vv[q4];
-        else if (c == DK + DV) sm.g[j] = vv[q4];
-        else if (c == DK + DV + 1) sm.beta[j] = vv[q4];
-      }
+    // 1. stage this unit's inputs (cp.async: every copy in flight at once)
+    for (int e = tid; e < R * (PS / 4); e += NT) gcp16(&sm.pr[0][0] + e * 4, pend + e * 4);
+    for (int e = tid; e < NCH * GDN_KMAX * (int)sizeof(T) / 16 && K == GDN_KMAX; e += NT) {
+      const int c = (e * 16 / (int)sizeof(T)) / GDN_KMAX;   // first channel of this 16-byte chunk
+      const int within = (e * 16 / (int)sizeof(T)) % GDN_KMAX;
+      gcp16(&sm.cwr[c][within], cw + (int64_t)gch(c) * GDN_KMAX + within);
     }
-    {
-      const T* cw = static_cast<const T*>(L.conv_w);
-      for (int e = tid; e < NCH * K; e += NT) {
-        const int c = e / K, j = e % K;
-        sm.cw[j][c] = dt<T>::to_f(cw[(int64_t)gch(c) * K + j]);
-      }
+    if (K != GDN_KMAX) {   // narrower conv kernels: element loads
+      for (int e = tid; e < NCH * K; e += NT) sm.cwr[e / K][e % K] = cw[(int64_t)gch(e / K) * K + e % K];
     }
-    auto load_tokens = [&](int t0, int nt, int row_base) {
-      for (int e = tid; e < nt * (NCH / EPV); e += NT) {
-        const int t = e / (NCH / EPV), c = (e % (NCH / EPV)) * EPV;
-        load16_as_float<T>(proj + (int64_t)(b * T_ + t0 + t) * L.ld_proj + gch(c), &sm.xin[row_base + t][c]);
-      }
-      for (int e = tid; e < nt * (DV / EPV); e += NT) {
-        const int t = e / (DV / EPV), c = (e % (DV / EPV)) * EPV;
-        load16_as_float<T>(proj + (int64_t)(b * T_ + t0 + t) * L.ld_proj + conv_dim + h * DV + c, &sm.z[t][c]);
+    auto stage_tokens = [&](int t0, int nt) {
+      for (int t = 0; t < nt; ++t) {
+        const T* prow = proj + (int64_t)(b * T_ + t0 + t) * L.ld_proj;
+        for (int c = tid * EPV; c < NCH; c += NT * EPV) gcp16(&sm.xr[K - 1 + t][c], prow + gch(c));
+        for (int c = tid * EPV; c < DV; c += NT * EPV) gcp16(&sm.zr[t][c], prow + conv_dim + h * DV + c);
       }
       if (tid < 2 * nt) {
         const int t = tid >> 1, w = tid & 1;   // w = 0: b, 1: a
         sm.ab[t][w] = dt<T>::to_f(proj[(int64_t)(b * T_ + t0 + t) * L.ld_proj + conv_dim + value_dim + w * Hv + h]);
       }
     };
-    for (int e = tid; e < (K - 1) * (NCH / EPV); e += NT) {
-      const int i = e / (NCH / EPV), c = (e % (NCH / EPV)) * EPV;
-      load16_as_float<T>(hist_in + (int64_t)(coff + i) * conv_dim + gch(c), &sm.xin[i][c]);
-    }
-    load_tokens(0, min(GDN_TB, T_), K - 1);
+    for (int i = 0; i < K - 1; ++i)
+      for (int c = tid * EPV; c < NCH; c += NT * EPV) gcp16(&sm.xr[i][c], hist_in + (int64_t)(coff + i) * conv_dim + gch(c));
+    stage_tokens(0, min(GDN_TB, T_));
+    asm volatile("cp.async.commit_group;" ::: "memory");
 
     // 2. this unit's state: prefetched into shared memory → registers
     gdn_wait(&sm.bar, it & 1u);
     float4 S[RPT];
 #pragma unroll
     for (int i = 0; i < RPT; ++i) S[i] = *reinterpret_cast<const float4*>(&sm.sst[(4 * i + rg) * DV + 4 * cg]);
+    asm volatile("cp.async.wait_all;" ::: "memory");
     __syncthreads();   // inputs staged; every thread holds its state slice
     // 3. prefetch the next unit's state while this one computes
     if (tid == 0 && u + (int)gridDim.x < units)
       gdn_prefetch_state(sm.sst, L.state + (int64_t)(u + gridDim.x) * DK * DV, &sm.bar, SBYTES);
 
     // 4. replay the kept tokens of the previous speculative call
-    for (int j = 0; j < R; ++j) gdn_update<RPT>(S, sm.k[j], sm.v[j], sm.g[j], sm.beta[j], rg, cg);
+    for (int j = 0; j < R; ++j) gdn_update<RPT>(S, &sm.pr[j][0], &sm.pr[j][DK], sm.pr[j][DK + DV], sm.pr[j][DK + DV + 1], rg, cg);
     if (R > 0 && spec) {
 #pragma unroll
       for (int i = 0; i < RPT; ++i)
@@ -273,13 +268,12 @@ gdn_verify_kernel(const qsp_gdn_layer L) {
 
     // conv-history ownership: every head writes its v channels; the first v head of a k-head
     // group also writes that group's q and k channels
-    const bool own_qk = (h % vpk) == 0;
+    const int c_first = ((h % vpk) == 0) ? 0 : 2 * DK;
     auto write_hist_rows = [&](int src_row0, int n_rows) {
-      for (int e = tid; e < n_rows * NCH; e += NT) {
-        const int i = e / NCH, c = e % NCH;
-        if (c < 2 * DK && !own_qk) continue;
-        hist_out[(int64_t)i * conv_dim + gch(c)] = dt<T>::from_f(sm.xin[src_row0 + i][c]);
-      }
+      for (int i = 0; i < n_rows; ++i)
+        for (int c = c_first + tid * EPV; c < NCH; c += NT * EPV)
+          *reinterpret_cast<uint4*>(hist_out + (int64_t)i * conv_dim + gch(c)) =
+              *reinterpret_cast<const uint4*>(&sm.xr[src_row0 + i][c]);
     };
     if (T_ == 0) write_hist_rows(0, K - 1);
 
@@ -288,16 +282,19 @@ gdn_verify_kernel(const qsp_gdn_layer L) {
 
     for (int t0 = 0; t0 < T_; t0 += GDN_TB) {
       const int nt = min(GDN_TB, T_ - t0);
-      __syncthreads();   // replay / previous block done with the k, v, q, o arrays
       // 5. conv + SiLU (fp32 accumulate, rounded like F.conv1d then F.silu), gates
-      for (int e = tid; e < nt * NCH; e += NT) {
-        const int t = e / NCH, c = e % NCH;
-        float acc = 0.f;
-        for (int j = 0; j < K; ++j) acc = fmaf(sm.cw[j][c], sm.xin[t + j][c], acc);
-        const float a = dt<T>::round(siluf_(dt<T>::round(acc)));
-        if (c < DK) sm.q[t][c] = a;
-        else if (c < 2 * DK) sm.k[t][c - DK] = a;
-        else sm.v[t][c - 2 * DK] = a;
+      for (int c = tid; c < NCH; c += NT) {
+        float w[GDN_KMAX];
+#pragma unroll
+        for (int j = 0; j < GDN_KMAX; ++j) w[j] = j < K ? dt<T>::to_f(sm.cwr[c][j]) : 0.f;
+        for (int t = 0; t < nt; ++t) {
+          float acc = 0.f;
+          for (int j = 0; j < K; ++j) acc = fmaf(w[j], dt<T>::to_f(sm.xr[t + j][c]), acc);
+          const float a = dt<T>::round(siluf_(dt<T>::round(acc)));
+          if (c < DK) sm.q[t][c] = a;
+          else if (c < 2 * DK) sm.k[t][c - DK] = a;
+          else sm.v[t][c - 2 * DK] = a;
+        }
       }
       if (tid < nt) {
         sm.beta[tid] = dt<T>::round(sigmoidf_(sm.ab[tid][0]));
@@ -318,17 +315,15 @@ gdn_verify_kernel(const qsp_gdn_layer L) {
         if (rg == 0) *reinterpret_cast<float4*>(&sm.o[t][4 * cg]) = o;
       }
       if (spec) {
-        for (int e = tid; e < nt * (PS / 4); e += NT) {
-          const int t = e / (PS / 4), c4 = (e % (PS / 4)) * 4;
-          float vv[4];
-#pragma unroll
-          for (int q4 = 0; q4 < 4; ++q4) {
-            const int c = c4 + q4;
-            vv[q4] = c < DK ? sm.k[t][c]
-                            : (c < DK + DV ? sm.v[t][c - DK]
-                                           : (c == DK + DV ? sm.g[t] : (c == DK + DV + 1 ? sm.beta[t] : 0.f)));
+        for (int t = 0; t < nt; ++t) {
+          float* prow = pend + (int64_t)(t0 + t) * PS;
+          for (int c4 = tid * 4; c4 < PS; c4 += NT * 4) {
+            float4 v4;
+            if (c4 < DK) v4 = *reinterpret_cast<const float4*>(&sm.k[t][c4]);
+            else if (c4 < DK + DV) v4 = *reinterpret_cast<const float4*>(&sm.v[t][c4 - DK]);
+            else v4 = make_float4(sm.g[t], sm.beta[t], 0.f, 0.f);
+            *reinterpret_cast<float4*>(prow + c4) = v4;
           }
-          *reinterpret_cast<float4*>(pend + (int64_t)(t0 + t) * PS + c4) = make_float4(vv[0], vv[1], vv[2], vv[3]);
         }
       }
       __syncthreads();
@@ -345,31 +340,33 @@ gdn_verify_kernel(const qsp_gdn_layer L) {
         for (int c = lane; c < DV; c += 32) {
           const float xh = dt<T>::round(dt<T>::round(sm.o[t][c]) * inv);
           const float wx = dt<T>::round(dt<T>::to_f(normw[c]) * xh);
-          orow[c] = dt<T>::from_f(wx * siluf_(sm.z[t][c]));
+          orow[c] = dt<T>::from_f(wx * siluf_(dt<T>::to_f(sm.zr[t][c])));
         }
       }
       const bool last = t0 + nt >= T_;
       if (last) {
         if (!spec) write_hist_rows(nt, K - 1);   // the window after the last token
       } else {
-        // slide the window (last K-1 combined rows to the front) and load the next block;
+        // slide the window (last K-1 combined rows to the front) and stage the next block;
         // source and destination rows may overlap: read everything, barrier, then write
         constexpr int SLIDE = ((GDN_KMAX - 1) * NCH + NT - 1) / NT;
-        float keep[SLIDE];
+        T keep[SLIDE];
         __syncthreads();
 #pragma unroll
         for (int q4 = 0; q4 < SLIDE; ++q4) {
           const int e = tid + q4 * NT;
-          keep[q4] = e < (K - 1) * NCH ? sm.xin[nt + e / NCH][e % NCH] : 0.f;
+          keep[q4] = e < (K - 1) * NCH ? sm.xr[nt + e / NCH][e % NCH] : T{};
         }
         __syncthreads();
 #pragma unroll
         for (int q4 = 0; q4 < SLIDE; ++q4) {
           const int e = tid + q4 * NT;
-          if (e < (K - 1) * NCH) sm.xin[e / NCH][e % NCH] = keep[q4];
+          if (e < (K - 1) * NCH) sm.xr[e / NCH][e % NCH] = keep[q4];
         }
+        stage_tokens(t0 + nt, min(GDN_TB, T_ - t0 - nt));
+        asm volatile("cp.async.commit_group;" ::: "memory");
+        asm volatile("cp.async.wait_all;" ::: "memory");
         __syncthreads();
-        load_tokens(t0 + nt, min(GDN_TB, T_ - t0 - nt), K - 1);
       }
     }
 
@@ -378,7 +375,7 @@ gdn_verify_kernel(const qsp_gdn_layer L) {
       for (int i = 0; i < RPT; ++i)
         *reinterpret_cast<float4*>(state + (int64_t)(4 * i + rg) * DV + 4 * cg) = S[i];
     }
-    __syncthreads();   // next unit's loads overwrite the staged inputs
+    __syncthreads();   // the next unit's staging overwrites the inputs
   }
 }
 
@@ -396,7 +393,7 @@ static int sm_count_gdn() {
 template <typename T, int DK, int DV>
 static int launch_gdn_dims(const qsp_gdn_layer& L, cudaStream_t st) {
   auto kern = gdn_verify_kernel<T, DK, DV>;
-  const size_t smem = sizeof(GdnSmem<DK, DV>);
+  const size_t smem = sizeof(GdnSmem<T, DK, DV>);
   static bool set = false;
   if (!set) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
