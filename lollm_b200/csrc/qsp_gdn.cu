@@ -18,83 +18,103 @@ constexpr int GDN_TB = 8;    // tokens per block (a whole verify step)
 constexpr int GDN_KMAX = 4;  // largest conv kernel
 
 
-// One state update S ← S·e^g; δ = (v − Sᵀk)·β; S ← S + k δᵀ. Explicit _rn intrinsics keep
-// the arithmetic identical wherever it is inlined (the replay of kept tokens must reproduce
+// Packed fp32x2 helpers (sm_100): each lane rounds exactly like the scalar instruction.
+__device__ __forceinline__ uint64_t pk2(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ float2 upk2(uint64_t r) {
+  float2 v;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(v.x), "=f"(v.y) : "l"(r));
+  return v;
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t fmul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float2 shfl_add2(float2 v, int o) {
+  v.x = __fadd_rn(v.x, __shfl_xor_sync(0xffffffffu, v.x, o));
+  v.y = __fadd_rn(v.y, __shfl_xor_sync(0xffffffffu, v.y, o));
+  return v;
+}
+
+// One state update S ← S·e^g; δ = (v − Sᵀk)·β; S ← S + k δᵀ, on packed column pairs. The
+// thread's state is S2[2i] = columns (4cg, 4cg+1), S2[2i+1] = (4cg+2, 4cg+3) of row 4i+rg.
+// kd holds k duplicated as (k, k) pairs. Every operation is an explicitly rounded IEEE op, so
+// the arithmetic is identical wherever this is inlined (the replay of kept tokens reproduces
 // the original forward bit for bit).
 template <int RPT>
-__device__ __forceinline__ void gdn_update(float4 (&S)[RPT], const float* __restrict__ kvec,
-                                           const float* __restrict__ vvec, float g, float beta,
-                                           int rg, int cg) {
+__device__ __forceinline__ void gdn_update(uint64_t (&S2)[2 * RPT], const float2* __restrict__ kd,
+                                           const float* __restrict__ vvec, float g, float beta, int rg, int cg) {
   const float d = expf(g);
-  float4 kv = make_float4(0.f, 0.f, 0.f, 0.f);
+  const uint64_t dd = pk2(d, d);
+  uint64_t a0 = 0, a1 = 0;   // (0.f, 0.f)
 #pragma unroll
   for (int i = 0; i < RPT; ++i) {
-    const float kr = kvec[4 * i + rg];
-    S[i].x = __fmul_rn(S[i].x, d);
-    S[i].y = __fmul_rn(S[i].y, d);
-    S[i].z = __fmul_rn(S[i].z, d);
-    S[i].w = __fmul_rn(S[i].w, d);
-    kv.x = __fmaf_rn(S[i].x, kr, kv.x);
-    kv.y = __fmaf_rn(S[i].y, kr, kv.y);
-    kv.z = __fmaf_rn(S[i].z, kr, kv.z);
-    kv.w = __fmaf_rn(S[i].w, kr, kv.w);
+    const float2 kr = kd[4 * i + rg];
+    const uint64_t kk = *reinterpret_cast<const uint64_t*>(&kr);
+    S2[2 * i] = fmul2(S2[2 * i], dd);
+    S2[2 * i + 1] = fmul2(S2[2 * i + 1], dd);
+    a0 = ffma2(S2[2 * i], kk, a0);
+    a1 = ffma2(S2[2 * i + 1], kk, a1);
   }
-#pragma unroll
-  for (int o = 8; o <= 16; o <<= 1) {
-    kv.x = __fadd_rn(kv.x, __shfl_xor_sync(0xffffffffu, kv.x, o));
-    kv.y = __fadd_rn(kv.y, __shfl_xor_sync(0xffffffffu, kv.y, o));
-    kv.z = __fadd_rn(kv.z, __shfl_xor_sync(0xffffffffu, kv.z, o));
-    kv.w = __fadd_rn(kv.w, __shfl_xor_sync(0xffffffffu, kv.w, o));
-  }
+  float2 kv0 = upk2(a0), kv1 = upk2(a1);
+  kv0 = shfl_add2(kv0, 8);
+  kv1 = shfl_add2(kv1, 8);
+  kv0 = shfl_add2(kv0, 16);
+  kv1 = shfl_add2(kv1, 16);
   const float4 vv = *reinterpret_cast<const float4*>(vvec + 4 * cg);
-  float4 dl;
-  dl.x = __fmul_rn(__fsub_rn(vv.x, kv.x), beta);
-  dl.y = __fmul_rn(__fsub_rn(vv.y, kv.y), beta);
-  dl.z = __fmul_rn(__fsub_rn(vv.z, kv.z), beta);
-  dl.w = __fmul_rn(__fsub_rn(vv.w, kv.w), beta);
+  const uint64_t dl0 = pk2(__fmul_rn(__fsub_rn(vv.x, kv0.x), beta), __fmul_rn(__fsub_rn(vv.y, kv0.y), beta));
+  const uint64_t dl1 = pk2(__fmul_rn(__fsub_rn(vv.z, kv1.x), beta), __fmul_rn(__fsub_rn(vv.w, kv1.y), beta));
 #pragma unroll
   for (int i = 0; i < RPT; ++i) {
-    const float kr = kvec[4 * i + rg];
-    S[i].x = __fmaf_rn(kr, dl.x, S[i].x);
-    S[i].y = __fmaf_rn(kr, dl.y, S[i].y);
-    S[i].z = __fmaf_rn(kr, dl.z, S[i].z);
-    S[i].w = __fmaf_rn(kr, dl.w, S[i].w);
+    const float2 kr = kd[4 * i + rg];
+    const uint64_t kk = *reinterpret_cast<const uint64_t*>(&kr);
+    S2[2 * i] = ffma2(kk, dl0, S2[2 * i]);
+    S2[2 * i + 1] = ffma2(kk, dl1, S2[2 * i + 1]);
   }
 }
 
+// o = Sᵀq for the thread's 4 columns (q duplicated as (q, q) pairs in qd).
 template <int RPT>
-__device__ __forceinline__ float4 gdn_readout(const float4 (&S)[RPT], const float* __restrict__ qvec,
-                                              int rg) {
-  float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+__device__ __forceinline__ float4 gdn_readout(const uint64_t (&S2)[2 * RPT], const float2* __restrict__ qd, int rg) {
+  uint64_t a0 = 0, a1 = 0;
 #pragma unroll
   for (int i = 0; i < RPT; ++i) {
-    const float qr = qvec[4 * i + rg];
-    o.x = __fmaf_rn(S[i].x, qr, o.x);
-    o.y = __fmaf_rn(S[i].y, qr, o.y);
-    o.z = __fmaf_rn(S[i].z, qr, o.z);
-    o.w = __fmaf_rn(S[i].w, qr, o.w);
+    const float2 qr = qd[4 * i + rg];
+    const uint64_t qq = *reinterpret_cast<const uint64_t*>(&qr);
+    a0 = ffma2(S2[2 * i], qq, a0);
+    a1 = ffma2(S2[2 * i + 1], qq, a1);
   }
-#pragma unroll
-  for (int s = 8; s <= 16; s <<= 1) {
-    o.x = __fadd_rn(o.x, __shfl_xor_sync(0xffffffffu, o.x, s));
-    o.y = __fadd_rn(o.y, __shfl_xor_sync(0xffffffffu, o.y, s));
-    o.z = __fadd_rn(o.z, __shfl_xor_sync(0xffffffffu, o.z, s));
-    o.w = __fadd_rn(o.w, __shfl_xor_sync(0xffffffffu, o.w, s));
-  }
-  return o;
+  float2 o0 = upk2(a0), o1 = upk2(a1);
+  o0 = shfl_add2(o0, 8);
+  o1 = shfl_add2(o1, 8);
+  o0 = shfl_add2(o0, 16);
+  o1 = shfl_add2(o1, 16);
+  return make_float4(o0.x, o0.y, o1.x, o1.y);
 }
 
 // l2norm in the reference's arithmetic: x·rsqrt(Σx² + 1e-6) evaluated in the model dtype
 // (each op rounded for bf16; plain fp32 otherwise). `x` is DK floats in shared memory,
 // normalised in place by one warp.
 template <typename T, int DK>
-__device__ __forceinline__ void warp_l2norm(float* x, float post_scale, int lane) {
+__device__ __forceinline__ void warp_l2norm(float2* x, float post_scale, int lane) {
   float ss = 0.f;
-  for (int i = lane; i < DK; i += 32) ss += dt<T>::round(x[i] * x[i]);
+  for (int i = lane; i < DK; i += 32) ss += dt<T>::round(x[i].x * x[i].x);
   ss = warp_sum(ss);
   const float s = dt<T>::round(dt<T>::round(ss) + 1e-6f);
   const float r = dt<T>::round(rsqrtf(s));
-  for (int i = lane; i < DK; i += 32) x[i] = dt<T>::round(x[i] * r) * post_scale;
+  for (int i = lane; i < DK; i += 32) {
+    const float y = dt<T>::round(x[i].x * r) * post_scale;
+    x[i] = make_float2(y, y);
+  }
 }
 
 // 16-byte vector of T converted to floats
@@ -123,8 +143,8 @@ struct __align__(128) GdnSmem {
   T zr[GDN_TB][DV];                         // raw output gate z
   T cwr[NCH][GDN_KMAX];                     // conv weights of this head's channels
   float pr[GDN_TB][PS];                     // pending rows to replay
-  float q[GDN_TB][DK];
-  float k[GDN_TB][DK];
+  float2 q[GDN_TB][DK];                     // q, k duplicated as (x, x) pairs (packed FMA operands)
+  float2 k[GDN_TB][DK];
   float v[GDN_TB][DV];
   float o[GDN_TB][DV];
   float g[GDN_TB];
@@ -249,22 +269,34 @@ gdn_verify_kernel(const qsp_gdn_layer L) {
 
     // 2. this unit's state: prefetched into shared memory → registers
     gdn_wait(&sm.bar, it & 1u);
-    float4 S[RPT];
+    uint64_t S[2 * RPT];
 #pragma unroll
-    for (int i = 0; i < RPT; ++i) S[i] = *reinterpret_cast<const float4*>(&sm.sst[(4 * i + rg) * DV + 4 * cg]);
+    for (int i = 0; i < RPT; ++i) {
+      const float4 v4 = *reinterpret_cast<const float4*>(&sm.sst[(4 * i + rg) * DV + 4 * cg]);
+      S[2 * i] = pk2(v4.x, v4.y);
+      S[2 * i + 1] = pk2(v4.z, v4.w);
+    }
     asm volatile("cp.async.wait_all;" ::: "memory");
     __syncthreads();   // inputs staged; every thread holds its state slice
+    for (int e = tid; e < R * DK; e += NT) {   // replay keys, duplicated into pairs
+      const float kv = sm.pr[e / DK][e % DK];
+      sm.k[e / DK][e % DK] = make_float2(kv, kv);
+    }
+    __syncthreads();
     // 3. prefetch the next unit's state while this one computes
     if (tid == 0 && u + (int)gridDim.x < units)
       gdn_prefetch_state(sm.sst, L.state + (int64_t)(u + gridDim.x) * DK * DV, &sm.bar, SBYTES);
 
     // 4. replay the kept tokens of the previous speculative call
-    for (int j = 0; j < R; ++j) gdn_update<RPT>(S, &sm.pr[j][0], &sm.pr[j][DK], sm.pr[j][DK + DV], sm.pr[j][DK + DV + 1], rg, cg);
-    if (R > 0 && spec) {
+    auto store_state = [&]() {
 #pragma unroll
-      for (int i = 0; i < RPT; ++i)
-        *reinterpret_cast<float4*>(state + (int64_t)(4 * i + rg) * DV + 4 * cg) = S[i];
-    }
+      for (int i = 0; i < RPT; ++i) {
+        const float2 lo = upk2(S[2 * i]), hi = upk2(S[2 * i + 1]);
+        *reinterpret_cast<float4*>(state + (int64_t)(4 * i + rg) * DV + 4 * cg) = make_float4(lo.x, lo.y, hi.x, hi.y);
+      }
+    };
+    for (int j = 0; j < R; ++j) gdn_update<RPT>(S, sm.k[j], &sm.pr[j][DK], sm.pr[j][DK + DV], sm.pr[j][DK + DV + 1], rg, cg);
+    if (R > 0 && spec) store_state();
 
     // conv-history ownership: every head writes its v channels; the first v head of a k-head
     // group also writes that group's q and k channels
@@ -282,6 +314,7 @@ gdn_verify_kernel(const qsp_gdn_layer L) {
 
     for (int t0 = 0; t0 < T_; t0 += GDN_TB) {
       const int nt = min(GDN_TB, T_ - t0);
+      __syncthreads();   // the replay is done with the k pairs
       // 5. conv + SiLU (fp32 accumulate, rounded like F.conv1d then F.silu), gates
       for (int c = tid; c < NCH; c += NT) {
         float w[GDN_KMAX];
@@ -291,8 +324,8 @@ gdn_verify_kernel(const qsp_gdn_layer L) {
           float acc = 0.f;
           for (int j = 0; j < K; ++j) acc = fmaf(w[j], dt<T>::to_f(sm.xr[t + j][c]), acc);
           const float a = dt<T>::round(siluf_(dt<T>::round(acc)));
-          if (c < DK) sm.q[t][c] = a;
-          else if (c < 2 * DK) sm.k[t][c - DK] = a;
+          if (c < DK) sm.q[t][c] = make_float2(a, a);
+          else if (c < 2 * DK) sm.k[t][c - DK] = make_float2(a, a);
           else sm.v[t][c - 2 * DK] = a;
         }
       }
@@ -319,7 +352,7 @@ gdn_verify_kernel(const qsp_gdn_layer L) {
           float* prow = pend + (int64_t)(t0 + t) * PS;
           for (int c4 = tid * 4; c4 < PS; c4 += NT * 4) {
             float4 v4;
-            if (c4 < DK) v4 = *reinterpret_cast<const float4*>(&sm.k[t][c4]);
+            if (c4 < DK) v4 = make_float4(sm.k[t][c4].x, sm.k[t][c4 + 1].x, sm.k[t][c4 + 2].x, sm.k[t][c4 + 3].x);
             else if (c4 < DK + DV) v4 = *reinterpret_cast<const float4*>(&sm.v[t][c4 - DK]);
             else v4 = make_float4(sm.g[t], sm.beta[t], 0.f, 0.f);
             *reinterpret_cast<float4*>(prow + c4) = v4;
@@ -370,11 +403,7 @@ gdn_verify_kernel(const qsp_gdn_layer L) {
       }
     }
 
-    if (!spec) {
-#pragma unroll
-      for (int i = 0; i < RPT; ++i)
-        *reinterpret_cast<float4*>(state + (int64_t)(4 * i + rg) * DV + 4 * cg) = S[i];
-    }
+    if (!spec) store_state();
     __syncthreads();   // the next unit's staging overwrites the inputs
   }
 }
