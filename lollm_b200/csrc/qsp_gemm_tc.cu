@@ -116,7 +116,9 @@ struct TcCfg {
   static constexpr int W_BYTES = TC_BN * TC_BK * 2;
   static constexpr int X_BYTES = MT * TC_BK * 2;
   static constexpr int STAGE_BYTES = W_BYTES + X_BYTES;
-  static constexpr int STAGES = (MT >= 256) ? 4 : (MT >= 128 ? 6 : 8);
+  // ring depth sized so two CTAs share an SM (~100 KB each): one CTA's pipeline fill and
+  // epilogue overlap the other's MMAs
+  static constexpr int STAGES = (100 * 1024) / STAGE_BYTES < 2 ? 2 : (100 * 1024) / STAGE_BYTES;
   static constexpr int TMEM_COLS = MT < 32 ? 32 : MT;
   static constexpr size_t SMEM = (size_t)STAGES * STAGE_BYTES + 1024 + 256;
 };
@@ -155,7 +157,7 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restr
 }
 
 template <int MT>
-__global__ void __launch_bounds__(TC_THREADS, 1)
+__global__ void __launch_bounds__(TC_THREADS, 2)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x, const TcArgs A) {
   using C = TcCfg<MT>;
   extern __shared__ uint8_t smem_raw[];
@@ -307,12 +309,14 @@ static TcPlan plan(int64_t m, int64_t n, int64_t k, int sm_count) {
   p.m_tiles = (int)((m + p.mt - 1) / p.mt);
   p.n_tiles = (int)((n + TC_BN - 1) / TC_BN);
   p.n_kb = (int)((k + TC_BK - 1) / TC_BK);
+  // two resident CTAs per SM: aim for ~2·SMs CTAs in one wave (K split when tiles are few)
   const int tiles = p.m_tiles * p.n_tiles;
+  const int target = 2 * sm_count;
   int splits = 1;
-  if (tiles < sm_count) {
-    splits = (sm_count + tiles - 1) / tiles;
+  if (tiles < target) {
+    splits = (target + tiles / 2) / tiles;
     splits = std::min(splits, std::max(1, p.n_kb / 4));
-    splits = std::min(splits, 16);
+    splits = std::max(1, std::min(splits, 16));
   }
   p.kb_per_split = (p.n_kb + splits - 1) / splits;
   p.splits = (p.n_kb + p.kb_per_split - 1) / p.kb_per_split;
