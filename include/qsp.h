@@ -70,6 +70,21 @@ int qsp_gemm(const void* a, int64_t lda, const void* w, int64_t ldw, void* c, in
              int64_t m, int64_t n, int64_t k, int dtype, int flags, void* workspace,
              size_t workspace_bytes, void* stream);
 
+/* x := x + round(a·wᵀ) (the residual add after o_proj / out_proj / down_proj), then
+ * y = RMSNorm(x)·(1+norm_w) (the next input_layernorm / post_attention_layernorm / final
+ * norm) — modeling_qwen3_5.py:59-60 + blocks.py:23-35. Split-K merges, the residual add and
+ * the norm run in one pass when the GEMM splits. */
+int qsp_gemm_residual_rmsnorm(const void* a, int64_t lda, const void* w, int64_t ldw, void* x,
+                              int64_t ldx, const void* norm_w, void* y, int64_t ldy, int64_t m,
+                              int64_t n, int64_t k, float eps, int dtype, void* workspace,
+                              size_t workspace_bytes, void* stream);
+
+/* act = silu(a·w_gateᵀ) ⊙ (a·w_upᵀ) with w_gu = [gate; up] (2·inter rows) — MLP
+ * (blocks.py:341-342). gu_tmp [m, 2·inter] holds the projection when the GEMM does not split. */
+int qsp_gemm_swiglu(const void* a, int64_t lda, const void* w_gu, int64_t ldw, void* act,
+                    int64_t ld_act, void* gu_tmp, int64_t ld_gu, int64_t m, int64_t inter,
+                    int64_t k, int dtype, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Workspace bytes qsp_gemm uses for this shape (0 when it never splits). */
 size_t qsp_gemm_workspace_bytes(int64_t m, int64_t n, int64_t k, int dtype);
 

@@ -55,6 +55,9 @@ SIGNATURES = {
     "qsp_swiglu": (C.c_int, [vp, i64, vp, i64, i64, i64, C.c_int, vp]),
     "qsp_gemm": (C.c_int, [vp, i64, vp, i64, vp, i64, i64, i64, i64, C.c_int, C.c_int, vp, sz, vp]),
     "qsp_gemm_workspace_bytes": (sz, [i64, i64, i64, C.c_int]),
+    "qsp_gemm_residual_rmsnorm": (C.c_int, [vp, i64, vp, i64, vp, i64, vp, vp, i64, i64, i64, i64, f32, C.c_int,
+                                            vp, sz, vp]),
+    "qsp_gemm_swiglu": (C.c_int, [vp, i64, vp, i64, vp, i64, vp, i64, i64, i64, i64, C.c_int, vp, sz, vp]),
     "qsp_device_status": (C.c_int, [C.POINTER(i32), i32]),
     "qsp_gdn_verify": (C.c_int, [C.POINTER(GdnLayer), vp]),
     "qsp_attn_prep": (C.c_int, [C.POINTER(AttnLayer), vp]),

@@ -1,13 +1,24 @@
-// qsp_gemm entry point: argument checks and the choice of kernel for the dtype.
+// GEMM entry points: argument checks and the choice of kernel for the dtype.
 // bf16 → tcgen05 tensor-core kernel (qsp_gemm_tc.cu); fp32 → CUDA-core kernel
 // (qsp_gemm_simt.cu), which keeps the fp32 parity configurations within 1e-4.
+// The fused variants apply the op that follows a projection in the decoder layer (residual
+// add + next RMSNorm, or SwiGLU) inside the split-K merge when the GEMM is split, and with
+// the standalone kernels otherwise: same results either way.
 #include "qsp_common.cuh"
 
 namespace qsp {
 int gemm_simt(const void* a, int64_t lda, const void* w, int64_t ldw, void* c, int64_t ldc,
               int64_t m, int64_t n, int64_t k, int dtype, int flags, cudaStream_t st);
+struct GemmEpi {
+  int kind;
+  const __nv_bfloat16* norm_w;
+  __nv_bfloat16* y;
+  int64_t ldy;
+  float eps;
+};
 int gemm_tc(const void* a, int64_t lda, const void* w, int64_t ldw, void* c, int64_t ldc, int64_t m,
-            int64_t n, int64_t k, int flags, void* workspace, size_t ws_bytes, cudaStream_t st);
+            int64_t n, int64_t k, int flags, void* workspace, size_t ws_bytes, cudaStream_t st,
+            const GemmEpi* epi, int* split_out);
 size_t gemm_tc_workspace(int64_t m, int64_t n, int64_t k);
 }  // namespace qsp
 
@@ -18,19 +29,67 @@ extern "C" size_t qsp_gemm_workspace_bytes(int64_t m, int64_t n, int64_t k, int 
   return gemm_tc_workspace(m, n, k);
 }
 
-extern "C" int qsp_gemm(const void* a, int64_t lda, const void* w, int64_t ldw, void* c,
-                        int64_t ldc, int64_t m, int64_t n, int64_t k, int dtype, int flags,
-                        void* workspace, size_t workspace_bytes, void* stream) {
+static int check_gemm_args(const void* a, const void* w, const void* c, int64_t m, int64_t n, int64_t k,
+                           int64_t lda, int64_t ldw, int64_t ldc) {
   QSP_REQUIRE(a && w && c, "qsp_gemm: null pointer");
   QSP_REQUIRE(m >= 0 && n > 0 && k > 0, "qsp_gemm: bad shape m=%lld n=%lld k=%lld", (long long)m,
               (long long)n, (long long)k);
   QSP_REQUIRE(lda >= k && ldw >= k && ldc >= n, "qsp_gemm: leading dimension too small");
   QSP_REQUIRE(m < (1ll << 31) && n < (1ll << 31), "qsp_gemm: shape too large");
-  if (m == 0) return QSP_OK;
-  cudaStream_t st = as_stream(stream);
+  return QSP_OK;
+}
+
+// product into c; *fused = 1 if a split-K merge already applied `epi`
+static int gemm_any(const void* a, int64_t lda, const void* w, int64_t ldw, void* c, int64_t ldc, int64_t m,
+                    int64_t n, int64_t k, int dtype, int flags, void* ws, size_t ws_bytes, cudaStream_t st,
+                    const GemmEpi* epi, int* fused) {
+  *fused = 0;
   if (dtype == QSP_BF16) {
-    const int rc = gemm_tc(a, lda, w, ldw, c, ldc, m, n, k, flags, workspace, workspace_bytes, st);
+    const int rc = gemm_tc(a, lda, w, ldw, c, ldc, m, n, k, flags, ws, ws_bytes, st, epi, fused);
     if (rc != QSP_ERR_UNSUPPORTED) return rc;
+    *fused = 0;
   }
   return gemm_simt(a, lda, w, ldw, c, ldc, m, n, k, dtype, flags, st);
+}
+
+extern "C" int qsp_gemm(const void* a, int64_t lda, const void* w, int64_t ldw, void* c,
+                        int64_t ldc, int64_t m, int64_t n, int64_t k, int dtype, int flags,
+                        void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_gemm_args(a, w, c, m, n, k, lda, ldw, ldc);
+  if (rc) return rc;
+  if (m == 0) return QSP_OK;
+  int fused = 0;
+  return gemm_any(a, lda, w, ldw, c, ldc, m, n, k, dtype, flags, workspace, workspace_bytes, as_stream(stream),
+                  nullptr, &fused);
+}
+
+extern "C" int qsp_gemm_residual_rmsnorm(const void* a, int64_t lda, const void* w, int64_t ldw, void* x,
+                                         int64_t ldx, const void* norm_w, void* y, int64_t ldy, int64_t m,
+                                         int64_t n, int64_t k, float eps, int dtype, void* workspace,
+                                         size_t workspace_bytes, void* stream) {
+  int rc = check_gemm_args(a, w, x, m, n, k, lda, ldw, ldx);
+  if (rc) return rc;
+  QSP_REQUIRE(norm_w && y && ldy >= n, "qsp_gemm_residual_rmsnorm: bad norm weight / output");
+  if (m == 0) return QSP_OK;
+  GemmEpi epi{1, static_cast<const __nv_bfloat16*>(norm_w), static_cast<__nv_bfloat16*>(y), ldy, eps};
+  int fused = 0;
+  rc = gemm_any(a, lda, w, ldw, x, ldx, m, n, k, dtype, QSP_GEMM_ACCUMULATE, workspace, workspace_bytes,
+                as_stream(stream), &epi, &fused);
+  if (rc || fused) return rc;
+  return qsp_rmsnorm(x, ldx, norm_w, y, ldy, m, n, eps, dtype, stream);
+}
+
+extern "C" int qsp_gemm_swiglu(const void* a, int64_t lda, const void* w_gu, int64_t ldw, void* act,
+                               int64_t ld_act, void* gu_tmp, int64_t ld_gu, int64_t m, int64_t inter, int64_t k,
+                               int dtype, void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_gemm_args(a, w_gu, gu_tmp, m, 2 * inter, k, lda, ldw, ld_gu);
+  if (rc) return rc;
+  QSP_REQUIRE(act && ld_act >= inter, "qsp_gemm_swiglu: bad activation output");
+  if (m == 0) return QSP_OK;
+  GemmEpi epi{2, nullptr, static_cast<__nv_bfloat16*>(act), ld_act, 0.f};
+  int fused = 0;
+  rc = gemm_any(a, lda, w_gu, ldw, gu_tmp, ld_gu, m, 2 * inter, k, dtype, 0, workspace, workspace_bytes,
+                as_stream(stream), &epi, &fused);
+  if (rc || fused) return rc;
+  return qsp_swiglu(gu_tmp, ld_gu, act, ld_act, m, inter, dtype, stream);
 }

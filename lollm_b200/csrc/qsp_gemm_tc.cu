@@ -130,21 +130,44 @@ struct TcArgs {
   float* partial;  // [splits][m_tiles*MT][n_tiles*128]
 };
 
-// Split-K merge: c = round(Σ_s partial[s]) (+ c), summed in split order (deterministic).
-// Each thread owns 4 consecutive output columns of one row.
-__global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restrict__ partial, int splits,
-                                                            int64_t split_stride, int ldp,
-                                                            __nv_bfloat16* __restrict__ c, int64_t ldc,
-                                                            int m, int n, int accumulate) {
+// What happens to the product after the split-K merge (the unsplit kernel always stores c).
+struct GemmEpi {
+  int kind;                     // GEMM_EPI_STORE / _RESNORM / _SWIGLU
+  const __nv_bfloat16* norm_w;  // RESNORM: RMSNorm weight (1+w convention)
+  __nv_bfloat16* y;             // RESNORM: normed output; SWIGLU: activation output
+  int64_t ldy;
+  float eps;
+};
+enum { GEMM_EPI_STORE = 0, GEMM_EPI_RESNORM = 1, GEMM_EPI_SWIGLU = 2 };
+
+// ---------------------------------------------------------------- split-K merges
+// Partials are summed in split order (deterministic); loads are issued four splits at a time.
+__device__ __forceinline__ float4 merge4(const float* __restrict__ p, int splits, int64_t stride) {
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int s = 0; s < splits; s += 4) {
+    float4 v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      v[u] = (s + u < splits) ? __ldcg(reinterpret_cast<const float4*>(p + (s + u) * stride)) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      if (s + u < splits) {
+        acc.x += v[u].x; acc.y += v[u].y; acc.z += v[u].z; acc.w += v[u].w;
+      }
+    }
+  }
+  return acc;
+}
+
+// c = round(Σ partial) (+ c)
+__global__ void __launch_bounds__(256) splitk_store_kernel(const float* __restrict__ partial, int splits,
+                                                           int64_t split_stride, int ldp,
+                                                           __nv_bfloat16* __restrict__ c, int64_t ldc, int n,
+                                                           int accumulate) {
   const int row = blockIdx.y;
   const int col = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
   if (col >= n) return;
-  const float* p = partial + (int64_t)row * ldp + col;
-  float4 acc = __ldcg(reinterpret_cast<const float4*>(p));
-  for (int s = 1; s < splits; ++s) {
-    const float4 v = __ldcg(reinterpret_cast<const float4*>(p + s * split_stride));
-    acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
-  }
+  const float4 acc = merge4(partial + (int64_t)row * ldp + col, splits, split_stride);
   const float a4[4] = {acc.x, acc.y, acc.z, acc.w};
   __nv_bfloat16* o = c + (int64_t)row * ldc + col;
 #pragma unroll
@@ -153,6 +176,65 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restr
     float r = dt<__nv_bfloat16>::round(a4[j]);
     if (accumulate) r += __bfloat162float(o[j]);
     o[j] = __float2bfloat16_rn(r);
+  }
+}
+
+// Residual add + the following RMSNorm, one CTA per row:
+// x := round(x + round(Σ partial)); y = round(x̂·(1 + w)) with x̂ = x·rsqrt(mean(x²) + eps).
+constexpr int RN_MAXV = 8;   // up to 8192 columns (256 threads x 4 x 8)
+__global__ void __launch_bounds__(256) splitk_residual_rmsnorm_kernel(
+    const float* __restrict__ partial, int splits, int64_t split_stride, int ldp, __nv_bfloat16* __restrict__ x,
+    int64_t ldx, const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ y, int64_t ldy, int n, float eps) {
+  __shared__ float red[32];
+  const int row = blockIdx.x;
+  float r[RN_MAXV][4];
+  float ss = 0.f;
+#pragma unroll
+  for (int v = 0; v < RN_MAXV; ++v) {
+    const int col = (threadIdx.x + v * 256) * 4;
+    if (col < n) {
+      const float4 acc = merge4(partial + (int64_t)row * ldp + col, splits, split_stride);
+      const float a4[4] = {acc.x, acc.y, acc.z, acc.w};
+      __nv_bfloat16* xo = x + (int64_t)row * ldx + col;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float val = dt<__nv_bfloat16>::round(dt<__nv_bfloat16>::round(a4[j]) + __bfloat162float(xo[j]));
+        xo[j] = __float2bfloat16_rn(val);
+        r[v][j] = val;
+        ss = fmaf(val, val, ss);
+      }
+    }
+  }
+  const float tot = block_sum(ss, red);
+  const float inv = rsqrtf(tot / (float)n + eps);
+#pragma unroll
+  for (int v = 0; v < RN_MAXV; ++v) {
+    const int col = (threadIdx.x + v * 256) * 4;
+    if (col < n) {
+      __nv_bfloat16* yo = y + (int64_t)row * ldy + col;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) yo[j] = __float2bfloat16_rn(r[v][j] * inv * (__bfloat162float(w[col + j]) + 1.0f));
+    }
+  }
+}
+
+// SwiGLU of a fused [gate | up] projection: act = round(round(silu(round(g))) · round(u)).
+__global__ void __launch_bounds__(256) splitk_swiglu_kernel(const float* __restrict__ partial, int splits,
+                                                            int64_t split_stride, int ldp,
+                                                            __nv_bfloat16* __restrict__ act, int64_t ld_act,
+                                                            int inter) {
+  const int row = blockIdx.y;
+  const int j = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
+  if (j >= inter) return;
+  const float* p = partial + (int64_t)row * ldp;
+  const float4 g = merge4(p + j, splits, split_stride);
+  const float4 u = merge4(p + inter + j, splits, split_stride);
+  const float g4[4] = {g.x, g.y, g.z, g.w}, u4[4] = {u.x, u.y, u.z, u.w};
+  __nv_bfloat16* o = act + (int64_t)row * ld_act + j;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const float s = dt<__nv_bfloat16>::round(siluf_(dt<__nv_bfloat16>::round(g4[q])));
+    o[q] = __float2bfloat16_rn(s * dt<__nv_bfloat16>::round(u4[q]));
   }
 }
 
@@ -337,7 +419,7 @@ static int sm_count() {
 
 template <int MT>
 static int launch_tc(const CUtensorMap& mw, const CUtensorMap& mx, const TcArgs& a, const TcPlan& p,
-                     cudaStream_t st) {
+                     const GemmEpi& epi, cudaStream_t st) {
   auto kern = gemm_tc_kernel<MT>;
   static bool attr_set = false;
   if (!attr_set) {
@@ -351,10 +433,20 @@ static int launch_tc(const CUtensorMap& mw, const CUtensorMap& mx, const TcArgs&
   if (rc || p.splits == 1) return rc;
   const int ldp = p.n_tiles * TC_BN;
   const int64_t split_stride = (int64_t)p.m_tiles * MT * ldp;
+  if (epi.kind == GEMM_EPI_RESNORM) {
+    splitk_residual_rmsnorm_kernel<<<a.m, 256, 0, st>>>(a.partial, p.splits, split_stride, ldp, a.c, a.ldc,
+                                                         epi.norm_w, epi.y, epi.ldy, a.n, epi.eps);
+    return check_launch("qsp_gemm(split-k merge + residual + rmsnorm)");
+  }
+  if (epi.kind == GEMM_EPI_SWIGLU) {
+    const int inter = a.n / 2;
+    dim3 g((unsigned)((inter / 4 + 255) / 256), (unsigned)a.m);
+    splitk_swiglu_kernel<<<g, 256, 0, st>>>(a.partial, p.splits, split_stride, ldp, epi.y, epi.ldy, inter);
+    return check_launch("qsp_gemm(split-k merge + swiglu)");
+  }
   dim3 rgrid((unsigned)((a.n / 4 + 255) / 256 + 1), (unsigned)a.m);
-  splitk_reduce_kernel<<<rgrid, 256, 0, st>>>(a.partial, p.splits, split_stride, ldp, a.c, a.ldc, a.m, a.n,
-                                              a.accumulate);
-  return check_launch("qsp_gemm(split-k reduce)");
+  splitk_store_kernel<<<rgrid, 256, 0, st>>>(a.partial, p.splits, split_stride, ldp, a.c, a.ldc, a.n, a.accumulate);
+  return check_launch("qsp_gemm(split-k merge)");
 }
 
 static size_t ws_need(const TcPlan& p) { return p.partial_bytes; }
@@ -363,8 +455,15 @@ size_t gemm_tc_workspace(int64_t m, int64_t n, int64_t k) { return ws_need(plan(
 
 // Returns QSP_ERR_UNSUPPORTED when the operands cannot go through TMA (alignment) or the
 // workspace is too small for the chosen split; the caller then uses the CUDA-core kernel.
+// `split_out` (optional) reports whether the product went through a split-K merge (which
+// then already applied `epi`); otherwise c holds the stored product and the caller applies
+// the epilogue with the standalone kernels.
 int gemm_tc(const void* a, int64_t lda, const void* w, int64_t ldw, void* c, int64_t ldc, int64_t m, int64_t n,
-            int64_t k, int flags, void* workspace, size_t ws_bytes, cudaStream_t st) {
+            int64_t k, int flags, void* workspace, size_t ws_bytes, cudaStream_t st, const GemmEpi* epi_in,
+            int* split_out) {
+  GemmEpi epi{};
+  if (epi_in) epi = *epi_in;
+  if (split_out) *split_out = 0;
   if (!aligned(a, 16) || !aligned(w, 16) || (lda * 2) % 16 != 0 || (ldw * 2) % 16 != 0 || k % 8 != 0)
     return QSP_ERR_UNSUPPORTED;
   TcPlan p = plan(m, n, k, sm_count());
@@ -376,6 +475,8 @@ int gemm_tc(const void* a, int64_t lda, const void* w, int64_t ldw, void* c, int
     }
   }
   if (p.splits > 1 && !aligned(workspace, 256)) return QSP_ERR_UNSUPPORTED;
+  if (p.splits > 1 && epi.kind == GEMM_EPI_RESNORM && n > RN_MAXV * 1024) return QSP_ERR_UNSUPPORTED;
+  if (p.splits > 1 && epi.kind != GEMM_EPI_STORE && (n % 8) != 0) return QSP_ERR_UNSUPPORTED;
   CUtensorMap mw, mx;
   if (!make_map(&mw, w, n, k, ldw, TC_BN) || !make_map(&mx, a, m, k, lda, p.mt)) return QSP_ERR_UNSUPPORTED;
   TcArgs args{};
@@ -388,11 +489,12 @@ int gemm_tc(const void* a, int64_t lda, const void* w, int64_t ldw, void* c, int
   args.splits = p.splits;
   args.accumulate = (flags & QSP_GEMM_ACCUMULATE) ? 1 : 0;
   if (p.splits > 1) args.partial = static_cast<float*>(workspace);
+  if (split_out) *split_out = p.splits > 1;
   switch (p.mt) {
-    case 32: return launch_tc<32>(mw, mx, args, p, st);
-    case 64: return launch_tc<64>(mw, mx, args, p, st);
-    case 128: return launch_tc<128>(mw, mx, args, p, st);
-    default: return launch_tc<256>(mw, mx, args, p, st);
+    case 32: return launch_tc<32>(mw, mx, args, p, epi, st);
+    case 64: return launch_tc<64>(mw, mx, args, p, epi, st);
+    case 128: return launch_tc<128>(mw, mx, args, p, epi, st);
+    default: return launch_tc<256>(mw, mx, args, p, epi, st);
   }
 }
 

@@ -77,6 +77,28 @@ def gemm(a, w, c, accumulate=False, m=None):
            L.QSP_GEMM_ACCUMULATE if accumulate else 0, ws.data_ptr(), ws.numel(), _s())
 
 
+def gemm_residual_rmsnorm(a, w, x, norm_w, y, eps, m=None):
+    """x[:m] += a[:m] @ w.T (bf16-rounded product), then y[:m] = RMSNorm(x[:m]) * (1 + norm_w)."""
+    _cuda(a, w, x, norm_w, y)
+    mm = a.shape[0] if m is None else m
+    n, k = w.shape
+    ws = gemm_workspace(a.device)
+    L.call("qsp_gemm_residual_rmsnorm", a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0), x.data_ptr(),
+           x.stride(0), norm_w.data_ptr(), y.data_ptr(), y.stride(0), mm, n, k, eps, L.dtype_code(a.dtype),
+           ws.data_ptr(), ws.numel(), _s())
+
+
+def gemm_swiglu(a, w_gu, act, gu_tmp, m=None):
+    """act[:m] = silu(a @ w_gate.T) * (a @ w_up.T) with w_gu = [w_gate; w_up]."""
+    _cuda(a, w_gu, act, gu_tmp)
+    mm = a.shape[0] if m is None else m
+    n2, k = w_gu.shape
+    ws = gemm_workspace(a.device)
+    L.call("qsp_gemm_swiglu", a.data_ptr(), a.stride(0), w_gu.data_ptr(), w_gu.stride(0), act.data_ptr(),
+           act.stride(0), gu_tmp.data_ptr(), gu_tmp.stride(0), mm, n2 // 2, k, L.dtype_code(a.dtype),
+           ws.data_ptr(), ws.numel(), _s())
+
+
 def device_status(reset=True) -> int:
     import ctypes as C
     v = C.c_int32(0)

@@ -10,11 +10,11 @@ head consumes. Extensions, all keyword-only and off by default:
                        engine uses this; they are overwritten by the next call).
 
 Per layer (modeling_qwen3_5.py:47-61), every box a C-ABI launch:
-    RMSNorm → [GDN: in_proj(qkv|z|b|a) GEMM → qsp_gdn_verify → out_proj GEMM(+residual)]
-            | [attn: q|k|v GEMM → qsp_attn_prep → qsp_attn_verify → o_proj GEMM(+residual)]
-    RMSNorm → gate|up GEMM → SwiGLU → down GEMM(+residual)
-then the final RMSNorm and the lm_head GEMM. Projections of one input are concatenated into
-one weight so each reads the activation once.
+    [GDN: in_proj(qkv|z|b|a) GEMM → qsp_gdn_verify → out_proj GEMM + residual + RMSNorm]
+  | [attn: q|k|v GEMM → qsp_attn_prep → qsp_attn_verify → o_proj GEMM + residual + RMSNorm]
+    gate|up GEMM + SwiGLU → down GEMM + residual + next layer's input RMSNorm
+then the lm_head GEMM. Projections of one input are concatenated into one weight so each
+reads the activation once; each residual add is fused with the RMSNorm that follows it.
 """
 
 from __future__ import annotations
@@ -195,33 +195,36 @@ class Qwen3_5Model:
         M = B * T
         eps = cfg.rms_norm_eps
         K.embed(ids, self.embed, ws.x, rows=M, bad=cache.bad_index)
+        K.rmsnorm(ws.x, self.layers[0]["in_norm"], ws.xn, eps, rows=M)
+        n_layers = len(self.layers)
         for i, lw in enumerate(self.layers):
-            K.rmsnorm(ws.x, lw["in_norm"], ws.xn, eps, rows=M)
+            # ws.xn holds input_layernorm(x) of this layer (fused into the previous residual add)
             if lw["type"] == "full_attention":
                 slot = cache.attn_slot[i]
                 K.gemm(ws.xn, lw["w_qkv"], ws.proj, m=M)
                 d = self.attn_desc(lw, cache, slot, ws, B, T)
                 K.attn_prep(d)
                 K.attn_verify(d)
-                K.gemm(ws.core, lw["o_proj"], ws.x, accumulate=True, m=M)
+                K.gemm_residual_rmsnorm(ws.core, lw["o_proj"], ws.x, lw["post_norm"], ws.xn, eps, m=M)
             else:
                 slot = cache.gdn_slot[i]
                 K.gemm(ws.xn, lw["w_in"], ws.proj, m=M)
                 d = cache.gdn_desc(slot, ws.proj, ws.proj.stride(0), T, lw["conv_w"], lw["a_log"],
                                    lw["dt_bias"], lw["norm_w"], None, ws.core, speculative)
                 K.gdn_verify(d)
-                K.gemm(ws.core, lw["out_proj"], ws.x, accumulate=True, m=M)
-            K.rmsnorm(ws.x, lw["post_norm"], ws.xn, eps, rows=M)
-            inter = lw["down"].shape[1]
-            K.gemm(ws.xn, lw["w_gu"], ws.gu, m=M)
-            K.swiglu(ws.gu, ws.act, inter, rows=M)
-            K.gemm(ws.act, lw["down"], ws.x, accumulate=True, m=M)
+                K.gemm_residual_rmsnorm(ws.core, lw["out_proj"], ws.x, lw["post_norm"], ws.xn, eps, m=M)
+            K.gemm_swiglu(ws.xn, lw["w_gu"], ws.act, ws.gu, m=M)
+            # residual add + the next norm: next layer's input_layernorm, or the final norm
+            nxt = self.layers[i + 1]["in_norm"] if i + 1 < n_layers else (None if last_only else self.final_norm)
+            if nxt is not None:
+                K.gemm_residual_rmsnorm(ws.act, lw["down"], ws.x, nxt, ws.xn, eps, m=M)
+            else:
+                K.gemm(ws.act, lw["down"], ws.x, accumulate=True, m=M)
         if last_only:
             K.select_rows(ws.x, B, T, ws.last_idx, ws.last_x)
             K.rmsnorm(ws.last_x, self.final_norm, ws.last_xn, eps, rows=B)
             K.gemm(ws.last_xn, self.lm_head, ws.last_logits, m=B)
         else:
-            K.rmsnorm(ws.x, self.final_norm, ws.xn, eps, rows=M)
             K.gemm(ws.xn, self.lm_head, ws.logits, m=M)
         K.cache_finalize(B, T, speculative, cache.seq_lens, cache.replay_n, cache.conv_off, cache.parity)
         cache.last_tokens, cache.last_speculative = T, speculative

@@ -79,12 +79,10 @@ class MTP:
             K.rmsnorm(w["x"], self.in_norm, w["xn"], eps)
             K.gemm(w["xn"], self.w_gv, w["gv"])
             K.mtp_single_token_attn(w["gv"], hd, w["gv"][:, nh * hd:], w["ao"], nh, nkv, hd)
-            K.gemm(w["ao"], self.o_proj, w["x"], accumulate=True)
-            K.rmsnorm(w["x"], self.post_norm, w["xn"], eps)
-            K.gemm(w["xn"], self.w_gu, w["gu"])
-            K.swiglu(w["gu"], w["act"], self.down.shape[1])
-            K.gemm(w["act"], self.down, w["x"], accumulate=True)
-            K.rmsnorm(w["x"], self.norm, w["xn"], eps)
+            K.gemm_residual_rmsnorm(w["ao"], self.o_proj, w["x"], self.post_norm, w["xn"], eps)
+            K.gemm_swiglu(w["xn"], self.w_gu, w["act"], w["gu"])
+            # x stays the pre-norm output (next depth's hidden); xn = final norm for lm_head
+            K.gemm_residual_rmsnorm(w["act"], self.down, w["x"], self.norm, w["xn"], eps)
             lg = w["logits"][:, d]
             K.gemm(w["xn"], m.lm_head, lg)
             if temperature <= 0:
