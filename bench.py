@@ -532,6 +532,46 @@ def run_attn_workload(args):
                          "traffic": None, "algorithmic_bytes_per_launch": algo}}
 
 
+def run_gemm_workload(args):
+    """One projection of the verify step alone: c = a·wᵀ (bf16, fp32 accumulate) with
+    M = batch·(k+1) token rows (default: the GDN in_proj shape 256 x 12352 x 2048)."""
+    from lollm_b200 import kernels as K
+    dev = torch.device("cuda", 0)
+    m, n, k = args.m, args.n, args.k_dim
+    g = torch.Generator(device=dev); g.manual_seed(0)
+    a = torch.randn(m, k, generator=g, device=dev).to(torch.bfloat16)
+    # several weight copies rotated so each launch streams its weights from HBM (> L2 in total)
+    n_w = max(1, int(math.ceil(256e6 / (n * k * 2))))
+    ws = [(torch.randn(n, k, generator=g, device=dev) * 0.02).to(torch.bfloat16) for _ in range(n_w)]
+    c = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+    it = {"i": 0}
+
+    def step():
+        K.gemm(a, ws[it["i"] % n_w], c)
+        it["i"] += 1
+
+    stream = torch.cuda.current_stream()
+    if args.profile:
+        torch.cuda.profiler.start()
+    ms = timed_loop(step, args.steps, args.warmup, stream)
+    if args.profile:
+        torch.cuda.profiler.stop()
+    hbm, tf, src = peaks()
+    t = statistics.mean(ms) / 1000
+    algo_b = n * k * 2 + m * k * 2 + m * n * 2
+    flops = 2 * m * n * k
+    gbs, tfs = algo_b / t / 1e9, flops / t / 1e12
+    bound = "hbm" if gbs / hbm >= tfs / tf else "tensor"
+    return {"metric": f"gemm {m}x{n}x{k} bf16", "value": tfs, "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": statistics.mean(ms), "higher_is_better": True, "dtype": "bf16",
+            "data": "synthetic", "config": {"workload": "gemm", "m": m, "n": n, "k": k, "weight_copies": n_w},
+            "roofline": {"kernel": "gemm_tc_kernel (+ split-k merge)", "bound": bound,
+                         "achieved": gbs if bound == "hbm" else tfs, "peak": hbm if bound == "hbm" else tf,
+                         "unit": "GB/s" if bound == "hbm" else "TFLOP/s",
+                         "frac": gbs / hbm if bound == "hbm" else tfs / tf, "peak_source": src, "traffic": None,
+                         "hbm_frac": gbs / hbm, "tensor_frac": tfs / tf}}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -547,14 +587,17 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", action="store_true",
                     help="bracket the timed steps with cudaProfilerStart/Stop (for ncu --profile-from-start off)")
-    ap.add_argument("--workload", choices=["step", "gdn", "attn"], default="step",
+    ap.add_argument("--m", type=int, default=256)
+    ap.add_argument("--n", type=int, default=12352)
+    ap.add_argument("--k-dim", type=int, default=2048)
+    ap.add_argument("--workload", choices=["step", "gdn", "attn", "gemm"], default="step",
                     help="step: the speculative step (headline); gdn / attn: BASELINE configs[3] / [2] kernels alone")
     args = ap.parse_args()
     from lollm_b200.qwen3_5.config import QWEN35_2B, Qwen3_5Config
     cfg = Qwen3_5Config.from_hf(QWEN35_2B)
     if args.workload != "step":
         torch.cuda.set_device(0)
-        out = run_gdn_workload(args) if args.workload == "gdn" else run_attn_workload(args)
+        out = {"gdn": run_gdn_workload, "attn": run_attn_workload, "gemm": run_gemm_workload}[args.workload](args)
         print(json.dumps(out), flush=True)
         return
     if args.impl == "reference":
