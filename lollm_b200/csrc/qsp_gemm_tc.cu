@@ -116,10 +116,11 @@ struct TcCfg {
   static constexpr int W_BYTES = TC_BN * TC_BK * 2;
   static constexpr int X_BYTES = MT * TC_BK * 2;
   static constexpr int STAGE_BYTES = W_BYTES + X_BYTES;
-  // ring depth sized so two CTAs share an SM (~100 KB each): one CTA's pipeline fill and
-  // epilogue overlap the other's MMAs
-  static constexpr int STAGES = (100 * 1024) / STAGE_BYTES < 2 ? 2 : (100 * 1024) / STAGE_BYTES;
-  static constexpr int TMEM_COLS = MT < 32 ? 32 : MT;
+  // one persistent CTA per SM: the ring fills ~192 KB of shared memory
+  static constexpr int STAGES = (192 * 1024) / STAGE_BYTES > 8 ? 8 : (192 * 1024) / STAGE_BYTES;
+  // two accumulators (the epilogue of one work unit overlaps the MMAs of the next)
+  static constexpr int ACC_COLS = MT < 32 ? 32 : MT;
+  static constexpr int TMEM_COLS = 2 * ACC_COLS;
   static constexpr size_t SMEM = (size_t)STAGES * STAGE_BYTES + 1024 + 256;
 };
 
@@ -127,6 +128,7 @@ struct TcArgs {
   __nv_bfloat16* c;
   int64_t ldc;
   int m, n, n_kb, kb_per_split, splits, accumulate;
+  int m_tiles, n_tiles, units;   // work unit u: split u / tiles, tile u % tiles (m-tile fastest)
   float* partial;  // [splits][m_tiles*MT][n_tiles*128]
 };
 
@@ -239,28 +241,29 @@ __global__ void __launch_bounds__(256) splitk_swiglu_kernel(const float* __restr
 }
 
 template <int MT>
-__global__ void __launch_bounds__(TC_THREADS, 2)
+__global__ void __launch_bounds__(TC_THREADS, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x, const TcArgs A) {
   using C = TcCfg<MT>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
   uint64_t* empty = full + C::STAGES;
-  uint64_t* accf = empty + C::STAGES;
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(accf + 1);
+  uint64_t* acc_full = empty + C::STAGES;   // [2]
+  uint64_t* acc_empty = acc_full + 2;       // [2]
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(acc_empty + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int mb = blockIdx.x, nb = blockIdx.y, sp = blockIdx.z;
-  const int n_tiles = gridDim.y;
-  const int kb0 = sp * A.kb_per_split;
-  const int nk = min(A.n_kb, kb0 + A.kb_per_split) - kb0;
+  const int tiles = A.m_tiles * A.n_tiles;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(accf, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 128);
+    }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
@@ -275,62 +278,90 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
   const uint32_t tmem = *tslot;
 
   if (warp == 0) {
+    // TMA producer: one continuous ring across every k-block of every unit of this CTA
     if (lane == 0) {
       asm volatile("prefetch.tensormap [%0];" ::"l"(&tm_w) : "memory");
       asm volatile("prefetch.tensormap [%0];" ::"l"(&tm_x) : "memory");
-      for (int i = 0; i < nk; ++i) {
-        const int s = i % C::STAGES;
-        const uint32_t ph = (uint32_t)(i / C::STAGES) & 1u;
-        if (i >= C::STAGES && !mbar_wait(&empty[s], ph ^ 1u, 101)) break;
-        uint8_t* st = smem + s * C::STAGE_BYTES;
-        mbar_expect_tx(&full[s], C::STAGE_BYTES);
-        tma_load_2d(st, &tm_w, &full[s], (kb0 + i) * TC_BK, nb * TC_BN);
-        tma_load_2d(st + C::W_BYTES, &tm_x, &full[s], (kb0 + i) * TC_BK, mb * MT);
+      uint32_t it = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < A.units && ok; u += gridDim.x) {
+        const int sp = u / tiles, tile = u % tiles, mb = tile % A.m_tiles, nb = tile / A.m_tiles;
+        const int kb0 = sp * A.kb_per_split, kb1 = min(A.n_kb, kb0 + A.kb_per_split);
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          const int s = it % C::STAGES;
+          const uint32_t ph = (it / C::STAGES) & 1u;
+          if (it >= (uint32_t)C::STAGES && !mbar_wait(&empty[s], ph ^ 1u, 101)) { ok = false; break; }
+          uint8_t* st = smem + s * C::STAGE_BYTES;
+          mbar_expect_tx(&full[s], C::STAGE_BYTES);
+          tma_load_2d(st, &tm_w, &full[s], kb * TC_BK, nb * TC_BN);
+          tma_load_2d(st + C::W_BYTES, &tm_x, &full[s], kb * TC_BK, mb * MT);
+        }
       }
     }
   } else if (warp == 1) {
+    // MMA issuer: accumulator buffer ui & 1 for the ui-th unit of this CTA
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_bf16(TC_BN, MT);
-      for (int i = 0; i < nk; ++i) {
-        const int s = i % C::STAGES;
-        const uint32_t ph = (uint32_t)(i / C::STAGES) & 1u;
-        if (!mbar_wait(&full[s], ph, 102)) break;
+      uint32_t it = 0, ui = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < A.units; u += gridDim.x, ++ui) {
+        const int sp = u / tiles;
+        const int kb0 = sp * A.kb_per_split, kb1 = min(A.n_kb, kb0 + A.kb_per_split);
+        const uint32_t buf = ui & 1u;
+        if (ok && ui >= 2 && !mbar_wait(&acc_empty[buf], ((ui >> 1) & 1u) ^ 1u, 104)) ok = false;
         tc_fence_after();
-        const uint32_t a0 = smem_u32(smem + s * C::STAGE_BYTES);
-        const uint32_t b0 = a0 + C::W_BYTES;
+        const uint32_t d = tmem + buf * C::ACC_COLS;
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          const int s = it % C::STAGES;
+          const uint32_t ph = (it / C::STAGES) & 1u;
+          if (ok && !mbar_wait(&full[s], ph, 102)) ok = false;
+          tc_fence_after();
+          if (ok) {
+            const uint32_t a0 = smem_u32(smem + s * C::STAGE_BYTES);
+            const uint32_t b0 = a0 + C::W_BYTES;
 #pragma unroll
-        for (int kk = 0; kk < TC_BK / 16; ++kk)
-          umma_bf16(tmem, sdesc_sw128(a0 + kk * 32), sdesc_sw128(b0 + kk * 32), idesc, (i > 0 || kk > 0) ? 1u : 0u);
-        umma_commit(&empty[s]);
+            for (int kk = 0; kk < TC_BK / 16; ++kk)
+              umma_bf16(d, sdesc_sw128(a0 + kk * 32), sdesc_sw128(b0 + kk * 32), idesc,
+                        (kb > kb0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(&empty[s]);
+        }
+        umma_commit(&acc_full[buf]);
       }
-      umma_commit(accf);
     }
   } else {
-    // epilogue: warp w may read TMEM lanes 32*(w%4)..+31, i.e. output columns n of that quadrant
+    // epilogue: warp w reads TMEM lanes 32*(w%4)..+31, i.e. output columns n of that quadrant
     const int quad = warp & 3;
-    const int n = nb * TC_BN + quad * 32 + lane;
-    const bool ok = mbar_wait(accf, 0, 103);
-    tc_fence_after();
-    const uint32_t tbase = tmem + ((uint32_t)(quad * 32) << 16);
-    const bool split = A.splits > 1;
-    const int ldp = n_tiles * TC_BN;
-    const int64_t prow0 = ((int64_t)sp * gridDim.x + mb) * MT;
-    for (int c0 = 0; c0 < MT; c0 += 32) {
-      float v[32];
-      tmem_ld32(tbase + c0, v);
-      if (!ok) continue;
+    uint32_t ui = 0;
+    for (int u = blockIdx.x; u < A.units; u += gridDim.x, ++ui) {
+      const int sp = u / tiles, tile = u % tiles, mb = tile % A.m_tiles, nb = tile / A.m_tiles;
+      const uint32_t buf = ui & 1u;
+      const bool ok = mbar_wait(&acc_full[buf], (ui >> 1) & 1u, 103);
+      tc_fence_after();
+      const int n = nb * TC_BN + quad * 32 + lane;
+      const uint32_t tbase = tmem + buf * C::ACC_COLS + ((uint32_t)(quad * 32) << 16);
+      const bool split = A.splits > 1;
+      const int ldp = A.n_tiles * TC_BN;
+      const int64_t prow0 = ((int64_t)sp * A.m_tiles + mb) * MT;
+      for (int c0 = 0; c0 < MT; c0 += 32) {
+        float v[32];
+        tmem_ld32(tbase + c0, v);
+        if (!ok) continue;
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const int m = mb * MT + c0 + j;
-        if (split) {
-          A.partial[(prow0 + c0 + j) * ldp + n] = v[j];
-        } else if (m < A.m && n < A.n) {
-          __nv_bfloat16* p = A.c + (int64_t)m * A.ldc + n;
-          float r = dt<__nv_bfloat16>::round(v[j]);
-          if (A.accumulate) r += __bfloat162float(*p);
-          *p = __float2bfloat16_rn(r);
+        for (int j = 0; j < 32; ++j) {
+          const int m = mb * MT + c0 + j;
+          if (split) {
+            A.partial[(prow0 + c0 + j) * ldp + n] = v[j];
+          } else if (m < A.m && n < A.n) {
+            __nv_bfloat16* p = A.c + (int64_t)m * A.ldc + n;
+            float r = dt<__nv_bfloat16>::round(v[j]);
+            if (A.accumulate) r += __bfloat162float(*p);
+            *p = __float2bfloat16_rn(r);
+          }
         }
       }
+      tc_fence_before();
+      asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&acc_empty[buf])) : "memory");
     }
   }
   tc_fence_before();
@@ -385,27 +416,36 @@ struct TcPlan {
   size_t partial_bytes;
 };
 
+// Split count: smallest estimated time over s in [1, 16], where one persistent CTA per SM
+// walks ceil(units / SMs) units of ceil(k_blocks / s) k-blocks each, and a split pays for
+// writing and merging s fp32 partials.
 static TcPlan plan(int64_t m, int64_t n, int64_t k, int sm_count) {
   TcPlan p{};
   p.mt = pick_mt(m);
   p.m_tiles = (int)((m + p.mt - 1) / p.mt);
   p.n_tiles = (int)((n + TC_BN - 1) / TC_BN);
   p.n_kb = (int)((k + TC_BK - 1) / TC_BK);
-  // two resident CTAs per SM: aim for ~2·SMs CTAs in one wave (K split when tiles are few)
   const int tiles = p.m_tiles * p.n_tiles;
-  const int target = 2 * sm_count;
-  int splits = 1;
-  if (tiles < target) {
-    splits = (target + tiles / 2) / tiles;
-    splits = std::min(splits, std::max(1, p.n_kb / 4));
-    splits = std::max(1, std::min(splits, 16));
+  const double t_kb = p.mt >= 256 ? 0.33 : (p.mt >= 128 ? 0.2 : 0.15);   // µs per k-block per SM
+  double best = 1e30;
+  int best_s = 1;
+  for (int s = 1; s <= 16; ++s) {
+    const int kps = (p.n_kb + s - 1) / s;
+    const int ss = (p.n_kb + kps - 1) / kps;
+    if (ss != s && s > 1) continue;
+    const int units = tiles * ss;
+    const int per_cta = (units + sm_count - 1) / sm_count;
+    double t = per_cta * kps * t_kb + 1.0;
+    if (ss > 1) t += 2.0 + (double)ss * p.m_tiles * p.mt * p.n_tiles * TC_BN * 4.0 * 2.0 / 6.0e6;   // bytes / (6 TB/s)
+    if (t < best - 1e-9) { best = t; best_s = ss; }
   }
-  p.kb_per_split = (p.n_kb + splits - 1) / splits;
+  p.kb_per_split = (p.n_kb + best_s - 1) / best_s;
   p.splits = (p.n_kb + p.kb_per_split - 1) / p.kb_per_split;
   p.partial_bytes = p.splits > 1 ? (size_t)p.splits * p.m_tiles * p.mt * p.n_tiles * TC_BN * sizeof(float) : 0;
   return p;
 }
 
+static int sm_count();
 static int sm_count() {
   static int n = 0;
   if (n == 0) {
@@ -427,8 +467,13 @@ static int launch_tc(const CUtensorMap& mw, const CUtensorMap& mx, const TcArgs&
       return set_error(QSP_ERR_CUDA, "qsp_gemm: cannot reserve %zu bytes of shared memory", TcCfg<MT>::SMEM);
     attr_set = true;
   }
-  dim3 grid(p.m_tiles, p.n_tiles, p.splits);
-  kern<<<grid, TC_THREADS, TcCfg<MT>::SMEM, st>>>(mw, mx, a);
+  const int units = p.m_tiles * p.n_tiles * p.splits;
+  TcArgs aa = a;
+  aa.m_tiles = p.m_tiles;
+  aa.n_tiles = p.n_tiles;
+  aa.units = units;
+  const int grid = std::min(units, sm_count());
+  kern<<<grid, TC_THREADS, TcCfg<MT>::SMEM, st>>>(mw, mx, aa);
   int rc = check_launch("qsp_gemm(tcgen05)");
   if (rc || p.splits == 1) return rc;
   const int ldp = p.n_tiles * TC_BN;
