@@ -393,20 +393,32 @@ def replay_split(graphs, events=None, stream=None):
 # ─────────────────────────────────────── isolated kernels ───────────────────────────────────────
 
 def timed_loop(fn, steps, warmup, stream, between=None):
-    """CUDA-event time of `steps` calls of fn (after `warmup`), per call in ms; `between`
-    (not timed) runs before each call."""
+    """CUDA-event time per call (ms) of `steps` calls of fn (after `warmup`); `between` runs
+    before each call. The calls are captured in one CUDA graph and replayed, so host launch
+    overhead does not leak into the device time; returns [per-call ms] * steps."""
     for _ in range(warmup):
         if between: between()
         fn()
     torch.cuda.synchronize()
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
-    for a, b in evs:
-        if between: between()
-        a.record(stream)
-        fn()
-        b.record(stream)
+    g = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream()
+    side.wait_stream(stream)
+    with torch.cuda.stream(side):
+        with torch.cuda.graph(g, stream=side):
+            for _ in range(steps):
+                if between: between()
+                fn()
+    stream.wait_stream(side)
     torch.cuda.synchronize()
-    return [a.elapsed_time(b) for a, b in evs]
+    g.replay()          # warm replay
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    g.replay()
+    b.record(stream)
+    torch.cuda.synchronize()
+    per = a.elapsed_time(b) / steps
+    return [per] * steps
 
 
 def run_gdn_workload(args):
