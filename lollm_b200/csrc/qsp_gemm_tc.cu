@@ -286,8 +286,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
       bool ok = true;
       for (int u = blockIdx.x; u < A.units && ok; u += gridDim.x) {
         const int sp = u / tiles, tile = u % tiles, mb = tile % A.m_tiles, nb = tile / A.m_tiles;
-        const int kb0 = sp * A.kb_per_split, kb1 = min(A.n_kb, kb0 + A.kb_per_split);
-        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+        const int kb0 = sp * A.kb_per_split, nk = min(A.n_kb, kb0 + A.kb_per_split) - kb0;
+        // units walk their k-blocks from a rotated start so concurrent CTAs read different
+        // activation slabs (all CTAs on the same slab at once hot-spots L2)
+        const int rot = u % nk;
+        for (int i = 0; i < nk; ++i, ++it) {
+          const int kb = kb0 + (i + rot) % nk;
           const int s = it % C::STAGES;
           const uint32_t ph = (it / C::STAGES) & 1u;
           if (it >= (uint32_t)C::STAGES && !mbar_wait(&empty[s], ph ^ 1u, 101)) { ok = false; break; }
@@ -306,12 +310,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
       bool ok = true;
       for (int u = blockIdx.x; u < A.units; u += gridDim.x, ++ui) {
         const int sp = u / tiles;
-        const int kb0 = sp * A.kb_per_split, kb1 = min(A.n_kb, kb0 + A.kb_per_split);
+        const int kb0 = sp * A.kb_per_split, nk = min(A.n_kb, kb0 + A.kb_per_split) - kb0;
         const uint32_t buf = ui & 1u;
         if (ok && ui >= 2 && !mbar_wait(&acc_empty[buf], ((ui >> 1) & 1u) ^ 1u, 104)) ok = false;
         tc_fence_after();
         const uint32_t d = tmem + buf * C::ACC_COLS;
-        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+        for (int i = 0; i < nk; ++i, ++it) {
           const int s = it % C::STAGES;
           const uint32_t ph = (it / C::STAGES) & 1u;
           if (ok && !mbar_wait(&full[s], ph, 102)) ok = false;
@@ -322,7 +326,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
 #pragma unroll
             for (int kk = 0; kk < TC_BK / 16; ++kk)
               umma_bf16(d, sdesc_sw128(a0 + kk * 32), sdesc_sw128(b0 + kk * 32), idesc,
-                        (kb > kb0 || kk > 0) ? 1u : 0u);
+                        (i > 0 || kk > 0) ? 1u : 0u);
           }
           umma_commit(&empty[s]);
         }
