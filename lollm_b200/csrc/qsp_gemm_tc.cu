@@ -23,7 +23,8 @@ namespace qsp {
 
 __device__ int g_qsp_dev_error = 0;
 
-constexpr int TC_BN = 128;          // weight rows per CTA (MMA M)
+constexpr int TC_BN = 256;          // weight rows per work unit: two M=128 MMAs share each activation tile
+constexpr int TC_MM = 128;          // MMA M (weight rows per accumulator)
 constexpr int TC_BK = 64;           // K elements per stage (128 bytes of bf16: one swizzle row)
 constexpr int TC_THREADS = 192;
 constexpr uint32_t WAIT_LIMIT = 1u << 24;
@@ -114,13 +115,17 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 template <int MT>
 struct TcCfg {
   static constexpr int W_BYTES = TC_BN * TC_BK * 2;
+  static constexpr int NACC = TC_BN / TC_MM;   // accumulators per unit
   static constexpr int X_BYTES = MT * TC_BK * 2;
   static constexpr int STAGE_BYTES = W_BYTES + X_BYTES;
   // one persistent CTA per SM: the ring fills ~192 KB of shared memory
   static constexpr int STAGES = (192 * 1024) / STAGE_BYTES > 8 ? 8 : (192 * 1024) / STAGE_BYTES;
-  // two accumulators (the epilogue of one work unit overlaps the MMAs of the next)
+  // NACC accumulators of MT fp32 columns per unit; double-buffered (the epilogue of one unit
+  // overlaps the MMAs of the next) when two sets fit in the 512 TMEM columns
   static constexpr int ACC_COLS = MT < 32 ? 32 : MT;
-  static constexpr int TMEM_COLS = 2 * ACC_COLS;
+  static constexpr int UNIT_COLS = NACC * ACC_COLS;
+  static constexpr int ACC_BUFS = (2 * UNIT_COLS <= 512) ? 2 : 1;
+  static constexpr int TMEM_COLS = ACC_BUFS * UNIT_COLS;
   static constexpr size_t SMEM = (size_t)STAGES * STAGE_BYTES + 1024 + 256;
 };
 
@@ -305,16 +310,17 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
   } else if (warp == 1) {
     // MMA issuer: accumulator buffer ui & 1 for the ui-th unit of this CTA
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_bf16(TC_BN, MT);
+      constexpr uint32_t idesc = idesc_bf16(TC_MM, MT);
       uint32_t it = 0, ui = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < A.units; u += gridDim.x, ++ui) {
         const int sp = u / tiles;
         const int kb0 = sp * A.kb_per_split, nk = min(A.n_kb, kb0 + A.kb_per_split) - kb0;
-        const uint32_t buf = ui & 1u;
-        if (ok && ui >= 2 && !mbar_wait(&acc_empty[buf], ((ui >> 1) & 1u) ^ 1u, 104)) ok = false;
+        const uint32_t buf = (C::ACC_BUFS == 2) ? (ui & 1u) : 0u;
+        const uint32_t use = (C::ACC_BUFS == 2) ? (ui >> 1) : ui;   // how often this buffer was used before
+        if (ok && use >= 1 && !mbar_wait(&acc_empty[buf], (use - 1) & 1u, 104)) ok = false;
         tc_fence_after();
-        const uint32_t d = tmem + buf * C::ACC_COLS;
+        const uint32_t d = tmem + buf * C::UNIT_COLS;
         for (int i = 0; i < nk; ++i, ++it) {
           const int s = it % C::STAGES;
           const uint32_t ph = (it / C::STAGES) & 1u;
@@ -324,9 +330,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
             const uint32_t a0 = smem_u32(smem + s * C::STAGE_BYTES);
             const uint32_t b0 = a0 + C::W_BYTES;
 #pragma unroll
-            for (int kk = 0; kk < TC_BK / 16; ++kk)
-              umma_bf16(d, sdesc_sw128(a0 + kk * 32), sdesc_sw128(b0 + kk * 32), idesc,
-                        (i > 0 || kk > 0) ? 1u : 0u);
+            for (int kk = 0; kk < TC_BK / 16; ++kk) {
+#pragma unroll
+              for (int q = 0; q < C::NACC; ++q)   // weight rows 128q..128q+127 → accumulator q
+                umma_bf16(d + q * C::ACC_COLS, sdesc_sw128(a0 + q * TC_MM * 128 + kk * 32), sdesc_sw128(b0 + kk * 32),
+                          idesc, (i > 0 || kk > 0) ? 1u : 0u);
+            }
           }
           umma_commit(&empty[s]);
         }
@@ -334,33 +343,38 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
       }
     }
   } else {
-    // epilogue: warp w reads TMEM lanes 32*(w%4)..+31, i.e. output columns n of that quadrant
+    // epilogue: warp w reads TMEM lanes 32*(w%4)..+31, i.e. weight rows (output columns n)
+    // 128q + 32*(w%4) + lane of accumulator q
     const int quad = warp & 3;
     uint32_t ui = 0;
     for (int u = blockIdx.x; u < A.units; u += gridDim.x, ++ui) {
       const int sp = u / tiles, tile = u % tiles, mb = tile % A.m_tiles, nb = tile / A.m_tiles;
-      const uint32_t buf = ui & 1u;
-      const bool ok = mbar_wait(&acc_full[buf], (ui >> 1) & 1u, 103);
+      const uint32_t buf = (C::ACC_BUFS == 2) ? (ui & 1u) : 0u;
+      const uint32_t use = (C::ACC_BUFS == 2) ? (ui >> 1) : ui;
+      const bool ok = mbar_wait(&acc_full[buf], use & 1u, 103);
       tc_fence_after();
-      const int n = nb * TC_BN + quad * 32 + lane;
-      const uint32_t tbase = tmem + buf * C::ACC_COLS + ((uint32_t)(quad * 32) << 16);
       const bool split = A.splits > 1;
       const int ldp = A.n_tiles * TC_BN;
       const int64_t prow0 = ((int64_t)sp * A.m_tiles + mb) * MT;
-      for (int c0 = 0; c0 < MT; c0 += 32) {
-        float v[32];
-        tmem_ld32(tbase + c0, v);
-        if (!ok) continue;
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const int m = mb * MT + c0 + j;
-          if (split) {
-            A.partial[(prow0 + c0 + j) * ldp + n] = v[j];
-          } else if (m < A.m && n < A.n) {
-            __nv_bfloat16* p = A.c + (int64_t)m * A.ldc + n;
-            float r = dt<__nv_bfloat16>::round(v[j]);
-            if (A.accumulate) r += __bfloat162float(*p);
-            *p = __float2bfloat16_rn(r);
+      for (int q = 0; q < C::NACC; ++q) {
+        const int n = nb * TC_BN + q * TC_MM + quad * 32 + lane;
+        const uint32_t tbase = tmem + buf * C::UNIT_COLS + q * C::ACC_COLS + ((uint32_t)(quad * 32) << 16);
+        for (int c0 = 0; c0 < MT; c0 += 32) {
+          float v[32];
+          tmem_ld32(tbase + c0, v);
+          if (!ok) continue;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int m = mb * MT + c0 + j;
+            if (split) {
+              A.partial[(prow0 + c0 + j) * ldp + n] = v[j];
+            } else if (m < A.m && n < A.n) {
+              __nv_bfloat16* p = A.c + (int64_t)m * A.ldc + n;
+              float r = dt<__nv_bfloat16>::round(v[j]);
+              if (A.accumulate) r += __bfloat162float(*p);
+              *p = __float2bfloat16_rn(r);
+            }
           }
         }
       }
@@ -430,7 +444,8 @@ static TcPlan plan(int64_t m, int64_t n, int64_t k, int sm_count) {
   p.n_tiles = (int)((n + TC_BN - 1) / TC_BN);
   p.n_kb = (int)((k + TC_BK - 1) / TC_BK);
   const int tiles = p.m_tiles * p.n_tiles;
-  const double t_kb = p.mt >= 256 ? 0.33 : (p.mt >= 128 ? 0.2 : 0.15);   // µs per k-block per SM
+  // µs per k-block per SM: ingest-bound (weight tile + activation tile at ~40 GB/s per SM)
+  const double t_kb = (double)(TC_BN + p.mt) * TC_BK * 2 / 40.0e3;
   double best = 1e30;
   int best_s = 1;
   for (int s = 1; s <= 16; ++s) {
