@@ -553,7 +553,7 @@ def run_gemm_workload(args):
     g = torch.Generator(device=dev); g.manual_seed(0)
     a = torch.randn(m, k, generator=g, device=dev).to(torch.bfloat16)
     # several weight copies rotated so each launch streams its weights from HBM (> L2 in total)
-    n_w = max(1, int(math.ceil(256e6 / (n * k * 2))))
+    n_w = 1 if args.l2_resident else max(1, int(math.ceil(256e6 / (n * k * 2))))
     ws = [(torch.randn(n, k, generator=g, device=dev) * 0.02).to(torch.bfloat16) for _ in range(n_w)]
     c = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
     it = {"i": 0}
@@ -602,6 +602,7 @@ def main():
     ap.add_argument("--m", type=int, default=256)
     ap.add_argument("--n", type=int, default=12352)
     ap.add_argument("--k-dim", type=int, default=2048)
+    ap.add_argument("--l2-resident", action="store_true", help="gemm workload: one weight copy (stays in L2)")
     ap.add_argument("--workload", choices=["step", "gdn", "attn", "gemm"], default="step",
                     help="step: the speculative step (headline); gdn / attn: BASELINE configs[3] / [2] kernels alone")
     args = ap.parse_args()

@@ -23,7 +23,6 @@ namespace qsp {
 
 __device__ int g_qsp_dev_error = 0;
 
-constexpr int TC_BN = 256;          // weight rows per work unit: two M=128 MMAs share each activation tile
 constexpr int TC_MM = 128;          // MMA M (weight rows per accumulator)
 constexpr int TC_BK = 64;           // K elements per stage (128 bytes of bf16: one swizzle row)
 constexpr int TC_THREADS = 192;
@@ -112,10 +111,13 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-template <int MT>
+// BN weight rows per work unit: 128 (one accumulator) or 256 (two M=128 MMAs share each
+// activation tile, halving the activation re-reads of a wide projection)
+template <int MT, int BN>
 struct TcCfg {
-  static constexpr int W_BYTES = TC_BN * TC_BK * 2;
-  static constexpr int NACC = TC_BN / TC_MM;   // accumulators per unit
+  static constexpr int TC_BN = BN;
+  static constexpr int W_BYTES = BN * TC_BK * 2;
+  static constexpr int NACC = BN / TC_MM;   // accumulators per unit
   static constexpr int X_BYTES = MT * TC_BK * 2;
   static constexpr int STAGE_BYTES = W_BYTES + X_BYTES;
   // one persistent CTA per SM: the ring fills ~192 KB of shared memory
@@ -245,10 +247,11 @@ __global__ void __launch_bounds__(256) splitk_swiglu_kernel(const float* __restr
   }
 }
 
-template <int MT>
+template <int MT, int BN>
 __global__ void __launch_bounds__(TC_THREADS, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x, const TcArgs A) {
-  using C = TcCfg<MT>;
+  using C = TcCfg<MT, BN>;
+  constexpr int TC_BN = BN;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
@@ -430,7 +433,7 @@ static int pick_mt(int64_t m) {
 }
 
 struct TcPlan {
-  int mt, m_tiles, n_tiles, n_kb, splits, kb_per_split;
+  int mt, bn, m_tiles, n_tiles, n_kb, splits, kb_per_split;
   size_t partial_bytes;
 };
 
@@ -441,11 +444,16 @@ static TcPlan plan(int64_t m, int64_t n, int64_t k, int sm_count) {
   TcPlan p{};
   p.mt = pick_mt(m);
   p.m_tiles = (int)((m + p.mt - 1) / p.mt);
-  p.n_tiles = (int)((n + TC_BN - 1) / TC_BN);
+  // 256-row units when they fill the SMs in about one round (wide projections), 128-row
+  // units otherwise (narrow outputs need many units; the vocabulary projection needs
+  // double-buffered accumulators across ~8 units per SM)
+  const int t256 = p.m_tiles * (int)((n + 255) / 256);
+  p.bn = (t256 >= sm_count / 5 && t256 <= sm_count) ? 256 : 128;
+  p.n_tiles = (int)((n + p.bn - 1) / p.bn);
   p.n_kb = (int)((k + TC_BK - 1) / TC_BK);
   const int tiles = p.m_tiles * p.n_tiles;
   // µs per k-block per SM: ingest-bound (weight tile + activation tile at ~40 GB/s per SM)
-  const double t_kb = (double)(TC_BN + p.mt) * TC_BK * 2 / 40.0e3;
+  const double t_kb = (double)(p.bn + p.mt) * TC_BK * 2 / 40.0e3;
   double best = 1e30;
   int best_s = 1;
   for (int s = 1; s <= 16; ++s) {
@@ -455,12 +463,12 @@ static TcPlan plan(int64_t m, int64_t n, int64_t k, int sm_count) {
     const int units = tiles * ss;
     const int per_cta = (units + sm_count - 1) / sm_count;
     double t = per_cta * kps * t_kb + 1.0;
-    if (ss > 1) t += 2.0 + (double)ss * p.m_tiles * p.mt * p.n_tiles * TC_BN * 4.0 * 2.0 / 6.0e6;   // bytes / (6 TB/s)
+    if (ss > 1) t += 2.0 + (double)ss * p.m_tiles * p.mt * p.n_tiles * p.bn * 4.0 * 2.0 / 6.0e6;   // bytes / (6 TB/s)
     if (t < best - 1e-9) { best = t; best_s = ss; }
   }
   p.kb_per_split = (p.n_kb + best_s - 1) / best_s;
   p.splits = (p.n_kb + p.kb_per_split - 1) / p.kb_per_split;
-  p.partial_bytes = p.splits > 1 ? (size_t)p.splits * p.m_tiles * p.mt * p.n_tiles * TC_BN * sizeof(float) : 0;
+  p.partial_bytes = p.splits > 1 ? (size_t)p.splits * p.m_tiles * p.mt * p.n_tiles * p.bn * sizeof(float) : 0;
   return p;
 }
 
@@ -476,14 +484,15 @@ static int sm_count() {
   return n;
 }
 
-template <int MT>
+template <int MT, int BN>
 static int launch_tc(const CUtensorMap& mw, const CUtensorMap& mx, const TcArgs& a, const TcPlan& p,
                      const GemmEpi& epi, cudaStream_t st) {
-  auto kern = gemm_tc_kernel<MT>;
+  auto kern = gemm_tc_kernel<MT, BN>;
+  using TcCfgMT = TcCfg<MT, BN>;
   static bool attr_set = false;
   if (!attr_set) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)TcCfg<MT>::SMEM) != cudaSuccess)
-      return set_error(QSP_ERR_CUDA, "qsp_gemm: cannot reserve %zu bytes of shared memory", TcCfg<MT>::SMEM);
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)TcCfgMT::SMEM) != cudaSuccess)
+      return set_error(QSP_ERR_CUDA, "qsp_gemm: cannot reserve %zu bytes of shared memory", TcCfgMT::SMEM);
     attr_set = true;
   }
   const int units = p.m_tiles * p.n_tiles * p.splits;
@@ -492,10 +501,10 @@ static int launch_tc(const CUtensorMap& mw, const CUtensorMap& mx, const TcArgs&
   aa.n_tiles = p.n_tiles;
   aa.units = units;
   const int grid = std::min(units, sm_count());
-  kern<<<grid, TC_THREADS, TcCfg<MT>::SMEM, st>>>(mw, mx, aa);
+  kern<<<grid, TC_THREADS, TcCfgMT::SMEM, st>>>(mw, mx, aa);
   int rc = check_launch("qsp_gemm(tcgen05)");
   if (rc || p.splits == 1) return rc;
-  const int ldp = p.n_tiles * TC_BN;
+  const int ldp = p.n_tiles * BN;
   const int64_t split_stride = (int64_t)p.m_tiles * MT * ldp;
   if (epi.kind == GEMM_EPI_RESNORM) {
     splitk_residual_rmsnorm_kernel<<<a.m, 256, 0, st>>>(a.partial, p.splits, split_stride, ldp, a.c, a.ldc,
@@ -542,7 +551,7 @@ int gemm_tc(const void* a, int64_t lda, const void* w, int64_t ldw, void* c, int
   if (p.splits > 1 && epi.kind == GEMM_EPI_RESNORM && n > RN_MAXV * 1024) return QSP_ERR_UNSUPPORTED;
   if (p.splits > 1 && epi.kind != GEMM_EPI_STORE && (n % 8) != 0) return QSP_ERR_UNSUPPORTED;
   CUtensorMap mw, mx;
-  if (!make_map(&mw, w, n, k, ldw, TC_BN) || !make_map(&mx, a, m, k, lda, p.mt)) return QSP_ERR_UNSUPPORTED;
+  if (!make_map(&mw, w, n, k, ldw, p.bn) || !make_map(&mx, a, m, k, lda, p.mt)) return QSP_ERR_UNSUPPORTED;
   TcArgs args{};
   args.c = static_cast<__nv_bfloat16*>(c);
   args.ldc = ldc;
@@ -554,11 +563,14 @@ int gemm_tc(const void* a, int64_t lda, const void* w, int64_t ldw, void* c, int
   args.accumulate = (flags & QSP_GEMM_ACCUMULATE) ? 1 : 0;
   if (p.splits > 1) args.partial = static_cast<float*>(workspace);
   if (split_out) *split_out = p.splits > 1;
+  const bool wide = p.bn == 256;
   switch (p.mt) {
-    case 32: return launch_tc<32>(mw, mx, args, p, epi, st);
-    case 64: return launch_tc<64>(mw, mx, args, p, epi, st);
-    case 128: return launch_tc<128>(mw, mx, args, p, epi, st);
-    default: return launch_tc<256>(mw, mx, args, p, epi, st);
+    case 32: return wide ? launch_tc<32, 256>(mw, mx, args, p, epi, st) : launch_tc<32, 128>(mw, mx, args, p, epi, st);
+    case 64: return wide ? launch_tc<64, 256>(mw, mx, args, p, epi, st) : launch_tc<64, 128>(mw, mx, args, p, epi, st);
+    case 128:
+      return wide ? launch_tc<128, 256>(mw, mx, args, p, epi, st) : launch_tc<128, 128>(mw, mx, args, p, epi, st);
+    default:
+      return wide ? launch_tc<256, 256>(mw, mx, args, p, epi, st) : launch_tc<256, 128>(mw, mx, args, p, epi, st);
   }
 }
 
