@@ -428,244 +428,6 @@ gdn_verify_kernel(const qsp_gdn_layer L) {
   }
 }
 
-// ------------------------------------------------------------------ warp-specialised variant
-// Used for calls of 1..GDN_TB tokens (every verify step). One persistent CTA per SM with two
-// groups of DV threads: the math group keeps the head's fp32 state in registers and runs only
-// the recurrence (replay, state store, updates, readouts); the helper group stages the next
-// head's inputs and computes its conv/SiLU/l2norm/gates into one of two shared-memory slots,
-// then writes the previous head's gated-norm output, pending rows and conv history. The groups
-// hand slots over with named barriers, so the recurrence, the state stream and the element-
-// wise work of neighbouring heads overlap.
-template <typename T, int DK, int DV>
-struct __align__(16) GdnSlot {
-  static constexpr int NCH = 2 * DK + DV;
-  static constexpr int PS = DK + DV + 4;
-  T xr[GDN_KMAX - 1 + GDN_TB][NCH];   // raw conv inputs (window + tokens)
-  T zr[GDN_TB][DV];
-  T cwr[NCH][GDN_KMAX];
-  float pr[GDN_TB][PS];               // pending rows to replay
-  float2 kr[GDN_TB][DK];              // replay keys as pairs
-  float2 q[GDN_TB][DK];
-  float2 k[GDN_TB][DK];
-  float v[GDN_TB][DV];
-  float o[GDN_TB][DV];
-  float g[GDN_TB];
-  float beta[GDN_TB];
-  float ab[GDN_TB][2];
-};
-
-template <typename T, int DK, int DV>
-struct __align__(128) GdnWsSmem {
-  float sst[DK * DV];
-  GdnSlot<T, DK, DV> slot[2];
-  uint64_t bar;
-};
-
-__device__ __forceinline__ void nb_sync(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
-__device__ __forceinline__ void nb_arrive(int id, int n) {
-  __threadfence_block();   // this thread's shared-memory writes before the hand-over
-  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(n) : "memory");
-}
-
-template <typename T, int DK, int DV>
-__global__ void __launch_bounds__(2 * DV, 1)
-gdn_ws_kernel(const qsp_gdn_layer L) {
-  using SMT = GdnWsSmem<T, DK, DV>;
-  using SL = GdnSlot<T, DK, DV>;
-  constexpr int RPT = DK / 4;
-  constexpr int NT = DV;                 // threads per group
-  constexpr int NCH = SL::NCH;
-  constexpr int PS = SL::PS;
-  constexpr int EPV = 16 / (int)sizeof(T);
-  constexpr uint32_t SBYTES = DK * DV * 4;
-  // named barriers: 1 math group; 2+b slot b ready (helper → math); 4+b outputs ready (math → helper)
-  constexpr int BAR_MATH = 1, BAR_READY = 2, BAR_OUT = 4;
-  extern __shared__ __align__(128) uint8_t gdn_ws_raw[];
-  SMT& sm = *reinterpret_cast<SMT*>(gdn_ws_raw);
-
-  const bool math = threadIdx.x < NT;
-  const int tid = threadIdx.x % NT, lane = tid & 31, warp = tid >> 5;
-  const int T_ = L.tokens, K = L.conv_kernel, Ts = L.max_spec_tokens;
-  const int Hv = L.n_v_heads, Hk = L.n_k_heads, vpk = Hv / Hk;
-  const int key_dim = Hk * DK, conv_dim = 2 * key_dim + Hv * DV, value_dim = Hv * DV;
-  const bool spec = L.speculative != 0;
-  const int par = L.parity[0];
-  const int hist_rows = K - 1 + Ts;
-  const int units = L.batch * Hv;
-  const int G = gridDim.x;
-  const int n_mine = units > (int)blockIdx.x ? (units - 1 - (int)blockIdx.x) / G + 1 : 0;
-
-  if (threadIdx.x == 0) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(gsm(&sm.bar)) : "memory");
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-  }
-  __syncthreads();
-
-  if (math) {
-    // ------------------------------------------------------------ math group
-    const int cg = warp * 8 + (lane & 7), rg = lane >> 3;
-    if (tid == 0 && n_mine > 0)
-      gdn_prefetch_state(sm.sst, L.state + (int64_t)blockIdx.x * DK * DV, &sm.bar, SBYTES);
-    for (int ui = 0; ui < n_mine; ++ui) {
-      const int u = blockIdx.x + ui * G;
-      const int b = u / Hv, h = u % Hv;
-      SL& P = sm.slot[ui & 1];
-      const int R = min(max(L.replay_n[b], 0), Ts);
-      float* state = L.state + ((int64_t)b * Hv + h) * DK * DV;
-      nb_sync(BAR_READY + (ui & 1), 2 * NT);   // the helpers staged this unit
-      gdn_wait(&sm.bar, (uint32_t)ui & 1u);
-      uint64_t S[2 * RPT];
-#pragma unroll
-      for (int i = 0; i < RPT; ++i) {
-        const float4 v4 = *reinterpret_cast<const float4*>(&sm.sst[(4 * i + rg) * DV + 4 * cg]);
-        S[2 * i] = pk2(v4.x, v4.y);
-        S[2 * i + 1] = pk2(v4.z, v4.w);
-      }
-      nb_sync(BAR_MATH, NT);
-      if (tid == 0 && ui + 1 < n_mine)
-        gdn_prefetch_state(sm.sst, L.state + (int64_t)(u + G) * DK * DV, &sm.bar, SBYTES);
-      auto store_state = [&]() {
-#pragma unroll
-        for (int i = 0; i < RPT; ++i) {
-          const float2 lo = upk2(S[2 * i]), hi = upk2(S[2 * i + 1]);
-          *reinterpret_cast<float4*>(state + (int64_t)(4 * i + rg) * DV + 4 * cg) = make_float4(lo.x, lo.y, hi.x, hi.y);
-        }
-      };
-      for (int j = 0; j < R; ++j) gdn_update<RPT>(S, P.kr[j], &P.pr[j][DK], P.pr[j][DK + DV], P.pr[j][DK + DV + 1], rg, cg);
-      if (R > 0 && spec) store_state();
-      for (int t = 0; t < T_; ++t) {
-        gdn_update<RPT>(S, P.k[t], P.v[t], P.g[t], P.beta[t], rg, cg);
-        const float4 o = gdn_readout<RPT>(S, P.q[t], rg);
-        if (rg == 0) *reinterpret_cast<float4*>(&P.o[t][4 * cg]) = o;
-      }
-      if (!spec) store_state();
-      nb_arrive(BAR_OUT + (ui & 1), 2 * NT);
-    }
-  } else {
-    // ------------------------------------------------------------ helper group
-    const float qscale = (float)(1.0 / sqrt((double)DK));
-    const T* proj = static_cast<const T*>(L.proj);
-    const T* cw = static_cast<const T*>(L.conv_w);
-    T* hist = static_cast<T*>(L.conv_hist);
-    T* out = static_cast<T*>(L.out);
-    const T* normw = static_cast<const T*>(L.norm_w);
-    auto prep = [&](int ui) {
-      const int u = blockIdx.x + ui * G;
-      const int b = u / Hv, h = u % Hv, kh = h / vpk;
-      SL& P = sm.slot[ui & 1];
-      const int R = min(max(L.replay_n[b], 0), Ts);
-      const int coff = min(max(L.conv_off[b], 0), Ts);
-      const T* hist_in = hist + ((int64_t)par * L.batch + b) * hist_rows * conv_dim;
-      const float* pend = L.pending + (((int64_t)b * Hv + h) * Ts) * PS;
-      const int seg0 = kh * DK, seg1 = key_dim + kh * DK - DK, seg2 = 2 * key_dim + h * DV - 2 * DK;
-      auto gch = [&](int c) -> int { return c + (c < DK ? seg0 : (c < 2 * DK ? seg1 : seg2)); };
-      for (int e = tid; e < R * (PS / 4); e += NT) gcp16(&P.pr[0][0] + e * 4, pend + e * 4);
-      if (K == GDN_KMAX) {
-        for (int e = tid; e < NCH * GDN_KMAX * (int)sizeof(T) / 16; e += NT) {
-          const int c = (e * 16 / (int)sizeof(T)) / GDN_KMAX;
-          gcp16(&P.cwr[c][0], cw + (int64_t)gch(c) * GDN_KMAX);
-        }
-      } else {
-        for (int e = tid; e < NCH * K; e += NT) P.cwr[e / K][e % K] = cw[(int64_t)gch(e / K) * K + e % K];
-      }
-      for (int i = 0; i < K - 1; ++i)
-        for (int c = tid * EPV; c < NCH; c += NT * EPV) gcp16(&P.xr[i][c], hist_in + (int64_t)(coff + i) * conv_dim + gch(c));
-      for (int t = 0; t < T_; ++t) {
-        const T* prow = proj + (int64_t)(b * T_ + t) * L.ld_proj;
-        for (int c = tid * EPV; c < NCH; c += NT * EPV) gcp16(&P.xr[K - 1 + t][c], prow + gch(c));
-        for (int c = tid * EPV; c < DV; c += NT * EPV) gcp16(&P.zr[t][c], prow + conv_dim + h * DV + c);
-      }
-      if (tid < 2 * T_) {
-        const int t = tid >> 1, w = tid & 1;
-        P.ab[t][w] = dt<T>::to_f(proj[(int64_t)(b * T_ + t) * L.ld_proj + conv_dim + value_dim + w * Hv + h]);
-      }
-      asm volatile("cp.async.commit_group;" ::: "memory");
-      asm volatile("cp.async.wait_all;" ::: "memory");
-      nb_sync(BAR_MATH + 6, NT);   // helper-group barrier (id 7)
-      for (int e = tid; e < R * DK; e += NT) {
-        const float kv = P.pr[e / DK][e % DK];
-        P.kr[e / DK][e % DK] = make_float2(kv, kv);
-      }
-      const float A = -expf(dt<T>::to_f(static_cast<const T*>(L.a_log)[h]));
-      const float dtb = dt<T>::to_f(static_cast<const T*>(L.dt_bias)[h]);
-      for (int c = tid; c < NCH; c += NT) {
-        float w[GDN_KMAX];
-#pragma unroll
-        for (int j = 0; j < GDN_KMAX; ++j) w[j] = j < K ? dt<T>::to_f(P.cwr[c][j]) : 0.f;
-        for (int t = 0; t < T_; ++t) {
-          float acc = 0.f;
-          for (int j = 0; j < K; ++j) acc = fmaf(w[j], dt<T>::to_f(P.xr[t + j][c]), acc);
-          const float a = dt<T>::round(siluf_(dt<T>::round(acc)));
-          if (c < DK) P.q[t][c] = make_float2(a, a);
-          else if (c < 2 * DK) P.k[t][c - DK] = make_float2(a, a);
-          else P.v[t][c - 2 * DK] = a;
-        }
-      }
-      if (tid < T_) {
-        P.beta[tid] = dt<T>::round(sigmoidf_(P.ab[tid][0]));
-        P.g[tid] = A * softplusf_(P.ab[tid][1] + dtb);
-      }
-      nb_sync(BAR_MATH + 6, NT);
-      for (int vidx = warp; vidx < 2 * T_; vidx += NT / 32) {
-        const int t = vidx >> 1;
-        if (vidx & 1) warp_l2norm<T, DK>(P.k[t], 1.0f, lane);
-        else warp_l2norm<T, DK>(P.q[t], qscale, lane);
-      }
-      nb_arrive(BAR_READY + (ui & 1), 2 * NT);   // hand the slot to the math group
-    };
-    auto epilogue = [&](int ui) {
-      const int u = blockIdx.x + ui * G;
-      const int b = u / Hv, h = u % Hv, kh = h / vpk;
-      SL& P = sm.slot[ui & 1];
-      nb_sync(BAR_OUT + (ui & 1), 2 * NT);   // the math group finished this unit
-      T* hist_out = hist + ((int64_t)(par ^ 1) * L.batch + b) * hist_rows * conv_dim;
-      float* pend = L.pending + (((int64_t)b * Hv + h) * Ts) * PS;
-      const int seg0 = kh * DK, seg1 = key_dim + kh * DK - DK, seg2 = 2 * key_dim + h * DV - 2 * DK;
-      auto gch = [&](int c) -> int { return c + (c < DK ? seg0 : (c < 2 * DK ? seg1 : seg2)); };
-      // RMSNormGated over dv per token: w·round(x̂) · silu(z), x = round(core)
-      for (int t = warp; t < T_; t += NT / 32) {
-        float ss = 0.f;
-        for (int c = lane; c < DV; c += 32) {
-          const float x = dt<T>::round(P.o[t][c]);
-          ss = fmaf(x, x, ss);
-        }
-        ss = warp_sum(ss);
-        const float inv = rsqrtf(ss / (float)DV + L.eps);
-        T* orow = out + (int64_t)(b * T_ + t) * L.ld_out + h * DV;
-        for (int c = lane; c < DV; c += 32) {
-          const float xh = dt<T>::round(dt<T>::round(P.o[t][c]) * inv);
-          const float wx = dt<T>::round(dt<T>::to_f(normw[c]) * xh);
-          orow[c] = dt<T>::from_f(wx * siluf_(dt<T>::to_f(P.zr[t][c])));
-        }
-      }
-      if (spec) {
-        for (int t = 0; t < T_; ++t) {
-          float* prow = pend + (int64_t)t * PS;
-          for (int c4 = tid * 4; c4 < PS; c4 += NT * 4) {
-            float4 v4;
-            if (c4 < DK) v4 = make_float4(P.k[t][c4].x, P.k[t][c4 + 1].x, P.k[t][c4 + 2].x, P.k[t][c4 + 3].x);
-            else if (c4 < DK + DV) v4 = *reinterpret_cast<const float4*>(&P.v[t][c4 - DK]);
-            else v4 = make_float4(P.g[t], P.beta[t], 0.f, 0.f);
-            *reinterpret_cast<float4*>(prow + c4) = v4;
-          }
-        }
-      }
-      // conv history: spec → the whole combined window; commit-all → the last K-1 rows
-      const int r0 = spec ? 0 : T_, nr = spec ? K - 1 + T_ : K - 1;
-      const int c_first = ((h % vpk) == 0) ? 0 : 2 * DK;
-      for (int i = 0; i < nr; ++i)
-        for (int c = c_first + tid * EPV; c < NCH; c += NT * EPV)
-          *reinterpret_cast<uint4*>(hist_out + (int64_t)i * conv_dim + gch(c)) =
-              *reinterpret_cast<const uint4*>(&P.xr[r0 + i][c]);
-    };
-    if (n_mine > 0) prep(0);
-    for (int ui = 0; ui < n_mine; ++ui) {
-      if (ui + 1 < n_mine) prep(ui + 1);
-      epilogue(ui);
-    }
-  }
-}
-
 static int sm_count_gdn() {
   static int n = 0;
   if (n == 0) {
@@ -693,29 +455,8 @@ static int launch_gdn_dims(const qsp_gdn_layer& L, cudaStream_t st) {
   return check_launch("qsp_gdn_verify");
 }
 
-template <typename T, int DK, int DV>
-static int launch_gdn_ws(const qsp_gdn_layer& L, cudaStream_t st) {
-  auto kern = gdn_ws_kernel<T, DK, DV>;
-  const size_t smem = sizeof(GdnWsSmem<T, DK, DV>);
-  static bool set = false;
-  if (!set) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-      return set_error(QSP_ERR_CUDA, "qsp_gdn_verify: cannot reserve %zu bytes of shared memory", smem);
-    set = true;
-  }
-  const int units = L.batch * L.n_v_heads;
-  const int grid = std::min(units, sm_count_gdn());
-  kern<<<grid, 2 * DV, smem, st>>>(L);
-  return check_launch("qsp_gdn_verify(ws)");
-}
-
 template <typename T>
 static int launch_gdn(const qsp_gdn_layer& L, cudaStream_t st) {
-  if (L.tokens >= 1 && L.tokens <= GDN_TB) {
-    if (L.head_k == 32 && L.head_v == 32) return launch_gdn_ws<T, 32, 32>(L, st);
-    if (L.head_k == 64 && L.head_v == 64) return launch_gdn_ws<T, 64, 64>(L, st);
-    if (L.head_k == 128 && L.head_v == 128) return launch_gdn_ws<T, 128, 128>(L, st);
-  }
   if (L.head_k == 32 && L.head_v == 32) return launch_gdn_dims<T, 32, 32>(L, st);
   if (L.head_k == 64 && L.head_v == 64) return launch_gdn_dims<T, 64, 64>(L, st);
   if (L.head_k == 128 && L.head_v == 128) return launch_gdn_dims<T, 128, 128>(L, st);
