@@ -191,6 +191,23 @@ int qsp_attn_verify(const qsp_attn_layer* layer, void* stream);
 size_t qsp_attn_workspace_bytes(int32_t batch, int32_t tokens, int32_t n_heads,
                                 int32_t head_dim, int32_t num_splits);
 
+/* qsp_attn_verify with the split-KV partials placed in a scratch region that the library
+ * reserves statically on each device (QSP_ATTN_STATIC_SCRATCH_BYTES), so the call itself
+ * allocates no device memory; layer->partial is ignored and may be NULL. It has no
+ * counterpart in the reference, whose attention allocates its temporaries through torch.
+ *
+ * - Limit: the shape's qsp_attn_workspace_bytes(...) must not exceed
+ *   QSP_ATTN_STATIC_SCRATCH_BYTES; larger requests return QSP_ERR_INVALID and launch nothing.
+ * - Set-up: the first call on a device looks up the region's address on the current device
+ *   (which may load the library's device code); make that first call outside any CUDA stream
+ *   capture. Later calls only launch kernels.
+ * - One region per device: calls that overlap in time on one device (two streams, two host
+ *   threads) race on it and must be serialised by the caller.
+ * - Nothing in the region has to start at zero: every partial the merge reads is written
+ *   earlier in the same call (an empty key split writes an all-masked partial). */
+#define QSP_ATTN_STATIC_SCRATCH_BYTES ((size_t)16 << 20)
+int qsp_attn_verify_static(const qsp_attn_layer* layer, void* stream);
+
 /* MTP attention with no cache over a single position: softmax over one key is 1, so the
  * output is the GQA-expanded v times σ(gate) (mtp.py:71-72 via blocks.py:226-235).
  * gate of head h at gate[r·ld_gate + h·gate_head_stride + d] (2·hd for the q_proj

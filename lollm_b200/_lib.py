@@ -19,6 +19,7 @@ LIB_PATH = os.environ.get("QSP_LIB", os.path.join(_HERE, "libqsp.so"))
 QSP_OK, QSP_ERR_INVALID, QSP_ERR_CUDA, QSP_ERR_UNSUPPORTED = 0, 1, 2, 3
 QSP_F32, QSP_BF16 = 0, 1
 QSP_GEMM_ACCUMULATE = 1
+QSP_ATTN_STATIC_SCRATCH_BYTES = 16 << 20   # include/qsp.h
 
 vp, i32, i64, f32, sz = C.c_void_p, C.c_int32, C.c_int64, C.c_float, C.c_size_t
 
@@ -63,6 +64,7 @@ SIGNATURES = {
     "qsp_attn_prep": (C.c_int, [C.POINTER(AttnLayer), vp]),
     "qsp_attn_verify": (C.c_int, [C.POINTER(AttnLayer), vp]),
     "qsp_attn_workspace_bytes": (sz, [i32, i32, i32, i32, i32]),
+    "qsp_attn_verify_static": (C.c_int, [C.POINTER(AttnLayer), vp]),
     "qsp_mtp_single_token_attn": (C.c_int, [vp, i64, i64, vp, i64, vp, i64, i64, i32, i32, i32,
                                             C.c_int, vp]),
     "qsp_select_rows": (C.c_int, [vp, i64, i32, i32, vp, vp, i64, i64, C.c_int, vp]),

@@ -3,6 +3,8 @@
 // output gate.
 #include "qsp_common.cuh"
 
+#include <atomic>
+
 namespace qsp {
 
 int launch_attn_mma(const qsp_attn_layer& L, cudaStream_t st);
@@ -236,6 +238,36 @@ static int launch_attn_simt(const qsp_attn_layer& L, cudaStream_t st) {
   return check_launch("qsp_attn_verify(combine)");
 }
 
+// Scratch for qsp_attn_verify_static. Some callers cannot allocate at the moment they
+// launch: an allocator hook that is itself running inside an allocation, a host that has
+// handed all free device memory to its own pool, or code that must not touch the caching
+// allocator while another thread captures a graph. For them the split-KV partials live in
+// this fixed region, one per device (a __device__ variable exists once per device context).
+__device__ __align__(256) float g_attn_static_scratch[QSP_ATTN_STATIC_SCRATCH_BYTES / sizeof(float)];
+
+constexpr int ATTN_STATIC_MAX_DEVICES = 64;
+static std::atomic<float*> g_attn_static_addr[ATTN_STATIC_MAX_DEVICES];
+
+// Device address of this device's region (looked up once per device, on that device).
+static int attn_static_scratch(float** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(QSP_ERR_CUDA, "qsp_attn_verify_static: cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= ATTN_STATIC_MAX_DEVICES)
+    return set_error(QSP_ERR_UNSUPPORTED, "qsp_attn_verify_static: device %d beyond %d", dev, ATTN_STATIC_MAX_DEVICES);
+  float* p = g_attn_static_addr[dev].load(std::memory_order_acquire);
+  if (p == nullptr) {
+    void* a = nullptr;
+    e = cudaGetSymbolAddress(&a, g_attn_static_scratch);
+    if (e != cudaSuccess || a == nullptr)
+      return set_error(QSP_ERR_CUDA, "qsp_attn_verify_static: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+    p = static_cast<float*>(a);
+    g_attn_static_addr[dev].store(p, std::memory_order_release);
+  }
+  *out = p;
+  return QSP_OK;
+}
+
 }  // namespace qsp
 
 using namespace qsp;
@@ -300,6 +332,23 @@ int qsp_attn_verify(const qsp_attn_layer* layer, void* stream) {
 size_t qsp_attn_workspace_bytes(int32_t batch, int32_t tokens, int32_t n_heads, int32_t head_dim,
                                 int32_t num_splits) {
   return (size_t)batch * tokens * n_heads * num_splits * (head_dim + 2) * sizeof(float);
+}
+
+int qsp_attn_verify_static(const qsp_attn_layer* layer, void* stream) {
+  QSP_REQUIRE(layer != nullptr, "qsp_attn_verify_static: null layer");
+  qsp_attn_layer L = *layer;
+  QSP_REQUIRE(L.batch > 0 && L.tokens > 0 && L.n_heads > 0 && L.head_dim > 0 && L.num_splits > 0,
+              "qsp_attn_verify_static: batch, tokens, heads, head_dim and num_splits must be positive");
+  const size_t need = qsp_attn_workspace_bytes(L.batch, L.tokens, L.n_heads, L.head_dim, L.num_splits);
+  QSP_REQUIRE(need <= QSP_ATTN_STATIC_SCRATCH_BYTES,
+              "qsp_attn_verify_static: this shape needs %zu bytes of split-KV scratch; the static region "
+              "holds %zu (use qsp_attn_verify with a caller workspace, or fewer splits)",
+              need, (size_t)QSP_ATTN_STATIC_SCRATCH_BYTES);
+  float* scratch = nullptr;
+  const int rc = attn_static_scratch(&scratch);
+  if (rc) return rc;
+  L.partial = scratch;
+  return qsp_attn_verify(&L, stream);
 }
 
 }  // extern "C"

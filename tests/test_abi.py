@@ -60,3 +60,17 @@ def test_kernel_wrappers_refuse_cpu_tensors():
     x = torch.zeros(2, 8)
     with pytest.raises(RuntimeError):
         K.rmsnorm(x, torch.zeros(8), x, 1e-6)
+
+
+def test_static_attention_scratch_limits_without_gpu():
+    """qsp_attn_verify_static checks its scratch limit on the host before touching the device."""
+    import ctypes
+    lib = L.load()
+    assert lib.qsp_attn_verify_static(None, None) == L.QSP_ERR_INVALID
+    d = L.AttnLayer()
+    d.batch, d.tokens, d.n_heads, d.head_dim = 64, 4, 16, 256
+    d.num_splits = L.QSP_ATTN_STATIC_SCRATCH_BYTES // lib.qsp_attn_workspace_bytes(64, 4, 16, 256, 1) + 1
+    assert lib.qsp_attn_verify_static(ctypes.byref(d), None) == L.QSP_ERR_INVALID
+    assert b"static region" in lib.qsp_last_error()
+    d.num_splits = 0
+    assert lib.qsp_attn_verify_static(ctypes.byref(d), None) == L.QSP_ERR_INVALID
