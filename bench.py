@@ -35,6 +35,11 @@ sys.path.insert(0, ROOT)
 
 METRIC = "generated tok/s (batch 64, k=3) at 1/2/4/8 B200; verify-step HBM % of peak"
 UNIT = "tok/s"
+# DRAM bytes (read + write) of one gdn_verify_kernel launch at the step's shape (64 sequences,
+# 32 value heads of 128x128, T=4), from an ncu capture of `bench.py --workload gdn`, which runs
+# exactly that launch; None until captured.
+GDN_TRAFFIC_PER_LAUNCH = None
+GDN_TRAFFIC_SOURCE = "ncu dram__bytes_read.sum + dram__bytes_write.sum of bench.py --workload gdn"
 
 
 # ─────────────────────────────────────────── helpers ───────────────────────────────────────────
@@ -329,6 +334,11 @@ def run_gpu_arm(args, cfg, ws, rank, local):
     vb = verify_step_bytes(cfg, B, T, ctx_lens)
     achieved = vb["total"] / (verify_ms / 1000.0) / 1e9
     acc_rate = (tokens / (args.steps * B) - 1.0) / args.k
+    # ---------------- the dominant kernel, timed live inside the step (after the timed region)
+    live = live_kernel_times(dec, graphs, max(3, min(args.steps, 10)))
+    n_gdn, gdn_ms, gdn_tot = live["gdn_verify"]
+    gdn_bytes = gdn_launch_bytes(cfg, B, T)
+    gdn_achieved = gdn_bytes / (gdn_ms / 1000.0) / 1e9
     out = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": max_ms / args.steps, "higher_is_better": True,
@@ -337,10 +347,17 @@ def run_gpu_arm(args, cfg, ws, rank, local):
         "config": config_block(args, cfg), "clocks": clk,
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": launches_per_step * args.steps,
-        "roofline": {"kernel": "verify step (24-layer forward, T=k+1)", "bound": "hbm",
-                     "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                     "peak_source": src, "traffic": None,
-                     "algorithmic_bytes": vb},
+        "roofline": {"kernel": "gdn_verify_kernel (one GDN layer of the verify forward, live in the step)",
+                     "bound": "hbm", "achieved": gdn_achieved, "peak": hbm, "unit": "GB/s",
+                     "frac": gdn_achieved / hbm, "peak_source": src,
+                     "traffic": GDN_TRAFFIC_PER_LAUNCH, "traffic_source": GDN_TRAFFIC_SOURCE,
+                     "algorithmic_bytes_per_launch": gdn_bytes, "launches_per_step": n_gdn,
+                     "ms_per_launch": gdn_ms},
+        "step_roofline": {"kernel": "verify phase (24-layer forward, T=k+1, all kernels)", "bound": "hbm",
+                          "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                          "algorithmic_bytes": vb},
+        "live_kernels_ms_per_step": {LIVE_CLASSES[k]: {"launches": v[0], "ms_per_launch": v[1], "ms_per_step": v[2]}
+                                     for k, v in live.items()},
         "phases_ms": {k: statistics.mean(v) for k, v in phase.items()},
         "acceptance_rate": acc_rate, "tokens_per_step_per_seq": tokens / (args.steps * B),
         "prefill_s": prefill_s, "setup_s": time.perf_counter() - t_setup,
@@ -379,6 +396,73 @@ def capture_split(dec):
             fn()
         graphs.append(gph)
     return graphs
+
+
+LIVE_CLASSES = {"gdn_verify": "gdn_verify_kernel", "attn_verify": "attn_mma_kernel + attn_combine_kernel",
+                "gemm": "gemm_tc_kernel", "gemm_residual_rmsnorm": "gemm_tc_kernel (+ residual/RMSNorm merge)",
+                "gemm_swiglu": "gemm_tc_kernel (+ SwiGLU merge)"}
+
+
+def live_kernel_times(dec, graphs, steps):
+    """Per-launch device time of the verify forward's kernel classes, measured inside the real
+    step: the verify phase is captured once more with an external (timing) event recorded
+    before and after every launch of each class, and the step (draft, instrumented verify,
+    accept) is replayed `steps` times on the live decoding state. Returns
+    {class: (launches per step, mean ms per launch, total ms per step)}."""
+    from lollm_b200 import kernels as K
+    m, B, T = dec.model, dec.B, dec.T
+    pairs = []
+    orig = {n: getattr(K, n) for n in LIVE_CLASSES}
+
+    def wrap(name, fn):
+        def timed(*a, **kw):
+            e0 = torch.cuda.Event(enable_timing=True, external=True)
+            e1 = torch.cuda.Event(enable_timing=True, external=True)
+            e0.record()
+            r = fn(*a, **kw)
+            e1.record()
+            pairs.append((name, e0, e1))
+            return r
+        return timed
+
+    gph = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    try:
+        for n, fn in orig.items():
+            setattr(K, n, wrap(n, fn))
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(gph, stream=s):
+                dec._ws = m._forward_into(dec.ids, dec.cache, B, T, True)
+    finally:
+        for n, fn in orig.items():
+            setattr(K, n, fn)
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    acc = {}
+    for _ in range(steps):
+        graphs[0].replay()
+        gph.replay()
+        graphs[2].replay()
+        torch.cuda.synchronize()
+        for name, e0, e1 in pairs:
+            acc.setdefault(name, []).append(e0.elapsed_time(e1))
+    del gph
+    out = {}
+    for name, v in acc.items():
+        n = len(v) // steps
+        out[name] = (n, statistics.mean(v), sum(v) / steps)
+    return out
+
+
+def gdn_launch_bytes(cfg, B, T):
+    """Algorithmic HBM bytes of one GDN verify launch: the fp32 state read and written once,
+    the conv window read and written, the token rows of the projection read (q, k, v, z, a, b)
+    and the gated output written."""
+    Hv, dk, dv = cfg.linear_num_value_heads, cfg.linear_key_head_dim, cfg.linear_value_head_dim
+    C, Vd = cfg.conv_dim, cfg.value_dim
+    return (2 * B * Hv * dk * dv * 4 + 2 * B * C * (cfg.linear_conv_kernel_dim - 1) * 2
+            + B * T * (C + Vd + 2 * Hv) * 2 + B * T * Vd * 2)
 
 
 def replay_split(graphs, events=None, stream=None):
@@ -474,7 +558,7 @@ def run_gdn_workload(args):
     # kernel-only time (finalize is a 2 µs bookkeeping launch): time the GDN launch alone too
     ms_k = timed_loop(lambda: K.gdn_verify(desc), args.steps, 1, stream)
     hbm, _, src = peaks()
-    algo = 2 * B * Hv * d * d * 4 + 2 * B * C * (Kc - 1) * 2 + B * T * (C + Vd) * 2 + B * T * Vd * 2
+    algo = 2 * B * Hv * d * d * 4 + 2 * B * C * (Kc - 1) * 2 + B * T * (C + Vd + 2 * Hv) * 2 + B * T * Vd * 2
     t = statistics.mean(ms_k) / 1000
     return {"metric": "GDN verify update (64 seq x 32 heads, T=4) state GB/s", "value": algo / t / 1e9,
             "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
