@@ -37,8 +37,9 @@ METRIC = "generated tok/s (batch 64, k=3) at 1/2/4/8 B200; verify-step HBM % of 
 UNIT = "tok/s"
 # DRAM bytes (read + write) of one gdn_verify_kernel launch at the step's shape (64 sequences,
 # 32 value heads of 128x128, T=4), from an ncu capture of `bench.py --workload gdn`, which runs
-# exactly that launch; None until captured.
-GDN_TRAFFIC_PER_LAUNCH = None
+# exactly that launch (149.73 MB read + 93.76 MB written; some state write-back is still in L2
+# when the kernel ends).
+GDN_TRAFFIC_PER_LAUNCH = 243_495_168
 GDN_TRAFFIC_SOURCE = "ncu dram__bytes_read.sum + dram__bytes_write.sum of bench.py --workload gdn"
 
 
@@ -88,7 +89,7 @@ def reduce_sum(x: float, ws: int) -> float:
 
 
 class ClockSampler:
-    """nvidia-smi clocks/throttle reasons sampled every 200 ms during the timed region."""
+    """nvidia-smi clocks/throttle reasons sampled every 50 ms during the timed region."""
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -101,7 +102,7 @@ class ClockSampler:
     def start(self):
         try:
             self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                                       "-i", str(self.idx), "-lms", "200"], stdout=self.f,
+                                       "-i", str(self.idx), "-lms", "50"], stdout=self.f,
                                       stderr=subprocess.DEVNULL)
         except OSError:
             self.p = None
@@ -217,28 +218,6 @@ def config_block(args, cfg):
 
 # ─────────────────────────────────────────── GPU arm ───────────────────────────────────────────
 
-# kernels launched per C-ABI call (entry points that launch more than one kernel)
-LAUNCHES = {"qsp_attn_verify": 2, "qsp_greedy_verify": 2, "qsp_spec_sample": 3, "qsp_sample_rows": 2}
-
-
-def count_launches(fn):
-    from lollm_b200 import _lib as L
-    n = {"calls": 0, "launches": 0}
-    orig = L.call
-
-    def counting(name, *a):
-        n["calls"] += 1
-        n["launches"] += LAUNCHES.get(name, 1)
-        return orig(name, *a)
-
-    L.call = counting
-    try:
-        fn()
-    finally:
-        L.call = orig
-    return n["launches"]
-
-
 def run_gpu_arm(args, cfg, ws, rank, local):
     from lollm_b200.qwen3_5 import MTP, Qwen3_5Model, SpecDecoder
     from lollm_b200.qwen3_5.weights import load_checkpoint, random_init
@@ -261,8 +240,9 @@ def run_gpu_arm(args, cfg, ws, rank, local):
     dec.prefill(prompts, chunk=args.prefill_chunk)
     torch.cuda.synchronize()
     prefill_s = time.perf_counter() - t_pf
-    launches_per_step = count_launches(dec.step)     # one eager step (also warms workspaces)
+    dec.step()                                       # one eager step (warms workspaces)
     graphs = capture_split(dec)
+    launches_per_step = graph_kernel_nodes(graphs)
     stream = torch.cuda.current_stream()
     for _ in range(args.warmup):
         replay_split(graphs)
@@ -391,11 +371,34 @@ def capture_split(dec):
         draft(); verify(); accept()          # one eager warm-up step on the capture stream
     torch.cuda.current_stream().wait_stream(s)
     for fn in (draft, verify, accept):
-        gph = torch.cuda.CUDAGraph()
+        gph = torch.cuda.CUDAGraph(keep_graph=True)
         with torch.cuda.graph(gph):
             fn()
+        gph.instantiate()
         graphs.append(gph)
     return graphs
+
+
+def graph_kernel_nodes(graphs) -> int:
+    """Kernel nodes in the captured step graphs (every one is a libqsp kernel: the step calls
+    no torch op that launches work), counted through the driver API."""
+    import ctypes as C
+    cu = C.CDLL("libcuda.so.1")
+    total = 0
+    for gph in graphs:
+        h = C.c_void_p(gph.raw_cuda_graph())
+        n = C.c_size_t(0)
+        if cu.cuGraphGetNodes(h, None, C.byref(n)) != 0:
+            raise RuntimeError("cuGraphGetNodes failed")
+        nodes = (C.c_void_p * n.value)()
+        if cu.cuGraphGetNodes(h, nodes, C.byref(n)) != 0:
+            raise RuntimeError("cuGraphGetNodes failed")
+        for i in range(n.value):
+            t = C.c_int(-1)
+            if cu.cuGraphNodeGetType(C.c_void_p(nodes[i]), C.byref(t)) != 0:
+                raise RuntimeError("cuGraphNodeGetType failed")
+            total += int(t.value == 0)          # CU_GRAPH_NODE_TYPE_KERNEL
+    return total
 
 
 LIVE_CLASSES = {"gdn_verify": "gdn_verify_kernel", "attn_verify": "attn_mma_kernel + attn_combine_kernel",
@@ -671,7 +674,7 @@ def run_gemm_workload(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--batch", type=int, default=64)
