@@ -521,7 +521,7 @@ def run_gdn_workload(args):
     rnd = lambda *s: torch.randn(*s, generator=g, device=dev)
     state = rnd(B, Hv, d, d) * 0.1
     hist = torch.zeros(2, B, Kc - 1 + 8, C, dtype=torch.bfloat16, device=dev)
-    pending = torch.zeros(B, Hv, 8, 2 * d + 4, device=dev)
+    pending = torch.zeros(K.gdn_pending_bytes(B, Hk, Hv, d, d, 8, torch.bfloat16), dtype=torch.uint8, device=dev)
     replay = torch.zeros(B, dtype=torch.int32, device=dev)
     coff = torch.zeros(B, dtype=torch.int32, device=dev)
     parity = torch.zeros(1, dtype=torch.int32, device=dev)

@@ -102,20 +102,22 @@ int qsp_device_status(int32_t* code, int32_t reset);
  * RMSNormGated(core, z) (blocks.py:38-51, 324). Output feeds out_proj.
  *
  * Deferred commit (rollback by index): in speculative mode the kernel does NOT write the
- * state after the T tokens. It stores each token's (k, v, g, β) in `pending` and the raw
- * conv inputs in `conv_hist`; the NEXT call first replays the `replay_n[b]` kept tokens
- * onto the stored state (same arithmetic, so the result is bit-identical to having run
- * only those tokens) and reads its conv window at row `conv_off[b]`. Commit-all mode
- * (speculative == 0, any T) writes the final state and window directly.
+ * state after the T tokens. It stores each token's prepared q̂, k̂, v, g, β and Gram products
+ * in the token ring `pending` and the raw conv inputs in `conv_hist`; the NEXT call first
+ * replays the `replay_n[b]` kept tokens onto the stored state (same arithmetic, so the
+ * result is bit-identical to having run only those tokens) and reads its conv window at row
+ * `conv_off[b]`. Commit-all mode (speculative == 0, any T) writes the final state and window
+ * directly.
  *
  * Buffers (per layer):
  *   proj       [B*T, ld_proj]           cols [0,C): raw qkv, [C,C+Vd): z, then b [Hv], a [Hv]
  *   state      [B, Hv, dk, dv] fp32     (same layout as the reference's recurrent_state)
  *   conv_hist  [2, B, K-1+Ts, C] dtype  ping-pong on *parity
- *   pending    [B, Hv, Ts, dk+dv+4] fp32  (k | v | g | β | 2 pad)
+ *   pending    token ring, qsp_gdn_pending_bytes(...) bytes (two parity halves of
+ *              [B, Ts] rows; the layout is private to the library)
  *   out        [B*T, ld_out]            cols [0, Vd)
  * with C = 2·Hk·dk + Hv·dv (conv_dim), Vd = Hv·dv, Ts = max_spec_tokens ≤ 8, conv kernel ≤ 4;
- * proj, state, pending and conv_hist 16-byte aligned, ld_proj a multiple of 16 bytes.
+ * proj, state, pending, conv_hist and conv_w 16-byte aligned, ld_proj a multiple of 16 bytes.
  */
 typedef struct qsp_gdn_layer {
   int32_t batch, tokens;
@@ -132,7 +134,7 @@ typedef struct qsp_gdn_layer {
   const void* norm_w;     /* [dv]     */
   float* state;
   void* conv_hist;
-  float* pending;
+  void* pending;
   const int32_t* replay_n; /* [B] */
   const int32_t* conv_off; /* [B] */
   const int32_t* parity;   /* [1] */
@@ -141,6 +143,12 @@ typedef struct qsp_gdn_layer {
 } qsp_gdn_layer;
 
 int qsp_gdn_verify(const qsp_gdn_layer* layer, void* stream);
+
+/* Bytes of the `pending` token ring of one GDN layer (0 for invalid sizes). It replaces the
+ * reference's cache clone + recompute on rejection (mtp.py:141,156-162), which keeps no
+ * per-token buffer. */
+size_t qsp_gdn_pending_bytes(int32_t batch, int32_t n_k_heads, int32_t n_v_heads, int32_t head_k,
+                             int32_t head_v, int32_t max_spec_tokens, int32_t dtype);
 
 /* ---------------------------------------------------------------- gated attention */
 

@@ -61,6 +61,7 @@ SIGNATURES = {
     "qsp_gemm_swiglu": (C.c_int, [vp, i64, vp, i64, vp, i64, vp, i64, i64, i64, i64, C.c_int, vp, sz, vp]),
     "qsp_device_status": (C.c_int, [C.POINTER(i32), i32]),
     "qsp_gdn_verify": (C.c_int, [C.POINTER(GdnLayer), vp]),
+    "qsp_gdn_pending_bytes": (sz, [i32, i32, i32, i32, i32, i32, i32]),
     "qsp_attn_prep": (C.c_int, [C.POINTER(AttnLayer), vp]),
     "qsp_attn_verify": (C.c_int, [C.POINTER(AttnLayer), vp]),
     "qsp_attn_workspace_bytes": (sz, [i32, i32, i32, i32, i32]),

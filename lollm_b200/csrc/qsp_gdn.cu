@@ -1,13 +1,24 @@
-// Gated DeltaNet verify/commit kernel: one CTA per (value head, sequence).
+// Gated DeltaNet verify/commit: the token mixer core of one GDN layer.
 //
-// The fp32 recurrent state of the head (dk x dv, 64 KB at 128x128) lives in registers for
-// the whole call: thread (warp w, lane l) owns columns 4*cg..4*cg+3 with cg = 8w + (l&7) and
-// rows rg, rg+4, rg+8, ... with rg = l>>3, so every reduction over rows (Sᵀk, Sᵀq) is an
-// in-thread sum plus two xor-shuffles, and a float4 load of one row by the 8 lanes of a row
-// group is a fully used 128-byte line. HBM traffic is one state read plus (when the state
-// changes) one write per call — the algorithmic minimum of the recurrence.
+// Calls of at most max_spec_tokens tokens (every speculative verify, flushes, short commits)
+// run two kernels:
+//   gdn_prep_kernel   one CTA per (sequence, key head): causal conv + SiLU over the head's
+//                     q, k and v channels, l2norm of q and k, the gates g and β, and the Gram
+//                     products k_s·k_t, k_s·q_t of the call's tokens. Results go to a per-layer
+//                     token ring (`pending`, two parity slots) that the NEXT call also reads
+//                     to replay kept tokens, and the raw inputs to the conv-history ring.
+//   gdn_chunk_kernel  persistent, one (sequence, value head) at a time: the fp32 state, one
+//                     column per thread, is updated over all the call's tokens at once in
+//                     chunked (WY) form — one pass computes Sᵀk_s and Sᵀq_t for every token,
+//                     a per-column triangular recursion gives the δ's, and one rank-n pass
+//                     writes the new state. The columns of S evolve independently under the
+//                     delta rule, so nothing is reduced across threads except the gated
+//                     RMSNorm of the output.
+// Longer commit calls (prefill) replay the kept tokens with gdn_chunk_kernel, then run
+// gdn_seq_kernel, which steps token by token through blocks of 8.
 //
-// Rollback by index: see the qsp_gdn_layer comment in include/qsp.h.
+// HBM traffic is one state read plus (when the state changes) one write per head and call —
+// the algorithmic minimum of the recurrence. Rollback by index: see include/qsp.h.
 #include "qsp_common.cuh"
 
 #include <algorithm>
@@ -157,12 +168,10 @@ __device__ __forceinline__ void load16_as_float(const T* src, float* dst) {
 template <typename T, int DK, int DV>
 struct __align__(128) GdnSmem {
   static constexpr int NCH = 2 * DK + DV;   // q, k, v conv channels of one value head
-  static constexpr int PS = DK + DV + 4;    // pending row: k | v | g | beta | pad
   float sst[DK * DV];                       // next head's state (TMA bulk prefetch target)
   T xr[GDN_KMAX - 1 + GDN_TB][NCH];         // raw conv inputs: window rows, then tokens
   T zr[GDN_TB][DV];                         // raw output gate z
   T cwr[NCH][GDN_KMAX];                     // conv weights of this head's channels
-  float pr[GDN_TB][PS];                     // pending rows to replay
   float2 q[GDN_TB][DK];                     // q, k duplicated as (x, x) pairs (packed FMA operands)
   float2 k[GDN_TB][DK];
   float v[GDN_TB][DV];
@@ -204,19 +213,20 @@ __device__ __forceinline__ void gdn_prefetch_state(float* dst, const float* src,
                : "memory");
 }
 
+// Sequential commit of T > max_spec_tokens tokens (prefill chunks); any kept tokens of a
+// previous speculative call were replayed into the state before this launch.
 // Persistent: CTA c handles (sequence, value head) units c, c+G, c+2G, ... . While a unit is
-// computed from registers, the next unit's state streams into shared memory, so the HBM
-// traffic of the recurrence (one state read and one write per head) overlaps the math. A
-// unit's small inputs (conv window, token rows, z, weights, pending rows) are staged with
-// cp.async (all in flight at once, raw in shared memory).
+// computed from registers, the next unit's state streams into shared memory. A unit's small
+// inputs (conv window, token rows, z, weights) are staged with cp.async.
+// Thread (warp w, lane l) owns columns 4*cg..4*cg+3 with cg = 8w + (l&7) and rows rg, rg+4, ...
+// with rg = l>>3, so every reduction over rows is an in-thread sum plus two xor-shuffles.
 template <typename T, int DK, int DV>
 __global__ void __launch_bounds__(DV, 2)
-gdn_verify_kernel(const qsp_gdn_layer L) {
+gdn_seq_kernel(const qsp_gdn_layer L) {
   using SMT = GdnSmem<T, DK, DV>;
   constexpr int RPT = DK / 4;
   constexpr int NT = DV;
   constexpr int NCH = SMT::NCH;
-  constexpr int PS = SMT::PS;
   constexpr int EPV = 16 / (int)sizeof(T);   // elements per 16-byte vector
   extern __shared__ __align__(128) uint8_t gdn_smem_raw[];
   SMT& sm = *reinterpret_cast<SMT*>(gdn_smem_raw);
@@ -226,7 +236,6 @@ gdn_verify_kernel(const qsp_gdn_layer L) {
   const int T_ = L.tokens, K = L.conv_kernel, Ts = L.max_spec_tokens;
   const int Hv = L.n_v_heads, Hk = L.n_k_heads, vpk = Hv / Hk;
   const int key_dim = Hk * DK, conv_dim = 2 * key_dim + Hv * DV, value_dim = Hv * DV;
-  const bool spec = L.speculative != 0;
   const T* proj = static_cast<const T*>(L.proj);
   const T* cw = static_cast<const T*>(L.conv_w);
   T* hist = static_cast<T*>(L.conv_hist);
@@ -251,18 +260,15 @@ gdn_verify_kernel(const qsp_gdn_layer L) {
     const int b = u / Hv, h = u % Hv, kh = h / vpk;
     // device-side counters are clamped to the buffers they index (they are produced by
     // qsp_cache_finalize / qsp_cache_accept and never exceed max_spec_tokens)
-    const int R = min(max(L.replay_n[b], 0), Ts);
     const int coff = min(max(L.conv_off[b], 0), Ts);
     const T* hist_in = hist + ((int64_t)par * L.batch + b) * hist_rows * conv_dim;
     T* hist_out = hist + ((int64_t)(par ^ 1) * L.batch + b) * hist_rows * conv_dim;
-    float* pend = L.pending + (((int64_t)b * Hv + h) * Ts) * PS;
     float* state = L.state + ((int64_t)b * Hv + h) * DK * DV;
     // global channel of local conv channel c (q | k | v segments of this head)
     const int seg0 = kh * DK, seg1 = key_dim + kh * DK - DK, seg2 = 2 * key_dim + h * DV - 2 * DK;
     auto gch = [&](int c) -> int { return c + (c < DK ? seg0 : (c < 2 * DK ? seg1 : seg2)); };
 
     // 1. stage this unit's inputs (cp.async: every copy in flight at once)
-    for (int e = tid; e < R * (PS / 4); e += NT) gcp16(&sm.pr[0][0] + e * 4, pend + e * 4);
     for (int e = tid; e < NCH * GDN_KMAX * (int)sizeof(T) / 16 && K == GDN_KMAX; e += NT) {
       const int c = (e * 16 / (int)sizeof(T)) / GDN_KMAX;   // first channel of this 16-byte chunk
       const int within = (e * 16 / (int)sizeof(T)) % GDN_KMAX;
@@ -298,16 +304,10 @@ gdn_verify_kernel(const qsp_gdn_layer L) {
     }
     asm volatile("cp.async.wait_all;" ::: "memory");
     __syncthreads();   // inputs staged; every thread holds its state slice
-    for (int e = tid; e < R * DK; e += NT) {   // replay keys, duplicated into pairs
-      const float kv = sm.pr[e / DK][e % DK];
-      sm.k[e / DK][e % DK] = make_float2(kv, kv);
-    }
-    __syncthreads();
     // 3. prefetch the next unit's state while this one computes
     if (tid == 0 && u + (int)gridDim.x < units)
       gdn_prefetch_state(sm.sst, L.state + (int64_t)(u + gridDim.x) * DK * DV, &sm.bar, SBYTES);
 
-    // 4. replay the kept tokens of the previous speculative call
     auto store_state = [&]() {
 #pragma unroll
       for (int i = 0; i < RPT; ++i) {
@@ -315,8 +315,6 @@ gdn_verify_kernel(const qsp_gdn_layer L) {
         *reinterpret_cast<float4*>(state + (int64_t)(4 * i + rg) * DV + 4 * cg) = make_float4(lo.x, lo.y, hi.x, hi.y);
       }
     };
-    for (int j = 0; j < R; ++j) gdn_update<RPT>(S, sm.k[j], &sm.pr[j][DK], sm.pr[j][DK + DV], sm.pr[j][DK + DV + 1], rg, cg);
-    if (R > 0 && spec) store_state();
 
     // conv-history ownership: every head writes its v channels; the first v head of a k-head
     // group also writes that group's q and k channels
@@ -327,14 +325,13 @@ gdn_verify_kernel(const qsp_gdn_layer L) {
           *reinterpret_cast<uint4*>(hist_out + (int64_t)i * conv_dim + gch(c)) =
               *reinterpret_cast<const uint4*>(&sm.xr[src_row0 + i][c]);
     };
-    if (T_ == 0) write_hist_rows(0, K - 1);
 
     const float A = -expf(dt<T>::to_f(static_cast<const T*>(L.a_log)[h]));
     const float dtb = dt<T>::to_f(static_cast<const T*>(L.dt_bias)[h]);
 
     for (int t0 = 0; t0 < T_; t0 += GDN_TB) {
       const int nt = min(GDN_TB, T_ - t0);
-      __syncthreads();   // the replay is done with the k pairs
+      __syncthreads();   // the previous block is done with the token buffers
       // 5. conv + SiLU (fp32 accumulate, rounded like F.conv1d then F.silu), gates
       for (int c = tid; c < NCH; c += NT) {
         float w[GDN_KMAX];
@@ -353,7 +350,6 @@ gdn_verify_kernel(const qsp_gdn_layer L) {
         sm.beta[tid] = dt<T>::round(sigmoidf_(sm.ab[tid][0]));
         sm.g[tid] = A * softplusf_(sm.ab[tid][1] + dtb);
       }
-      if (spec && t0 == 0) write_hist_rows(0, K - 1 + nt);
       __syncthreads();
       for (int vidx = warp; vidx < 2 * nt; vidx += NT / 32) {
         const int t = vidx >> 1;
@@ -361,23 +357,11 @@ gdn_verify_kernel(const qsp_gdn_layer L) {
         else warp_l2norm<T, DK>(sm.q[t], qscale, lane);
       }
       __syncthreads();
-      // 6. recurrence + readout; pending (k, v, g, β) for the next call's replay
+      // 6. recurrence + readout
       for (int t = 0; t < nt; ++t) {
         gdn_update<RPT>(S, sm.k[t], sm.v[t], sm.g[t], sm.beta[t], rg, cg);
         const float4 o = gdn_readout<RPT>(S, sm.q[t], rg);
         if (rg == 0) *reinterpret_cast<float4*>(&sm.o[t][4 * cg]) = o;
-      }
-      if (spec) {
-        for (int t = 0; t < nt; ++t) {
-          float* prow = pend + (int64_t)(t0 + t) * PS;
-          for (int c4 = tid * 4; c4 < PS; c4 += NT * 4) {
-            float4 v4;
-            if (c4 < DK) v4 = make_float4(sm.k[t][c4].x, sm.k[t][c4 + 1].x, sm.k[t][c4 + 2].x, sm.k[t][c4 + 3].x);
-            else if (c4 < DK + DV) v4 = *reinterpret_cast<const float4*>(&sm.v[t][c4 - DK]);
-            else v4 = make_float4(sm.g[t], sm.beta[t], 0.f, 0.f);
-            *reinterpret_cast<float4*>(prow + c4) = v4;
-          }
-        }
       }
       __syncthreads();
       // 7. RMSNormGated over dv per token: w·round(x̂) · silu(z), x = round(core)
@@ -398,7 +382,7 @@ gdn_verify_kernel(const qsp_gdn_layer L) {
       }
       const bool last = t0 + nt >= T_;
       if (last) {
-        if (!spec) write_hist_rows(nt, K - 1);   // the window after the last token
+        write_hist_rows(nt, K - 1);   // the window after the last token
       } else {
         // slide the window (last K-1 combined rows to the front) and stage the next block;
         // source and destination rows may overlap: read everything, barrier, then write
@@ -423,7 +407,480 @@ gdn_verify_kernel(const qsp_gdn_layer L) {
       }
     }
 
-    if (!spec) store_state();
+    store_state();
+    __syncthreads();   // the next unit's staging overwrites the inputs
+  }
+}
+
+// ------------------------------------------------------------------ token ring
+// Per layer, `pending` holds [2 parity][B][Ts slots] rows; row (p, b, t) describes token t
+// of the call that wrote parity p:
+//   q̂ [Hk·dk] | k̂ [Hk·dk] | v [Hv·dv]      model dtype (q̂ before the dk^-1/2 scale)
+//   (16-byte pad) fp32 tail:
+//   Gkk [Hk][8]   k_s·k_t for s < t           Gkq [Hk][8]   k_s·(dk^-1/2 q_t) for s <= t
+//   d [Hv]        β [Hv]                      d = e^g, g = −exp(A_log)·softplus(a + dt_bias)
+// A speculative call writes the slot of parity^1 and replays kept tokens from parity.
+struct GdnRing {
+  int64_t pitch;      // bytes per row
+  int64_t f32_off;    // byte offset of the fp32 tail
+  int off_k, off_v;   // element offsets of k̂ and v
+  int off_gkk, off_gkq, off_d, off_beta;   // float offsets inside the tail
+};
+
+inline GdnRing gdn_ring(int Hk, int Hv, int DK, int DV, int esz) {
+  GdnRing r;
+  const int64_t vec = (int64_t)(2 * Hk * DK + Hv * DV) * esz;
+  r.f32_off = (vec + 15) / 16 * 16;
+  const int64_t nf = 2 * Hk * GDN_TB + 2 * Hv;
+  r.pitch = r.f32_off + (nf * 4 + 15) / 16 * 16;
+  r.off_k = Hk * DK;
+  r.off_v = 2 * Hk * DK;
+  r.off_gkk = 0;
+  r.off_gkq = Hk * GDN_TB;
+  r.off_d = 2 * Hk * GDN_TB;
+  r.off_beta = 2 * Hk * GDN_TB + Hv;
+  return r;
+}
+
+__device__ __forceinline__ void gcp4(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(gsm(dst)), "l"(src) : "memory");
+}
+
+// ------------------------------------------------------------------ prep
+// One CTA per (sequence b, key head kh): the q and k channels of kh and the v channels of its
+// v_per_k value heads. Every input (conv window, token rows, conv weights) is staged into
+// shared memory with cp.async first, so the CTA waits for global memory once. Arithmetic per
+// element is the reference's: conv accumulated in fp32 and rounded like F.conv1d, SiLU
+// rounded, l2norm x·rsqrt(Σx² + 1e-6) with each op rounded to the model dtype.
+// Dynamic shared memory: xr [K-1+T][nchg] T | cwr [nchg][K] T | qk [T][2·dk] fp32.
+inline size_t gdn_prep_smem(int nchg, int K, int T, int DK, int esz) {
+  size_t a = (size_t)(K - 1 + T) * nchg * esz;
+  a = (a + 15) / 16 * 16;
+  size_t b = (size_t)nchg * K * esz;
+  b = (b + 15) / 16 * 16;
+  return a + b + (size_t)(T > 0 ? T : 1) * 2 * DK * 4;
+}
+
+template <typename T, int DK, int DV>
+__global__ void __launch_bounds__(256) gdn_prep_kernel(const qsp_gdn_layer L, const GdnRing RG) {
+  extern __shared__ __align__(16) uint8_t gdn_prep_raw[];
+  constexpr int ESZ = (int)sizeof(T), EPV = 16 / ESZ;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+  const int Hk = L.n_k_heads, Hv = L.n_v_heads, vpk = Hv / Hk;
+  const int b = blockIdx.x / Hk, kh = blockIdx.x % Hk;
+  const int T_ = L.tokens, K = L.conv_kernel, Ts = L.max_spec_tokens;
+  const int key_dim = Hk * DK, conv_dim = 2 * key_dim + Hv * DV, value_dim = Hv * DV;
+  const int nchg = 2 * DK + vpk * DV;
+  const int nrows = K - 1 + T_;
+  const bool spec = L.speculative != 0;
+  T* xr = reinterpret_cast<T*>(gdn_prep_raw);
+  T* cwr = reinterpret_cast<T*>(gdn_prep_raw + ((size_t)nrows * nchg * ESZ + 15) / 16 * 16);
+  float* qk = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(cwr) + ((size_t)nchg * K * ESZ + 15) / 16 * 16);
+  const T* __restrict__ proj = static_cast<const T*>(L.proj);
+  const T* __restrict__ cw = static_cast<const T*>(L.conv_w);
+  T* hist = static_cast<T*>(L.conv_hist);
+  const int par = L.parity[0];
+  const int coff = min(max(L.conv_off[b], 0), Ts);
+  const int hist_rows = K - 1 + Ts;
+  const T* hin = hist + ((int64_t)par * L.batch + b) * hist_rows * conv_dim;
+  T* hout = hist + ((int64_t)(par ^ 1) * L.batch + b) * hist_rows * conv_dim;
+  uint8_t* ring = static_cast<uint8_t*>(L.pending) + ((int64_t)(par ^ 1) * L.batch + b) * Ts * RG.pitch;
+  auto vrow = [&](int t) { return reinterpret_cast<T*>(ring + (int64_t)t * RG.pitch); };
+  auto frow = [&](int t) { return reinterpret_cast<float*>(ring + (int64_t)t * RG.pitch + RG.f32_off); };
+  // global channel of local channel c (q of kh | k of kh | v of the group's heads)
+  auto gch = [&](int c) -> int {
+    return c < DK ? kh * DK + c : (c < 2 * DK ? key_dim + kh * DK + (c - DK) : 2 * key_dim + kh * vpk * DV + (c - 2 * DK));
+  };
+
+  // 1. stage: window rows, token rows, conv weights (16-byte chunks, all in flight)
+  const int cpr = nchg / EPV;   // chunks per row (segments are multiples of 16 bytes)
+  for (int e = tid; e < nrows * cpr; e += blockDim.x) {
+    const int i = e / cpr, c = (e % cpr) * EPV;
+    const T* src = i < K - 1 ? hin + (int64_t)(coff + i) * conv_dim + gch(c)
+                             : proj + (int64_t)(b * T_ + i - (K - 1)) * L.ld_proj + gch(c);
+    gcp16(xr + (int64_t)i * nchg + c, src);
+  }
+  for (int e = tid; e < nchg * K / EPV; e += blockDim.x) {
+    const int c = e * EPV / K;   // first channel of the chunk; a chunk never crosses a segment
+    gcp16(cwr + (int64_t)e * EPV, cw + (int64_t)gch(c) * K + (e * EPV - c * K));
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  // gates of the group's value heads (scalar loads, in flight with the copies)
+  float gate_g = 0.f, gate_b = 0.f;
+  int gate_t = -1, gate_h = 0;
+  if (tid < vpk * T_) {
+    gate_t = tid / vpk;
+    gate_h = kh * vpk + tid % vpk;
+    const T* prow = proj + (int64_t)(b * T_ + gate_t) * L.ld_proj + conv_dim + value_dim;
+    const float bb = dt<T>::to_f(prow[gate_h]), aa = dt<T>::to_f(prow[Hv + gate_h]);
+    const float A = -expf(dt<T>::to_f(static_cast<const T*>(L.a_log)[gate_h]));
+    const float dtb = dt<T>::to_f(static_cast<const T*>(L.dt_bias)[gate_h]);
+    gate_g = expf(A * softplusf_(aa + dtb));   // the per-token decay d = e^g
+    gate_b = dt<T>::round(sigmoidf_(bb));
+  }
+  asm volatile("cp.async.wait_all;" ::: "memory");
+  __syncthreads();
+
+  // 2. conv-history ring: spec keeps window + tokens (the next call starts at row keep),
+  //    commit keeps the window after the last token
+  {
+    const int r0 = spec ? 0 : T_, nr = spec ? nrows : K - 1;
+    for (int e = tid; e < nr * cpr; e += blockDim.x) {
+      const int i = e / cpr, c = (e % cpr) * EPV;
+      *reinterpret_cast<uint4*>(hout + (int64_t)i * conv_dim + gch(c)) =
+          *reinterpret_cast<const uint4*>(xr + (int64_t)(r0 + i) * nchg + c);
+    }
+  }
+  // 3. conv + SiLU
+  for (int e = tid; e < nchg * T_; e += blockDim.x) {
+    const int t = e / nchg, c = e % nchg;
+    float acc = 0.f;
+    for (int jj = 0; jj < K; ++jj)
+      acc = fmaf(dt<T>::to_f(cwr[c * K + jj]), dt<T>::to_f(xr[(int64_t)(t + jj) * nchg + c]), acc);
+    const float a = dt<T>::round(siluf_(dt<T>::round(acc)));
+    if (c < 2 * DK) qk[t * 2 * DK + c] = a;
+    else vrow(t)[RG.off_v + kh * vpk * DV + (c - 2 * DK)] = dt<T>::from_f(a);
+  }
+  if (gate_t >= 0) {
+    frow(gate_t)[RG.off_d + gate_h] = gate_g;
+    frow(gate_t)[RG.off_beta + gate_h] = gate_b;
+  }
+  __syncthreads();
+  // 4. l2norm of q and k, one warp per vector
+  const float qscale = (float)(1.0 / sqrt((double)DK));   // dk^-0.5 rounded once to fp32
+  for (int vi = warp; vi < 2 * T_; vi += nw) {
+    const int t = vi >> 1;
+    const bool isk = vi & 1;
+    float* xv = qk + t * 2 * DK + (isk ? DK : 0);
+    float ss = 0.f;
+    for (int i = lane; i < DK; i += 32) ss += dt<T>::round(xv[i] * xv[i]);
+    ss = warp_sum(ss);
+    const float sq = dt<T>::round(dt<T>::round(ss) + 1e-6f);
+    const float r = dt<T>::round(rsqrtf(sq));
+    T* dst = vrow(t) + (isk ? RG.off_k : 0) + kh * DK;
+    for (int i = lane; i < DK; i += 32) {
+      const float y = dt<T>::round(xv[i] * r);
+      dst[i] = dt<T>::from_f(y);
+      xv[i] = isk ? y : y * qscale;
+    }
+  }
+  __syncthreads();
+  // 5. Gram products of the call's tokens (fixed summation order: they are replayed later)
+  const int nkk = T_ * (T_ - 1) / 2, nkq = T_ * (T_ + 1) / 2;
+  for (int e = warp; e < nkk + nkq; e += nw) {
+    int s, t;
+    const bool isq = e >= nkk;
+    if (!isq) {   // pairs s < t, t = 1..T-1
+      int rem = e;
+      t = 1;
+      while (rem >= t) { rem -= t; ++t; }
+      s = rem;
+    } else {      // pairs s <= t, t = 0..T-1
+      int rem = e - nkk;
+      t = 0;
+      while (rem >= t + 1) { rem -= t + 1; ++t; }
+      s = rem;
+    }
+    const float* ks = qk + s * 2 * DK + DK;
+    const float* o = qk + t * 2 * DK + (isq ? 0 : DK);
+    float acc = 0.f;
+    for (int i = lane; i < DK; i += 32) acc = fmaf(ks[i], o[i], acc);
+    acc = warp_sum(acc);
+    if (lane == 0) frow(t)[(isq ? RG.off_gkq : RG.off_gkk) + kh * GDN_TB + s] = acc;
+  }
+}
+
+// ------------------------------------------------------------------ chunked update
+// Column j of the state evolves on its own: with d_s = e^{g_s}, Γ(r, s) = d_{r+1}···d_s and
+// P_s = (S_0ᵀk_s)_j, Q_t = (S_0ᵀq_t)_j over the call's tokens s, t:
+//   δ_s = β_s·(v_s − Γ(−1, s)·P_s − Σ_{r<s} Γ(r, s)(k_r·k_s)·δ_r)
+//   o_t = Γ(−1, t)·Q_t + Σ_{r<=t} Γ(r, t)(k_r·q_t)·δ_r
+//   S_n = Γ(−1, n−1)·S_0 + Σ_s Γ(s, n−1)·k_s δ_sᵀ
+// which is the reference's token-by-token recurrence (S ← S·d; δ = (v − Sᵀk)β; S += kδᵀ;
+// o = Sᵀq) reassociated. Every quantity is computed by one fixed formula from the tokens up
+// to it, so the replay of kept tokens reproduces a fresh forward over them bit for bit.
+template <typename T, int DK, int DV>
+struct __align__(128) GdnChunkSmem {
+  float sst[DK * DV];                 // state of the next unit (TMA bulk prefetch target)
+  float kq[6][DK / 2][8];             // vector slots as fp32 row pairs: group g, pair p, 4 slots x 2
+  T kraw[2 * GDN_TB][DK];             // k̂ rows: replay 0..7, new 8..15
+  T qraw[GDN_TB][DK];
+  T vraw[2 * GDN_TB][DV];
+  T zraw[GDN_TB][DV];
+  float gkk[2 * GDN_TB][GDN_TB];
+  float gkq[GDN_TB][GDN_TB];
+  float gb[2 * GDN_TB][2];            // d = e^g, β
+  float tabA[2][GDN_TB][GDN_TB];      // Γ(r, s)·k_r·k_s   (replay, new)
+  float tabB[GDN_TB][GDN_TB];         // Γ(r, t)·k_r·q_t   (new)
+  float gam[2][GDN_TB];               // Γ(−1, s)
+  float tail[2][GDN_TB];              // Γ(s, n−1)
+  float red[(DV + 31) / 32][GDN_TB];
+  uint64_t bar;
+};
+
+__device__ __forceinline__ float gdn_fin(uint64_t a, uint64_t c) {
+  const float2 x = upk2(a), y = upk2(c);
+  return __fadd_rn(__fadd_rn(x.x, x.y), __fadd_rn(y.x, y.y));
+}
+
+// P[i] = Σ_rows S[row]·x_i[row] for the 4 vector slots of one group
+template <int DK>
+__device__ __forceinline__ void gdn_dot4(const uint64_t (&S)[DK / 2], const float* __restrict__ grp, float* P) {
+  uint64_t a0 = 0, a1 = 0, a2 = 0, a3 = 0, c0 = 0, c1 = 0, c2 = 0, c3 = 0;
+#pragma unroll
+  for (int p = 0; p < DK / 2; ++p) {
+    const ulonglong2 lo = *reinterpret_cast<const ulonglong2*>(grp + p * 8);
+    const ulonglong2 hi = *reinterpret_cast<const ulonglong2*>(grp + p * 8 + 4);
+    if (p & 1) {
+      c0 = ffma2(S[p], lo.x, c0); c1 = ffma2(S[p], lo.y, c1);
+      c2 = ffma2(S[p], hi.x, c2); c3 = ffma2(S[p], hi.y, c3);
+    } else {
+      a0 = ffma2(S[p], lo.x, a0); a1 = ffma2(S[p], lo.y, a1);
+      a2 = ffma2(S[p], hi.x, a2); a3 = ffma2(S[p], hi.y, a3);
+    }
+  }
+  P[0] = gdn_fin(a0, c0);
+  P[1] = gdn_fin(a1, c1);
+  P[2] = gdn_fin(a2, c2);
+  P[3] = gdn_fin(a3, c3);
+}
+
+// S ← γ·S + Σ_{s<n} c_s·x_s, x_s = slot s of the two groups starting at grp (terms added in
+// order of s)
+template <int DK>
+__device__ __forceinline__ void gdn_rank_update(uint64_t (&S)[DK / 2], const float* __restrict__ grp, float gamma,
+                                                const float (&c)[GDN_TB], int n) {
+  const uint64_t gg = pk2(gamma, gamma);
+#pragma unroll
+  for (int p = 0; p < DK / 2; ++p) S[p] = fmul2(S[p], gg);
+#pragma unroll 1
+  for (int s = 0; s < n; ++s) {
+    float cs = c[0];
+#pragma unroll
+    for (int i = 1; i < GDN_TB; ++i) cs = s == i ? c[i] : cs;
+    const uint64_t cc = pk2(cs, cs);
+    const float* xs = grp + (s / 4) * (DK / 2) * 8 + (s % 4) * 2;
+#pragma unroll
+    for (int p = 0; p < DK / 2; ++p) S[p] = ffma2(*reinterpret_cast<const uint64_t*>(xs + p * 8), cc, S[p]);
+  }
+}
+
+// δ_s for this column over n tokens
+template <typename T, int DV>
+__device__ __forceinline__ void gdn_deltas(const float (&P)[GDN_TB], const T* vcol, const float (*gb)[2],
+                                           const float (*A)[GDN_TB], const float* gam, int n, float (&dl)[GDN_TB]) {
+#pragma unroll
+  for (int s = 0; s < GDN_TB; ++s) {
+    dl[s] = 0.f;
+    if (s < n) {
+      float acc = __fmul_rn(gam[s], P[s]);
+#pragma unroll
+      for (int r = 0; r < s; ++r) acc = __fmaf_rn(A[r][s], dl[r], acc);
+      dl[s] = __fmul_rn(__fsub_rn(dt<T>::to_f(vcol[s * DV]), acc), gb[s][1]);
+    }
+  }
+}
+
+// Persistent: CTA c handles (sequence, value head) units c, c+G, ... ; one thread per state
+// column. While a unit computes, the next unit's state streams into shared memory.
+template <typename T, int DK, int DV>
+__global__ void __launch_bounds__(DV, 2)
+gdn_chunk_kernel(const qsp_gdn_layer L, const GdnRing RG, const int n_new) {
+  using SM = GdnChunkSmem<T, DK, DV>;
+  extern __shared__ __align__(128) uint8_t gdn_chunk_raw[];
+  SM& sm = *reinterpret_cast<SM*>(gdn_chunk_raw);
+  constexpr int P2 = DK / 2;
+  constexpr int ESZ = (int)sizeof(T);
+  constexpr int CK = DK * ESZ / 16, CV = DV * ESZ / 16;   // 16-byte chunks per row
+  const int j = threadIdx.x, lane = j & 31, warp = j >> 5;
+  const int Hk = L.n_k_heads, Hv = L.n_v_heads, vpk = Hv / Hk;
+  const int Ts = L.max_spec_tokens;
+  const int conv_dim = 2 * Hk * DK + Hv * DV;
+  const bool spec = L.speculative != 0;
+  const int par = L.parity[0];
+  const int units = L.batch * Hv;
+  const int N = n_new;
+  const float qscale = (float)(1.0 / sqrt((double)DK));
+  const uint8_t* ring = static_cast<const uint8_t*>(L.pending);
+  const T* proj = static_cast<const T*>(L.proj);
+  T* out = static_cast<T*>(L.out);
+  const float wn = dt<T>::to_f(static_cast<const T*>(L.norm_w)[j]);
+  constexpr uint32_t SBYTES = DK * DV * 4;
+
+  if (j == 0) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(gsm(&sm.bar)) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  if (j == 0 && blockIdx.x < units)
+    gdn_prefetch_state(sm.sst, L.state + (int64_t)blockIdx.x * DK * DV, &sm.bar, SBYTES);
+
+  uint32_t it = 0;
+  for (int u = blockIdx.x; u < units; u += gridDim.x, ++it) {
+    const int b = u / Hv, h = u % Hv, kh = h / vpk;
+    const int R = min(max(L.replay_n[b], 0), Ts);
+    const uint8_t* rowR = ring + ((int64_t)par * L.batch + b) * Ts * RG.pitch;
+    const uint8_t* rowN = ring + ((int64_t)(par ^ 1) * L.batch + b) * Ts * RG.pitch;
+    float* state = L.state + (int64_t)u * DK * DV;
+
+    // 1. stage this unit's token rows (cp.async, all in flight at once)
+    for (int e = j; e < R * CK; e += DV)
+      gcp16(reinterpret_cast<uint8_t*>(sm.kraw[e / CK]) + (e % CK) * 16,
+            rowR + (e / CK) * RG.pitch + (int64_t)(RG.off_k + kh * DK) * ESZ + (e % CK) * 16);
+    for (int e = j; e < R * CV; e += DV)
+      gcp16(reinterpret_cast<uint8_t*>(sm.vraw[e / CV]) + (e % CV) * 16,
+            rowR + (e / CV) * RG.pitch + (int64_t)(RG.off_v + h * DV) * ESZ + (e % CV) * 16);
+    for (int e = j; e < N * CK; e += DV) {
+      const uint8_t* src = rowN + (e / CK) * RG.pitch + (e % CK) * 16;
+      gcp16(reinterpret_cast<uint8_t*>(sm.kraw[GDN_TB + e / CK]) + (e % CK) * 16, src + (int64_t)(RG.off_k + kh * DK) * ESZ);
+      gcp16(reinterpret_cast<uint8_t*>(sm.qraw[e / CK]) + (e % CK) * 16, src + (int64_t)(kh * DK) * ESZ);
+    }
+    for (int e = j; e < N * CV; e += DV) {
+      const int t = e / CV, c = e % CV;
+      gcp16(reinterpret_cast<uint8_t*>(sm.vraw[GDN_TB + t]) + c * 16,
+            rowN + t * RG.pitch + (int64_t)(RG.off_v + h * DV) * ESZ + c * 16);
+      gcp16(reinterpret_cast<uint8_t*>(sm.zraw[t]) + c * 16,
+            reinterpret_cast<const uint8_t*>(proj + (int64_t)(b * N + t) * L.ld_proj + conv_dim + h * DV) + c * 16);
+    }
+    for (int e = j; e < 2 * R + 4 * N; e += DV) {   // Gram rows: 32 bytes = 2 chunks each
+      const int c = e & 1, r = e >> 1;
+      if (r < R) {
+        gcp16(reinterpret_cast<uint8_t*>(sm.gkk[r]) + c * 16,
+              rowR + r * RG.pitch + RG.f32_off + (int64_t)(RG.off_gkk + kh * GDN_TB) * 4 + c * 16);
+      } else if (r < R + N) {
+        const int t = r - R;
+        gcp16(reinterpret_cast<uint8_t*>(sm.gkk[GDN_TB + t]) + c * 16,
+              rowN + t * RG.pitch + RG.f32_off + (int64_t)(RG.off_gkk + kh * GDN_TB) * 4 + c * 16);
+      } else {
+        const int t = r - R - N;
+        gcp16(reinterpret_cast<uint8_t*>(sm.gkq[t]) + c * 16,
+              rowN + t * RG.pitch + RG.f32_off + (int64_t)(RG.off_gkq + kh * GDN_TB) * 4 + c * 16);
+      }
+    }
+    for (int e = j; e < 2 * (R + N); e += DV) {     // d, β
+      const int w = e & 1, r = e >> 1;
+      const uint8_t* base = r < R ? rowR + r * RG.pitch : rowN + (r - R) * RG.pitch;
+      gcp4(&sm.gb[r < R ? r : GDN_TB + r - R][w], base + RG.f32_off + (int64_t)((w ? RG.off_beta : RG.off_d) + h) * 4);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+
+    // 2. this unit's state: prefetched into shared memory → registers (column j)
+    gdn_wait(&sm.bar, it & 1u);
+    uint64_t S[P2];
+#pragma unroll
+    for (int p = 0; p < P2; ++p) S[p] = pk2(sm.sst[(2 * p) * DV + j], sm.sst[(2 * p + 1) * DV + j]);
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    __syncthreads();   // inputs staged; sst consumed
+    if (j == 0 && u + (int)gridDim.x < units)
+      gdn_prefetch_state(sm.sst, L.state + (int64_t)(u + gridDim.x) * DK * DV, &sm.bar, SBYTES);
+
+    // 3. fp32 vector slots (replay k 0..7, new k 8..15, scaled new q 16..23) and the tables
+    for (int e = j; e < 3 * GDN_TB * CK; e += DV) {
+      const int v = e / CK, c = e % CK;   // vector slot, 16-byte chunk of it
+      const T* src;
+      float sc = 1.f;
+      if (v < GDN_TB) {
+        if (v >= R) continue;
+        src = sm.kraw[v];
+      } else if (v < 2 * GDN_TB) {
+        if (v - GDN_TB >= N) continue;
+        src = sm.kraw[v];
+      } else {
+        if (v - 2 * GDN_TB >= N) continue;
+        src = sm.qraw[v - 2 * GDN_TB];
+        sc = qscale;
+      }
+      constexpr int EPV = 16 / ESZ;
+      float x[EPV];
+      load16_as_float<T>(src + c * EPV, x);
+#pragma unroll
+      for (int i = 0; i < EPV / 2; ++i) {
+        const int p = c * (EPV / 2) + i;
+        *reinterpret_cast<float2*>(&sm.kq[v / 4][p][(v % 4) * 2]) = make_float2(x[2 * i] * sc, x[2 * i + 1] * sc);
+      }
+    }
+    for (int e = j; e < 2 * (GDN_TB + 1) * GDN_TB; e += DV) {
+      const int ch = e / ((GDN_TB + 1) * GDN_TB);           // 0 replay, 1 new
+      const int r = (e / GDN_TB) % (GDN_TB + 1) - 1, s = e % GDN_TB;
+      const int n = ch ? N : R, row0 = ch ? GDN_TB : 0;
+      if (s >= n || r > s) continue;
+      float ratio = 1.f;                                      // Γ(r, s) = d_{r+1}···d_s
+      for (int i = r + 1; i <= s; ++i) ratio = __fmul_rn(ratio, sm.gb[row0 + i][0]);
+      if (r < 0) sm.gam[ch][s] = ratio;
+      if (r >= 0 && r < s) sm.tabA[ch][r][s] = __fmul_rn(ratio, sm.gkk[row0 + s][r]);
+      if (ch == 1 && r >= 0) sm.tabB[r][s] = __fmul_rn(ratio, sm.gkq[s][r]);
+      if (r >= 0 && s == n - 1) sm.tail[ch][r] = ratio;
+    }
+    __syncthreads();
+
+    auto store_state = [&]() {
+#pragma unroll
+      for (int p = 0; p < P2; ++p) {
+        const float2 v = upk2(S[p]);
+        state[(int64_t)(2 * p) * DV + j] = v.x;
+        state[(int64_t)(2 * p + 1) * DV + j] = v.y;
+      }
+    };
+    // 4. replay the kept tokens of the previous speculative call
+    if (R > 0) {
+      float P[GDN_TB], dl[GDN_TB], c[GDN_TB];
+      gdn_dot4<DK>(S, &sm.kq[0][0][0], P);
+      if (R > 4) gdn_dot4<DK>(S, &sm.kq[1][0][0], P + 4);
+      gdn_deltas<T, DV>(P, &sm.vraw[0][j], sm.gb, sm.tabA[0], sm.gam[0], R, dl);
+#pragma unroll
+      for (int s = 0; s < GDN_TB; ++s) c[s] = s < R ? __fmul_rn(sm.tail[0][s], dl[s]) : 0.f;
+      gdn_rank_update<DK>(S, &sm.kq[0][0][0], sm.gam[0][R - 1], c, R);
+      if (spec || N == 0) store_state();
+    }
+    // 5. this call's tokens
+    if (N > 0) {
+      float Pk[GDN_TB], Pq[GDN_TB], dl[GDN_TB], o[GDN_TB];
+      gdn_dot4<DK>(S, &sm.kq[2][0][0], Pk);
+      gdn_dot4<DK>(S, &sm.kq[4][0][0], Pq);
+      if (N > 4) {
+        gdn_dot4<DK>(S, &sm.kq[3][0][0], Pk + 4);
+        gdn_dot4<DK>(S, &sm.kq[5][0][0], Pq + 4);
+      }
+      gdn_deltas<T, DV>(Pk, &sm.vraw[GDN_TB][j], sm.gb + GDN_TB, sm.tabA[1], sm.gam[1], N, dl);
+#pragma unroll
+      for (int t = 0; t < GDN_TB; ++t) {
+        o[t] = 0.f;
+        if (t < N) {
+          float acc = __fmul_rn(sm.gam[1][t], Pq[t]);
+#pragma unroll
+          for (int r = 0; r <= t; ++r) acc = __fmaf_rn(sm.tabB[r][t], dl[r], acc);
+          o[t] = acc;
+        }
+      }
+      if (!spec) {
+        float c[GDN_TB];
+#pragma unroll
+        for (int s = 0; s < GDN_TB; ++s) c[s] = s < N ? __fmul_rn(sm.tail[1][s], dl[s]) : 0.f;
+        gdn_rank_update<DK>(S, &sm.kq[2][0][0], sm.gam[1][N - 1], c, N);
+        store_state();
+      }
+      // 6. RMSNormGated over the dv columns of each token: w·round(x̂)·silu(z), x = round(core)
+#pragma unroll
+      for (int t = 0; t < GDN_TB; ++t) {
+        if (t < N) {
+          const float x = dt<T>::round(o[t]);
+          const float ss = warp_sum(x * x);
+          if (lane == 0) sm.red[warp][t] = ss;
+        }
+      }
+      __syncthreads();
+#pragma unroll
+      for (int t = 0; t < GDN_TB; ++t) {
+        if (t < N) {
+          float ss = 0.f;
+          for (int w = 0; w < (DV + 31) / 32; ++w) ss += sm.red[w][t];
+          const float inv = rsqrtf(ss / (float)DV + L.eps);
+          const float xh = dt<T>::round(dt<T>::round(o[t]) * inv);
+          const float wx = dt<T>::round(wn * xh);
+          out[(int64_t)(b * N + t) * L.ld_out + h * DV + j] = dt<T>::from_f(wx * siluf_(dt<T>::to_f(sm.zraw[t][j])));
+        }
+      }
+    }
     __syncthreads();   // the next unit's staging overwrites the inputs
   }
 }
@@ -439,20 +896,53 @@ static int sm_count_gdn() {
   return n;
 }
 
-template <typename T, int DK, int DV>
-static int launch_gdn_dims(const qsp_gdn_layer& L, cudaStream_t st) {
-  auto kern = gdn_verify_kernel<T, DK, DV>;
-  const size_t smem = sizeof(GdnSmem<T, DK, DV>);
-  static bool set = false;
-  if (!set) {
+template <typename K>
+static int reserve_smem(K kern, size_t smem, bool& done) {
+  if (!done) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
       return set_error(QSP_ERR_CUDA, "qsp_gdn_verify: cannot reserve %zu bytes of shared memory", smem);
-    set = true;
+    done = true;
   }
+  return QSP_OK;
+}
+
+template <typename T, int DK, int DV>
+static int launch_gdn_dims(const qsp_gdn_layer& L, cudaStream_t st) {
+  const GdnRing RG = gdn_ring(L.n_k_heads, L.n_v_heads, DK, DV, (int)sizeof(T));
   const int units = L.batch * L.n_v_heads;
   const int grid = std::min(units, 2 * sm_count_gdn());
-  kern<<<grid, DV, smem, st>>>(L);
-  return check_launch("qsp_gdn_verify");
+  auto chunk = gdn_chunk_kernel<T, DK, DV>;
+  const size_t csmem = sizeof(GdnChunkSmem<T, DK, DV>);
+  static bool chunk_set = false;
+  int rc = reserve_smem(chunk, csmem, chunk_set);
+  if (rc) return rc;
+  if (L.tokens <= L.max_spec_tokens) {
+    const int nchg = 2 * DK + (L.n_v_heads / L.n_k_heads) * DV;
+    const size_t psmem = gdn_prep_smem(nchg, L.conv_kernel, L.tokens, DK, (int)sizeof(T));
+    auto prep = gdn_prep_kernel<T, DK, DV>;
+    static size_t prep_set = 0;
+    if (psmem > prep_set) {
+      if (cudaFuncSetAttribute(prep, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)psmem) != cudaSuccess)
+        return set_error(QSP_ERR_CUDA, "qsp_gdn_verify: cannot reserve %zu bytes of shared memory", psmem);
+      prep_set = psmem;
+    }
+    prep<<<L.batch * L.n_k_heads, 256, psmem, st>>>(L, RG);
+    rc = check_launch("qsp_gdn_verify(prep)");
+    if (rc) return rc;
+    chunk<<<grid, DV, csmem, st>>>(L, RG, L.tokens);
+    return check_launch("qsp_gdn_verify(chunk)");
+  }
+  // long commit call: replay kept tokens into the state, then step through the tokens
+  chunk<<<grid, DV, csmem, st>>>(L, RG, 0);
+  rc = check_launch("qsp_gdn_verify(replay)");
+  if (rc) return rc;
+  auto seq = gdn_seq_kernel<T, DK, DV>;
+  const size_t ssmem = sizeof(GdnSmem<T, DK, DV>);
+  static bool seq_set = false;
+  rc = reserve_smem(seq, ssmem, seq_set);
+  if (rc) return rc;
+  seq<<<grid, DV, ssmem, st>>>(L);
+  return check_launch("qsp_gdn_verify(seq)");
 }
 
 template <typename T>
@@ -497,9 +987,19 @@ extern "C" int qsp_gdn_verify(const qsp_gdn_layer* layer, void* stream) {
   QSP_REQUIRE(L.ld_proj >= conv_dim + (int64_t)L.n_v_heads * L.head_v + 2 * L.n_v_heads,
               "qsp_gdn_verify: ld_proj too small");
   QSP_REQUIRE(L.ld_out >= (int64_t)L.n_v_heads * L.head_v, "qsp_gdn_verify: ld_out too small");
-  QSP_REQUIRE(aligned(L.state, 16) && aligned(L.pending, 16) && aligned(L.proj, 16) && aligned(L.conv_hist, 16),
-              "qsp_gdn_verify: state/pending/proj/conv_hist must be 16-byte aligned");
+  QSP_REQUIRE(aligned(L.state, 16) && aligned(L.pending, 16) && aligned(L.proj, 16) && aligned(L.conv_hist, 16) &&
+                  aligned(L.conv_w, 16),
+              "qsp_gdn_verify: state/pending/proj/conv_hist/conv_w must be 16-byte aligned");
   const int esz = L.dtype == QSP_F32 ? 4 : 2;
   QSP_REQUIRE((L.ld_proj * esz) % 16 == 0, "qsp_gdn_verify: ld_proj must be a multiple of 16 bytes");
   QSP_DISPATCH_DTYPE(L.dtype, T, { return launch_gdn<T>(L, as_stream(stream)); });
+}
+
+extern "C" size_t qsp_gdn_pending_bytes(int32_t batch, int32_t n_k_heads, int32_t n_v_heads, int32_t head_k,
+                                        int32_t head_v, int32_t max_spec_tokens, int32_t dtype) {
+  if (batch <= 0 || n_k_heads <= 0 || n_v_heads <= 0 || head_k <= 0 || head_v <= 0 || max_spec_tokens <= 0)
+    return 0;
+  const int esz = dtype == QSP_F32 ? 4 : 2;
+  const GdnRing RG = gdn_ring(n_k_heads, n_v_heads, head_k, head_v, esz);
+  return (size_t)2 * batch * max_spec_tokens * RG.pitch;
 }

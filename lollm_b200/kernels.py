@@ -110,6 +110,15 @@ def gdn_verify(desc: L.GdnLayer):
     L.call("qsp_gdn_verify", C.byref(desc), _s())
 
 
+def gdn_pending_bytes(batch, n_k_heads, n_v_heads, head_k, head_v, max_spec_tokens, dtype) -> int:
+    """Bytes of one GDN layer's token ring (the `pending` buffer of qsp_gdn_verify)."""
+    n = int(L.load().qsp_gdn_pending_bytes(batch, n_k_heads, n_v_heads, head_k, head_v, max_spec_tokens,
+                                            L.dtype_code(dtype)))
+    if n <= 0:
+        raise RuntimeError("qsp_gdn_pending_bytes: invalid sizes")
+    return n
+
+
 def attn_prep(desc: L.AttnLayer):
     L.call("qsp_attn_prep", C.byref(desc), _s())
 

@@ -11,8 +11,8 @@ kv.py:1-14 / modeling_qwen3_5.py:8-11):
 * every sequence has its own length (`seq_lens`, device int32) instead of one scalar
   `seen_tokens` (kv.py:23), so a batch can be ragged;
 * GDN layers keep the fp32 recurrent state [B, Hv, dk, dv] (the reference layout) plus a
-  ping-pong conv-input history and a per-token "pending update" buffer. A speculative
-  forward leaves its T tokens pending; `accept(keep)` keeps a prefix by index and the next
+  ping-pong conv-input history and a token ring of prepared per-token inputs (`pending`,
+  sized by the library). A speculative forward leaves its T tokens pending; `accept(keep)` keeps a prefix by index and the next
   call replays exactly those tokens — no `clone()` snapshot and no recompute
   (mtp.py:141,156-162 is what this replaces). `flush()` materialises pending updates.
 
@@ -59,8 +59,8 @@ class Qwen3_5Cache:
         self.state = torch.zeros(n_gdn, batch, Hv, dk, dv, dtype=torch.float32, device=dev)
         self.conv_hist = torch.zeros(n_gdn, 2, batch, Kc - 1 + max_spec_tokens, cfg.conv_dim,
                                      dtype=dtype, device=dev)
-        self.pending = torch.zeros(n_gdn, batch, Hv, max_spec_tokens, dk + dv + 4,
-                                   dtype=torch.float32, device=dev)
+        ring = K.gdn_pending_bytes(batch, cfg.linear_num_key_heads, Hv, dk, dv, max_spec_tokens, dtype)
+        self.pending = torch.zeros(n_gdn, ring, dtype=torch.uint8, device=dev)
         self.replay_n = torch.zeros(batch, dtype=torch.int32, device=dev)
         self.conv_off = torch.zeros(batch, dtype=torch.int32, device=dev)
         self.parity = torch.zeros(1, dtype=torch.int32, device=dev)

@@ -116,7 +116,7 @@ class GdnCase:
         self.g = g
         self.state = torch.zeros(B, Hv, d, d, device=DEV)
         self.hist = torch.zeros(2, B, Kc - 1 + Ts, self.C, dtype=dt, device=DEV)
-        self.pending = torch.zeros(B, Hv, Ts, 2 * d + 4, device=DEV)
+        self.pending = torch.zeros(K().gdn_pending_bytes(B, Hk, Hv, d, d, Ts, dt), dtype=torch.uint8, device=DEV)
         self.replay = torch.zeros(B, dtype=torch.int32, device=DEV)
         self.coff = torch.zeros(B, dtype=torch.int32, device=DEV)
         self.parity = torch.zeros(1, dtype=torch.int32, device=DEV)
