@@ -413,37 +413,39 @@ gdn_seq_kernel(const qsp_gdn_layer L) {
 }
 
 // ------------------------------------------------------------------ token ring
-// Per layer, `pending` holds [2 parity][B][Ts slots] rows; row (p, b, t) describes token t
-// of the call that wrote parity p:
-//   q̂ [Hk·dk] | k̂ [Hk·dk] | v [Hv·dv]      model dtype (q̂ before the dk^-1/2 scale)
-//   (16-byte pad) fp32 tail:
-//   Gkk [Hk][8]   k_s·k_t for s < t           Gkq [Hk][8]   k_s·(dk^-1/2 q_t) for s <= t
-//   d [Hv]        β [Hv]                      d = e^g, g = −exp(A_log)·softplus(a + dt_bias)
-// A speculative call writes the slot of parity^1 and replays kept tokens from parity.
-struct GdnRing {
-  int64_t pitch;      // bytes per row
-  int64_t f32_off;    // byte offset of the fp32 tail
-  int off_k, off_v;   // element offsets of k̂ and v
-  int off_gkk, off_gkq, off_d, off_beta;   // float offsets inside the tail
+// Per layer, `pending` holds two arrays of per-(parity, sequence, value head, slot) records;
+// slot t describes token t of the call that wrote that parity:
+//   A: k̂ [dk] | v [dv] (model dtype) | Gkk [8] (k_s·k_t, s < t) | (d, β, 0, 0)   fp32 tail
+//   B: q̂ [dk] | z [dv] (model dtype) | Gkq [8] (k_s·(dk^-1/2 q_t), s <= t)         fp32 tail
+// with d = e^g, g = −exp(A_log)·softplus(a + dt_bias), q̂ before the dk^-1/2 scale. k̂, q̂ and
+// the Gram products belong to the key head and are repeated in each of its value heads'
+// records, so one unit's rows are contiguous: a speculative call writes the slots of
+// parity^1, and the next call replays kept tokens from the A records of parity.
+template <typename T, int DK, int DV>
+struct __align__(16) GdnRecA {
+  T k[DK];
+  T v[DV];
+  float gkk[GDN_TB];
+  float4 db;
+};
+template <typename T, int DK, int DV>
+struct __align__(16) GdnRecB {
+  T q[DK];
+  T z[DV];
+  float gkq[GDN_TB];
 };
 
-inline GdnRing gdn_ring(int Hk, int Hv, int DK, int DV, int esz) {
-  GdnRing r;
-  const int64_t vec = (int64_t)(2 * Hk * DK + Hv * DV) * esz;
-  r.f32_off = (vec + 15) / 16 * 16;
-  const int64_t nf = 2 * Hk * GDN_TB + 2 * Hv;
-  r.pitch = r.f32_off + (nf * 4 + 15) / 16 * 16;
-  r.off_k = Hk * DK;
-  r.off_v = 2 * Hk * DK;
-  r.off_gkk = 0;
-  r.off_gkq = Hk * GDN_TB;
-  r.off_d = 2 * Hk * GDN_TB;
-  r.off_beta = 2 * Hk * GDN_TB + Hv;
-  return r;
-}
+struct GdnRing {
+  int64_t recA, recB;   // bytes per record
+  int64_t offB;         // byte offset of array B
+};
 
-__device__ __forceinline__ void gcp4(void* dst, const void* src) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(gsm(dst)), "l"(src) : "memory");
+inline GdnRing gdn_ring(int batch, int Hv, int Ts, int DK, int DV, int esz) {
+  GdnRing r;
+  r.recA = (int64_t)(DK + DV) * esz + GDN_TB * 4 + 16;
+  r.recB = (int64_t)(DK + DV) * esz + GDN_TB * 4;
+  r.offB = 2ll * batch * Hv * Ts * r.recA;
+  return r;
 }
 
 // ------------------------------------------------------------------ prep
@@ -463,6 +465,8 @@ inline size_t gdn_prep_smem(int nchg, int K, int T, int DK, int esz) {
 
 template <typename T, int DK, int DV>
 __global__ void __launch_bounds__(256) gdn_prep_kernel(const qsp_gdn_layer L, const GdnRing RG) {
+  using RA = GdnRecA<T, DK, DV>;
+  using RB = GdnRecB<T, DK, DV>;
   extern __shared__ __align__(16) uint8_t gdn_prep_raw[];
   constexpr int ESZ = (int)sizeof(T), EPV = 16 / ESZ;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
@@ -484,9 +488,14 @@ __global__ void __launch_bounds__(256) gdn_prep_kernel(const qsp_gdn_layer L, co
   const int hist_rows = K - 1 + Ts;
   const T* hin = hist + ((int64_t)par * L.batch + b) * hist_rows * conv_dim;
   T* hout = hist + ((int64_t)(par ^ 1) * L.batch + b) * hist_rows * conv_dim;
-  uint8_t* ring = static_cast<uint8_t*>(L.pending) + ((int64_t)(par ^ 1) * L.batch + b) * Ts * RG.pitch;
-  auto vrow = [&](int t) { return reinterpret_cast<T*>(ring + (int64_t)t * RG.pitch); };
-  auto frow = [&](int t) { return reinterpret_cast<float*>(ring + (int64_t)t * RG.pitch + RG.f32_off); };
+  uint8_t* ring = static_cast<uint8_t*>(L.pending);
+  // records of (value head hh, slot t) written by this call
+  auto recA = [&](int hh, int t) {
+    return reinterpret_cast<RA*>(ring + ((((int64_t)(par ^ 1) * L.batch + b) * Hv + hh) * Ts + t) * RG.recA);
+  };
+  auto recB = [&](int hh, int t) {
+    return reinterpret_cast<RB*>(ring + RG.offB + ((((int64_t)(par ^ 1) * L.batch + b) * Hv + hh) * Ts + t) * RG.recB);
+  };
   // global channel of local channel c (q of kh | k of kh | v of the group's heads)
   auto gch = [&](int c) -> int {
     return c < DK ? kh * DK + c : (c < 2 * DK ? key_dim + kh * DK + (c - DK) : 2 * key_dim + kh * vpk * DV + (c - 2 * DK));
@@ -506,7 +515,7 @@ __global__ void __launch_bounds__(256) gdn_prep_kernel(const qsp_gdn_layer L, co
   }
   asm volatile("cp.async.commit_group;" ::: "memory");
   // gates of the group's value heads (scalar loads, in flight with the copies)
-  float gate_g = 0.f, gate_b = 0.f;
+  float gate_d = 0.f, gate_b = 0.f;
   int gate_t = -1, gate_h = 0;
   if (tid < vpk * T_) {
     gate_t = tid / vpk;
@@ -515,8 +524,15 @@ __global__ void __launch_bounds__(256) gdn_prep_kernel(const qsp_gdn_layer L, co
     const float bb = dt<T>::to_f(prow[gate_h]), aa = dt<T>::to_f(prow[Hv + gate_h]);
     const float A = -expf(dt<T>::to_f(static_cast<const T*>(L.a_log)[gate_h]));
     const float dtb = dt<T>::to_f(static_cast<const T*>(L.dt_bias)[gate_h]);
-    gate_g = expf(A * softplusf_(aa + dtb));   // the per-token decay d = e^g
+    gate_d = expf(A * softplusf_(aa + dtb));   // the per-token decay d = e^g
     gate_b = dt<T>::round(sigmoidf_(bb));
+  }
+  // output gate z of the group's heads: copied into the B records (16-byte chunks)
+  for (int e = tid; e < T_ * vpk * (DV / EPV); e += blockDim.x) {
+    const int t = e / (vpk * (DV / EPV)), r = e % (vpk * (DV / EPV));
+    const int hh = kh * vpk + r / (DV / EPV), c = (r % (DV / EPV)) * EPV;
+    *reinterpret_cast<uint4*>(recB(hh, t)->z + c) =
+        *reinterpret_cast<const uint4*>(proj + (int64_t)(b * T_ + t) * L.ld_proj + conv_dim + hh * DV + c);
   }
   asm volatile("cp.async.wait_all;" ::: "memory");
   __syncthreads();
@@ -539,12 +555,9 @@ __global__ void __launch_bounds__(256) gdn_prep_kernel(const qsp_gdn_layer L, co
       acc = fmaf(dt<T>::to_f(cwr[c * K + jj]), dt<T>::to_f(xr[(int64_t)(t + jj) * nchg + c]), acc);
     const float a = dt<T>::round(siluf_(dt<T>::round(acc)));
     if (c < 2 * DK) qk[t * 2 * DK + c] = a;
-    else vrow(t)[RG.off_v + kh * vpk * DV + (c - 2 * DK)] = dt<T>::from_f(a);
+    else recA(kh * vpk + (c - 2 * DK) / DV, t)->v[(c - 2 * DK) % DV] = dt<T>::from_f(a);
   }
-  if (gate_t >= 0) {
-    frow(gate_t)[RG.off_d + gate_h] = gate_g;
-    frow(gate_t)[RG.off_beta + gate_h] = gate_b;
-  }
+  if (gate_t >= 0) recA(gate_h, gate_t)->db = make_float4(gate_d, gate_b, 0.f, 0.f);
   __syncthreads();
   // 4. l2norm of q and k, one warp per vector
   const float qscale = (float)(1.0 / sqrt((double)DK));   // dk^-0.5 rounded once to fp32
@@ -557,10 +570,13 @@ __global__ void __launch_bounds__(256) gdn_prep_kernel(const qsp_gdn_layer L, co
     ss = warp_sum(ss);
     const float sq = dt<T>::round(dt<T>::round(ss) + 1e-6f);
     const float r = dt<T>::round(rsqrtf(sq));
-    T* dst = vrow(t) + (isk ? RG.off_k : 0) + kh * DK;
     for (int i = lane; i < DK; i += 32) {
       const float y = dt<T>::round(xv[i] * r);
-      dst[i] = dt<T>::from_f(y);
+      const T yt = dt<T>::from_f(y);
+      for (int g = 0; g < vpk; ++g) {
+        if (isk) recA(kh * vpk + g, t)->k[i] = yt;
+        else recB(kh * vpk + g, t)->q[i] = yt;
+      }
       xv[i] = isk ? y : y * qscale;
     }
   }
@@ -586,7 +602,10 @@ __global__ void __launch_bounds__(256) gdn_prep_kernel(const qsp_gdn_layer L, co
     float acc = 0.f;
     for (int i = lane; i < DK; i += 32) acc = fmaf(ks[i], o[i], acc);
     acc = warp_sum(acc);
-    if (lane == 0) frow(t)[(isq ? RG.off_gkq : RG.off_gkk) + kh * GDN_TB + s] = acc;
+    if (lane < vpk) {
+      if (isq) recB(kh * vpk + lane, t)->gkq[s] = acc;
+      else recA(kh * vpk + lane, t)->gkk[s] = acc;
+    }
   }
 }
 
@@ -599,75 +618,112 @@ __global__ void __launch_bounds__(256) gdn_prep_kernel(const qsp_gdn_layer L, co
 // which is the reference's token-by-token recurrence (S ← S·d; δ = (v − Sᵀk)β; S += kδᵀ;
 // o = Sᵀq) reassociated. Every quantity is computed by one fixed formula from the tokens up
 // to it, so the replay of kept tokens reproduces a fresh forward over them bit for bit.
+//
+// Thread (warp w, lane l) holds rows [dk/4·rg, dk/4·(rg+1)) of columns 4cg..4cg+3, rg = l>>3,
+// cg = 8w + (l&7), as packed pairs of adjacent rows. A pass over the state reads each vector
+// with 16-byte loads shared by the 8 lanes of a row block; the 4 row blocks are combined by a
+// butterfly after which lane l owns column 4cg + rg for the per-column recursion.
+template <typename T, int DK, int DV>
+struct __align__(16) GdnChunkIn {     // one unit's token records (filled by bulk copies)
+  GdnRecA<T, DK, DV> rep[GDN_TB];     // the previous call's tokens (replay)
+  GdnRecA<T, DK, DV> na[GDN_TB];      // this call's tokens
+  GdnRecB<T, DK, DV> nb[GDN_TB];
+};
+
 template <typename T, int DK, int DV>
 struct __align__(128) GdnChunkSmem {
   float sst[DK * DV];                 // state of the next unit (TMA bulk prefetch target)
-  float kq[6][DK / 2][8];             // vector slots as fp32 row pairs: group g, pair p, 4 slots x 2
-  T kraw[2 * GDN_TB][DK];             // k̂ rows: replay 0..7, new 8..15
-  T qraw[GDN_TB][DK];
-  T vraw[2 * GDN_TB][DV];
-  T zraw[GDN_TB][DV];
-  float gkk[2 * GDN_TB][GDN_TB];
-  float gkq[GDN_TB][GDN_TB];
-  float gb[2 * GDN_TB][2];            // d = e^g, β
+  float vec[3 * GDN_TB][DK];          // fp32 slots: replay k 0..7, new k 8..15, scaled new q 16..23
+  GdnChunkIn<T, DK, DV> in[2];        // double-buffered token records
   float tabA[2][GDN_TB][GDN_TB];      // Γ(r, s)·k_r·k_s   (replay, new)
   float tabB[GDN_TB][GDN_TB];         // Γ(r, t)·k_r·q_t   (new)
   float gam[2][GDN_TB];               // Γ(−1, s)
   float tail[2][GDN_TB];              // Γ(s, n−1)
   float red[(DV + 31) / 32][GDN_TB];
-  uint64_t bar;
+  uint64_t bar;                       // state prefetch
+  uint64_t ibar[2];                   // token records
 };
 
-__device__ __forceinline__ float gdn_fin(uint64_t a, uint64_t c) {
-  const float2 x = upk2(a), y = upk2(c);
-  return __fadd_rn(__fadd_rn(x.x, x.y), __fadd_rn(y.x, y.y));
-}
-
-// P[i] = Σ_rows S[row]·x_i[row] for the 4 vector slots of one group
+// Column sums over this thread's rows of S·x_v for 4 consecutive vector slots, reduced over
+// the 4 row blocks by a butterfly: on return own[v] = (Sᵀx_v) at column 4cg + rg.
 template <int DK>
-__device__ __forceinline__ void gdn_dot4(const uint64_t (&S)[DK / 2], const float* __restrict__ grp, float* P) {
-  uint64_t a0 = 0, a1 = 0, a2 = 0, a3 = 0, c0 = 0, c1 = 0, c2 = 0, c3 = 0;
+__device__ __forceinline__ void gdn_dots4(const uint64_t (&S)[4][DK / 8], const float* __restrict__ vec0, int rg,
+                                          float* own) {
+  constexpr int RB = DK / 4;
+  uint64_t acc[4][4];
 #pragma unroll
-  for (int p = 0; p < DK / 2; ++p) {
-    const ulonglong2 lo = *reinterpret_cast<const ulonglong2*>(grp + p * 8);
-    const ulonglong2 hi = *reinterpret_cast<const ulonglong2*>(grp + p * 8 + 4);
-    if (p & 1) {
-      c0 = ffma2(S[p], lo.x, c0); c1 = ffma2(S[p], lo.y, c1);
-      c2 = ffma2(S[p], hi.x, c2); c3 = ffma2(S[p], hi.y, c3);
-    } else {
-      a0 = ffma2(S[p], lo.x, a0); a1 = ffma2(S[p], lo.y, a1);
-      a2 = ffma2(S[p], hi.x, a2); a3 = ffma2(S[p], hi.y, a3);
+  for (int v = 0; v < 4; ++v)
+#pragma unroll
+    for (int c = 0; c < 4; ++c) acc[v][c] = 0;
+#pragma unroll
+  for (int m = 0; m < RB / 4; ++m) {
+#pragma unroll
+    for (int v = 0; v < 4; ++v) {
+      const ulonglong2 kk = *reinterpret_cast<const ulonglong2*>(vec0 + v * DK + RB * rg + 4 * m);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        acc[v][c] = ffma2(S[c][2 * m], kk.x, acc[v][c]);
+        acc[v][c] = ffma2(S[c][2 * m + 1], kk.y, acc[v][c]);
+      }
     }
   }
-  P[0] = gdn_fin(a0, c0);
-  P[1] = gdn_fin(a1, c1);
-  P[2] = gdn_fin(a2, c2);
-  P[3] = gdn_fin(a3, c3);
-}
-
-// S ← γ·S + Σ_{s<n} c_s·x_s, x_s = slot s of the two groups starting at grp (terms added in
-// order of s)
-template <int DK>
-__device__ __forceinline__ void gdn_rank_update(uint64_t (&S)[DK / 2], const float* __restrict__ grp, float gamma,
-                                                const float (&c)[GDN_TB], int n) {
-  const uint64_t gg = pk2(gamma, gamma);
+  const bool hi = rg & 2, lo = rg & 1;
 #pragma unroll
-  for (int p = 0; p < DK / 2; ++p) S[p] = fmul2(S[p], gg);
-#pragma unroll 1
-  for (int s = 0; s < n; ++s) {
-    float cs = c[0];
+  for (int v = 0; v < 4; ++v) {
+    float p[4];
 #pragma unroll
-    for (int i = 1; i < GDN_TB; ++i) cs = s == i ? c[i] : cs;
-    const uint64_t cc = pk2(cs, cs);
-    const float* xs = grp + (s / 4) * (DK / 2) * 8 + (s % 4) * 2;
-#pragma unroll
-    for (int p = 0; p < DK / 2; ++p) S[p] = ffma2(*reinterpret_cast<const uint64_t*>(xs + p * 8), cc, S[p]);
+    for (int c = 0; c < 4; ++c) {
+      const float2 x = upk2(acc[v][c]);
+      p[c] = __fadd_rn(x.x, x.y);
+    }
+    // rows blocks {0,2} ↔ {1,3} halves of the column group, then pairs
+    const float s0 = hi ? p[0] : p[2], s1 = hi ? p[1] : p[3];
+    float k0 = hi ? p[2] : p[0], k1 = hi ? p[3] : p[1];
+    k0 = __fadd_rn(k0, __shfl_xor_sync(0xffffffffu, s0, 16));
+    k1 = __fadd_rn(k1, __shfl_xor_sync(0xffffffffu, s1, 16));
+    const float snd = lo ? k0 : k1, keep = lo ? k1 : k0;
+    own[v] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, snd, 8));
   }
 }
 
-// δ_s for this column over n tokens
-template <typename T, int DV>
-__device__ __forceinline__ void gdn_deltas(const float (&P)[GDN_TB], const T* vcol, const float (*gb)[2],
+// S ← γ·S + Σ_{s<n} c_s·x_s (terms in order of s); c_s of column 4cg+c comes from lane
+// (c, cg), which owns that column's recursion.
+template <int DK>
+__device__ __forceinline__ void gdn_rank(uint64_t (&S)[4][DK / 8], const float* __restrict__ vec0, float gamma,
+                                         const float (&cown)[GDN_TB], int n, int rg, int lane) {
+  constexpr int RB = DK / 4;
+  const uint64_t gg = pk2(gamma, gamma);
+#pragma unroll
+  for (int c = 0; c < 4; ++c)
+#pragma unroll
+    for (int p = 0; p < RB / 2; ++p) S[c][p] = fmul2(S[c][p], gg);
+#pragma unroll 1
+  for (int s = 0; s < n; ++s) {
+    float cs = cown[0];
+#pragma unroll
+    for (int i = 1; i < GDN_TB; ++i) cs = s == i ? cown[i] : cs;
+    uint64_t cc[4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const float x = __shfl_sync(0xffffffffu, cs, (c << 3) | (lane & 7));
+      cc[c] = pk2(x, x);
+    }
+    const float* x = vec0 + s * DK + RB * rg;
+#pragma unroll
+    for (int m = 0; m < RB / 4; ++m) {
+      const ulonglong2 kk = *reinterpret_cast<const ulonglong2*>(x + 4 * m);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        S[c][2 * m] = ffma2(kk.x, cc[c], S[c][2 * m]);
+        S[c][2 * m + 1] = ffma2(kk.y, cc[c], S[c][2 * m + 1]);
+      }
+    }
+  }
+}
+
+// δ_s of this lane's column over n tokens (P = Sᵀk_s of the column, v_s from the records)
+template <typename T, int DK, int DV>
+__device__ __forceinline__ void gdn_deltas(const float (&P)[GDN_TB], const GdnRecA<T, DK, DV>* rec, int col,
                                            const float (*A)[GDN_TB], const float* gam, int n, float (&dl)[GDN_TB]) {
 #pragma unroll
   for (int s = 0; s < GDN_TB; ++s) {
@@ -676,172 +732,175 @@ __device__ __forceinline__ void gdn_deltas(const float (&P)[GDN_TB], const T* vc
       float acc = __fmul_rn(gam[s], P[s]);
 #pragma unroll
       for (int r = 0; r < s; ++r) acc = __fmaf_rn(A[r][s], dl[r], acc);
-      dl[s] = __fmul_rn(__fsub_rn(dt<T>::to_f(vcol[s * DV]), acc), gb[s][1]);
+      dl[s] = __fmul_rn(__fsub_rn(dt<T>::to_f(rec[s].v[col]), acc), rec[s].db.y);
     }
   }
 }
 
-// Persistent: CTA c handles (sequence, value head) units c, c+G, ... ; one thread per state
-// column. While a unit computes, the next unit's state streams into shared memory.
+__device__ __forceinline__ void gdn_bulk(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(gsm(dst)),
+               "l"(src), "r"(bytes), "r"(gsm(bar))
+               : "memory");
+}
+
+// Warp 0 stages unit u's records into `in` with three bulk copies completing on `bar`: the A
+// records of all Ts replay slots (parity par; the unit uses the first replay_n of them) and
+// this call's N A and B records (parity par^1).
+template <typename T, int DK, int DV>
+__device__ __forceinline__ void gdn_stage(GdnChunkIn<T, DK, DV>& in, uint64_t* bar, const qsp_gdn_layer& L,
+                                          const GdnRing& RG, int u, int N, int par, int lane) {
+  const int Ts = L.max_spec_tokens;
+  const uint8_t* ring = static_cast<const uint8_t*>(L.pending);
+  const int64_t a_par = ((int64_t)par * L.batch * L.n_v_heads + u) * Ts;        // record index of slot 0
+  const int64_t a_new = ((int64_t)(par ^ 1) * L.batch * L.n_v_heads + u) * Ts;
+  if (lane == 0) {
+    const uint32_t total = (uint32_t)(Ts * RG.recA + N * (RG.recA + RG.recB));
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(gsm(bar)), "r"(total) : "memory");
+  }
+  __syncwarp();
+  if (lane == 0) gdn_bulk(in.rep, ring + a_par * RG.recA, (uint32_t)(Ts * RG.recA), bar);
+  if (lane == 1 && N > 0) gdn_bulk(in.na, ring + a_new * RG.recA, (uint32_t)(N * RG.recA), bar);
+  if (lane == 2 && N > 0) gdn_bulk(in.nb, ring + RG.offB + a_new * RG.recB, (uint32_t)(N * RG.recB), bar);
+}
+
+// Persistent: CTA c handles (sequence, value head) units c, c+G, ... . While a unit computes,
+// the next unit's state and token records stream into shared memory.
 template <typename T, int DK, int DV>
 __global__ void __launch_bounds__(DV, 2)
 gdn_chunk_kernel(const qsp_gdn_layer L, const GdnRing RG, const int n_new) {
   using SM = GdnChunkSmem<T, DK, DV>;
   extern __shared__ __align__(128) uint8_t gdn_chunk_raw[];
   SM& sm = *reinterpret_cast<SM*>(gdn_chunk_raw);
-  constexpr int P2 = DK / 2;
+  constexpr int RB = DK / 4;          // rows per thread
   constexpr int ESZ = (int)sizeof(T);
-  constexpr int CK = DK * ESZ / 16, CV = DV * ESZ / 16;   // 16-byte chunks per row
-  const int j = threadIdx.x, lane = j & 31, warp = j >> 5;
-  const int Hk = L.n_k_heads, Hv = L.n_v_heads, vpk = Hv / Hk;
+  constexpr int EPV = 16 / ESZ;
+  constexpr int CK = DK / EPV;        // 16-byte chunks per k/q row
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int rg = lane >> 3, cg = warp * 8 + (lane & 7);
+  const int col = 4 * cg + rg;        // the column this lane owns after a butterfly
+  const int Hv = L.n_v_heads;
   const int Ts = L.max_spec_tokens;
-  const int conv_dim = 2 * Hk * DK + Hv * DV;
   const bool spec = L.speculative != 0;
   const int par = L.parity[0];
   const int units = L.batch * Hv;
   const int N = n_new;
   const float qscale = (float)(1.0 / sqrt((double)DK));
-  const uint8_t* ring = static_cast<const uint8_t*>(L.pending);
-  const T* proj = static_cast<const T*>(L.proj);
   T* out = static_cast<T*>(L.out);
-  const float wn = dt<T>::to_f(static_cast<const T*>(L.norm_w)[j]);
+  const float wn = dt<T>::to_f(static_cast<const T*>(L.norm_w)[col]);
   constexpr uint32_t SBYTES = DK * DV * 4;
+  const int G = gridDim.x;
 
-  if (j == 0) {
+  if (tid == 0) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(gsm(&sm.bar)) : "memory");
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(gsm(&sm.ibar[0])) : "memory");
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(gsm(&sm.ibar[1])) : "memory");
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
-  if (j == 0 && blockIdx.x < units)
-    gdn_prefetch_state(sm.sst, L.state + (int64_t)blockIdx.x * DK * DV, &sm.bar, SBYTES);
+  if ((int)blockIdx.x < units) {
+    if (tid == 0) gdn_prefetch_state(sm.sst, L.state + (int64_t)blockIdx.x * DK * DV, &sm.bar, SBYTES);
+    if (warp == 0) gdn_stage<T, DK, DV>(sm.in[0], &sm.ibar[0], L, RG, blockIdx.x, N, par, lane);
+  }
+  int r_next = (int)blockIdx.x < units ? L.replay_n[blockIdx.x / Hv] : 0;
 
   uint32_t it = 0;
-  for (int u = blockIdx.x; u < units; u += gridDim.x, ++it) {
-    const int b = u / Hv, h = u % Hv, kh = h / vpk;
-    const int R = min(max(L.replay_n[b], 0), Ts);
-    const uint8_t* rowR = ring + ((int64_t)par * L.batch + b) * Ts * RG.pitch;
-    const uint8_t* rowN = ring + ((int64_t)(par ^ 1) * L.batch + b) * Ts * RG.pitch;
+  for (int u = blockIdx.x; u < units; u += G, ++it) {
+    const int b = u / Hv, h = u % Hv;
+    // device-side counters are clamped to the buffers they index (they are produced by
+    // qsp_cache_finalize / qsp_cache_accept and never exceed max_spec_tokens)
+    const int R = min(max(r_next, 0), Ts);
+    const int buf = it & 1;
+    GdnChunkIn<T, DK, DV>& in = sm.in[buf];
+    // 1. the next unit's records go into the other buffer (free since the last unit ended)
+    if (u + G < units) {
+      if (warp == 0) gdn_stage<T, DK, DV>(sm.in[buf ^ 1], &sm.ibar[buf ^ 1], L, RG, u + G, N, par, lane);
+      r_next = L.replay_n[(u + G) / Hv];
+    }
     float* state = L.state + (int64_t)u * DK * DV;
 
-    // 1. stage this unit's token rows (cp.async, all in flight at once)
-    for (int e = j; e < R * CK; e += DV)
-      gcp16(reinterpret_cast<uint8_t*>(sm.kraw[e / CK]) + (e % CK) * 16,
-            rowR + (e / CK) * RG.pitch + (int64_t)(RG.off_k + kh * DK) * ESZ + (e % CK) * 16);
-    for (int e = j; e < R * CV; e += DV)
-      gcp16(reinterpret_cast<uint8_t*>(sm.vraw[e / CV]) + (e % CV) * 16,
-            rowR + (e / CV) * RG.pitch + (int64_t)(RG.off_v + h * DV) * ESZ + (e % CV) * 16);
-    for (int e = j; e < N * CK; e += DV) {
-      const uint8_t* src = rowN + (e / CK) * RG.pitch + (e % CK) * 16;
-      gcp16(reinterpret_cast<uint8_t*>(sm.kraw[GDN_TB + e / CK]) + (e % CK) * 16, src + (int64_t)(RG.off_k + kh * DK) * ESZ);
-      gcp16(reinterpret_cast<uint8_t*>(sm.qraw[e / CK]) + (e % CK) * 16, src + (int64_t)(kh * DK) * ESZ);
-    }
-    for (int e = j; e < N * CV; e += DV) {
-      const int t = e / CV, c = e % CV;
-      gcp16(reinterpret_cast<uint8_t*>(sm.vraw[GDN_TB + t]) + c * 16,
-            rowN + t * RG.pitch + (int64_t)(RG.off_v + h * DV) * ESZ + c * 16);
-      gcp16(reinterpret_cast<uint8_t*>(sm.zraw[t]) + c * 16,
-            reinterpret_cast<const uint8_t*>(proj + (int64_t)(b * N + t) * L.ld_proj + conv_dim + h * DV) + c * 16);
-    }
-    for (int e = j; e < 2 * R + 4 * N; e += DV) {   // Gram rows: 32 bytes = 2 chunks each
-      const int c = e & 1, r = e >> 1;
-      if (r < R) {
-        gcp16(reinterpret_cast<uint8_t*>(sm.gkk[r]) + c * 16,
-              rowR + r * RG.pitch + RG.f32_off + (int64_t)(RG.off_gkk + kh * GDN_TB) * 4 + c * 16);
-      } else if (r < R + N) {
-        const int t = r - R;
-        gcp16(reinterpret_cast<uint8_t*>(sm.gkk[GDN_TB + t]) + c * 16,
-              rowN + t * RG.pitch + RG.f32_off + (int64_t)(RG.off_gkk + kh * GDN_TB) * 4 + c * 16);
-      } else {
-        const int t = r - R - N;
-        gcp16(reinterpret_cast<uint8_t*>(sm.gkq[t]) + c * 16,
-              rowN + t * RG.pitch + RG.f32_off + (int64_t)(RG.off_gkq + kh * GDN_TB) * 4 + c * 16);
-      }
-    }
-    for (int e = j; e < 2 * (R + N); e += DV) {     // d, β
-      const int w = e & 1, r = e >> 1;
-      const uint8_t* base = r < R ? rowR + r * RG.pitch : rowN + (r - R) * RG.pitch;
-      gcp4(&sm.gb[r < R ? r : GDN_TB + r - R][w], base + RG.f32_off + (int64_t)((w ? RG.off_beta : RG.off_d) + h) * 4);
-    }
-    asm volatile("cp.async.commit_group;" ::: "memory");
-
-    // 2. this unit's state: prefetched into shared memory → registers (column j)
+    // 2. this unit's state: prefetched into shared memory → registers
     gdn_wait(&sm.bar, it & 1u);
-    uint64_t S[P2];
+    uint64_t S[4][RB / 2];
 #pragma unroll
-    for (int p = 0; p < P2; ++p) S[p] = pk2(sm.sst[(2 * p) * DV + j], sm.sst[(2 * p + 1) * DV + j]);
-    asm volatile("cp.async.wait_all;" ::: "memory");
-    __syncthreads();   // inputs staged; sst consumed
-    if (j == 0 && u + (int)gridDim.x < units)
-      gdn_prefetch_state(sm.sst, L.state + (int64_t)(u + gridDim.x) * DK * DV, &sm.bar, SBYTES);
+    for (int p = 0; p < RB / 2; ++p) {
+      const float4 r0 = *reinterpret_cast<const float4*>(&sm.sst[(RB * rg + 2 * p) * DV + 4 * cg]);
+      const float4 r1 = *reinterpret_cast<const float4*>(&sm.sst[(RB * rg + 2 * p + 1) * DV + 4 * cg]);
+      S[0][p] = pk2(r0.x, r1.x);
+      S[1][p] = pk2(r0.y, r1.y);
+      S[2][p] = pk2(r0.z, r1.z);
+      S[3][p] = pk2(r0.w, r1.w);
+    }
+    gdn_wait(&sm.ibar[buf], (it >> 1) & 1u);
+    __syncthreads();   // sst consumed by every thread
+    if (tid == 0 && u + G < units)
+      gdn_prefetch_state(sm.sst, L.state + (int64_t)(u + G) * DK * DV, &sm.bar, SBYTES);
 
-    // 3. fp32 vector slots (replay k 0..7, new k 8..15, scaled new q 16..23) and the tables
-    for (int e = j; e < 3 * GDN_TB * CK; e += DV) {
+    // 3. fp32 vector slots and the coefficient tables
+    for (int e = tid; e < 3 * GDN_TB * CK; e += DV) {
       const int v = e / CK, c = e % CK;   // vector slot, 16-byte chunk of it
       const T* src;
       float sc = 1.f;
       if (v < GDN_TB) {
         if (v >= R) continue;
-        src = sm.kraw[v];
+        src = in.rep[v].k;
       } else if (v < 2 * GDN_TB) {
         if (v - GDN_TB >= N) continue;
-        src = sm.kraw[v];
+        src = in.na[v - GDN_TB].k;
       } else {
         if (v - 2 * GDN_TB >= N) continue;
-        src = sm.qraw[v - 2 * GDN_TB];
+        src = in.nb[v - 2 * GDN_TB].q;
         sc = qscale;
       }
-      constexpr int EPV = 16 / ESZ;
       float x[EPV];
       load16_as_float<T>(src + c * EPV, x);
 #pragma unroll
-      for (int i = 0; i < EPV / 2; ++i) {
-        const int p = c * (EPV / 2) + i;
-        *reinterpret_cast<float2*>(&sm.kq[v / 4][p][(v % 4) * 2]) = make_float2(x[2 * i] * sc, x[2 * i + 1] * sc);
-      }
+      for (int i = 0; i < EPV; ++i) sm.vec[v][c * EPV + i] = x[i] * sc;
     }
-    for (int e = j; e < 2 * (GDN_TB + 1) * GDN_TB; e += DV) {
+    for (int e = tid; e < 2 * (GDN_TB + 1) * GDN_TB; e += DV) {
       const int ch = e / ((GDN_TB + 1) * GDN_TB);           // 0 replay, 1 new
       const int r = (e / GDN_TB) % (GDN_TB + 1) - 1, s = e % GDN_TB;
-      const int n = ch ? N : R, row0 = ch ? GDN_TB : 0;
+      const int n = ch ? N : R;
+      const GdnRecA<T, DK, DV>* ra = ch ? in.na : in.rep;
       if (s >= n || r > s) continue;
       float ratio = 1.f;                                      // Γ(r, s) = d_{r+1}···d_s
-      for (int i = r + 1; i <= s; ++i) ratio = __fmul_rn(ratio, sm.gb[row0 + i][0]);
+      for (int i = r + 1; i <= s; ++i) ratio = __fmul_rn(ratio, ra[i].db.x);
       if (r < 0) sm.gam[ch][s] = ratio;
-      if (r >= 0 && r < s) sm.tabA[ch][r][s] = __fmul_rn(ratio, sm.gkk[row0 + s][r]);
-      if (ch == 1 && r >= 0) sm.tabB[r][s] = __fmul_rn(ratio, sm.gkq[s][r]);
+      if (r >= 0 && r < s) sm.tabA[ch][r][s] = __fmul_rn(ratio, ra[s].gkk[r]);
+      if (ch == 1 && r >= 0) sm.tabB[r][s] = __fmul_rn(ratio, in.nb[s].gkq[r]);
       if (r >= 0 && s == n - 1) sm.tail[ch][r] = ratio;
     }
     __syncthreads();
 
     auto store_state = [&]() {
 #pragma unroll
-      for (int p = 0; p < P2; ++p) {
-        const float2 v = upk2(S[p]);
-        state[(int64_t)(2 * p) * DV + j] = v.x;
-        state[(int64_t)(2 * p + 1) * DV + j] = v.y;
+      for (int p = 0; p < RB / 2; ++p) {
+        const float2 a = upk2(S[0][p]), bq = upk2(S[1][p]), c2 = upk2(S[2][p]), d2 = upk2(S[3][p]);
+        *reinterpret_cast<float4*>(state + (int64_t)(RB * rg + 2 * p) * DV + 4 * cg) = make_float4(a.x, bq.x, c2.x, d2.x);
+        *reinterpret_cast<float4*>(state + (int64_t)(RB * rg + 2 * p + 1) * DV + 4 * cg) = make_float4(a.y, bq.y, c2.y, d2.y);
       }
     };
     // 4. replay the kept tokens of the previous speculative call
     if (R > 0) {
       float P[GDN_TB], dl[GDN_TB], c[GDN_TB];
-      gdn_dot4<DK>(S, &sm.kq[0][0][0], P);
-      if (R > 4) gdn_dot4<DK>(S, &sm.kq[1][0][0], P + 4);
-      gdn_deltas<T, DV>(P, &sm.vraw[0][j], sm.gb, sm.tabA[0], sm.gam[0], R, dl);
+      gdn_dots4<DK>(S, sm.vec[0], rg, P);
+      if (R > 4) gdn_dots4<DK>(S, sm.vec[4], rg, P + 4);
+      gdn_deltas<T, DK, DV>(P, in.rep, col, sm.tabA[0], sm.gam[0], R, dl);
 #pragma unroll
       for (int s = 0; s < GDN_TB; ++s) c[s] = s < R ? __fmul_rn(sm.tail[0][s], dl[s]) : 0.f;
-      gdn_rank_update<DK>(S, &sm.kq[0][0][0], sm.gam[0][R - 1], c, R);
+      gdn_rank<DK>(S, sm.vec[0], sm.gam[0][R - 1], c, R, rg, lane);
       if (spec || N == 0) store_state();
     }
     // 5. this call's tokens
     if (N > 0) {
       float Pk[GDN_TB], Pq[GDN_TB], dl[GDN_TB], o[GDN_TB];
-      gdn_dot4<DK>(S, &sm.kq[2][0][0], Pk);
-      gdn_dot4<DK>(S, &sm.kq[4][0][0], Pq);
+      gdn_dots4<DK>(S, sm.vec[GDN_TB], rg, Pk);
+      gdn_dots4<DK>(S, sm.vec[2 * GDN_TB], rg, Pq);
       if (N > 4) {
-        gdn_dot4<DK>(S, &sm.kq[3][0][0], Pk + 4);
-        gdn_dot4<DK>(S, &sm.kq[5][0][0], Pq + 4);
+        gdn_dots4<DK>(S, sm.vec[GDN_TB + 4], rg, Pk + 4);
+        gdn_dots4<DK>(S, sm.vec[2 * GDN_TB + 4], rg, Pq + 4);
       }
-      gdn_deltas<T, DV>(Pk, &sm.vraw[GDN_TB][j], sm.gb + GDN_TB, sm.tabA[1], sm.gam[1], N, dl);
+      gdn_deltas<T, DK, DV>(Pk, in.na, col, sm.tabA[1], sm.gam[1], N, dl);
 #pragma unroll
       for (int t = 0; t < GDN_TB; ++t) {
         o[t] = 0.f;
@@ -856,7 +915,7 @@ gdn_chunk_kernel(const qsp_gdn_layer L, const GdnRing RG, const int n_new) {
         float c[GDN_TB];
 #pragma unroll
         for (int s = 0; s < GDN_TB; ++s) c[s] = s < N ? __fmul_rn(sm.tail[1][s], dl[s]) : 0.f;
-        gdn_rank_update<DK>(S, &sm.kq[2][0][0], sm.gam[1][N - 1], c, N);
+        gdn_rank<DK>(S, sm.vec[GDN_TB], sm.gam[1][N - 1], c, N, rg, lane);
         store_state();
       }
       // 6. RMSNormGated over the dv columns of each token: w·round(x̂)·silu(z), x = round(core)
@@ -877,11 +936,11 @@ gdn_chunk_kernel(const qsp_gdn_layer L, const GdnRing RG, const int n_new) {
           const float inv = rsqrtf(ss / (float)DV + L.eps);
           const float xh = dt<T>::round(dt<T>::round(o[t]) * inv);
           const float wx = dt<T>::round(wn * xh);
-          out[(int64_t)(b * N + t) * L.ld_out + h * DV + j] = dt<T>::from_f(wx * siluf_(dt<T>::to_f(sm.zraw[t][j])));
+          out[(int64_t)(b * N + t) * L.ld_out + h * DV + col] = dt<T>::from_f(wx * siluf_(dt<T>::to_f(in.nb[t].z[col])));
         }
       }
     }
-    __syncthreads();   // the next unit's staging overwrites the inputs
+    __syncthreads();   // the next unit's staging overwrites this unit's buffers
   }
 }
 
@@ -908,7 +967,7 @@ static int reserve_smem(K kern, size_t smem, bool& done) {
 
 template <typename T, int DK, int DV>
 static int launch_gdn_dims(const qsp_gdn_layer& L, cudaStream_t st) {
-  const GdnRing RG = gdn_ring(L.n_k_heads, L.n_v_heads, DK, DV, (int)sizeof(T));
+  const GdnRing RG = gdn_ring(L.batch, L.n_v_heads, L.max_spec_tokens, DK, DV, (int)sizeof(T));
   const int units = L.batch * L.n_v_heads;
   const int grid = std::min(units, 2 * sm_count_gdn());
   auto chunk = gdn_chunk_kernel<T, DK, DV>;
@@ -1000,6 +1059,6 @@ extern "C" size_t qsp_gdn_pending_bytes(int32_t batch, int32_t n_k_heads, int32_
   if (batch <= 0 || n_k_heads <= 0 || n_v_heads <= 0 || head_k <= 0 || head_v <= 0 || max_spec_tokens <= 0)
     return 0;
   const int esz = dtype == QSP_F32 ? 4 : 2;
-  const GdnRing RG = gdn_ring(n_k_heads, n_v_heads, head_k, head_v, esz);
-  return (size_t)2 * batch * max_spec_tokens * RG.pitch;
+  const GdnRing RG = gdn_ring(batch, n_v_heads, max_spec_tokens, head_k, head_v, esz);
+  return (size_t)2 * batch * n_v_heads * max_spec_tokens * (RG.recA + RG.recB);
 }
