@@ -8,6 +8,7 @@
 namespace qsp {
 
 int launch_attn_mma(const qsp_attn_layer& L, cudaStream_t st);
+int launch_attn_tma(const qsp_attn_layer& L, cudaStream_t st);
 
 // ------------------------------------------------------------------ prep
 // One CTA per token row m = b*T + t; warps loop over the q and k heads.
@@ -315,7 +316,8 @@ int qsp_attn_verify(const qsp_attn_layer* layer, void* stream) {
   cudaStream_t st = as_stream(stream);
   if (L.dtype == QSP_BF16) {
     // tensor-core path (head_dim 64/128/256); other shapes use the CUDA-core kernel below
-    int rc2 = launch_attn_mma(L, st);
+    int rc2 = launch_attn_tma(L, st);
+    if (rc2 == QSP_ERR_UNSUPPORTED) rc2 = launch_attn_mma(L, st);
     if (rc2 == QSP_OK) return launch_combine<__nv_bfloat16>(L, st);
     if (rc2 != QSP_ERR_UNSUPPORTED) return rc2;
   }

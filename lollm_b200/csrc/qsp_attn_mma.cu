@@ -12,6 +12,10 @@
 // the output gate.
 #include "qsp_common.cuh"
 
+#include <cuda.h>
+
+#include <mutex>
+
 namespace qsp {
 
 constexpr int AM_KT = 64;        // keys per tile
@@ -322,6 +326,394 @@ int launch_attn_mma(const qsp_attn_layer& L, cudaStream_t st) {
       return QSP_ERR_UNSUPPORTED;
   }
 #undef QSP_AM_CASE
+}
+
+
+// ------------------------------------------------------------------ TMA-fed variant
+// Same math and work split as attn_mma_kernel, fed differently: key tiles of 32 rows arrive by
+// TMA (one 2-D box per 64 head dims of K and of V, 128-byte swizzled) into a 4-stage ring, so
+// three tiles are in flight while one is computed and no thread spends time on page-table
+// lookups or per-row copies. Q fragments stay in registers for the whole key range; the
+// running row maximum is only raised when a tile exceeds it by more than 2^8 (scores are
+// exponentiated against the stale maximum otherwise, exactly, since l uses the same one), so
+// the O accumulators are rarely rescaled. Requires bf16, page_size a multiple of 32.
+constexpr int AT2_KT = 32;     // keys per tile
+constexpr int AT2_NST = 4;     // ring stages
+constexpr float AT2_SLACK = 8.f;   // log2 units the running max may lag
+
+__device__ int g_attn_error = 0;
+
+template <int HD>
+struct At2Smem {
+  static constexpr int NB = HD / 64;               // 128-byte boxes per key row
+  static constexpr int BOX = AT2_KT * 128;         // bytes per box
+  static constexpr int KV = NB * BOX;              // bytes of K (or V) per tile
+  static constexpr int STAGE = 2 * KV;
+  static constexpr int QP = HD + 8;                // padded Q row (elements)
+  static constexpr size_t RING = (size_t)AT2_NST * STAGE;
+  static constexpr size_t QBYTES = (size_t)AM_ROWS * QP * 2;
+  static constexpr size_t BYTES = 1024 + RING + QBYTES + 128;
+};
+
+__device__ __forceinline__ void at2_tma(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          su32(dst)),
+      "l"(map), "r"(su32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+__device__ __forceinline__ void at2_wait(uint64_t* bar, uint32_t parity) {
+  for (uint32_t i = 0; i < (1u << 24); ++i) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok) : "r"(su32(bar)), "r"(parity) : "memory");
+    if (ok) return;
+    if (i > 256) __nanosleep(64);
+  }
+  atomicExch(&g_attn_error, 301);
+}
+
+// byte offset of (row r, 16-byte chunk c) inside a 128-byte-swizzled box
+__device__ __forceinline__ int at2_swz(int r, int c) { return r * 128 + ((c ^ (r & 7)) << 4); }
+
+template <int HD>
+__global__ void __launch_bounds__(AM_THREADS, 1)
+attn_tma_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                const qsp_attn_layer L, int n_row_groups) {
+  using SM = At2Smem<HD>;
+  constexpr int QP = SM::QP;
+  constexpr int NKS = HD / 16;
+  constexpr int NNT = HD / 8;
+  extern __shared__ __align__(16) uint8_t at2_raw[];
+  uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(at2_raw) + 1023) & ~uintptr_t(1023));
+  __nv_bfloat16* sQ = reinterpret_cast<__nv_bfloat16*>(ring + SM::RING);
+  uint64_t* full = reinterpret_cast<uint64_t*>(ring + SM::RING + SM::QBYTES);
+  int* valid = reinterpret_cast<int*>(full + AT2_NST);
+
+  const int s = blockIdx.x, g = blockIdx.y;
+  const int b = blockIdx.z / n_row_groups, rgp = blockIdx.z % n_row_groups;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int nrep = L.n_heads / L.n_kv_heads;
+  const int rows_total = nrep * L.tokens;
+  const int row0 = rgp * AM_ROWS;
+  const int nrows = min(AM_ROWS, rows_total - row0);
+  const int base_len = L.seq_lens[b];
+  const int kv_len = base_len + L.tokens;
+  int chunk = (kv_len + L.num_splits - 1) / L.num_splits;
+  chunk = ((chunk + AT2_KT - 1) / AT2_KT) * AT2_KT;
+  const int k_begin = s * chunk;
+  const int k_end = min(kv_len, k_begin + chunk);
+  const int64_t idx0 = ((int64_t)b * L.n_heads) * L.tokens;
+
+  if (k_begin >= k_end) {  // empty split: an all-masked partial
+    for (int r = tid; r < nrows; r += AM_THREADS) {
+      const int rr = row0 + r, t = rr / nrep, hq = g * nrep + rr % nrep;
+      float* po = L.partial + ((idx0 + (int64_t)hq * L.tokens + t) * L.num_splits + s) * (HD + 2);
+      po[HD] = -INFINITY;
+      po[HD + 1] = 0.f;
+    }
+    return;
+  }
+  const int n_tiles = (k_end - k_begin + AT2_KT - 1) / AT2_KT;
+
+  if (tid == 0) {
+    for (int i = 0; i < AT2_NST; ++i)
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(su32(&full[i])) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  // Q rows of this group (rows beyond nrows zero-filled)
+  const __nv_bfloat16* qb = static_cast<const __nv_bfloat16*>(L.q_buf);
+  for (int e = tid; e < AM_ROWS * (HD / 8); e += AM_THREADS) {
+    const int r = e / (HD / 8), c = e % (HD / 8);
+    const int rr = row0 + r;
+    const bool ok = r < nrows;
+    const int t = ok ? rr / nrep : 0, hq = ok ? g * nrep + rr % nrep : 0;
+    const __nv_bfloat16* src = qb + (((int64_t)b * L.tokens + t) * L.n_heads + hq) * HD + c * 8;
+    cp16(sQ + r * QP + c * 8, ok ? src : qb, ok);
+  }
+  cp_commit();
+  __syncthreads();   // barriers initialised
+
+  // tile j of this split → ring stage j % NST (one thread issues every copy)
+  auto issue = [&](int j) {
+    const int st = j % AT2_NST;
+    const int key0 = k_begin + j * AT2_KT;
+    const int lp = key0 / L.page_size;
+    const int page = lp < L.max_pages ? L.page_table[(int64_t)b * L.max_pages + lp] : -1;
+    const bool ok = page >= 0 && page < L.num_pages;
+    const int row = ok ? (page * L.n_kv_heads + g) * L.page_size + key0 % L.page_size : 0;
+    valid[st] = ok;
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(&full[st])), "r"(SM::STAGE)
+                 : "memory");
+    uint8_t* kd = ring + st * SM::STAGE;
+#pragma unroll
+    for (int nb = 0; nb < SM::NB; ++nb) {
+      at2_tma(kd + nb * SM::BOX, &tmK, &full[st], nb * 64, row);
+      at2_tma(kd + SM::KV + nb * SM::BOX, &tmV, &full[st], nb * 64, row);
+    }
+  };
+  if (tid == 0)
+    for (int j = 0; j < AT2_NST - 1 && j < n_tiles; ++j) issue(j);
+
+  const int mt = warp & 1, kh = warp >> 1;       // row tile, key half (16 keys of a tile)
+  const int gq = lane >> 2, tq = lane & 3;
+  const float sl2 = L.scale * 1.4426950408889634f;  // scale in log2 units
+  int qpos[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int r = mt * 16 + gq + 8 * h;
+    qpos[h] = (r < nrows) ? base_len + (row0 + r) / nrep : -1;
+  }
+  cp_wait<0>();
+  __syncthreads();   // Q staged
+  uint32_t qa[NKS][4];
+#pragma unroll
+  for (int ks = 0; ks < NKS; ++ks)
+    ldsm_x4(qa[ks], sQ + (mt * 16 + (lane & 7) + 8 * ((lane >> 3) & 1)) * QP + ks * 16 + 8 * (lane >> 4));
+
+  float o[NNT][4];
+#pragma unroll
+  for (int i = 0; i < NNT; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
+  // this lane's ldmatrix rows inside a tile
+  const int kr = kh * 16 + (lane & 7) + 8 * (lane >> 4);          // K (QKᵀ, non-transposed)
+  const int kc = (lane >> 3) & 1;
+  const int vr = kh * 16 + (lane & 7) + 8 * ((lane >> 3) & 1);    // V (PV, transposed)
+  const int vc = lane >> 4;
+
+  for (int it = 0; it < n_tiles; ++it) {
+    const int st = it % AT2_NST;
+    if (tid == 0 && it + AT2_NST - 1 < n_tiles) issue(it + AT2_NST - 1);   // its stage was freed last iteration
+    at2_wait(&full[st], (uint32_t)(it / AT2_NST) & 1u);
+    const bool tile_ok = valid[st] != 0;
+    const uint8_t* kt = ring + st * SM::STAGE;
+    const uint8_t* vt = kt + SM::KV;
+    const int k0 = k_begin + it * AT2_KT;
+    // S = Q Kᵀ for 16 rows x 16 keys; even and odd k-steps accumulate separately
+    float sa[2][4], sb[2][4];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) sa[i][0] = sa[i][1] = sa[i][2] = sa[i][3] = sb[i][0] = sb[i][1] = sb[i][2] = sb[i][3] = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < NKS; ++ks) {
+      uint32_t bb[4];
+      const int d0 = ks * 16 + 8 * kc;
+      ldsm_x4(bb, kt + (d0 >> 6) * SM::BOX + at2_swz(kr, (d0 & 63) >> 3));
+      if (ks & 1) {
+        mma16816(sb[0], qa[ks], bb[0], bb[1]);
+        mma16816(sb[1], qa[ks], bb[2], bb[3]);
+      } else {
+        mma16816(sa[0], qa[ks], bb[0], bb[1]);
+        mma16816(sa[1], qa[ks], bb[2], bb[3]);
+      }
+    }
+    // mask (causal over the new tokens, split end, unmapped pages), scale
+    float tmax[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int h = e >> 1;
+        const int key = k0 + kh * 16 + nt * 8 + 2 * tq + (e & 1);
+        const bool vis = tile_ok && key < k_end && key <= qpos[h];
+        const float v = vis ? (sa[nt][e] + sb[nt][e]) * sl2 : -INFINITY;
+        sa[nt][e] = v;
+        tmax[h] = fmaxf(tmax[h], v);
+      }
+    }
+    bool need[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      tmax[h] = fmaxf(tmax[h], __shfl_xor_sync(0xffffffffu, tmax[h], 1));
+      tmax[h] = fmaxf(tmax[h], __shfl_xor_sync(0xffffffffu, tmax[h], 2));
+      need[h] = tmax[h] > mrow[h] + AT2_SLACK;
+    }
+    if (__any_sync(0xffffffffu, need[0] || need[1])) {
+      float alpha[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        alpha[h] = 1.f;
+        if (need[h]) {
+          alpha[h] = (mrow[h] == -INFINITY) ? 0.f : exp2f(mrow[h] - tmax[h]);
+          mrow[h] = tmax[h];
+          lrow[h] *= alpha[h];
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < NNT; ++i) {
+        o[i][0] *= alpha[0];
+        o[i][1] *= alpha[0];
+        o[i][2] *= alpha[1];
+        o[i][3] *= alpha[1];
+      }
+    }
+    float psum[2] = {0.f, 0.f};
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int h = e >> 1;
+        const float p = (mrow[h] == -INFINITY) ? 0.f : exp2f(sa[nt][e] - mrow[h]);
+        sa[nt][e] = p;
+        psum[h] += p;
+      }
+    }
+    lrow[0] += psum[0];
+    lrow[1] += psum[1];
+    // O += P V over this warp's 16 keys (one k-step)
+    uint32_t pa[4];
+    pa[0] = pack_bf16(sa[0][0], sa[0][1]);
+    pa[1] = pack_bf16(sa[0][2], sa[0][3]);
+    pa[2] = pack_bf16(sa[1][0], sa[1][1]);
+    pa[3] = pack_bf16(sa[1][2], sa[1][3]);
+#pragma unroll
+    for (int dp = 0; dp < NNT / 2; ++dp) {
+      uint32_t vb[4];
+      const int d0 = dp * 16 + 8 * vc;
+      ldsm_x4_t(vb, vt + (d0 >> 6) * SM::BOX + at2_swz(vr, (d0 & 63) >> 3));
+      mma16816(o[2 * dp], pa, vb[0], vb[1]);
+      mma16816(o[2 * dp + 1], pa, vb[2], vb[3]);
+    }
+    __syncthreads();  // every warp is done with this stage; it is refilled next iteration
+  }
+
+  // row sums over the 4 threads of a row
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    lrow[h] += __shfl_xor_sync(0xffffffffu, lrow[h], 1);
+    lrow[h] += __shfl_xor_sync(0xffffffffu, lrow[h], 2);
+  }
+  // merge the two key halves of each row tile through shared memory (the idle ring)
+  float* xo = reinterpret_cast<float*>(ring);             // [2 row tiles][16][HD]
+  float* xm = xo + 2 * 16 * HD;                           // [2][16] m, then l
+  if (kh == 1) {
+#pragma unroll
+    for (int i = 0; i < NNT; ++i) {
+      const int d = i * 8 + 2 * tq;
+      float* r0 = xo + ((mt * 16) + gq) * HD + d;
+      float* r1 = xo + ((mt * 16) + gq + 8) * HD + d;
+      r0[0] = o[i][0]; r0[1] = o[i][1];
+      r1[0] = o[i][2]; r1[1] = o[i][3];
+    }
+    if (tq == 0) {
+      xm[mt * 16 + gq] = mrow[0];
+      xm[mt * 16 + gq + 8] = mrow[1];
+      xm[32 + mt * 16 + gq] = lrow[0];
+      xm[32 + mt * 16 + gq + 8] = lrow[1];
+    }
+  }
+  __syncthreads();
+  if (kh == 0) {
+    float f0[2], f1[2], mm[2], ll[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int r = mt * 16 + gq + 8 * h;
+      const float m2 = xm[r], l2 = xm[32 + r];
+      const float M = fmaxf(mrow[h], m2);
+      f0[h] = (mrow[h] == -INFINITY) ? 0.f : exp2f(mrow[h] - M);
+      f1[h] = (m2 == -INFINITY) ? 0.f : exp2f(m2 - M);
+      mm[h] = M;
+      ll[h] = lrow[h] * f0[h] + l2 * f1[h];
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int r = mt * 16 + gq + 8 * h;
+      if (r >= nrows) continue;
+      const int rr = row0 + r, t = rr / nrep, hq = g * nrep + rr % nrep;
+      float* po = L.partial + ((idx0 + (int64_t)hq * L.tokens + t) * L.num_splits + s) * (HD + 2);
+      const float* x = xo + r * HD;
+#pragma unroll
+      for (int i = 0; i < NNT; ++i) {
+        const int d = i * 8 + 2 * tq;
+        po[d] = o[i][2 * h] * f0[h] + x[d] * f1[h];
+        po[d + 1] = o[i][2 * h + 1] * f0[h] + x[d + 1] * f1[h];
+      }
+      if (tq == 0) {
+        po[HD] = mm[h] * 0.6931471805599453f;  // log2 units → natural log (attn_combine_kernel)
+        po[HD + 1] = ll[h];
+      }
+    }
+  }
+}
+
+using At2Encode = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                               const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                               CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static At2Encode at2_encode() {
+  static At2Encode fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<At2Encode>(p);
+  });
+  return fn;
+}
+
+// Paged K or V of one layer as a 2-D bf16 tensor [num_pages·n_kv·page_size rows, hd], box of
+// 32 rows x 64 head dims, 128-byte swizzle.
+static bool at2_map(CUtensorMap* m, const void* base, int64_t rows, int hd) {
+  At2Encode enc = at2_encode();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)hd, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)hd * 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)AT2_KT};
+  cuuint32_t es[2] = {1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int launch_attn_tma(const qsp_attn_layer& L, cudaStream_t st);
+
+// QSP_ERR_UNSUPPORTED when the shape is not one this path handles (the caller falls back).
+int launch_attn_tma(const qsp_attn_layer& L, cudaStream_t st) {
+  if (L.head_dim != 64 && L.head_dim != 128 && L.head_dim != 256) return QSP_ERR_UNSUPPORTED;
+  if (L.page_size % AT2_KT != 0) return QSP_ERR_UNSUPPORTED;
+  const int64_t rows = (int64_t)L.num_pages * L.n_kv_heads * L.page_size;
+  if (rows >= (1ll << 31) || !aligned(L.k_pages, 16) || !aligned(L.v_pages, 16)) return QSP_ERR_UNSUPPORTED;
+  CUtensorMap mk, mv;
+  if (!at2_map(&mk, L.k_pages, rows, L.head_dim) || !at2_map(&mv, L.v_pages, rows, L.head_dim))
+    return QSP_ERR_UNSUPPORTED;
+  const int rows_total = (L.n_heads / L.n_kv_heads) * L.tokens;
+  const int n_rg = (rows_total + AM_ROWS - 1) / AM_ROWS;
+  dim3 grid(L.num_splits, L.n_kv_heads, L.batch * n_rg);
+#define QSP_AT2_CASE(HDV)                                                                    \
+  case HDV: {                                                                                \
+    auto kern = attn_tma_kernel<HDV>;                                                        \
+    const size_t smem = At2Smem<HDV>::BYTES;                                                 \
+    static bool set = false;                                                                 \
+    if (!set) {                                                                              \
+      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) \
+          != cudaSuccess)                                                                    \
+        return set_error(QSP_ERR_CUDA, "qsp_attn_verify: cannot reserve shared memory");     \
+      set = true;                                                                            \
+    }                                                                                        \
+    kern<<<grid, AM_THREADS, smem, st>>>(mk, mv, L, n_rg);                                   \
+    return check_launch("qsp_attn_verify(tma)");                                             \
+  }
+  switch (L.head_dim) {
+    QSP_AT2_CASE(64)
+    QSP_AT2_CASE(128)
+    QSP_AT2_CASE(256)
+    default:
+      return QSP_ERR_UNSUPPORTED;
+  }
+#undef QSP_AT2_CASE
+}
+
+int attn_device_error(int reset) {
+  int v = 0;
+  cudaMemcpyFromSymbol(&v, g_attn_error, sizeof(int));
+  if (reset && v) {
+    const int z = 0;
+    cudaMemcpyToSymbol(g_attn_error, &z, sizeof(int));
+  }
+  return v;
 }
 
 }  // namespace qsp
