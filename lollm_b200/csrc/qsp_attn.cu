@@ -9,6 +9,7 @@ namespace qsp {
 
 int launch_attn_mma(const qsp_attn_layer& L, cudaStream_t st);
 int launch_attn_tma(const qsp_attn_layer& L, cudaStream_t st);
+int launch_attn_ws(const qsp_attn_layer& L, cudaStream_t st);
 
 // ------------------------------------------------------------------ prep
 // One CTA per token row m = b*T + t; warps loop over the q and k heads.
@@ -183,31 +184,48 @@ __global__ void __launch_bounds__(128) attn_simt_kernel(const qsp_attn_layer L, 
 }
 
 // ------------------------------------------------------------------ merge splits + gate
+// One warp per (token row m, q head): the np partials (o unnormalised, m natural-log max,
+// l) of the row are merged with weights e^{m_p − M}, then σ(gate) is applied.
 template <typename T>
-__global__ void attn_combine_kernel(const qsp_attn_layer L) {
-  const int m = blockIdx.x, hq = blockIdx.y;
+__global__ void __launch_bounds__(256) attn_combine_kernel(const qsp_attn_layer L, int np) {
+  const int lane = threadIdx.x & 31;
+  const int pair = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (pair >= L.batch * L.tokens * L.n_heads) return;
+  const int m = pair / L.n_heads, hq = pair % L.n_heads;
   const int b = m / L.tokens, t = m % L.tokens;
-  const int hd = L.head_dim, ns = L.num_splits;
-  const float* base = L.partial + ((((int64_t)b * L.n_heads + hq) * L.tokens + t) * ns) * (hd + 2);
+  const int hd = L.head_dim;
+  const float* base = L.partial + ((((int64_t)b * L.n_heads + hq) * L.tokens + t) * np) * (hd + 2);
   float M = -INFINITY;
-  for (int s = 0; s < ns; ++s) M = fmaxf(M, base[(int64_t)s * (hd + 2) + hd]);
+  for (int p = lane; p < np; p += 32) M = fmaxf(M, base[(int64_t)p * (hd + 2) + hd]);
+  M = warp_max(M);
+  float den = 0.f;
+  for (int p = lane; p < np; p += 32) {
+    const float mp = base[(int64_t)p * (hd + 2) + hd];
+    if (mp != -INFINITY) den = fmaf(expf(mp - M), base[(int64_t)p * (hd + 2) + hd + 1], den);
+  }
+  den = warp_sum(den);
   const T* row = static_cast<const T*>(L.qkv) + (int64_t)m * L.ld_qkv;
   T* o = static_cast<T*>(L.out) + (int64_t)m * L.ld_out + (int64_t)hq * hd;
-  for (int d = threadIdx.x; d < hd; d += blockDim.x) {
-    float num = 0.f, den = 0.f;
+  for (int d0 = 2 * lane; d0 < hd; d0 += 64) {
+    float n0 = 0.f, n1 = 0.f;
     if (M != -INFINITY) {
-      for (int s = 0; s < ns; ++s) {
-        const float* p = base + (int64_t)s * (hd + 2);
-        const float ms = p[hd];
-        if (ms == -INFINITY) continue;
-        const float w = expf(ms - M);
-        num = fmaf(w, p[d], num);
-        den = fmaf(w, p[hd + 1], den);
+      for (int p = 0; p < np; ++p) {
+        const float* q = base + (int64_t)p * (hd + 2);
+        const float mp = q[hd];
+        if (mp == -INFINITY) continue;
+        const float w = expf(mp - M);
+        const float2 v = *reinterpret_cast<const float2*>(q + d0);
+        n0 = fmaf(w, v.x, n0);
+        n1 = fmaf(w, v.y, n1);
       }
     }
-    const float attn = dt<T>::round(den > 0.f ? num / den : 0.f);
-    const float gate = dt<T>::to_f(row[(int64_t)hq * 2 * hd + hd + d]);
-    o[d] = dt<T>::from_f(attn * dt<T>::round(sigmoidf_(gate)));
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int d = d0 + k;
+      const float attn = dt<T>::round(den > 0.f ? (k ? n1 : n0) / den : 0.f);
+      const float gate = dt<T>::to_f(row[(int64_t)hq * 2 * hd + hd + d]);
+      o[d] = dt<T>::from_f(attn * dt<T>::round(sigmoidf_(gate)));
+    }
   }
 }
 
@@ -219,8 +237,9 @@ static int attn_chunk(const qsp_attn_layer& L) {
 }
 
 template <typename T>
-static int launch_combine(const qsp_attn_layer& L, cudaStream_t st) {
-  attn_combine_kernel<T><<<dim3(L.batch * L.tokens, L.n_heads), 128, 0, st>>>(L);
+static int launch_combine(const qsp_attn_layer& L, int np, cudaStream_t st) {
+  const int pairs = L.batch * L.tokens * L.n_heads;
+  attn_combine_kernel<T><<<(pairs + 7) / 8, 256, 0, st>>>(L, np);
   return check_launch("qsp_attn_verify(combine)");
 }
 
@@ -235,8 +254,7 @@ static int launch_attn_simt(const qsp_attn_layer& L, cudaStream_t st) {
   kern<<<grid, 128, smem, st>>>(L, attn_chunk(L), n_rg);
   int rc = check_launch("qsp_attn_verify(simt)");
   if (rc) return rc;
-  attn_combine_kernel<T><<<dim3(L.batch * L.tokens, L.n_heads), 128, 0, st>>>(L);
-  return check_launch("qsp_attn_verify(combine)");
+  return launch_combine<T>(L, L.num_splits, st);
 }
 
 // Scratch for qsp_attn_verify_static. Some callers cannot allocate at the moment they
@@ -316,9 +334,10 @@ int qsp_attn_verify(const qsp_attn_layer* layer, void* stream) {
   cudaStream_t st = as_stream(stream);
   if (L.dtype == QSP_BF16) {
     // tensor-core path (head_dim 64/128/256); other shapes use the CUDA-core kernel below
-    int rc2 = launch_attn_tma(L, st);
+    int rc2 = launch_attn_ws(L, st);
+    if (rc2 == QSP_OK) return launch_combine<__nv_bfloat16>(L, 2 * L.num_splits, st);
     if (rc2 == QSP_ERR_UNSUPPORTED) rc2 = launch_attn_mma(L, st);
-    if (rc2 == QSP_OK) return launch_combine<__nv_bfloat16>(L, st);
+    if (rc2 == QSP_OK) return launch_combine<__nv_bfloat16>(L, L.num_splits, st);
     if (rc2 != QSP_ERR_UNSUPPORTED) return rc2;
   }
   QSP_DISPATCH_DTYPE(L.dtype, T, {
@@ -333,7 +352,8 @@ int qsp_attn_verify(const qsp_attn_layer* layer, void* stream) {
 
 size_t qsp_attn_workspace_bytes(int32_t batch, int32_t tokens, int32_t n_heads, int32_t head_dim,
                                 int32_t num_splits) {
-  return (size_t)batch * tokens * n_heads * num_splits * (head_dim + 2) * sizeof(float);
+  // two partials per split (the tensor-core path writes one per key half)
+  return (size_t)batch * tokens * n_heads * num_splits * 2 * (head_dim + 2) * sizeof(float);
 }
 
 int qsp_attn_verify_static(const qsp_attn_layer* layer, void* stream) {

@@ -14,6 +14,7 @@
 
 #include <cuda.h>
 
+#include <algorithm>
 #include <mutex>
 
 namespace qsp {
@@ -704,6 +705,349 @@ int launch_attn_tma(const qsp_attn_layer& L, cudaStream_t st) {
       return QSP_ERR_UNSUPPORTED;
   }
 #undef QSP_AT2_CASE
+}
+
+
+// ------------------------------------------------------------------ persistent, warp-specialised
+// Warp 4 produces: for every work item (split s, kv head g, sequence b x row group) of this CTA
+// it brings the item's Q rows (bulk copies) and its key tiles (TMA, as above) into a 5-stage
+// ring, running ahead across item boundaries. Warps 0-3 consume as in attn_tma_kernel, and
+// each key-half warp writes its own partial (o, m, l), so a split yields two partials that
+// the merge kernel combines with the rest. Empty/full barriers per stage; no CTA-wide sync.
+constexpr int AT3_NST = 5;
+constexpr int AT3_THREADS = 160;
+
+template <int HD>
+struct At3Smem {
+  static constexpr int NB = HD / 64;
+  static constexpr int BOX = AT2_KT * 128;
+  static constexpr int KV = NB * BOX;
+  static constexpr int STAGE = 2 * KV;
+  static constexpr int QB = AM_ROWS * HD * 2;      // unpadded Q rows of one item
+  static constexpr size_t RING = (size_t)AT3_NST * STAGE;
+  static constexpr size_t BYTES = 1024 + RING + 2 * (size_t)QB + 256;
+};
+
+struct At3Item {
+  int s, g, b, row0, nrows, k_begin, k_end, base_len;
+};
+
+__device__ __forceinline__ At3Item at3_item(const qsp_attn_layer& L, int item, int n_rg) {
+  At3Item w;
+  w.s = item % L.num_splits;
+  int rest = item / L.num_splits;
+  w.g = rest % L.n_kv_heads;
+  rest /= L.n_kv_heads;
+  w.b = rest / n_rg;
+  const int rgp = rest % n_rg;
+  const int nrep = L.n_heads / L.n_kv_heads;
+  w.row0 = rgp * AM_ROWS;
+  w.nrows = min(AM_ROWS, nrep * L.tokens - w.row0);
+  w.base_len = L.seq_lens[w.b];
+  const int kv_len = w.base_len + L.tokens;
+  int chunk = (kv_len + L.num_splits - 1) / L.num_splits;
+  chunk = ((chunk + AT2_KT - 1) / AT2_KT) * AT2_KT;
+  w.k_begin = w.s * chunk;
+  w.k_end = min(kv_len, w.k_begin + chunk);
+  return w;
+}
+
+__device__ __forceinline__ void at3_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(bar)) : "memory");
+}
+
+template <int HD>
+__global__ void __launch_bounds__(AT3_THREADS, 1)
+attn_ws_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+               const qsp_attn_layer L, int n_rg, int n_items) {
+  using SM = At3Smem<HD>;
+  constexpr int NKS = HD / 16;
+  constexpr int NNT = HD / 8;
+  extern __shared__ __align__(16) uint8_t at3_raw[];
+  uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(at3_raw) + 1023) & ~uintptr_t(1023));
+  __nv_bfloat16* sQ = reinterpret_cast<__nv_bfloat16*>(ring + SM::RING);   // [2][32][HD]
+  uint64_t* full = reinterpret_cast<uint64_t*>(ring + SM::RING + 2 * SM::QB);
+  uint64_t* empty = full + AT3_NST;
+  uint64_t* qfull = empty + AT3_NST;
+  uint64_t* qempty = qfull + 2;
+  int* valid = reinterpret_cast<int*>(qempty + 2);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int nrep = L.n_heads / L.n_kv_heads;
+  if (tid == 0) {
+    for (int i = 0; i < AT3_NST; ++i) {
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(su32(&full[i])) : "memory");
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 4;" ::"r"(su32(&empty[i])) : "memory");
+    }
+    for (int i = 0; i < 2; ++i) {
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(su32(&qfull[i])) : "memory");
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 4;" ::"r"(su32(&qempty[i])) : "memory");
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+
+  if (warp == 4) {
+    // ---------------- producer (one lane)
+    if (lane != 0) return;
+    const __nv_bfloat16* qbuf = static_cast<const __nv_bfloat16*>(L.q_buf);
+    uint32_t tc = 0, qc = 0;
+    for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+      const At3Item w = at3_item(L, item, n_rg);
+      if (w.k_begin >= w.k_end) continue;
+      const int qb = qc & 1;
+      at2_wait(&qempty[qb], ((qc >> 1) & 1u) ^ 1u);
+      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(&qfull[qb])),
+                   "r"((uint32_t)(w.nrows * HD * 2))
+                   : "memory");
+      __nv_bfloat16* qd = sQ + qb * AM_ROWS * HD;
+      for (int r = 0; r < w.nrows;) {   // one bulk copy per token: its run of q heads
+        const int rr = w.row0 + r, t = rr / nrep, h0 = rr % nrep;
+        const int cnt = min(nrep - h0, w.nrows - r);
+        const __nv_bfloat16* src = qbuf + (((int64_t)w.b * L.tokens + t) * L.n_heads + w.g * nrep + h0) * HD;
+        asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                         su32(qd + r * HD)),
+                     "l"(src), "r"((uint32_t)(cnt * HD * 2)), "r"(su32(&qfull[qb]))
+                     : "memory");
+        r += cnt;
+      }
+      ++qc;
+      const int n_tiles = (w.k_end - w.k_begin + AT2_KT - 1) / AT2_KT;
+      for (int j = 0; j < n_tiles; ++j, ++tc) {
+        const int st = tc % AT3_NST;
+        at2_wait(&empty[st], ((tc / AT3_NST) & 1u) ^ 1u);
+        const int key0 = w.k_begin + j * AT2_KT;
+        const int lp = key0 / L.page_size;
+        const int page = lp < L.max_pages ? L.page_table[(int64_t)w.b * L.max_pages + lp] : -1;
+        const bool ok = page >= 0 && page < L.num_pages;
+        const int row = ok ? (page * L.n_kv_heads + w.g) * L.page_size + key0 % L.page_size : 0;
+        valid[st] = ok;
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(&full[st])), "r"(SM::STAGE)
+                     : "memory");
+        uint8_t* kd = ring + st * SM::STAGE;
+#pragma unroll
+        for (int nb = 0; nb < SM::NB; ++nb) {
+          at2_tma(kd + nb * SM::BOX, &tmK, &full[st], nb * 64, row);
+          at2_tma(kd + SM::KV + nb * SM::BOX, &tmV, &full[st], nb * 64, row);
+        }
+      }
+    }
+    return;
+  }
+
+  // ---------------- consumers: warps 0-3
+  const int mt = warp & 1, kh = warp >> 1;
+  const int gq = lane >> 2, tq = lane & 3;
+  const float sl2 = L.scale * 1.4426950408889634f;
+  const int kr = kh * 16 + (lane & 7) + 8 * (lane >> 4);
+  const int kc = (lane >> 3) & 1;
+  const int vr = kh * 16 + (lane & 7) + 8 * ((lane >> 3) & 1);
+  const int vc = lane >> 4;
+  const int NP = 2 * L.num_splits;   // partials per row: two key halves per split
+  uint32_t tc = 0, qc = 0;
+  for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+    const At3Item w = at3_item(L, item, n_rg);
+    const int64_t idx0 = ((int64_t)w.b * L.n_heads) * L.tokens;
+    if (w.k_begin >= w.k_end) {   // empty split: all-masked partials for both halves
+      if (kh == 0 && tq == 0) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int r = mt * 16 + gq + 8 * h;
+          if (r >= w.nrows) continue;
+          const int rr = w.row0 + r, t = rr / nrep, hq = w.g * nrep + rr % nrep;
+          for (int half = 0; half < 2; ++half) {
+            float* po = L.partial + ((idx0 + (int64_t)hq * L.tokens + t) * NP + 2 * w.s + half) * (HD + 2);
+            po[HD] = -INFINITY;
+            po[HD + 1] = 0.f;
+          }
+        }
+      }
+      continue;
+    }
+    int qpos[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int r = mt * 16 + gq + 8 * h;
+      qpos[h] = (r < w.nrows) ? w.base_len + (w.row0 + r) / nrep : -1;
+    }
+    const int qb = qc & 1;
+    at2_wait(&qfull[qb], (qc >> 1) & 1u);
+    uint32_t qa[NKS][4];
+    const __nv_bfloat16* qs = sQ + qb * AM_ROWS * HD;
+#pragma unroll
+    for (int ks = 0; ks < NKS; ++ks)
+      ldsm_x4(qa[ks], qs + (mt * 16 + (lane & 7) + 8 * ((lane >> 3) & 1)) * HD + ks * 16 + 8 * (lane >> 4));
+    __syncwarp();
+    if (lane == 0) at3_arrive(&qempty[qb]);
+    ++qc;
+
+    float o[NNT][4];
+#pragma unroll
+    for (int i = 0; i < NNT; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+    float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
+    const int n_tiles = (w.k_end - w.k_begin + AT2_KT - 1) / AT2_KT;
+    for (int it = 0; it < n_tiles; ++it, ++tc) {
+      const int st = tc % AT3_NST;
+      at2_wait(&full[st], (tc / AT3_NST) & 1u);
+      const bool tile_ok = valid[st] != 0;
+      const uint8_t* kt = ring + st * SM::STAGE;
+      const uint8_t* vt = kt + SM::KV;
+      const int k0 = w.k_begin + it * AT2_KT;
+      float sa[2][4], sb[2][4];
+#pragma unroll
+      for (int i = 0; i < 2; ++i) sa[i][0] = sa[i][1] = sa[i][2] = sa[i][3] = sb[i][0] = sb[i][1] = sb[i][2] = sb[i][3] = 0.f;
+#pragma unroll
+      for (int ks = 0; ks < NKS; ++ks) {
+        uint32_t bb[4];
+        const int d0 = ks * 16 + 8 * kc;
+        ldsm_x4(bb, kt + (d0 >> 6) * SM::BOX + at2_swz(kr, (d0 & 63) >> 3));
+        if (ks & 1) {
+          mma16816(sb[0], qa[ks], bb[0], bb[1]);
+          mma16816(sb[1], qa[ks], bb[2], bb[3]);
+        } else {
+          mma16816(sa[0], qa[ks], bb[0], bb[1]);
+          mma16816(sa[1], qa[ks], bb[2], bb[3]);
+        }
+      }
+      float tmax[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int h = e >> 1;
+          const int key = k0 + kh * 16 + nt * 8 + 2 * tq + (e & 1);
+          const bool vis = tile_ok && key < w.k_end && key <= qpos[h];
+          const float v = vis ? (sa[nt][e] + sb[nt][e]) * sl2 : -INFINITY;
+          sa[nt][e] = v;
+          tmax[h] = fmaxf(tmax[h], v);
+        }
+      }
+      bool need[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        tmax[h] = fmaxf(tmax[h], __shfl_xor_sync(0xffffffffu, tmax[h], 1));
+        tmax[h] = fmaxf(tmax[h], __shfl_xor_sync(0xffffffffu, tmax[h], 2));
+        need[h] = tmax[h] > mrow[h] + AT2_SLACK;
+      }
+      if (__any_sync(0xffffffffu, need[0] || need[1])) {
+        float alpha[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          alpha[h] = 1.f;
+          if (need[h]) {
+            alpha[h] = (mrow[h] == -INFINITY) ? 0.f : exp2f(mrow[h] - tmax[h]);
+            mrow[h] = tmax[h];
+            lrow[h] *= alpha[h];
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < NNT; ++i) {
+          o[i][0] *= alpha[0];
+          o[i][1] *= alpha[0];
+          o[i][2] *= alpha[1];
+          o[i][3] *= alpha[1];
+        }
+      }
+      float psum[2] = {0.f, 0.f};
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int h = e >> 1;
+          const float p = (mrow[h] == -INFINITY) ? 0.f : exp2f(sa[nt][e] - mrow[h]);
+          sa[nt][e] = p;
+          psum[h] += p;
+        }
+      }
+      lrow[0] += psum[0];
+      lrow[1] += psum[1];
+      uint32_t pa[4];
+      pa[0] = pack_bf16(sa[0][0], sa[0][1]);
+      pa[1] = pack_bf16(sa[0][2], sa[0][3]);
+      pa[2] = pack_bf16(sa[1][0], sa[1][1]);
+      pa[3] = pack_bf16(sa[1][2], sa[1][3]);
+#pragma unroll
+      for (int dp = 0; dp < NNT / 2; ++dp) {
+        uint32_t vb[4];
+        const int d0 = dp * 16 + 8 * vc;
+        ldsm_x4_t(vb, vt + (d0 >> 6) * SM::BOX + at2_swz(vr, (d0 & 63) >> 3));
+        mma16816(o[2 * dp], pa, vb[0], vb[1]);
+        mma16816(o[2 * dp + 1], pa, vb[2], vb[3]);
+      }
+      __syncwarp();
+      if (lane == 0) at3_arrive(&empty[st]);
+    }
+    // this warp's partial: rows of its row tile over its key half
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      lrow[h] += __shfl_xor_sync(0xffffffffu, lrow[h], 1);
+      lrow[h] += __shfl_xor_sync(0xffffffffu, lrow[h], 2);
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int r = mt * 16 + gq + 8 * h;
+      if (r >= w.nrows) continue;
+      const int rr = w.row0 + r, t = rr / nrep, hq = w.g * nrep + rr % nrep;
+      float* po = L.partial + ((idx0 + (int64_t)hq * L.tokens + t) * NP + 2 * w.s + kh) * (HD + 2);
+#pragma unroll
+      for (int i = 0; i < NNT; ++i) {
+        const int d = i * 8 + 2 * tq;
+        *reinterpret_cast<float2*>(po + d) = make_float2(o[i][2 * h], o[i][2 * h + 1]);
+      }
+      if (tq == 0) {
+        po[HD] = mrow[h] == -INFINITY ? -INFINITY : mrow[h] * 0.6931471805599453f;
+        po[HD + 1] = lrow[h];
+      }
+    }
+  }
+}
+
+int launch_attn_ws(const qsp_attn_layer& L, cudaStream_t st);
+
+int launch_attn_ws(const qsp_attn_layer& L, cudaStream_t st) {
+  if (L.head_dim != 64 && L.head_dim != 128 && L.head_dim != 256) return QSP_ERR_UNSUPPORTED;
+  if (L.page_size % AT2_KT != 0) return QSP_ERR_UNSUPPORTED;
+  const int64_t rows = (int64_t)L.num_pages * L.n_kv_heads * L.page_size;
+  if (rows >= (1ll << 31) || !aligned(L.k_pages, 16) || !aligned(L.v_pages, 16) || !aligned(L.q_buf, 16))
+    return QSP_ERR_UNSUPPORTED;
+  CUtensorMap mk, mv;
+  if (!at2_map(&mk, L.k_pages, rows, L.head_dim) || !at2_map(&mv, L.v_pages, rows, L.head_dim))
+    return QSP_ERR_UNSUPPORTED;
+  const int rows_total = (L.n_heads / L.n_kv_heads) * L.tokens;
+  const int n_rg = (rows_total + AM_ROWS - 1) / AM_ROWS;
+  const int64_t n_items64 = (int64_t)L.num_splits * L.n_kv_heads * L.batch * n_rg;
+  if (n_items64 >= (1ll << 31)) return QSP_ERR_UNSUPPORTED;
+  const int n_items = (int)n_items64;
+  static int sms = 0;
+  if (sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms <= 0) sms = 148;
+  }
+  const int grid = std::min(n_items, sms);
+#define QSP_AT3_CASE(HDV)                                                                    \
+  case HDV: {                                                                                \
+    auto kern = attn_ws_kernel<HDV>;                                                         \
+    const size_t smem = At3Smem<HDV>::BYTES;                                                 \
+    static bool set = false;                                                                 \
+    if (!set) {                                                                              \
+      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) \
+          != cudaSuccess)                                                                    \
+        return set_error(QSP_ERR_CUDA, "qsp_attn_verify: cannot reserve shared memory");     \
+      set = true;                                                                            \
+    }                                                                                        \
+    kern<<<grid, AT3_THREADS, smem, st>>>(mk, mv, L, n_rg, n_items);                          \
+    return check_launch("qsp_attn_verify(ws)");                                              \
+  }
+  switch (L.head_dim) {
+    QSP_AT3_CASE(64)
+    QSP_AT3_CASE(128)
+    QSP_AT3_CASE(256)
+    default:
+      return QSP_ERR_UNSUPPORTED;
+  }
+#undef QSP_AT3_CASE
 }
 
 int attn_device_error(int reset) {
