@@ -580,9 +580,10 @@ def run_attn_workload(args):
     from lollm_b200.qwen3_5.modeling_qwen3_5 import rope_table
     dev = torch.device("cuda", 0)
     B, T, nh, nkv, hd, rd, ps = 64, 4, 16, 2, 256, 64, 64
+    lo, hi = (int(x) for x in args.attn_len.split(","))
     g = torch.Generator(device=dev); g.manual_seed(0)
-    lens = torch.randint(1024, 32768 + 1 - T, (B,), generator=g, device=dev, dtype=torch.int32)
-    max_pages = (32768 + ps - 1) // ps
+    lens = torch.randint(lo, hi + 1 - T, (B,), generator=g, device=dev, dtype=torch.int32)
+    max_pages = (hi + ps - 1) // ps
     # only the pages each sequence uses are allocated, in shuffled order (a paged pool)
     need = [(int(l) + T + ps - 1) // ps for l in lens.tolist()]
     num_pages = sum(need)
@@ -596,9 +597,9 @@ def run_attn_workload(args):
     vp = torch.empty_like(kp).normal_(generator=g)
     qkv = torch.randn(B * T, 2 * nh * hd + 2 * nkv * hd, generator=g, device=dev).to(torch.bfloat16)
     qn = torch.zeros(hd, dtype=torch.bfloat16, device=dev); kn = torch.zeros_like(qn)
-    cos, sin = rope_table(rd, 1e7, 32768 + 8, torch.bfloat16)
+    cos, sin = rope_table(rd, 1e7, hi + 8, torch.bfloat16)
     cos, sin = cos.to(dev), sin.to(dev)
-    splits = max(1, (32768 + 511) // 512)
+    splits = max(1, (hi + 511) // 512)
     q_buf = torch.empty(B * T, nh * hd, dtype=torch.bfloat16, device=dev)
     out = torch.empty(B * T, nh * hd, dtype=torch.bfloat16, device=dev)
     part = torch.empty(K.attn_workspace_bytes(B, T, nh, hd, splits) // 4, device=dev)
@@ -606,7 +607,7 @@ def run_attn_workload(args):
     d.batch, d.tokens, d.n_heads, d.n_kv_heads, d.head_dim, d.rotary_dim = B, T, nh, nkv, hd, rd
     d.page_size, d.max_pages, d.num_pages, d.dtype, d.eps, d.scale = ps, max_pages, num_pages, L.QSP_BF16, 1e-6, 1 / 16
     d.qkv, d.ld_qkv, d.q_norm_w, d.k_norm_w = qkv.data_ptr(), qkv.stride(0), qn.data_ptr(), kn.data_ptr()
-    d.rope_cos, d.rope_sin, d.rope_rows = cos.data_ptr(), sin.data_ptr(), 32768 + 8
+    d.rope_cos, d.rope_sin, d.rope_rows = cos.data_ptr(), sin.data_ptr(), hi + 8
     d.k_pages, d.v_pages, d.page_table, d.seq_lens = kp.data_ptr(), vp.data_ptr(), page_table.data_ptr(), lens.data_ptr()
     d.q_buf, d.out, d.ld_out, d.partial, d.num_splits, d.bad_index = (q_buf.data_ptr(), out.data_ptr(), out.stride(0),
                                                                      part.data_ptr(), splits, 0)
@@ -621,12 +622,12 @@ def run_attn_workload(args):
     Ls = lens.tolist()
     algo = sum((l + T) * nkv * hd * 2 * 2 for l in Ls)
     t = statistics.mean(ms) / 1000
-    return {"metric": "verify attention (64 seq, T=4, L~U[1024,32768]) KV GB/s", "value": algo / t / 1e9,
+    return {"metric": f"verify attention (64 seq, T=4, L~U[{lo},{hi}]) KV GB/s", "value": algo / t / 1e9,
             "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": statistics.mean(ms), "higher_is_better": True, "dtype": "bf16",
             "data": "synthetic (BASELINE configs[2] shapes)",
-            "config": {"workload": "attn (BASELINE configs[2])", "mean_L": sum(Ls) / B, "splits": splits},
-            "roofline": {"kernel": "attn_mma_kernel + attn_combine_kernel", "bound": "hbm", "achieved": algo / t / 1e9,
+            "config": {"workload": "attn (BASELINE configs[2] shapes)", "mean_L": sum(Ls) / B, "splits": splits},
+            "roofline": {"kernel": "attn_ws_kernel + attn_combine_kernel", "bound": "hbm", "achieved": algo / t / 1e9,
                          "peak": hbm, "unit": "GB/s", "frac": algo / t / 1e9 / hbm, "peak_source": src,
                          "traffic": None, "algorithmic_bytes_per_launch": algo}}
 
@@ -684,6 +685,8 @@ def main():
     ap.add_argument("--cpu-batch", type=int, default=2)
     ap.add_argument("--cpu-steps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--attn-len", default="1024,32768",
+                    help="attn workload: per-sequence context lengths ~ U[lo, hi] (configs[2]: 1024,32768)")
     ap.add_argument("--profile", action="store_true",
                     help="bracket the timed steps with cudaProfilerStart/Stop (for ncu --profile-from-start off)")
     ap.add_argument("--m", type=int, default=256)
