@@ -35,12 +35,12 @@ sys.path.insert(0, ROOT)
 
 METRIC = "generated tok/s (batch 64, k=3) at 1/2/4/8 B200; verify-step HBM % of peak"
 UNIT = "tok/s"
-# DRAM bytes (read + write) of one gdn_verify_kernel launch at the step's shape (64 sequences,
-# 32 value heads of 128x128, T=4), from an ncu capture of `bench.py --workload gdn`, which runs
-# exactly that launch (149.73 MB read + 93.76 MB written; some state write-back is still in L2
-# when the kernel ends).
-GDN_TRAFFIC_PER_LAUNCH = 243_495_168
-GDN_TRAFFIC_SOURCE = "ncu dram__bytes_read.sum + dram__bytes_write.sum of bench.py --workload gdn"
+# DRAM bytes (read + write) of one GDN layer update at the step's shape (64 sequences, 32 value
+# heads of 128x128, T=4): gdn_chunk_kernel from an ncu capture of `bench.py --workload gdn`,
+# which runs exactly that launch (152.65 MB read + 77.90 MB written; some state write-back is
+# still in L2 when the kernel ends). gdn_prep_kernel's few MB are not included.
+GDN_TRAFFIC_PER_LAUNCH = 230_550_528
+GDN_TRAFFIC_SOURCE = "ncu dram__bytes_read.sum + dram__bytes_write.sum of gdn_chunk_kernel, bench.py --workload gdn"
 
 
 # ─────────────────────────────────────────── helpers ───────────────────────────────────────────
@@ -327,7 +327,7 @@ def run_gpu_arm(args, cfg, ws, rank, local):
         "config": config_block(args, cfg), "clocks": clk,
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": launches_per_step * args.steps,
-        "roofline": {"kernel": "gdn_verify_kernel (one GDN layer of the verify forward, live in the step)",
+        "roofline": {"kernel": "qsp_gdn_verify = gdn_prep_kernel + gdn_chunk_kernel (one GDN layer of the verify forward, live in the step)",
                      "bound": "hbm", "achieved": gdn_achieved, "peak": hbm, "unit": "GB/s",
                      "frac": gdn_achieved / hbm, "peak_source": src,
                      "traffic": GDN_TRAFFIC_PER_LAUNCH, "traffic_source": GDN_TRAFFIC_SOURCE,
@@ -401,7 +401,7 @@ def graph_kernel_nodes(graphs) -> int:
     return total
 
 
-LIVE_CLASSES = {"gdn_verify": "gdn_verify_kernel", "attn_verify": "attn_mma_kernel + attn_combine_kernel",
+LIVE_CLASSES = {"gdn_verify": "gdn_prep_kernel + gdn_chunk_kernel", "attn_verify": "attn_ws_kernel + attn_combine_kernel",
                 "gemm": "gemm_tc_kernel", "gemm_residual_rmsnorm": "gemm_tc_kernel (+ residual/RMSNorm merge)",
                 "gemm_swiglu": "gemm_tc_kernel (+ SwiGLU merge)"}
 
@@ -567,7 +567,7 @@ def run_gdn_workload(args):
             "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": statistics.mean(ms), "higher_is_better": True, "dtype": "f32 state, bf16 io",
             "data": "synthetic (BASELINE configs[3] shapes)", "config": {"workload": "gdn (BASELINE configs[3])"},
-            "roofline": {"kernel": "gdn_verify_kernel", "bound": "hbm", "achieved": algo / t / 1e9, "peak": hbm,
+            "roofline": {"kernel": "gdn_prep_kernel + gdn_chunk_kernel", "bound": "hbm", "achieved": algo / t / 1e9, "peak": hbm,
                          "unit": "GB/s", "frac": algo / t / 1e9 / hbm, "peak_source": src, "traffic": None,
                          "algorithmic_bytes_per_launch": algo}}
 
