@@ -880,44 +880,60 @@ gdn_chunk_kernel(const qsp_gdn_layer L, const GdnRing RG, const int n_new) {
         *reinterpret_cast<float4*>(state + (int64_t)(RB * rg + 2 * p + 1) * DV + 4 * cg) = make_float4(a.y, bq.y, c2.y, d2.y);
       }
     };
-    // 4. replay the kept tokens of the previous speculative call
-    if (R > 0) {
-      float P[GDN_TB], dl[GDN_TB], c[GDN_TB];
-      gdn_dots4<DK>(S, sm.vec[0], rg, P);
-      if (R > 4) gdn_dots4<DK>(S, sm.vec[4], rg, P + 4);
-      gdn_deltas<T, DK, DV>(P, in.rep, col, sm.tabA[0], sm.gam[0], R, dl);
+    // 4. phase 0 replays the kept tokens of the previous speculative call; phase 1 applies this
+    //    call's tokens. One copy of the pass code serves both (and keeps the replay's
+    //    arithmetic identical to a fresh forward over the same tokens).
+    float o[GDN_TB];
+#pragma unroll 1
+    for (int ph = 0; ph < 2; ++ph) {
+      const int n = ph ? N : R;
+      if (n == 0) continue;
+      const int kslot = ph ? GDN_TB : 0;
+      const int ngk = (n + 3) >> 2, ng = ph ? 2 * ngk : ngk;
+      float Pk[GDN_TB], Pq[GDN_TB], dl[GDN_TB];
 #pragma unroll
-      for (int s = 0; s < GDN_TB; ++s) c[s] = s < R ? __fmul_rn(sm.tail[0][s], dl[s]) : 0.f;
-      gdn_rank<DK>(S, sm.vec[0], sm.gam[0][R - 1], c, R, rg, lane);
-      if (spec || N == 0) store_state();
-    }
-    // 5. this call's tokens
-    if (N > 0) {
-      float Pk[GDN_TB], Pq[GDN_TB], dl[GDN_TB], o[GDN_TB];
-      gdn_dots4<DK>(S, sm.vec[GDN_TB], rg, Pk);
-      gdn_dots4<DK>(S, sm.vec[2 * GDN_TB], rg, Pq);
-      if (N > 4) {
-        gdn_dots4<DK>(S, sm.vec[GDN_TB + 4], rg, Pk + 4);
-        gdn_dots4<DK>(S, sm.vec[2 * GDN_TB + 4], rg, Pq + 4);
-      }
-      gdn_deltas<T, DK, DV>(Pk, in.na, col, sm.tabA[1], sm.gam[1], N, dl);
+      for (int i = 0; i < GDN_TB; ++i) Pk[i] = Pq[i] = 0.f;
+#pragma unroll 1
+      for (int g = 0; g < ng; ++g) {   // pass 1: Sᵀk_s, then (phase 1) Sᵀq_t, four slots at a time
+        const bool isq = g >= ngk;
+        const int g4 = isq ? g - ngk : g;
+        float t4[4];
+        gdn_dots4<DK>(S, sm.vec[(isq ? 2 * GDN_TB : kslot) + 4 * g4], rg, t4);
 #pragma unroll
-      for (int t = 0; t < GDN_TB; ++t) {
-        o[t] = 0.f;
-        if (t < N) {
-          float acc = __fmul_rn(sm.gam[1][t], Pq[t]);
+        for (int i = 0; i < 4; ++i) {
 #pragma unroll
-          for (int r = 0; r <= t; ++r) acc = __fmaf_rn(sm.tabB[r][t], dl[r], acc);
-          o[t] = acc;
+          for (int jj = 0; jj < GDN_TB / 4; ++jj) {
+            if (g4 == jj) {
+              if (isq) Pq[4 * jj + i] = t4[i];
+              else Pk[4 * jj + i] = t4[i];
+            }
+          }
         }
       }
-      if (!spec) {
+      gdn_deltas<T, DK, DV>(Pk, ph ? in.na : in.rep, col, sm.tabA[ph], sm.gam[ph], n, dl);
+      if (ph) {
+#pragma unroll
+        for (int t = 0; t < GDN_TB; ++t) {
+          o[t] = 0.f;
+          if (t < N) {
+            float acc = __fmul_rn(sm.gam[1][t], Pq[t]);
+#pragma unroll
+            for (int r = 0; r <= t; ++r) acc = __fmaf_rn(sm.tabB[r][t], dl[r], acc);
+            o[t] = acc;
+          }
+        }
+      }
+      // the state after these tokens: needed by phase 1 after a replay, and stored when it is
+      // committed (the replay always; this call's tokens only when not speculative)
+      if (ph == 0 || !spec) {
         float c[GDN_TB];
 #pragma unroll
-        for (int s = 0; s < GDN_TB; ++s) c[s] = s < N ? __fmul_rn(sm.tail[1][s], dl[s]) : 0.f;
-        gdn_rank<DK>(S, sm.vec[GDN_TB], sm.gam[1][N - 1], c, N, rg, lane);
-        store_state();
+        for (int s = 0; s < GDN_TB; ++s) c[s] = s < n ? __fmul_rn(sm.tail[ph][s], dl[s]) : 0.f;
+        gdn_rank<DK>(S, sm.vec[kslot], sm.gam[ph][n - 1], c, n, rg, lane);
+        if (ph == 1 || spec || N == 0) store_state();
       }
+    }
+    if (N > 0) {
       // 6. RMSNormGated over the dv columns of each token: w·round(x̂)·silu(z), x = round(core)
 #pragma unroll
       for (int t = 0; t < GDN_TB; ++t) {
