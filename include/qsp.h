@@ -270,6 +270,50 @@ int qsp_sample_rows(const void* logits, int64_t ld, int64_t rows, int64_t vocab,
 /* Bytes of fp32 workspace the selection kernels need for `rows` rows of `vocab`. */
 size_t qsp_select_workspace_bytes(int64_t rows, int64_t vocab);
 
+/* Sampling filters of sample_next (src/generate.py:17-37): repetition penalty over a
+ * context, temperature, top-k, top-p. Row r of a call belongs to sequence b = r / rows_per_seq
+ * and scores position t = r % rows_per_seq; its penalty context is
+ *   hist[b, 0 : hist_n[b]]  ∪  step_ids[b, 0 : step_base + t]
+ * (either part may be NULL; lengths are clamped to hist_ld and step_ld). Duplicates in the
+ * context are penalised once. */
+typedef struct qsp_sample_params {
+  float temperature;         /* <= 0: greedy (argmax of the penalised logits) */
+  int32_t top_k;             /* <= 0 or >= vocab: off */
+  float top_p;               /* outside (0, 1): off */
+  float repetition_penalty;  /* 1: off; else x/p for x > 0, x·p for x <= 0 on context tokens */
+  const int64_t* hist;       /* [B, hist_ld] token history (prompt + committed tokens) */
+  int64_t hist_ld;
+  const int32_t* hist_n;     /* [B] */
+  const int64_t* step_ids;   /* [B, step_ld] tokens of the step being scored */
+  int64_t step_ld;
+  int32_t step_base;
+} qsp_sample_params;
+
+/* Bytes of workspace qsp_sample_filtered / qsp_spec_sample_filtered need for `rows` scored
+ * rows of `vocab` (the penalised, scaled rows in fp32 plus per-row statistics). */
+size_t qsp_filter_workspace_bytes(int64_t rows, int64_t vocab);
+
+/* sample_next for every row (src/generate.py:17-37): penalty → argmax when
+ * temperature <= 0; else /temperature → top-k → top-p → categorical draw by inverse CDF at
+ * u[r] over the kept tokens (the reference draws with torch.multinomial from the same
+ * distribution). Ties at the top-p boundary value are all kept. */
+int qsp_sample_filtered(const void* logits, int64_t ld, int64_t rows, int32_t rows_per_seq,
+                        int64_t vocab, const qsp_sample_params* params, const float* u,
+                        int64_t* out, int64_t out_stride, void* workspace, size_t workspace_bytes,
+                        int dtype, void* stream);
+
+/* qsp_spec_sample / qsp_greedy_verify with the filters: p and q are the filtered target
+ * (B·(k+1) rows) and draft (B·k rows) distributions, each row's penalty context being the
+ * history plus the step's tokens up to the scored position (step_ids = the step's
+ * [pending, d1..dk], step_base = 1). temperature <= 0: greedy verification of the
+ * penalised argmax, as generate_mtp does (mtp.py:139-148). */
+int qsp_spec_sample_filtered(const void* target_logits, int64_t ld_t, const void* draft_logits,
+                             int64_t ld_d, int32_t batch, int32_t k, int64_t vocab,
+                             const qsp_sample_params* params, const int64_t* drafts,
+                             int64_t drafts_ld, const float* u_accept, const float* u_resample,
+                             int32_t* accept_n, int64_t* next_tok, void* workspace,
+                             size_t workspace_bytes, int dtype, void* stream);
+
 /* ---------------------------------------------------------------- cache bookkeeping */
 
 /* After a forward of T tokens: seq_lens[b] += T; parity ^= 1; speculative → replay_n =

@@ -34,6 +34,13 @@ class GdnLayer(C.Structure):
                 ("replay_n", vp), ("conv_off", vp), ("parity", vp), ("out", vp), ("ld_out", i64)]
 
 
+class SampleParams(C.Structure):
+    """Mirror of `qsp_sample_params`."""
+    _fields_ = [("temperature", f32), ("top_k", i32), ("top_p", f32), ("repetition_penalty", f32),
+                ("hist", vp), ("hist_ld", i64), ("hist_n", vp), ("step_ids", vp), ("step_ld", i64),
+                ("step_base", i32)]
+
+
 class AttnLayer(C.Structure):
     """Mirror of `qsp_attn_layer`."""
     _fields_ = [("batch", i32), ("tokens", i32), ("n_heads", i32), ("n_kv_heads", i32),
@@ -75,6 +82,11 @@ SIGNATURES = {
                                   vp, C.c_int, vp]),
     "qsp_sample_rows": (C.c_int, [vp, i64, i64, i64, f32, vp, vp, i64, vp, C.c_int, vp]),
     "qsp_select_workspace_bytes": (sz, [i64, i64]),
+    "qsp_filter_workspace_bytes": (sz, [i64, i64]),
+    "qsp_sample_filtered": (C.c_int, [vp, i64, i64, i32, i64, C.POINTER(SampleParams), vp, vp, i64, vp, sz,
+                                      C.c_int, vp]),
+    "qsp_spec_sample_filtered": (C.c_int, [vp, i64, vp, i64, i32, i32, i64, C.POINTER(SampleParams), vp, i64,
+                                           vp, vp, vp, vp, vp, sz, C.c_int, vp]),
     "qsp_cache_finalize": (C.c_int, [i32, i32, i32, vp, vp, vp, vp, vp]),
     "qsp_cache_accept": (C.c_int, [i32, i32, vp, vp, vp, vp, vp]),
     "qsp_commit_tokens": (C.c_int, [i32, i32, vp, vp, vp, vp, i64, vp, vp]),

@@ -241,6 +241,233 @@ __global__ void __launch_bounds__(SEL_THREADS) sample_rows_kernel(const T* __res
   if (threadIdx.x == 0) out[r * out_stride] = pick;
 }
 
+
+// ------------------------------------------------------------------ filtered sampling
+// The token filters of sample_next (src/generate.py:17-37), row by row: repetition penalty
+// over a context, temperature, top-k, top-p. filter_rows_kernel materialises the row's
+// penalised, scaled logits w (fp32, rounded to the model dtype after every op the reference
+// does in that dtype) and a threshold `thr`: the kept tokens are exactly {j : w[j] ≥ thr}.
+// Thresholds come from exact radix selects over the order-preserving 32-bit keys of w: top-k
+// is the k-th largest value (ties with it survive, like torch.topk + `<`), top-p is the value
+// of the first token, in descending order, at which the cumulative softmax mass exceeds
+// top_p (masses as 2^-40 fixed point, so the select is exact and order-independent; tokens
+// tied with that value are all kept, where the reference keeps them in sort order).
+struct FilterRow {
+  float m, z, thr, pad;   // max kept w, Σ_kept e^{w−m}, threshold
+};
+
+__device__ __forceinline__ uint32_t fkey(float f) {
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float fkey_inv(uint32_t k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+
+constexpr double FIX_SCALE = 1099511627776.0;   // 2^40
+
+template <typename T>
+__global__ void __launch_bounds__(SEL_THREADS) filter_rows_kernel(
+    const T* __restrict__ logits, int64_t ld, int rows_per_seq, int64_t vocab, qsp_sample_params sp,
+    float* __restrict__ wrows, FilterRow* __restrict__ stats, int64_t* __restrict__ amax) {
+  __shared__ unsigned long long hist[256];
+  __shared__ float red[32];
+  __shared__ uint32_t sel_sh;
+  __shared__ unsigned long long above_sh, tot_sh;
+  const int64_t r = blockIdx.x;
+  const int b = (int)(r / rows_per_seq), t = (int)(r % rows_per_seq);
+  const T* row = logits + r * ld;
+  float* w = wrows + r * vocab;
+  const bool greedy = !(sp.temperature > 0.f);
+  const int tid = threadIdx.x;
+  // 1. w = logits (/ temperature, in the logits dtype), then the penalty on the context
+  for (int64_t j = tid; j < vocab; j += blockDim.x) {
+    const float x = dt<T>::to_f(row[j]);
+    w[j] = greedy ? x : dt<T>::round(x / sp.temperature);
+  }
+  __syncthreads();
+  if (sp.repetition_penalty != 1.f) {
+    // context lengths are clamped to the rows they index
+    const int nh = sp.hist ? (int)min((int64_t)max(sp.hist_n[b], 0), sp.hist_ld) : 0;
+    const int ns = sp.step_ids ? (int)min((int64_t)(sp.step_base + t), sp.step_ld) : 0;
+    for (int i = tid; i < nh + ns; i += blockDim.x) {
+      const int64_t id = i < nh ? sp.hist[(int64_t)b * sp.hist_ld + i] : sp.step_ids[(int64_t)b * sp.step_ld + (i - nh)];
+      if (id < 0 || id >= vocab) continue;
+      const float x = dt<T>::to_f(row[id]);
+      const float y = dt<T>::round(x > 0.f ? x / sp.repetition_penalty : x * sp.repetition_penalty);
+      w[id] = greedy ? y : dt<T>::round(y / sp.temperature);   // duplicates write the same value
+    }
+  }
+  __syncthreads();
+  if (greedy) {
+    if (amax) {
+      const long long i = row_argmax<float>(w, vocab);
+      if (tid == 0) amax[r] = i;
+    }
+    return;
+  }
+  // 2. top-k: the k-th largest w (radix select over 8-bit digits, most significant first)
+  float thr = -INFINITY;
+  if (sp.top_k > 0 && sp.top_k < vocab) {
+    uint32_t prefix = 0, mask = 0;
+    long long kk = sp.top_k;
+    for (int shift = 24; shift >= 0; shift -= 8) {
+      for (int i = tid; i < 256; i += blockDim.x) hist[i] = 0;
+      __syncthreads();
+      for (int64_t j = tid; j < vocab; j += blockDim.x) {
+        const uint32_t key = fkey(w[j]);
+        if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1ull);
+      }
+      __syncthreads();
+      if (tid == 0) {
+        unsigned long long c = 0;
+        uint32_t sel = 0;
+        for (int d = 255; d >= 0; --d) {
+          if (c + hist[d] >= (unsigned long long)kk) { sel = (uint32_t)d; break; }
+          c += hist[d];
+        }
+        kk -= (long long)c;
+        sel_sh = sel;
+        above_sh = (unsigned long long)kk;
+      }
+      __syncthreads();
+      prefix |= sel_sh << shift;
+      mask |= 255u << shift;
+      kk = (long long)above_sh;
+      __syncthreads();
+    }
+    thr = fkey_inv(prefix);
+  }
+  // 3. max over the kept tokens
+  float m = -INFINITY;
+  for (int64_t j = tid; j < vocab; j += blockDim.x)
+    if (w[j] >= thr) m = fmaxf(m, w[j]);
+  m = warp_max(m);
+  {
+    const int lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+    if (lane == 0) red[warp] = m;
+    __syncthreads();
+    m = warp_max(lane < nw ? red[lane] : -INFINITY);
+    __syncthreads();
+  }
+  // 4. top-p: descend the key digits by fixed-point softmax mass
+  if (sp.top_p > 0.f && sp.top_p < 1.f && m > -INFINITY) {
+    if (tid == 0) tot_sh = 0;
+    __syncthreads();
+    unsigned long long q = 0;
+    for (int64_t j = tid; j < vocab; j += blockDim.x)
+      if (w[j] >= thr) q += (unsigned long long)((double)expf(w[j] - m) * FIX_SCALE);
+    atomicAdd(&tot_sh, q);
+    __syncthreads();
+    const unsigned long long tgt = (unsigned long long)((double)sp.top_p * (double)tot_sh);
+    if (tgt < tot_sh) {
+      uint32_t prefix = 0, mask = 0;
+      unsigned long long above = 0;
+      for (int shift = 24; shift >= 0; shift -= 8) {
+        for (int i = tid; i < 256; i += blockDim.x) hist[i] = 0;
+        __syncthreads();
+        for (int64_t j = tid; j < vocab; j += blockDim.x) {
+          const float x = w[j];
+          if (!(x >= thr)) continue;
+          const uint32_t key = fkey(x);
+          if ((key & mask) == prefix)
+            atomicAdd(&hist[(key >> shift) & 255u], (unsigned long long)((double)expf(x - m) * FIX_SCALE));
+        }
+        __syncthreads();
+        if (tid == 0) {
+          unsigned long long c = above;
+          uint32_t sel = 0;
+          for (int d = 255; d >= 0; --d) {
+            if (c + hist[d] > tgt) { sel = (uint32_t)d; break; }
+            c += hist[d];
+          }
+          sel_sh = sel;
+          above_sh = c;
+        }
+        __syncthreads();
+        prefix |= sel_sh << shift;
+        mask |= 255u << shift;
+        above = above_sh;
+        __syncthreads();
+      }
+      thr = fmaxf(thr, fkey_inv(prefix));
+    }
+  }
+  // 5. normaliser over the kept tokens
+  float z = 0.f;
+  for (int64_t j = tid; j < vocab; j += blockDim.x)
+    if (w[j] >= thr) z += expf(w[j] - m);
+  z = block_sum(z, red);
+  if (tid == 0) stats[r] = FilterRow{m, z, thr, 0.f};
+}
+
+__device__ __forceinline__ float filtered_p(const float* w, const FilterRow& s, int64_t x) {
+  const float v = w[x];
+  return v >= s.thr ? expf(v - s.m) / s.z : 0.f;
+}
+
+__global__ void __launch_bounds__(SEL_THREADS) sample_filtered_kernel(const float* __restrict__ wrows, int64_t vocab,
+                                                                      const FilterRow* __restrict__ stats,
+                                                                      const float* __restrict__ u, int64_t* out,
+                                                                      int64_t out_stride) {
+  __shared__ double part[SEL_THREADS + 1];
+  __shared__ long long res[2];
+  const int64_t r = blockIdx.x;
+  const float* w = wrows + r * vocab;
+  const FilterRow s = stats[r];
+  auto pw = [&](int64_t x) -> float { return filtered_p(w, s, x); };
+  const long long pick = block_inverse_cdf(pw, vocab, u[r], part, res);
+  if (threadIdx.x == 0) out[r * out_stride] = pick;
+}
+
+__global__ void amax_copy_kernel(const int64_t* __restrict__ amax, int64_t rows, int64_t* out, int64_t out_stride) {
+  const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (r < rows) out[r * out_stride] = amax[r];
+}
+
+// Per sequence: speculative accept chain over the filtered p (target) and q (draft) rows,
+// then the residual / bonus draw.
+__global__ void __launch_bounds__(SEL_THREADS) spec_filtered_kernel(
+    const float* __restrict__ tw, const float* __restrict__ dw, int k, int64_t vocab,
+    const FilterRow* __restrict__ ts, const FilterRow* __restrict__ ds, const int64_t* __restrict__ drafts,
+    int64_t dld, const float* __restrict__ u_acc, const float* __restrict__ u_res, int32_t* accept_n,
+    int64_t* next_tok) {
+  __shared__ double part[SEL_THREADS + 1];
+  __shared__ long long res[2];
+  const int b = blockIdx.x;
+  int a = 0;
+  for (; a < k; ++a) {
+    const int64_t d = drafts[(int64_t)b * dld + a];
+    const int64_t tr = (int64_t)b * (k + 1) + a, dr = (int64_t)b * k + a;
+    const float p = (d >= 0 && d < vocab) ? filtered_p(tw + tr * vocab, ts[tr], d) : 0.f;
+    const float q = (d >= 0 && d < vocab) ? filtered_p(dw + dr * vocab, ds[dr], d) : 0.f;
+    if (!(u_acc[(int64_t)b * k + a] * q < p)) break;
+  }
+  const int64_t tr = (int64_t)b * (k + 1) + a;
+  const float* pw_row = tw + tr * vocab;
+  const FilterRow pst = ts[tr];
+  long long pick;
+  if (a < k) {
+    const int64_t dr = (int64_t)b * k + a;
+    const float* qw_row = dw + dr * vocab;
+    const FilterRow qst = ds[dr];
+    auto resid = [&](int64_t x) -> float { return fmaxf(0.f, filtered_p(pw_row, pst, x) - filtered_p(qw_row, qst, x)); };
+    pick = block_inverse_cdf(resid, vocab, u_res[b], part, res);
+    if (part[SEL_THREADS] <= 0.0) {   // p == q everywhere leaves no residual mass: draw from p
+      __syncthreads();
+      auto pw = [&](int64_t x) -> float { return filtered_p(pw_row, pst, x); };
+      pick = block_inverse_cdf(pw, vocab, u_res[b], part, res);
+    }
+  } else {
+    auto pw = [&](int64_t x) -> float { return filtered_p(pw_row, pst, x); };
+    pick = block_inverse_cdf(pw, vocab, u_res[b], part, res);
+  }
+  if (threadIdx.x == 0) {
+    accept_n[b] = a;
+    next_tok[b] = pick;
+  }
+}
+
 }  // namespace qsp
 
 using namespace qsp;
@@ -332,6 +559,110 @@ int qsp_sample_rows(const void* logits, int64_t ld, int64_t rows, int64_t vocab,
                                                                   out, out_stride);
   });
   return check_launch("qsp_sample_rows");
+}
+
+}  // extern "C"
+
+static size_t filter_layout(int64_t rows, int64_t vocab, size_t* stats_off, size_t* amax_off) {
+  size_t off = (size_t)rows * vocab * sizeof(float);
+  off = (off + 255) / 256 * 256;
+  *stats_off = off;
+  off += (size_t)rows * sizeof(FilterRow);
+  off = (off + 255) / 256 * 256;
+  *amax_off = off;
+  off += (size_t)rows * sizeof(int64_t);
+  return off;
+}
+
+extern "C" size_t qsp_filter_workspace_bytes(int64_t rows, int64_t vocab) {
+  if (rows <= 0 || vocab <= 0) return 0;
+  size_t a, b;
+  return filter_layout(rows, vocab, &a, &b);
+}
+
+static int check_params(const qsp_sample_params* sp, const char* who) {
+  QSP_REQUIRE(sp != nullptr, "%s: null params", who);
+  QSP_REQUIRE(sp->repetition_penalty > 0.f, "%s: repetition_penalty must be > 0", who);
+  QSP_REQUIRE(sp->hist == nullptr || (sp->hist_n != nullptr && sp->hist_ld >= 0), "%s: hist needs hist_n", who);
+  QSP_REQUIRE(sp->step_ids == nullptr || (sp->step_ld >= 0 && sp->step_base >= 0), "%s: bad step ids", who);
+  return QSP_OK;
+}
+
+template <typename T>
+static int launch_filter(const void* logits, int64_t ld, int64_t rows, int32_t rows_per_seq, int64_t vocab,
+                         const qsp_sample_params& sp, float* w, FilterRow* st, int64_t* amax, cudaStream_t s) {
+  filter_rows_kernel<T><<<(unsigned)rows, SEL_THREADS, 0, s>>>((const T*)logits, ld, rows_per_seq, vocab, sp, w, st,
+                                                                amax);
+  return check_launch("qsp filter_rows");
+}
+
+extern "C" {
+
+int qsp_sample_filtered(const void* logits, int64_t ld, int64_t rows, int32_t rows_per_seq, int64_t vocab,
+                        const qsp_sample_params* params, const float* u, int64_t* out, int64_t out_stride,
+                        void* workspace, size_t workspace_bytes, int dtype, void* stream) {
+  int rc = check_params(params, "qsp_sample_filtered");
+  if (rc) return rc;
+  QSP_REQUIRE(logits && out && out_stride >= 1 && rows_per_seq >= 1, "qsp_sample_filtered: null pointer / bad stride");
+  QSP_REQUIRE(rows >= 0 && rows < (1ll << 31) && vocab > 0 && ld >= vocab, "qsp_sample_filtered: bad shape");
+  if (rows == 0) return QSP_OK;
+  const bool greedy = !(params->temperature > 0.f);
+  QSP_REQUIRE(greedy || u != nullptr, "qsp_sample_filtered: uniforms required");
+  size_t so, ao;
+  const size_t need = filter_layout(rows, vocab, &so, &ao);
+  QSP_REQUIRE(workspace && aligned(workspace, 256) && workspace_bytes >= need,
+              "qsp_sample_filtered: workspace of %zu bytes (256-byte aligned) required", need);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  float* w = reinterpret_cast<float*>(ws);
+  FilterRow* st = reinterpret_cast<FilterRow*>(ws + so);
+  int64_t* amax = reinterpret_cast<int64_t*>(ws + ao);
+  cudaStream_t s = as_stream(stream);
+  QSP_DISPATCH_DTYPE(dtype, T, { rc = launch_filter<T>(logits, ld, rows, rows_per_seq, vocab, *params, w, st, amax, s); });
+  if (rc) return rc;
+  if (greedy) {
+    amax_copy_kernel<<<(unsigned)((rows + 127) / 128), 128, 0, s>>>(amax, rows, out, out_stride);
+    return check_launch("qsp_sample_filtered(argmax)");
+  }
+  sample_filtered_kernel<<<(unsigned)rows, SEL_THREADS, 0, s>>>(w, vocab, st, u, out, out_stride);
+  return check_launch("qsp_sample_filtered");
+}
+
+int qsp_spec_sample_filtered(const void* target_logits, int64_t ld_t, const void* draft_logits, int64_t ld_d,
+                             int32_t batch, int32_t k, int64_t vocab, const qsp_sample_params* params,
+                             const int64_t* drafts, int64_t drafts_ld, const float* u_accept,
+                             const float* u_resample, int32_t* accept_n, int64_t* next_tok, void* workspace,
+                             size_t workspace_bytes, int dtype, void* stream) {
+  int rc = check_params(params, "qsp_spec_sample_filtered");
+  if (rc) return rc;
+  QSP_REQUIRE(target_logits && accept_n && next_tok, "qsp_spec_sample_filtered: null pointer");
+  QSP_REQUIRE(batch > 0 && k >= 0 && vocab > 0 && ld_t >= vocab, "qsp_spec_sample_filtered: bad shape");
+  QSP_REQUIRE(k == 0 || drafts != nullptr, "qsp_spec_sample_filtered: drafts missing");
+  const bool greedy = !(params->temperature > 0.f);
+  QSP_REQUIRE(greedy || (u_resample && (k == 0 || (draft_logits && u_accept && ld_d >= vocab))),
+              "qsp_spec_sample_filtered: draft logits and uniforms required");
+  const int64_t trows = (int64_t)batch * (k + 1), drows = greedy ? 0 : (int64_t)batch * k;
+  size_t so, ao;
+  const size_t need = filter_layout(trows + drows, vocab, &so, &ao);
+  QSP_REQUIRE(workspace && aligned(workspace, 256) && workspace_bytes >= need,
+              "qsp_spec_sample_filtered: workspace of %zu bytes (256-byte aligned) required", need);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  float* w = reinterpret_cast<float*>(ws);
+  FilterRow* st = reinterpret_cast<FilterRow*>(ws + so);
+  int64_t* amax = reinterpret_cast<int64_t*>(ws + ao);
+  cudaStream_t s = as_stream(stream);
+  QSP_DISPATCH_DTYPE(dtype, T, {
+    rc = launch_filter<T>(target_logits, ld_t, trows, k + 1, vocab, *params, w, st, amax, s);
+    if (!rc && drows > 0)
+      rc = launch_filter<T>(draft_logits, ld_d, drows, k, vocab, *params, w + trows * vocab, st + trows, nullptr, s);
+  });
+  if (rc) return rc;
+  if (greedy) {
+    greedy_accept_kernel<<<(batch + 127) / 128, 128, 0, s>>>(batch, k + 1, amax, drafts, drafts_ld, accept_n, next_tok);
+    return check_launch("qsp_spec_sample_filtered(greedy accept)");
+  }
+  spec_filtered_kernel<<<batch, SEL_THREADS, 0, s>>>(w, w + trows * vocab, k, vocab, st, st + trows, drafts, drafts_ld,
+                                                     u_accept, u_resample, accept_n, next_tok);
+  return check_launch("qsp_spec_sample_filtered");
 }
 
 }  // extern "C"

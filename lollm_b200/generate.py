@@ -2,10 +2,10 @@
 
 `generate` keeps the reference signature and its prefill → decode → stop structure; the
 model is any family model with `forward(ids, past) -> (logits, past)`. `sample_next` keeps
-the reference signature. Greedy (temperature <= 0, repetition penalty 1) runs the argmax
-kernel; temperature > 0 draws by inverse CDF from softmax(logits/τ) with a uniform from a
-seeded device generator. top-k, top-p and repetition penalty are rejected rather than
-silently ignored (not built into the fused sampler).
+the reference signature and semantics: repetition penalty over `prev_ids`, then argmax
+(temperature <= 0) or temperature → top-k → top-p → a categorical draw, by inverse CDF at a
+uniform from a seeded device generator (the reference uses torch.multinomial over the same
+distribution). Without any filter the plain argmax / softmax kernels run.
 """
 
 from __future__ import annotations
@@ -26,17 +26,25 @@ def _uniform(device, seed=0):
 
 
 def sample_next(logits, temperature, top_k, top_p, repetition_penalty=1.0, prev_ids=None):
-    if repetition_penalty != 1.0 and prev_ids:
-        raise NotImplementedError("sample_next: repetition_penalty is not supported by the qsp sampler")
-    if (top_k and top_k > 0) or (top_p and 0.0 < top_p < 1.0):
-        raise NotImplementedError("sample_next: top_k/top_p are not supported by the qsp sampler")
     row = logits.reshape(1, -1).contiguous()
-    out = torch.empty(1, dtype=torch.int64, device=row.device)
-    if temperature <= 0.0:
-        K.argmax_rows(row, out)
-    else:
-        ws = torch.empty(16, dtype=torch.float32, device=row.device)
-        K.sample_rows(row, temperature, _uniform(row.device), out, ws)
+    dev = row.device
+    out = torch.empty(1, dtype=torch.int64, device=dev)
+    filtered = ((repetition_penalty != 1.0 and prev_ids) or (top_k and top_k > 0)
+                or (top_p is not None and 0.0 < top_p < 1.0))
+    if not filtered:
+        if temperature <= 0.0:
+            K.argmax_rows(row, out)
+        else:
+            ws = torch.empty(16, dtype=torch.float32, device=dev)
+            K.sample_rows(row, temperature, _uniform(dev), out, ws)
+        return int(out.item())
+    hist = hist_n = None
+    if repetition_penalty != 1.0 and prev_ids:
+        hist = torch.tensor([list(prev_ids)], dtype=torch.int64, device=dev)
+        hist_n = torch.tensor([hist.shape[1]], dtype=torch.int32, device=dev)
+    sp = K.sample_params(temperature, top_k, top_p, repetition_penalty, hist=hist, hist_n=hist_n)
+    ws = torch.empty(K.filter_workspace_bytes(1, row.shape[1]), dtype=torch.uint8, device=dev)
+    K.sample_filtered(row, sp, _uniform(dev) if temperature > 0 else None, out, ws)
     return int(out.item())
 
 

@@ -182,6 +182,46 @@ def select_workspace_bytes(rows, vocab) -> int:
     return int(L.load().qsp_select_workspace_bytes(rows, vocab))
 
 
+def filter_workspace_bytes(rows, vocab) -> int:
+    return int(L.load().qsp_filter_workspace_bytes(rows, vocab))
+
+
+def sample_params(temperature=0.0, top_k=0, top_p=1.0, repetition_penalty=1.0, hist=None, hist_n=None,
+                  step_ids=None, step_base=0) -> L.SampleParams:
+    """qsp_sample_params for the filters of sample_next; hist [B, ·] / hist_n [B] is each
+    sequence's token context, step_ids [B, ·] the tokens of the step being scored."""
+    sp = L.SampleParams()
+    sp.temperature, sp.top_k = float(temperature), int(top_k or 0)
+    sp.top_p = float(top_p if top_p is not None else 1.0)
+    sp.repetition_penalty = float(repetition_penalty)
+    if hist is not None:
+        _cuda(hist, hist_n)
+        sp.hist, sp.hist_ld, sp.hist_n = hist.data_ptr(), hist.stride(0), hist_n.data_ptr()
+    if step_ids is not None:
+        _cuda(step_ids)
+        sp.step_ids, sp.step_ld, sp.step_base = step_ids.data_ptr(), step_ids.stride(0), int(step_base)
+    sp._keep = (hist, hist_n, step_ids)   # the struct holds raw pointers: keep the tensors alive
+    return sp
+
+
+def sample_filtered(logits, params: L.SampleParams, u, out, workspace, rows=None, rows_per_seq=1, out_stride=1):
+    _cuda(logits, out, workspace)
+    n = logits.shape[0] if rows is None else rows
+    L.call("qsp_sample_filtered", logits.data_ptr(), logits.stride(0), n, rows_per_seq, logits.shape[1],
+           C.byref(params), L.ptr(u), out.data_ptr(), out_stride, workspace.data_ptr(),
+           workspace.numel() * workspace.element_size(), L.dtype_code(logits.dtype), _s())
+
+
+def spec_sample_filtered(target_logits, draft_logits, batch, k, params: L.SampleParams, drafts, drafts_ld,
+                         u_accept, u_resample, accept_n, next_tok, workspace):
+    _cuda(target_logits, accept_n, next_tok, workspace)
+    L.call("qsp_spec_sample_filtered", target_logits.data_ptr(), target_logits.stride(0), L.ptr(draft_logits),
+           0 if draft_logits is None else draft_logits.stride(0), batch, k, target_logits.shape[1],
+           C.byref(params), L.ptr(drafts), drafts_ld, L.ptr(u_accept), L.ptr(u_resample), accept_n.data_ptr(),
+           next_tok.data_ptr(), workspace.data_ptr(), workspace.numel() * workspace.element_size(),
+           L.dtype_code(target_logits.dtype), _s())
+
+
 def cache_finalize(batch, tokens, speculative, seq_lens, replay_n, conv_off, parity):
     L.call("qsp_cache_finalize", batch, tokens, 1 if speculative else 0, seq_lens.data_ptr(),
            replay_n.data_ptr(), conv_off.data_ptr(), parity.data_ptr(), _s())

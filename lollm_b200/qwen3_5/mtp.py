@@ -61,10 +61,11 @@ class MTP:
 
     @torch.no_grad()
     def draft(self, hidden_last: torch.Tensor, ids: torch.Tensor, k: int, temperature: float = 0.0,
-              u_draft: torch.Tensor | None = None):
+              u_draft: torch.Tensor | None = None, filtered=None):
         """Fill ids[:, 1..k] with k drafted tokens, given ids[:, 0] (the pending token) and the
         main model's pre-norm hidden at the last kept position. Returns the [B, k, V] draft
-        logits buffer (row d = the head's logits at depth d)."""
+        logits buffer (row d = the head's logits at depth d). `filtered(d, logits_d)`, when
+        given, draws depth d's token with the sampling filters (stochastic drafts)."""
         cfg, m = self.cfg, self.model
         B = ids.shape[0]
         H, nh, nkv, hd = cfg.hidden_size, cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
@@ -87,6 +88,8 @@ class MTP:
             K.gemm(w["xn"], m.lm_head, lg)
             if temperature <= 0:
                 K.argmax_rows(lg, ids[:, d + 1:], rows=B, out_stride=k + 1)
+            elif filtered is not None:
+                filtered(d, lg)
             else:
                 K.sample_rows(lg, temperature, u_draft[:, d].contiguous() if u_draft.stride(0) != 1 else u_draft[:, d],
                               ids[:, d + 1:], self._sel_ws(B), rows=B, out_stride=k + 1)
@@ -104,10 +107,15 @@ class SpecDecoder:
     """Batched k-deep speculative decoding over independent sequences on one GPU."""
 
     def __init__(self, model: Qwen3_5Model, mtp: MTP, batch: int, k: int, max_len: int, *,
-                 temperature: float = 0.0, out_capacity: int | None = None, **cache_kw):
+                 temperature: float = 0.0, top_k: int = 0, top_p: float = 1.0,
+                 repetition_penalty: float = 1.0, out_capacity: int | None = None, **cache_kw):
         self.model, self.mtp, self.B, self.k = model, mtp, batch, k
         self.T = k + 1
         self.temperature = float(temperature)
+        self.top_k, self.top_p, self.rep = int(top_k or 0), float(top_p if top_p is not None else 1.0), float(repetition_penalty)
+        # sample_next's filters (generate.py:17-37): the penalty context of a scored position
+        # is the sequence's prompt + committed tokens (`out`) plus the step's tokens before it
+        self.filtered = self.rep != 1.0 or self.top_k > 0 or 0.0 < self.top_p < 1.0
         dev = model.device
         self.cache = model.new_cache(batch, max_len, max_spec_tokens=max(self.T, 2), **cache_kw)
         self.ids = torch.zeros(batch, self.T, dtype=torch.int64, device=dev)
@@ -116,9 +124,14 @@ class SpecDecoder:
         self.next_tok = torch.zeros(batch, dtype=torch.int64, device=dev)
         self.amax = torch.zeros(batch * self.T, dtype=torch.int64, device=dev)
         self.cap = out_capacity or max_len
-        self.out = torch.zeros(batch, self.cap, dtype=torch.int64, device=dev)
+        self.prompt_len = 0
+        self.out = torch.zeros(batch, self.cap, dtype=torch.int64, device=dev)   # prompt + committed
         self.n_out = torch.zeros(batch, dtype=torch.int32, device=dev)
         self.sel_ws = torch.empty(4 * batch * self.T + 64, dtype=torch.float32, device=dev)
+        self.filt_ws = None
+        if self.filtered:
+            V = model.cfg.vocab_size
+            self.filt_ws = torch.empty(K.filter_workspace_bytes(batch * (2 * k + 1), V), dtype=torch.uint8, device=dev)
         self.u = None            # uniforms for stochastic steps: dict of device tensors
         self.graph = None
 
@@ -132,22 +145,44 @@ class SpecDecoder:
         prompts = prompts.to(self.model.device).contiguous()
         for s in range(0, P, chunk):
             lrow, hid = self.model.prefill_last(prompts[:, s:s + chunk], self.cache)
-        if self.temperature <= 0:
+        # the output rows start with the prompt (the repetition-penalty context)
+        self.prompt_len = P
+        self.out = torch.zeros(B, P + self.cap, dtype=torch.int64, device=self.model.device)
+        self.out[:, :P] = prompts
+        self.n_out.fill_(P)
+        if self.filtered:
+            sp = self._params(None, 0)
+            K.sample_filtered(lrow, sp, u_first, self.ids, self.filt_ws, rows=B, out_stride=self.T)
+        elif self.temperature <= 0:
             K.argmax_rows(lrow, self.ids, rows=B, out_stride=self.T)
         else:
             K.sample_rows(lrow, self.temperature, u_first, self.ids, self.sel_ws, rows=B, out_stride=self.T)
         self.hidden_last.copy_(hid)
-        self.n_out.zero_()
+
+    def _params(self, step_ids, step_base):
+        return K.sample_params(self.temperature, self.top_k, self.top_p, self.rep, hist=self.out,
+                               hist_n=self.n_out, step_ids=step_ids, step_base=step_base)
 
     # ------------------------------------------------------------------ one step
     @torch.no_grad()
     def step(self):
         m, B, T, k = self.model, self.B, self.T, self.k
         stochastic = self.temperature > 0
+        filt = None
+        if self.filtered and stochastic:
+            def filt(d, lg):   # depth d predicts token d+1 after [pending, d1..dd]
+                K.sample_filtered(lg, self._params(self.ids, d + 1), self.u["draft"][:, d].contiguous(),
+                                  self.ids[:, d + 1:], self.filt_ws, rows=B, out_stride=k + 1)
         dl = self.mtp.draft(self.hidden_last, self.ids, k, self.temperature,
-                            self.u["draft"] if stochastic else None)
+                            self.u["draft"] if stochastic else None, filtered=filt)
         ws = m._forward_into(self.ids, self.cache, B, T, True)
-        if not stochastic:
+        if self.filtered:
+            K.spec_sample_filtered(ws.logits, dl.view(B * k, -1) if stochastic else None, B, k,
+                                   self._params(self.ids, 1), self.ids[:, 1:], T,
+                                   self.u["accept"] if stochastic else None,
+                                   self.u["resample"] if stochastic else None,
+                                   self.accept_n, self.next_tok, self.filt_ws)
+        elif not stochastic:
             K.greedy_verify(ws.logits, B, T, self.ids[:, 1:], T, self.accept_n, self.next_tok, self.amax)
         else:
             K.spec_sample(ws.logits, dl.view(B * k, -1), B, k, self.temperature, self.ids[:, 1:], T,
@@ -176,26 +211,27 @@ class SpecDecoder:
             self.graph.replay()
 
     def outputs(self):
+        """The committed tokens of every sequence (after its prompt)."""
         n = self.n_out.tolist()
         o = self.out.cpu()
-        return [o[b, :min(n[b], self.cap)].tolist() for b in range(self.B)]
+        P = self.prompt_len
+        return [o[b, P:min(n[b], P + self.cap)].tolist() for b in range(self.B)]
 
 
 @torch.no_grad()
 def generate_mtp(model: Qwen3_5Model, mtp: MTP, ids, decode, stop_ids, device=None, *,
-                 max_new_tokens=128, temperature=0.0, top_k=0, top_p=1.0,
-                 repetition_penalty=1.0, k: int = 1, seed: int = 0):
-    """Drop-in for the reference generator (mtp.py:92-162): yields text pieces of one sequence.
-    Greedy output equals `generate()`; temperature > 0 uses the lossless sampler with uniforms
-    from a seeded device generator. top-k / top-p / repetition penalty are not implemented
-    in the fused sampler and are rejected rather than silently ignored."""
-    if repetition_penalty != 1.0 or (top_k and top_k > 0) or (top_p and 0.0 < top_p < 1.0):
-        raise NotImplementedError("generate_mtp: repetition_penalty/top_k/top_p are not supported "
-                                  "by the fused sampler (pass 1.0 / 0 / 1.0)")
+                 max_new_tokens=128, temperature=0.7, top_k=20, top_p=0.8,
+                 repetition_penalty=1.1, k: int = 1, seed: int = 0):
+    """Drop-in for the reference generator (mtp.py:92-162), same defaults: yields text pieces
+    of one sequence. Greedy (temperature <= 0) output equals `generate()` with the same
+    repetition penalty. temperature > 0 uses the lossless p/q sampler over the filtered
+    target and draft distributions (penalty → temperature → top-k → top-p, as sample_next),
+    with uniforms from a seeded device generator."""
     eos = set(stop_ids)
     prompt = torch.tensor([list(ids)], dtype=torch.int64, device=model.device)
     dec = SpecDecoder(model, mtp, 1, k, prompt.shape[1] + max_new_tokens + k + 2,
-                      temperature=temperature, out_capacity=max_new_tokens + k + 1)
+                      temperature=temperature, top_k=top_k, top_p=top_p,
+                      repetition_penalty=repetition_penalty, out_capacity=max_new_tokens + k + 1)
     gen = torch.Generator(device=model.device)
     gen.manual_seed(seed)
     rand = lambda *s: torch.rand(*s, generator=gen, device=model.device)

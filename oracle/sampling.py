@@ -35,7 +35,7 @@ def filtered_logits(logits, temperature, top_k, top_p):
     """generate.py:25-36 without the draw: temperature, then top-k (ties with the k-th value
     survive), then top-p (keep the shortest sorted prefix whose mass reaches top_p,
     including the token that crosses it)."""
-    x = logits.float() / temperature
+    x = (logits / temperature).float()     # the reference divides in the logits' dtype
     if top_k and top_k > 0:
         kth = torch.topk(x, top_k).values[..., -1:]
         x = x.masked_fill(x < kth, float("-inf"))

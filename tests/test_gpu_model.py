@@ -105,7 +105,7 @@ def test_tiny_speculative_stream_equals_reference_greedy(golden, k):
     n = 64
     dec = SpecDecoder(model, mtp, 1, k, 128 + n + 2 * k + 4, out_capacity=n + k + 1)
     dec.prefill(prompt)
-    while int(dec.n_out[0]) < n:
+    while int(dec.n_out[0]) - dec.prompt_len < n:
         dec.step()
     got = dec.outputs()[0][:n]
     assert got == golden["tiny.greedy"][:n].tolist()
@@ -135,13 +135,61 @@ def test_micro_batched_spec_matches_oracle_greedy():
     want = OL.greedy_generate(P, cfg, prompt, n, scan="recurrent")
     dec = SpecDecoder(model, mtp, B, 3, 9 + n + 12, out_capacity=n + 8)
     dec.prefill(prompt.cuda())
-    while int(dec.n_out.min()) < n:
+    while int(dec.n_out.min()) - dec.prompt_len < n:
         dec.step()
     assert [o[:n] for o in dec.outputs()] == want.tolist()
     # the same through a captured CUDA graph (one eager warm-up step, then replays)
     dec2 = SpecDecoder(model, mtp, B, 3, 9 + n + 12, out_capacity=n + 8)
     dec2.prefill(prompt.cuda())
     dec2.capture(warmup=1)
-    while int(dec2.n_out.min()) < n:
+    while int(dec2.n_out.min()) - dec2.prompt_len < n:
         dec2.replay()
     assert [o[:n] for o in dec2.outputs()] == want.tolist()
+
+
+def test_tiny_speculative_with_repetition_penalty_equals_plain_generate():
+    """Greedy decoding with the reference's repetition penalty: the speculative decoder (k=3;
+    penalty context = prompt + committed tokens + the step's tokens up to each position)
+    commits exactly the stream of plain autoregressive generate() with the same penalty."""
+    from lollm_b200.generate import generate
+    from lollm_b200.qwen3_5 import SpecDecoder
+    cfg, model, mtp, _ = build(TINY, torch.float32, max_positions=512)
+    g = torch.Generator().manual_seed(3)
+    prompt = torch.randint(0, cfg.vocab_size, (48,), generator=g).tolist()
+    n, rp = 32, 1.3
+    dec_txt = lambda toks: "".join(chr(0x1000 + t) for t in toks)
+    text = "".join(generate(model, prompt, dec_txt, [], "cuda", max_new_tokens=n, temperature=0.0,
+                            top_k=0, top_p=1.0, repetition_penalty=rp))
+    want = [ord(c) - 0x1000 for c in text]
+    dec = SpecDecoder(model, mtp, 1, 3, len(prompt) + n + 12, repetition_penalty=rp, out_capacity=n + 4)
+    dec.prefill(torch.tensor([prompt]).cuda())
+    while int(dec.n_out[0]) - dec.prompt_len < n:
+        dec.step()
+    assert dec.outputs()[0][:n] == want
+
+
+def test_micro_filtered_stochastic_spec_runs_in_a_graph():
+    """The reference generate_mtp's default sampling (T 0.7, top-k 20, top-p 0.8, penalty 1.1)
+    through the lossless sampler, batched and captured in a CUDA graph: tokens are valid and
+    every step commits 1..k+1 tokens per sequence."""
+    from lollm_b200.qwen3_5 import SpecDecoder
+    cfg, model, mtp, _ = build(MICRO, torch.bfloat16, max_positions=256)
+    B, k = 3, 3
+    g = torch.Generator(device="cuda").manual_seed(9)
+    dec = SpecDecoder(model, mtp, B, k, 16 + 40 * (k + 1), temperature=0.7, top_k=20, top_p=0.8,
+                      repetition_penalty=1.1, out_capacity=40 * (k + 1))
+    dec.u = {"draft": torch.rand(B, k, device="cuda", generator=g), "accept": torch.rand(B, k, device="cuda", generator=g),
+             "resample": torch.rand(B, device="cuda", generator=g)}
+    dec.prefill(torch.randint(0, cfg.vocab_size, (B, 16), device="cuda"),
+                u_first=torch.rand(B, device="cuda", generator=g))
+    dec.capture(warmup=1)
+    prev = dec.n_out.clone()
+    for _ in range(10):
+        for t in dec.u.values():
+            t.copy_(torch.rand(t.shape, device="cuda", generator=g))
+        dec.replay()
+        d = (dec.n_out - prev).tolist()
+        assert all(1 <= x <= k + 1 for x in d)
+        prev = dec.n_out.clone()
+    for toks in dec.outputs():
+        assert all(0 <= t < cfg.vocab_size for t in toks)
