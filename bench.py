@@ -672,6 +672,57 @@ def run_gemm_workload(args):
                          "hbm_frac": gbs / hbm, "tensor_frac": tfs / tf}}
 
 
+def run_moe_workload(args):
+    """BASELINE configs[4] FFN: one qwen3_5_moe sparse block (hidden 2048, 512 experts top-10
+    of width 512, shared expert 512) over the verify rows of `--batch` sequences x (k+1)
+    tokens, with the residual add and the next RMSNorm. Random-init N(0, 0.02) weights,
+    N(0, 1) inputs. Algorithmic bytes: the weights of every expert hit in the call (read
+    once), the router/shared weights and the activations."""
+    from lollm_b200.qwen3_5.config import QWEN35_MOE, Qwen3_5Config
+    from lollm_b200.qwen3_5.moe import SparseMoeBlock
+    dev = torch.device("cuda", 0)
+    cfg = Qwen3_5Config.from_hf(QWEN35_MOE)
+    H, E, I, Is = cfg.hidden_size, cfg.num_experts, cfg.moe_intermediate_size, cfg.shared_expert_intermediate_size
+    m = args.batch * (args.k + 1)
+    g = torch.Generator(device=dev); g.manual_seed(0)
+    w = lambda *s: (torch.randn(*s, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    P = {"mlp.gate.weight": w(E, H), "mlp.experts.gate_up_proj": w(E, 2 * I, H), "mlp.experts.down_proj": w(E, H, I),
+         "mlp.shared_expert.gate_proj.weight": w(Is, H), "mlp.shared_expert.up_proj.weight": w(Is, H),
+         "mlp.shared_expert.down_proj.weight": w(H, Is), "mlp.shared_expert_gate.weight": w(1, H)}
+    blk = SparseMoeBlock(cfg, P, "", dtype=torch.bfloat16, device=dev)
+    del P
+    xn = torch.randn(m, H, generator=g, device=dev).to(torch.bfloat16)
+    x = torch.randn(m, H, generator=g, device=dev).to(torch.bfloat16)
+    nw = w(H)
+    y = torch.empty_like(x)
+    ws = torch.empty(blk.workspace_bytes(m), dtype=torch.uint8, device=dev)
+    counts = torch.zeros(E, dtype=torch.int32, device=dev)
+
+    def step():
+        blk(xn, x, nw, y, cfg.rms_norm_eps, m, ws, expert_counts=counts)
+
+    stream = torch.cuda.current_stream()
+    if args.profile:
+        torch.cuda.profiler.start()
+    ms = timed_loop(step, args.steps, args.warmup, stream)
+    if args.profile:
+        torch.cuda.profiler.stop()
+    hbm, _, src = peaks()
+    t = statistics.mean(ms) / 1000
+    hit = int((counts > 0).sum())
+    algo = blk.weight_bytes(counts) + m * H * 2 * 4
+    return {"metric": f"MoE FFN layer (configs[4] shape, {m} rows) weight GB/s", "value": algo / t / 1e9,
+            "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": statistics.mean(ms), "higher_is_better": True, "dtype": "bf16",
+            "data": "synthetic (BASELINE configs[4] FFN shapes, random-init N(0,0.02) weights)",
+            "config": {"workload": "moe (BASELINE configs[4] FFN)", "rows": m, "experts_hit": hit,
+                       "tokens_per_hit_expert": m * cfg.num_experts_per_tok / max(hit, 1),
+                       "l2": "weights 3.2 GB per call (> L2)"},
+            "roofline": {"kernel": "qsp_moe_ffn (moe_tc_kernel gate|up + down dominate)", "bound": "hbm",
+                         "achieved": algo / t / 1e9, "peak": hbm, "unit": "GB/s", "frac": algo / t / 1e9 / hbm,
+                         "peak_source": src, "traffic": None, "algorithmic_bytes_per_launch": algo}}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -693,14 +744,16 @@ def main():
     ap.add_argument("--n", type=int, default=12352)
     ap.add_argument("--k-dim", type=int, default=2048)
     ap.add_argument("--l2-resident", action="store_true", help="gemm workload: one weight copy (stays in L2)")
-    ap.add_argument("--workload", choices=["step", "gdn", "attn", "gemm"], default="step",
-                    help="step: the speculative step (headline); gdn / attn: BASELINE configs[3] / [2] kernels alone")
+    ap.add_argument("--workload", choices=["step", "gdn", "attn", "gemm", "moe"], default="step",
+                    help="step: the speculative step (headline); gdn / attn: BASELINE configs[3] / [2] kernels "
+                         "alone; moe: one configs[4] sparse FFN block")
     args = ap.parse_args()
     from lollm_b200.qwen3_5.config import QWEN35_2B, Qwen3_5Config
     cfg = Qwen3_5Config.from_hf(QWEN35_2B)
     if args.workload != "step":
         torch.cuda.set_device(0)
-        out = {"gdn": run_gdn_workload, "attn": run_attn_workload, "gemm": run_gemm_workload}[args.workload](args)
+        out = {"gdn": run_gdn_workload, "attn": run_attn_workload, "gemm": run_gemm_workload,
+               "moe": run_moe_workload}[args.workload](args)
         print(json.dumps(out), flush=True)
         return
     if args.impl == "reference":

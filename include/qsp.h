@@ -314,6 +314,61 @@ int qsp_spec_sample_filtered(const void* target_logits, int64_t ld_t, const void
                              int32_t* accept_n, int64_t* next_tok, void* workspace,
                              size_t workspace_bytes, int dtype, void* stream);
 
+/* ---------------------------------------------------------------- sparse MoE FFN */
+
+/*
+ * The qwen3_5_moe FFN block followed by the residual add and the next RMSNorm
+ * (SparseMoeBlock.forward, src/qwen3_5_moe/blocks.py:399-421, inside DecoderLayer.forward,
+ * src/qwen3_5_moe/modeling_qwen3_5_moe.py:57-59):
+ *   p = softmax(xn·gateᵀ) in fp32; top_k experts (largest p; equal values → lower index);
+ *   renormalised to sum 1 when norm_topk_prob; rounded to dtype;
+ *   out = Σ_e p_e·SwiGLU_e(xn) accumulated in ascending expert order with a rounding to dtype
+ *   after each add (index_add_ into a dtype buffer) + σ(shared_gate·xn)·SwiGLU_s(xn);
+ *   x := x + out; y = RMSNorm(x)·(1 + norm_w) (skipped when norm_w is NULL).
+ *
+ * Weights (dtype, row-major, 16-byte aligned):
+ *   w_in        [n_route + 2·shared_inter, hidden] — rows [0, n_experts): router
+ *               (mlp.gate.weight); row n_experts: mlp.shared_expert_gate.weight (when
+ *               shared_inter > 0); zero rows up to n_route = qsp_moe_router_rows(...); then
+ *               mlp.shared_expert.gate_proj.weight and .up_proj.weight. One GEMM reads xn once
+ *               for all of them.
+ *   gate_up     [n_experts, 2·inter, hidden]   mlp.experts.gate_up_proj (gate rows first)
+ *   down        [n_experts, hidden, inter]     mlp.experts.down_proj
+ *   shared_down [hidden, shared_inter]         mlp.shared_expert.down_proj.weight
+ * Limits: n_experts ≤ 1024, top_k ≤ 16 (and ≤ n_experts), hidden ≤ 8192.
+ * y may alias xn (xn is last read before y is written).
+ */
+typedef struct qsp_moe_layer {
+  int32_t tokens;          /* rows of this call (batch · tokens per sequence) */
+  int32_t hidden, n_experts, top_k, inter, shared_inter;
+  int32_t norm_topk_prob;
+  int32_t dtype;
+  float eps;
+  const void* xn;          /* [tokens, ld_xn] post_attention_layernorm(x) */
+  int64_t ld_xn;
+  const void* w_in;
+  const void* gate_up;
+  const void* down;
+  const void* shared_down; /* may be NULL when shared_inter == 0 */
+  void* x;                 /* [tokens, ld_x] residual stream, updated in place */
+  int64_t ld_x;
+  const void* norm_w;      /* [hidden] next RMSNorm weight, or NULL */
+  void* y;                 /* [tokens, ld_y] RMSNorm output */
+  int64_t ld_y;
+  void* workspace;         /* qsp_moe_workspace_bytes(...) bytes, 256-byte aligned */
+  size_t workspace_bytes;
+  int32_t* expert_counts;  /* optional [n_experts]: tokens routed to each expert */
+} qsp_moe_layer;
+
+int qsp_moe_ffn(const qsp_moe_layer* layer, void* stream);
+
+/* Rows of w_in before the shared expert's gate|up block (router + shared gate, padded to 8). */
+int64_t qsp_moe_router_rows(int32_t n_experts, int32_t shared_inter);
+
+/* Workspace bytes qsp_moe_ffn needs for `tokens` rows (0 for invalid sizes). */
+size_t qsp_moe_workspace_bytes(int32_t tokens, int32_t hidden, int32_t n_experts, int32_t top_k,
+                               int32_t inter, int32_t shared_inter, int32_t dtype);
+
 /* ---------------------------------------------------------------- cache bookkeeping */
 
 /* After a forward of T tokens: seq_lens[b] += T; parity ^= 1; speculative → replay_n =

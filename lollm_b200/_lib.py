@@ -53,6 +53,15 @@ class AttnLayer(C.Structure):
                 ("bad_index", vp)]
 
 
+class MoeLayer(C.Structure):
+    """Mirror of `qsp_moe_layer`."""
+    _fields_ = [("tokens", i32), ("hidden", i32), ("n_experts", i32), ("top_k", i32), ("inter", i32),
+                ("shared_inter", i32), ("norm_topk_prob", i32), ("dtype", i32), ("eps", f32),
+                ("xn", vp), ("ld_xn", i64), ("w_in", vp), ("gate_up", vp), ("down", vp),
+                ("shared_down", vp), ("x", vp), ("ld_x", i64), ("norm_w", vp), ("y", vp), ("ld_y", i64),
+                ("workspace", vp), ("workspace_bytes", sz), ("expert_counts", vp)]
+
+
 # name -> (restype, argtypes)
 SIGNATURES = {
     "qsp_last_error": (C.c_char_p, []),
@@ -87,6 +96,9 @@ SIGNATURES = {
                                       C.c_int, vp]),
     "qsp_spec_sample_filtered": (C.c_int, [vp, i64, vp, i64, i32, i32, i64, C.POINTER(SampleParams), vp, i64,
                                            vp, vp, vp, vp, vp, sz, C.c_int, vp]),
+    "qsp_moe_ffn": (C.c_int, [C.POINTER(MoeLayer), vp]),
+    "qsp_moe_router_rows": (i64, [i32, i32]),
+    "qsp_moe_workspace_bytes": (sz, [i32, i32, i32, i32, i32, i32, i32]),
     "qsp_cache_finalize": (C.c_int, [i32, i32, i32, vp, vp, vp, vp, vp]),
     "qsp_cache_accept": (C.c_int, [i32, i32, vp, vp, vp, vp, vp]),
     "qsp_commit_tokens": (C.c_int, [i32, i32, vp, vp, vp, vp, i64, vp, vp]),

@@ -579,16 +579,18 @@ int gemm_tc(const void* a, int64_t lda, const void* w, int64_t ldw, void* c, int
 namespace qsp {
 int gdn_device_error(int reset);
 int attn_device_error(int reset);
+int moe_device_error(int reset);
 }
 
 extern "C" int qsp_device_status(int32_t* code, int32_t reset) {
   QSP_REQUIRE(code != nullptr, "qsp_device_status: null pointer");
   const int gdn = qsp::gdn_device_error(reset);
   const int attn = qsp::attn_device_error(reset);
+  const int moe = qsp::moe_device_error(reset);
   int v = 0;
   cudaError_t e = cudaMemcpyFromSymbol(&v, qsp::g_qsp_dev_error, sizeof(int));
   if (e != cudaSuccess) return qsp::set_error(QSP_ERR_CUDA, "qsp_device_status: %s", cudaGetErrorString(e));
-  *code = v != 0 ? v : (gdn != 0 ? gdn : attn);
+  *code = v != 0 ? v : (gdn != 0 ? gdn : (attn != 0 ? attn : moe));
   if (reset && v != 0) {
     const int zero = 0;
     e = cudaMemcpyToSymbol(qsp::g_qsp_dev_error, &zero, sizeof(int));

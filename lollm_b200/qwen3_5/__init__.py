@@ -11,10 +11,11 @@ import torch
 from .config import Qwen3_5Config, build_config
 from .kv import Qwen3_5Cache
 from .modeling_qwen3_5 import Qwen3_5Model
+from .moe import SparseMoeBlock
 from .mtp import MTP, SpecDecoder, generate_mtp
 from .weights import load_checkpoint, random_init
 
-MODEL_TYPES = ["qwen3_5"]
+MODEL_TYPES = ["qwen3_5", "qwen3_5_moe"]   # the MoE sibling (src/qwen3_5_moe/__init__.py) shares the backbone
 DEFAULTS = {"temperature": 0.7, "top_p": 0.8, "top_k": 20, "repetition_penalty": 1.05}
 
 
@@ -34,5 +35,5 @@ def load_mtp(model: Qwen3_5Model, weights: dict, fmt: str = "hf", device=None, d
     return MTP(model, params)
 
 
-__all__ = ["Qwen3_5Config", "Qwen3_5Cache", "Qwen3_5Model", "MTP", "SpecDecoder", "generate_mtp",
+__all__ = ["Qwen3_5Config", "Qwen3_5Cache", "Qwen3_5Model", "MTP", "SpecDecoder", "SparseMoeBlock", "generate_mtp",
            "load", "load_mtp", "random_init", "MODEL_TYPES", "DEFAULTS"]

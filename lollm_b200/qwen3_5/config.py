@@ -45,6 +45,8 @@ class Qwen3_5Config:
     moe_intermediate_size: int = 0
     shared_expert_intermediate_size: int = 0
     norm_topk_prob: bool = True
+    decoder_sparse_step: int = 1
+    mlp_only_layers: list = field(default_factory=list)
     extra: dict = field(default_factory=dict)
 
     # derived dimensions (same definitions as src/qwen3_5/config.py:43-68)
@@ -87,16 +89,30 @@ class Qwen3_5Config:
     def is_moe(self) -> bool:
         return self.num_experts > 0
 
+    def is_moe_layer(self, i: int) -> bool:
+        """Sparse FFN on layer i unless it is forced dense — the HF rule of
+        `Qwen3_5MoeConfig.is_moe_layer` (src/qwen3_5_moe/config.py:80-86). The MTP head's
+        single block asks for layer 0 (src/qwen3_5_moe/mtp.py:34-36)."""
+        if i in self.mlp_only_layers or self.num_experts <= 0:
+            return False
+        return (i + 1) % self.decoder_sparse_step == 0
+
     @classmethod
     def from_hf(cls, raw: dict) -> "Qwen3_5Config":
         t = raw.get("text_config", raw)
         hidden = t["hidden_size"]
         n_head = t["num_attention_heads"]
         rp = t.get("rope_parameters", {}) or {}
+        n_experts = t.get("num_experts", t.get("n_routed_experts", 0))
+        moe_inter = t.get("moe_intermediate_size", t.get("intermediate_size", 0))
+        top_k = t.get("num_experts_per_tok", t.get("num_experts_per_token"))
+        if n_experts > 0 and top_k is None:
+            # the reference refuses to default the router width (src/qwen3_5_moe/config.py:100-113)
+            raise KeyError("qwen3_5_moe config has no 'num_experts_per_tok' (router top-k width)")
         return cls(
             vocab_size=t["vocab_size"],
             hidden_size=hidden,
-            intermediate_size=t.get("intermediate_size", 0),
+            intermediate_size=t.get("intermediate_size", moe_inter),
             num_hidden_layers=t["num_hidden_layers"],
             num_attention_heads=n_head,
             num_key_value_heads=t.get("num_key_value_heads", n_head),
@@ -117,11 +133,13 @@ class Qwen3_5Config:
             linear_key_head_dim=t["linear_key_head_dim"],
             linear_value_head_dim=t["linear_value_head_dim"],
             linear_conv_kernel_dim=t["linear_conv_kernel_dim"],
-            num_experts=t.get("num_experts", 0),
-            num_experts_per_tok=t.get("num_experts_per_tok", 0),
-            moe_intermediate_size=t.get("moe_intermediate_size", 0),
+            num_experts=n_experts,
+            num_experts_per_tok=top_k or 0,
+            moe_intermediate_size=moe_inter if n_experts > 0 else 0,
             shared_expert_intermediate_size=t.get("shared_expert_intermediate_size", 0),
             norm_topk_prob=t.get("norm_topk_prob", True),
+            decoder_sparse_step=t.get("decoder_sparse_step", 1),
+            mlp_only_layers=list(t.get("mlp_only_layers", [])),
         )
 
 
@@ -139,13 +157,13 @@ def _schedule(n_layers: int, interval: int = 4) -> list:
             for i in range(n_layers)]
 
 
-def _raw(**kw) -> dict:
+def _raw(model_type="qwen3_5", **kw) -> dict:
     base = dict(rms_norm_eps=1e-6, rope_theta=1e7, partial_rotary_factor=0.25,
                 tie_word_embeddings=True, hidden_act="silu", full_attention_interval=4,
                 attn_output_gate=True, linear_conv_kernel_dim=4)
     base.update(kw)
     base["layer_types"] = _schedule(base["num_hidden_layers"])
-    return {"model_type": "qwen3_5", "text_config": base}
+    return {"model_type": model_type, "text_config": base}
 
 
 # tiny, fp32 CPU-parity shape.
@@ -173,3 +191,21 @@ MICRO_WIDE = _raw(vocab_size=1024, hidden_size=256, intermediate_size=512,
                   num_hidden_layers=4, num_attention_heads=4, num_key_value_heads=2,
                   head_dim=256, linear_num_key_heads=2, linear_num_value_heads=4,
                   linear_key_head_dim=128, linear_value_head_dim=128)
+
+# the qwen3_5_moe shape (bf16): 48 layers, every FFN a sparse MoE block
+# with 512 routed experts (top-10, width 512) plus one always-on shared expert of width 512.
+QWEN35_MOE = _raw(model_type="qwen3_5_moe", vocab_size=151936, hidden_size=2048,
+                  intermediate_size=512, num_hidden_layers=48, num_attention_heads=16,
+                  num_key_value_heads=2, head_dim=256, linear_num_key_heads=16,
+                  linear_num_value_heads=32, linear_key_head_dim=128, linear_value_head_dim=128,
+                  num_experts=512, num_experts_per_tok=10, moe_intermediate_size=512,
+                  shared_expert_intermediate_size=512, norm_topk_prob=True)
+
+# MICRO with a sparse FFN: 8 experts (top-2, width 64) + a shared expert; layer 1 is forced
+# dense through `mlp_only_layers` so both FFN kinds and the sparse stride rule are exercised.
+MICRO_MOE = _raw(model_type="qwen3_5_moe", vocab_size=512, hidden_size=128,
+                 intermediate_size=256, num_hidden_layers=8, num_attention_heads=4,
+                 num_key_value_heads=2, head_dim=32, linear_num_key_heads=2,
+                 linear_num_value_heads=4, linear_key_head_dim=32, linear_value_head_dim=32,
+                 num_experts=8, num_experts_per_tok=2, moe_intermediate_size=64,
+                 shared_expert_intermediate_size=64, norm_topk_prob=True, mlp_only_layers=[1])

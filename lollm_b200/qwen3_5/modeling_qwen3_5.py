@@ -13,6 +13,8 @@ Per layer (modeling_qwen3_5.py:47-61), every box a C-ABI launch:
     [GDN: in_proj(qkv|z|b|a) GEMM → qsp_gdn_verify → out_proj GEMM + residual + RMSNorm]
   | [attn: q|k|v GEMM → qsp_attn_prep → qsp_attn_verify → o_proj GEMM + residual + RMSNorm]
     gate|up GEMM + SwiGLU → down GEMM + residual + next layer's input RMSNorm
+  | (qwen3_5_moe layers where cfg.is_moe_layer(i), modeling_qwen3_5_moe.py:42-43)
+    qsp_moe_ffn: router + experts + shared expert + residual + next RMSNorm
 then the lm_head GEMM. Projections of one input are concatenated into one weight so each
 reads the activation once; each residual add is fused with the RMSNorm that follows it.
 """
@@ -27,6 +29,7 @@ from .. import kernels as K
 from .. import _lib as L
 from .config import Qwen3_5Config
 from .kv import Qwen3_5Cache
+from .moe import SparseMoeBlock
 
 
 def rope_table(rotary_dim: int, theta: float, rows: int, dtype):
@@ -56,9 +59,11 @@ class _Workspace:
         self.proj = e(M, max(n_in, n_qkv))
         self.core = e(M, max(cfg.value_dim, cfg.num_attention_heads * cfg.head_dim))
         self.q_buf = e(M, cfg.num_attention_heads * cfg.head_dim)
-        inter = cfg.intermediate_size if not cfg.is_moe else cfg.moe_intermediate_size
+        inter = cfg.intermediate_size
         self.gu = e(M, 2 * max(inter, 1))
         self.act = e(M, max(inter, 1))
+        moe_ws = max([lw["moe"].workspace_bytes(M) for lw in model.layers if "moe" in lw] + [0])
+        self.moe_ws = torch.empty(moe_ws, dtype=torch.uint8, device=dev) if moe_ws else None
         self.logits = e(M, cfg.vocab_size)
         self.last_x = e(B, H)
         self.last_xn = e(B, H)
@@ -76,8 +81,6 @@ class Qwen3_5Model:
         self.cfg, self.dtype, self.device = cfg, dtype, torch.device(device)
         if self.device.type != "cuda":
             raise RuntimeError("Qwen3_5Model runs on CUDA only (no CPU fallback)")
-        if cfg.is_moe:
-            raise NotImplementedError("qwen3_5_moe sparse FFN is not built yet")
         self.page_size, self.max_spec_tokens = page_size, max_spec_tokens
         self.max_positions = max_positions
         dev = self.device
@@ -90,9 +93,12 @@ class Qwen3_5Model:
         for i in range(cfg.num_hidden_layers):
             p = f"model.layers.{i}."
             lw = {"type": cfg.layer_type(i), "in_norm": g(p + "input_layernorm.weight"),
-                  "post_norm": g(p + "post_attention_layernorm.weight"),
-                  "w_gu": torch.cat([g(p + "mlp.gate_proj.weight"), g(p + "mlp.up_proj.weight")]).contiguous(),
-                  "down": g(p + "mlp.down_proj.weight")}
+                  "post_norm": g(p + "post_attention_layernorm.weight")}
+            if cfg.is_moe_layer(i):
+                lw["moe"] = SparseMoeBlock(cfg, params, p, dtype=dtype, device=dev)
+            else:
+                lw["w_gu"] = torch.cat([g(p + "mlp.gate_proj.weight"), g(p + "mlp.up_proj.weight")]).contiguous()
+                lw["down"] = g(p + "mlp.down_proj.weight")
             if lw["type"] == "full_attention":
                 a = p + "self_attn."
                 lw["w_qkv"] = torch.cat([g(a + "q_proj.weight"), g(a + "k_proj.weight"),
@@ -213,9 +219,12 @@ class Qwen3_5Model:
                                    lw["dt_bias"], lw["norm_w"], None, ws.core, speculative)
                 K.gdn_verify(d)
                 K.gemm_residual_rmsnorm(ws.core, lw["out_proj"], ws.x, lw["post_norm"], ws.xn, eps, m=M)
-            K.gemm_swiglu(ws.xn, lw["w_gu"], ws.act, ws.gu, m=M)
             # residual add + the next norm: next layer's input_layernorm, or the final norm
             nxt = self.layers[i + 1]["in_norm"] if i + 1 < n_layers else (None if last_only else self.final_norm)
+            if "moe" in lw:
+                lw["moe"](ws.xn, ws.x, nxt, ws.xn, eps, M, ws.moe_ws)
+                continue
+            K.gemm_swiglu(ws.xn, lw["w_gu"], ws.act, ws.gu, m=M)
             if nxt is not None:
                 K.gemm_residual_rmsnorm(ws.act, lw["down"], ws.x, nxt, ws.xn, eps, m=M)
             else:

@@ -26,6 +26,7 @@ import torch
 
 from .. import kernels as K
 from .modeling_qwen3_5 import Qwen3_5Model
+from .moe import SparseMoeBlock
 
 
 class MTP:
@@ -43,8 +44,11 @@ class MTP:
         q = g(p + "self_attn.q_proj.weight").view(nh, 2, hd, H)
         self.w_gv = torch.cat([q[:, 1].reshape(nh * hd, H), g(p + "self_attn.v_proj.weight")]).contiguous()
         self.o_proj = g(p + "self_attn.o_proj.weight")
-        self.w_gu = torch.cat([g(p + "mlp.gate_proj.weight"), g(p + "mlp.up_proj.weight")]).contiguous()
-        self.down = g(p + "mlp.down_proj.weight")
+        # the MoE family's MTP block takes the FFN kind of layer 0 (qwen3_5_moe/mtp.py:34-36)
+        self.moe = SparseMoeBlock(cfg, params, p, dtype=dt, device=dev) if cfg.is_moe_layer(0) else None
+        if self.moe is None:
+            self.w_gu = torch.cat([g(p + "mlp.gate_proj.weight"), g(p + "mlp.up_proj.weight")]).contiguous()
+            self.down = g(p + "mlp.down_proj.weight")
         self.norm = g("mtp.norm.weight")
         self._ws = {}
 
@@ -53,10 +57,12 @@ class MTP:
             cfg, dt, dev = self.cfg, self.model.dtype, self.model.device
             H, nh, nkv, hd = cfg.hidden_size, cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
             e = lambda *s: torch.empty(*s, dtype=dt, device=dev)
-            I = self.down.shape[1]
+            I = 1 if self.moe is not None else self.down.shape[1]
             self._ws[(B, k)] = dict(emb=e(B, H), cat=e(B, 2 * H), x=e(B, H), xn=e(B, H),
                                     gv=e(B, (nh + nkv) * hd), ao=e(B, nh * hd), gu=e(B, 2 * I),
                                     act=e(B, I), logits=e(B, k, cfg.vocab_size))
+            if self.moe is not None:
+                self._ws[(B, k)]["moe_ws"] = torch.empty(self.moe.workspace_bytes(B), dtype=torch.uint8, device=dev)
         return self._ws[(B, k)]
 
     @torch.no_grad()
@@ -81,9 +87,12 @@ class MTP:
             K.gemm(w["xn"], self.w_gv, w["gv"])
             K.mtp_single_token_attn(w["gv"], hd, w["gv"][:, nh * hd:], w["ao"], nh, nkv, hd)
             K.gemm_residual_rmsnorm(w["ao"], self.o_proj, w["x"], self.post_norm, w["xn"], eps)
-            K.gemm_swiglu(w["xn"], self.w_gu, w["act"], w["gu"])
             # x stays the pre-norm output (next depth's hidden); xn = final norm for lm_head
-            K.gemm_residual_rmsnorm(w["act"], self.down, w["x"], self.norm, w["xn"], eps)
+            if self.moe is not None:
+                self.moe(w["xn"], w["x"], self.norm, w["xn"], eps, B, w["moe_ws"])
+            else:
+                K.gemm_swiglu(w["xn"], self.w_gu, w["act"], w["gu"])
+                K.gemm_residual_rmsnorm(w["act"], self.down, w["x"], self.norm, w["xn"], eps)
             lg = w["logits"][:, d]
             K.gemm(w["xn"], m.lm_head, lg)
             if temperature <= 0:

@@ -62,28 +62,30 @@ def _gdn_specs(cfg: Qwen3_5Config, pre: str):
     ]
 
 
-def _ffn_specs(cfg: Qwen3_5Config, pre: str):
+def _ffn_specs(cfg: Qwen3_5Config, pre: str, moe: bool):
     h = cfg.hidden_size
-    if not cfg.is_moe:
+    if not moe:
         i = cfg.intermediate_size
         return [(pre + "mlp.gate_proj.weight", (i, h)),
                 (pre + "mlp.up_proj.weight", (i, h)),
                 (pre + "mlp.down_proj.weight", (h, i))]
     e, im, ish = cfg.num_experts, cfg.moe_intermediate_size, cfg.shared_expert_intermediate_size
-    return [(pre + "mlp.gate.weight", (e, h)),
-            (pre + "mlp.experts.gate_up_proj", (e, 2 * im, h)),
-            (pre + "mlp.experts.down_proj", (e, h, im)),
-            (pre + "mlp.shared_expert.gate_proj.weight", (ish, h)),
-            (pre + "mlp.shared_expert.up_proj.weight", (ish, h)),
-            (pre + "mlp.shared_expert.down_proj.weight", (h, ish)),
-            (pre + "mlp.shared_expert_gate.weight", (1, h))]
+    specs = [(pre + "mlp.gate.weight", (e, h)),
+             (pre + "mlp.experts.gate_up_proj", (e, 2 * im, h)),
+             (pre + "mlp.experts.down_proj", (e, h, im))]
+    if ish > 0:
+        specs += [(pre + "mlp.shared_expert.gate_proj.weight", (ish, h)),
+                  (pre + "mlp.shared_expert.up_proj.weight", (ish, h)),
+                  (pre + "mlp.shared_expert.down_proj.weight", (h, ish)),
+                  (pre + "mlp.shared_expert_gate.weight", (1, h))]
+    return specs
 
 
-def _layer_specs(cfg: Qwen3_5Config, pre: str, layer_type: str):
+def _layer_specs(cfg: Qwen3_5Config, pre: str, layer_type: str, moe: bool):
     h = cfg.hidden_size
     mixer = _attn_specs(cfg, pre) if layer_type == "full_attention" else _gdn_specs(cfg, pre)
     return ([(pre + "input_layernorm.weight", (h,))] + mixer
-            + [(pre + "post_attention_layernorm.weight", (h,))] + _ffn_specs(cfg, pre))
+            + [(pre + "post_attention_layernorm.weight", (h,))] + _ffn_specs(cfg, pre, moe))
 
 
 def param_specs(cfg: Qwen3_5Config, with_mtp: bool = True):
@@ -91,7 +93,7 @@ def param_specs(cfg: Qwen3_5Config, with_mtp: bool = True):
     h = cfg.hidden_size
     specs = [("model.embed_tokens.weight", (cfg.vocab_size, h))]
     for i in range(cfg.num_hidden_layers):
-        specs += _layer_specs(cfg, f"model.layers.{i}.", cfg.layer_type(i))
+        specs += _layer_specs(cfg, f"model.layers.{i}.", cfg.layer_type(i), cfg.is_moe_layer(i))
     specs.append(("model.norm.weight", (h,)))
     if not cfg.tie_word_embeddings:
         specs.append(("lm_head.weight", (cfg.vocab_size, h)))
@@ -99,7 +101,7 @@ def param_specs(cfg: Qwen3_5Config, with_mtp: bool = True):
         specs += [("mtp.pre_fc_norm_embedding.weight", (h,)),
                   ("mtp.pre_fc_norm_hidden.weight", (h,)),
                   ("mtp.fc.weight", (h, 2 * h))]
-        specs += _layer_specs(cfg, "mtp.layers.0.", "full_attention")
+        specs += _layer_specs(cfg, "mtp.layers.0.", "full_attention", cfg.is_moe_layer(0))
         specs.append(("mtp.norm.weight", (h,)))
     return specs
 

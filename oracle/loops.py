@@ -27,15 +27,27 @@ def prefill(P, cfg, prompts, scan="reference"):
     return logits, cache, hidden
 
 
-def greedy_generate(P, cfg, prompts, n_new, scan="reference"):
-    """Returns (B, n_new) generated ids (temperature 0, repetition penalty 1)."""
+def greedy_generate(P, cfg, prompts, n_new, scan="reference", repetition_penalty=1.0):
+    """Returns (B, n_new) generated ids at temperature 0. With a repetition penalty each
+    pick is `sample_next`'s penalised argmax over the sequence's context so far
+    (src/generate.py:17-27, 52-61)."""
+    ctx = [row.tolist() for row in prompts]
+
+    def pick(lg):
+        if repetition_penalty == 1.0:
+            return lg.float().argmax(-1)
+        return torch.tensor([S.sample_next(lg[b].float(), 0.0, 0, 1.0, repetition_penalty, ctx[b])
+                             for b in range(lg.shape[0])])
+
     logits, cache, _ = prefill(P, cfg, prompts, scan)
-    nxt = logits[:, -1].float().argmax(-1)
+    nxt = pick(logits[:, -1])
     out = []
     for _ in range(n_new):
         out.append(nxt)
+        for b in range(len(ctx)):
+            ctx[b].append(int(nxt[b]))
         logits, cache, _ = Q.model_forward(P, cfg, nxt[:, None], cache, scan)
-        nxt = logits[:, -1].float().argmax(-1)
+        nxt = pick(logits[:, -1])
     return torch.stack(out, dim=1)
 
 

@@ -269,22 +269,55 @@ def attn_mixer(P, pre, cfg, x, positions, kv_seqs):
     return linear(o, P[pre + "o_proj.weight"]), new_kv
 
 
-def ffn(P, pre, cfg, x):
-    """SwiGLU MLP (blocks.py:332-342) or the sparse MoE block
-    (src/qwen3_5_moe/blocks.py:399-421)."""
-    if not cfg.is_moe:
+def ffn(P, pre, cfg, x, moe=False):
+    """SwiGLU MLP (blocks.py:332-342) or, on layers where `cfg.is_moe_layer` holds, the
+    sparse MoE block (src/qwen3_5_moe/blocks.py:399-421)."""
+    if not moe:
         return linear(silu_mul(linear(x, P[pre + "mlp.gate_proj.weight"]),
                                linear(x, P[pre + "mlp.up_proj.weight"])),
                       P[pre + "mlp.down_proj.weight"])
     return moe_ffn(P, pre + "mlp.", cfg, x)
 
 
+# When a list, moe_ffn appends (prefix, margins) per call: margins[n] is the gap between
+# token n's k-th and (k+1)-th router logits in units of the model dtype's rounding step at
+# the k-th logit (inf in fp32). A bf16 gap of a step or two is a near-tie: rounding noise
+# upstream (accumulation order of any earlier op) can swap which expert is selected, so
+# tests flag those tokens instead of comparing them.
+ROUTER_MARGINS = None
+
+
+def router_margin_ulps(logits, k):
+    """Gap between the k-th and (k+1)-th largest logit per row, in bf16 steps."""
+    if logits.dtype != torch.bfloat16 or k >= logits.shape[-1]:
+        return torch.full(logits.shape[:-1], float("inf"))
+    s = logits.float().sort(-1, descending=True).values
+    ulp = torch.exp2(torch.floor(torch.log2(s[..., k - 1].abs().clamp_min(1e-30))) - 7)
+    return (s[..., k - 1] - s[..., k]) / ulp
+
+
+def near_tie_rows(margin_log, B, T, thresh=2.0):
+    """(B, T) bool: tokens of a (B, T) forward whose routing was a near-tie (margin below
+    `thresh` bf16 steps) on any MoE layer of the logged call, with every later position of
+    the same sequence (they attend to / scan over the flagged one)."""
+    flag = torch.zeros(B, T, dtype=torch.bool)
+    for pre, m in margin_log:
+        if not pre.startswith("model."):
+            continue
+        flag |= (m.reshape(B, T) < thresh)
+    return flag.int().cummax(dim=1).values.bool()
+
+
 def moe_ffn(P, pre, cfg, x):
     """Router softmax (fp32) → top-k → renorm → Σ p·SwiGLU_e(x) + σ(gate_s x)·SwiGLU_s(x) —
-    src/qwen3_5_moe/blocks.py:399-421, computed densely per token (same sums)."""
+    src/qwen3_5_moe/blocks.py:399-421, the same per-expert loop in ascending expert order
+    (so the model-dtype accumulation of index_add_ rounds in the same order)."""
     shp = x.shape
     xt = x.reshape(-1, shp[-1])
-    probs = F.softmax(linear(xt, P[pre + "gate.weight"]), dim=-1, dtype=torch.float32)
+    router = linear(xt, P[pre + "gate.weight"])
+    if ROUTER_MARGINS is not None:
+        ROUTER_MARGINS.append((pre, router_margin_ulps(router, cfg.num_experts_per_tok)))
+    probs = F.softmax(router, dim=-1, dtype=torch.float32)
     w, idx = torch.topk(probs, cfg.num_experts_per_tok, dim=-1)
     if cfg.norm_topk_prob:
         w = w / w.sum(-1, keepdim=True)
@@ -308,7 +341,9 @@ def moe_ffn(P, pre, cfg, x):
 # ─────────────────────────────────── model ───────────────────────────────────
 
 def model_forward(P, cfg, ids, cache=None, scan="reference"):
-    """Qwen3_5Model.forward — src/qwen3_5/modeling_qwen3_5.py:82-102, with per-sequence
+    """Qwen3_5Model.forward — src/qwen3_5/modeling_qwen3_5.py:82-102 (and its MoE sibling
+    src/qwen3_5_moe/modeling_qwen3_5_moe.py:81-102, whose layers pick the FFN per
+    `is_moe_layer`, modeling_qwen3_5_moe.py:42-43), with per-sequence
     positions (lens[b] + t). ids: (B,T) int64. Returns (logits (B,T,V), cache, hidden)."""
     B, T = ids.shape
     if cache is None:
@@ -324,7 +359,7 @@ def model_forward(P, cfg, ids, cache=None, scan="reference"):
             h, cache.gdn[i] = gdn_mixer(P, pre + "linear_attn.", cfg, h, cache.gdn.get(i), scan)
         x = x + h
         x = x + ffn(P, pre, cfg, rms_norm(x, P[pre + "post_attention_layernorm.weight"],
-                                          cfg.rms_norm_eps))
+                                          cfg.rms_norm_eps), moe=cfg.is_moe_layer(i))
     cache.lens = [n + T for n in cache.lens]
     hidden = x
     logits = linear(rms_norm(hidden, P["model.norm.weight"], cfg.rms_norm_eps), P["lm_head.weight"])
@@ -348,7 +383,8 @@ def mtp_forward(P, cfg, hidden, next_emb):
     positions = torch.arange(1, L + 1)[None].expand(B, L)
     h, _ = attn_mixer(P, pre + "self_attn.", cfg, h, positions, None)
     x = x + h
-    x = x + ffn(P, pre, cfg, rms_norm(x, P[pre + "post_attention_layernorm.weight"], cfg.rms_norm_eps))
+    x = x + ffn(P, pre, cfg, rms_norm(x, P[pre + "post_attention_layernorm.weight"], cfg.rms_norm_eps),
+                moe=cfg.is_moe_layer(0))   # the MoE family's MTP block asks for layer 0
     return rms_norm(x, P["mtp.norm.weight"], cfg.rms_norm_eps), x
 
 
