@@ -645,9 +645,21 @@ def run_gemm_workload(args):
     ws = [(torch.randn(n, k, generator=g, device=dev) * 0.02).to(torch.bfloat16) for _ in range(n_w)]
     c = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
     it = {"i": 0}
+    epi = args.gemm_epi
+    if epi == "swiglu":      # n = 2·inter rows of a [gate; up] weight, SwiGLU of the product out
+        act = torch.empty(m, n // 2, dtype=torch.bfloat16, device=dev)
+    if epi == "resnorm":     # residual add into c, then the next RMSNorm into y
+        y = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+        nw = torch.zeros(n, dtype=torch.bfloat16, device=dev)
 
     def step():
-        K.gemm(a, ws[it["i"] % n_w], c)
+        w_i = ws[it["i"] % n_w]
+        if epi == "swiglu":
+            K.gemm_swiglu(a, w_i, act, c)
+        elif epi == "resnorm":
+            K.gemm_residual_rmsnorm(a, w_i, c, nw, y, 1e-6)
+        else:
+            K.gemm(a, w_i, c)
         it["i"] += 1
 
     stream = torch.cuda.current_stream()
@@ -662,7 +674,7 @@ def run_gemm_workload(args):
     flops = 2 * m * n * k
     gbs, tfs = algo_b / t / 1e9, flops / t / 1e12
     bound = "hbm" if gbs / hbm >= tfs / tf else "tensor"
-    return {"metric": f"gemm {m}x{n}x{k} bf16", "value": tfs, "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps,
+    return {"metric": f"gemm {m}x{n}x{k} bf16" + ("" if epi == "store" else f" + {epi}"), "value": tfs, "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": statistics.mean(ms), "higher_is_better": True, "dtype": "bf16",
             "data": "synthetic", "config": {"workload": "gemm", "m": m, "n": n, "k": k, "weight_copies": n_w},
             "roofline": {"kernel": "gemm_tc_kernel (+ split-k merge)", "bound": bound,
@@ -744,6 +756,8 @@ def main():
     ap.add_argument("--n", type=int, default=12352)
     ap.add_argument("--k-dim", type=int, default=2048)
     ap.add_argument("--l2-resident", action="store_true", help="gemm workload: one weight copy (stays in L2)")
+    ap.add_argument("--gemm-epi", choices=["store", "resnorm", "swiglu"], default="store",
+                    help="gemm workload: plain product, + residual add and RMSNorm, or SwiGLU of [gate; up]")
     ap.add_argument("--workload", choices=["step", "gdn", "attn", "gemm", "moe"], default="step",
                     help="step: the speculative step (headline); gdn / attn: BASELINE configs[3] / [2] kernels "
                          "alone; moe: one configs[4] sparse FFN block")

@@ -15,6 +15,8 @@ int launch_attn_ws(const qsp_attn_layer& L, cudaStream_t st);
 // One CTA per token row m = b*T + t; warps loop over the q and k heads.
 template <typename T>
 __global__ void attn_prep_kernel(const qsp_attn_layer L) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ float sx[];  // [warps][hd]
   const int m = blockIdx.x;
   const int b = m / L.tokens, t = m % L.tokens;
@@ -80,6 +82,8 @@ constexpr int AT_KT = 32;
 template <typename T, int HD, int RPW>
 __global__ void __launch_bounds__(128) attn_simt_kernel(const qsp_attn_layer L, int chunk,
                                                         int n_row_groups) {
+  pdl_trigger();
+  pdl_wait();
   constexpr int DPL = HD / 32;
   extern __shared__ float smem[];
   const int s = blockIdx.x, g = blockIdx.y;
@@ -188,6 +192,8 @@ __global__ void __launch_bounds__(128) attn_simt_kernel(const qsp_attn_layer L, 
 // l) of the row are merged with weights e^{m_p − M}, then σ(gate) is applied.
 template <typename T>
 __global__ void __launch_bounds__(256) attn_combine_kernel(const qsp_attn_layer L, int np) {
+  pdl_trigger();
+  pdl_wait();
   const int lane = threadIdx.x & 31;
   const int pair = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (pair >= L.batch * L.tokens * L.n_heads) return;
@@ -239,8 +245,8 @@ static int attn_chunk(const qsp_attn_layer& L) {
 template <typename T>
 static int launch_combine(const qsp_attn_layer& L, int np, cudaStream_t st) {
   const int pairs = L.batch * L.tokens * L.n_heads;
-  attn_combine_kernel<T><<<(pairs + 7) / 8, 256, 0, st>>>(L, np);
-  return check_launch("qsp_attn_verify(combine)");
+  return launch_pdl("qsp_attn_verify(combine)", attn_combine_kernel<T>, dim3((pairs + 7) / 8), dim3(256), 0, st, L,
+                    np);
 }
 
 template <typename T, int HD, int RPW>
@@ -251,8 +257,7 @@ static int launch_attn_simt(const qsp_attn_layer& L, cudaStream_t st) {
   auto kern = attn_simt_kernel<T, HD, RPW>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   dim3 grid(L.num_splits, L.n_kv_heads, L.batch * n_rg);
-  kern<<<grid, 128, smem, st>>>(L, attn_chunk(L), n_rg);
-  int rc = check_launch("qsp_attn_verify(simt)");
+  int rc = launch_pdl("qsp_attn_verify(simt)", kern, grid, dim3(128), smem, st, L, attn_chunk(L), n_rg);
   if (rc) return rc;
   return launch_combine<T>(L, L.num_splits, st);
 }
@@ -322,9 +327,10 @@ int qsp_attn_prep(const qsp_attn_layer* layer, void* stream) {
   const qsp_attn_layer& L = *layer;
   const size_t smem = 4 * L.head_dim * sizeof(float);
   QSP_DISPATCH_DTYPE(L.dtype, T, {
-    attn_prep_kernel<T><<<L.batch * L.tokens, 128, smem, as_stream(stream)>>>(L);
+    return launch_pdl("qsp_attn_prep", attn_prep_kernel<T>, dim3(L.batch * L.tokens), dim3(128), smem,
+                      as_stream(stream), L);
   });
-  return check_launch("qsp_attn_prep");
+  return QSP_OK;
 }
 
 int qsp_attn_verify(const qsp_attn_layer* layer, void* stream) {

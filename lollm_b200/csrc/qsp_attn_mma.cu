@@ -65,6 +65,8 @@ struct AmSmem {
 template <int HD>
 __global__ void __launch_bounds__(AM_THREADS, 1)
 attn_mma_kernel(const qsp_attn_layer L, int n_row_groups) {
+  pdl_trigger();
+  pdl_wait();
   using SM = AmSmem<HD>;
   constexpr int P = SM::PITCH;
   constexpr int NKS = HD / 16;   // k-steps over head_dim
@@ -316,8 +318,7 @@ int launch_attn_mma(const qsp_attn_layer& L, cudaStream_t st) {
         return set_error(QSP_ERR_CUDA, "qsp_attn_verify: cannot reserve shared memory");     \
       set = true;                                                                            \
     }                                                                                        \
-    kern<<<grid, AM_THREADS, smem, st>>>(L, n_rg);                                           \
-    return check_launch("qsp_attn_verify(mma)");                                             \
+    return launch_pdl("qsp_attn_verify(mma)", kern, grid, dim3(AM_THREADS), smem, st, L, n_rg); \
   }
   switch (L.head_dim) {
     QSP_AM_CASE(64)
@@ -383,6 +384,8 @@ template <int HD>
 __global__ void __launch_bounds__(AM_THREADS, 1)
 attn_tma_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                 const qsp_attn_layer L, int n_row_groups) {
+  pdl_trigger();
+  pdl_wait();
   using SM = At2Smem<HD>;
   constexpr int QP = SM::QP;
   constexpr int NKS = HD / 16;
@@ -694,8 +697,7 @@ int launch_attn_tma(const qsp_attn_layer& L, cudaStream_t st) {
         return set_error(QSP_ERR_CUDA, "qsp_attn_verify: cannot reserve shared memory");     \
       set = true;                                                                            \
     }                                                                                        \
-    kern<<<grid, AM_THREADS, smem, st>>>(mk, mv, L, n_rg);                                   \
-    return check_launch("qsp_attn_verify(tma)");                                             \
+    return launch_pdl("qsp_attn_verify(tma)", kern, grid, dim3(AM_THREADS), smem, st, mk, mv, L, n_rg); \
   }
   switch (L.head_dim) {
     QSP_AT2_CASE(64)
@@ -760,6 +762,8 @@ template <int HD>
 __global__ void __launch_bounds__(AT3_THREADS, 1)
 attn_ws_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                const qsp_attn_layer L, int n_rg, int n_items) {
+  pdl_trigger();
+  pdl_wait();
   using SM = At3Smem<HD>;
   constexpr int NKS = HD / 16;
   constexpr int NNT = HD / 8;
@@ -1037,8 +1041,7 @@ int launch_attn_ws(const qsp_attn_layer& L, cudaStream_t st) {
         return set_error(QSP_ERR_CUDA, "qsp_attn_verify: cannot reserve shared memory");     \
       set = true;                                                                            \
     }                                                                                        \
-    kern<<<grid, AT3_THREADS, smem, st>>>(mk, mv, L, n_rg, n_items);                          \
-    return check_launch("qsp_attn_verify(ws)");                                              \
+    return launch_pdl("qsp_attn_verify(ws)", kern, grid, dim3(AT3_THREADS), smem, st, mk, mv, L, n_rg, n_items); \
   }
   switch (L.head_dim) {
     QSP_AT3_CASE(64)

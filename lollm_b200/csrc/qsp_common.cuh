@@ -7,6 +7,8 @@
 #include <stdio.h>
 #include <stdarg.h>
 
+#include <utility>
+
 #include "../../include/qsp.h"
 
 namespace qsp {
@@ -24,6 +26,38 @@ inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s
 
 inline bool aligned(const void* p, size_t a) {
   return (reinterpret_cast<uintptr_t>(p) % a) == 0;
+}
+
+// ---------------------------------------------------------------- programmatic dependent launch
+// Kernels launched with launch_pdl may begin while the previous kernel on the stream is still
+// finishing (its CTAs take whatever SM room is left). Such a kernel calls pdl_wait() in every
+// CTA before it touches memory that earlier kernels write or read — only immutable data
+// (weights) may be read before it — so "the previous kernel completed" stays transitive along
+// the stream. pdl_trigger() lets the next kernel start launching; it is issued at the top of
+// every kernel here, so a chain of kernels overlaps each one's launch, prologue and weight
+// prefetch with its predecessor's tail.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+inline int launch_pdl(const char* what, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                      cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+  if (e != cudaSuccess) {
+    (void)cudaGetLastError();
+    return set_error(QSP_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  }
+  return check_launch(what);
 }
 
 // ---------------------------------------------------------------- dtype plumbing

@@ -46,6 +46,8 @@ template <typename T, bool ADD>
 __global__ void rmsnorm_kernel(T* __restrict__ x, int64_t ld_x, const T* __restrict__ h,
                                const T* __restrict__ w, T* __restrict__ y, int64_t ld_y,
                                int64_t dim, float eps) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ float srow[];
   __shared__ float red[32];
   const int64_t r = blockIdx.x;
@@ -73,6 +75,8 @@ __global__ void rmsnorm_kernel(T* __restrict__ x, int64_t ld_x, const T* __restr
 template <typename T>
 __global__ void swiglu_kernel(const T* __restrict__ gu, int64_t ld_gu, T* __restrict__ y,
                               int64_t ld_y, int64_t inter) {
+  pdl_trigger();
+  pdl_wait();
   const int64_t r = blockIdx.y;
   for (int64_t j = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; j < inter;
        j += (int64_t)gridDim.x * blockDim.x) {
@@ -179,10 +183,11 @@ int qsp_rmsnorm(const void* x, int64_t ld_x, const void* w, void* y, int64_t ld_
               "qsp_rmsnorm: bad shape");
   if (rows == 0) return QSP_OK;
   QSP_DISPATCH_DTYPE(dtype, T, {
-    rmsnorm_kernel<T, false><<<(unsigned)rows, 256, dim * sizeof(float), as_stream(stream)>>>(
-        (T*)x, ld_x, nullptr, (const T*)w, (T*)y, ld_y, dim, eps);
+    return launch_pdl("qsp_rmsnorm", rmsnorm_kernel<T, false>, dim3((unsigned)rows), dim3(256),
+                      dim * sizeof(float), as_stream(stream), (T*)x, ld_x, (const T*)nullptr, (const T*)w, (T*)y,
+                      ld_y, dim, eps);
   });
-  return check_launch("qsp_rmsnorm");
+  return QSP_OK;
 }
 
 int qsp_add_rmsnorm(void* x, const void* h, const void* w, void* y, int64_t rows, int64_t dim,
@@ -191,10 +196,11 @@ int qsp_add_rmsnorm(void* x, const void* h, const void* w, void* y, int64_t rows
   QSP_REQUIRE(rows >= 0 && dim > 0 && dim <= 12288, "qsp_add_rmsnorm: bad shape");
   if (rows == 0) return QSP_OK;
   QSP_DISPATCH_DTYPE(dtype, T, {
-    rmsnorm_kernel<T, true><<<(unsigned)rows, 256, dim * sizeof(float), as_stream(stream)>>>(
-        (T*)x, dim, (const T*)h, (const T*)w, (T*)y, dim, dim, eps);
+    return launch_pdl("qsp_add_rmsnorm", rmsnorm_kernel<T, true>, dim3((unsigned)rows), dim3(256),
+                      dim * sizeof(float), as_stream(stream), (T*)x, dim, (const T*)h, (const T*)w, (T*)y, dim,
+                      dim, eps);
   });
-  return check_launch("qsp_add_rmsnorm");
+  return QSP_OK;
 }
 
 int qsp_swiglu(const void* gu, int64_t ld_gu, void* y, int64_t ld_y, int64_t rows, int64_t inter,
@@ -205,10 +211,10 @@ int qsp_swiglu(const void* gu, int64_t ld_gu, void* y, int64_t ld_y, int64_t row
   if (rows == 0) return QSP_OK;
   const unsigned gx = (unsigned)((inter + 255) / 256 < 64 ? (inter + 255) / 256 : 64);
   QSP_DISPATCH_DTYPE(dtype, T, {
-    swiglu_kernel<T><<<dim3(gx, (unsigned)rows), 256, 0, as_stream(stream)>>>(
-        (const T*)gu, ld_gu, (T*)y, ld_y, inter);
+    return launch_pdl("qsp_swiglu", swiglu_kernel<T>, dim3(gx, (unsigned)rows), dim3(256), 0, as_stream(stream),
+                      (const T*)gu, ld_gu, (T*)y, ld_y, inter);
   });
-  return check_launch("qsp_swiglu");
+  return QSP_OK;
 }
 
 int qsp_mtp_single_token_attn(const void* qg, int64_t ld_qg, int64_t gate_head_stride,

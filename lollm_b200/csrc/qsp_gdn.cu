@@ -223,6 +223,8 @@ __device__ __forceinline__ void gdn_prefetch_state(float* dst, const float* src,
 template <typename T, int DK, int DV>
 __global__ void __launch_bounds__(DV, 2)
 gdn_seq_kernel(const qsp_gdn_layer L) {
+  pdl_trigger();
+  pdl_wait();
   using SMT = GdnSmem<T, DK, DV>;
   constexpr int RPT = DK / 4;
   constexpr int NT = DV;
@@ -465,6 +467,8 @@ inline size_t gdn_prep_smem(int nchg, int K, int T, int DK, int esz) {
 
 template <typename T, int DK, int DV>
 __global__ void __launch_bounds__(256) gdn_prep_kernel(const qsp_gdn_layer L, const GdnRing RG) {
+  pdl_trigger();
+  pdl_wait();
   using RA = GdnRecA<T, DK, DV>;
   using RB = GdnRecB<T, DK, DV>;
   extern __shared__ __align__(16) uint8_t gdn_prep_raw[];
@@ -769,6 +773,8 @@ __device__ __forceinline__ void gdn_stage(GdnChunkIn<T, DK, DV>& in, uint64_t* b
 template <typename T, int DK, int DV>
 __global__ void __launch_bounds__(DV, 2)
 gdn_chunk_kernel(const qsp_gdn_layer L, const GdnRing RG, const int n_new) {
+  pdl_trigger();
+  pdl_wait();
   using SM = GdnChunkSmem<T, DK, DV>;
   extern __shared__ __align__(128) uint8_t gdn_chunk_raw[];
   SM& sm = *reinterpret_cast<SM*>(gdn_chunk_raw);
@@ -1001,23 +1007,19 @@ static int launch_gdn_dims(const qsp_gdn_layer& L, cudaStream_t st) {
         return set_error(QSP_ERR_CUDA, "qsp_gdn_verify: cannot reserve %zu bytes of shared memory", psmem);
       prep_set = psmem;
     }
-    prep<<<L.batch * L.n_k_heads, 256, psmem, st>>>(L, RG);
-    rc = check_launch("qsp_gdn_verify(prep)");
+    rc = launch_pdl("qsp_gdn_verify(prep)", prep, dim3(L.batch * L.n_k_heads), dim3(256), psmem, st, L, RG);
     if (rc) return rc;
-    chunk<<<grid, DV, csmem, st>>>(L, RG, L.tokens);
-    return check_launch("qsp_gdn_verify(chunk)");
+    return launch_pdl("qsp_gdn_verify(chunk)", chunk, dim3(grid), dim3(DV), csmem, st, L, RG, (int)L.tokens);
   }
   // long commit call: replay kept tokens into the state, then step through the tokens
-  chunk<<<grid, DV, csmem, st>>>(L, RG, 0);
-  rc = check_launch("qsp_gdn_verify(replay)");
+  rc = launch_pdl("qsp_gdn_verify(replay)", chunk, dim3(grid), dim3(DV), csmem, st, L, RG, 0);
   if (rc) return rc;
   auto seq = gdn_seq_kernel<T, DK, DV>;
   const size_t ssmem = sizeof(GdnSmem<T, DK, DV>);
   static bool seq_set = false;
   rc = reserve_smem(seq, ssmem, seq_set);
   if (rc) return rc;
-  seq<<<grid, DV, ssmem, st>>>(L);
-  return check_launch("qsp_gdn_verify(seq)");
+  return launch_pdl("qsp_gdn_verify(seq)", seq, dim3(grid), dim3(DV), ssmem, st, L);
 }
 
 template <typename T>

@@ -173,6 +173,8 @@ __global__ void __launch_bounds__(256) splitk_store_kernel(const float* __restri
                                                            int64_t split_stride, int ldp,
                                                            __nv_bfloat16* __restrict__ c, int64_t ldc, int n,
                                                            int accumulate) {
+  pdl_trigger();
+  pdl_wait();
   const int row = blockIdx.y;
   const int col = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
   if (col >= n) return;
@@ -194,6 +196,8 @@ constexpr int RN_MAXV = 8;   // up to 8192 columns (256 threads x 4 x 8)
 __global__ void __launch_bounds__(256) splitk_residual_rmsnorm_kernel(
     const float* __restrict__ partial, int splits, int64_t split_stride, int ldp, __nv_bfloat16* __restrict__ x,
     int64_t ldx, const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ y, int64_t ldy, int n, float eps) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ float red[32];
   const int row = blockIdx.x;
   float r[RN_MAXV][4];
@@ -232,6 +236,8 @@ __global__ void __launch_bounds__(256) splitk_swiglu_kernel(const float* __restr
                                                             int64_t split_stride, int ldp,
                                                             __nv_bfloat16* __restrict__ act, int64_t ld_act,
                                                             int inter) {
+  pdl_trigger();
+  pdl_wait();
   const int row = blockIdx.y;
   const int j = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
   if (j >= inter) return;
@@ -262,6 +268,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tiles = A.m_tiles * A.n_tiles;
+  pdl_trigger();
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
@@ -290,6 +297,25 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
     if (lane == 0) {
       asm volatile("prefetch.tensormap [%0];" ::"l"(&tm_w) : "memory");
       asm volatile("prefetch.tensormap [%0];" ::"l"(&tm_x) : "memory");
+      // The weights do not depend on the previous kernel: the first ring pass issues its
+      // weight tiles before the dependency wait, and its activation tiles after it.
+      int pre_kb[C::STAGES], pre_mb[C::STAGES];
+      uint32_t npre = 0;
+      for (int u = blockIdx.x; u < A.units && npre < (uint32_t)C::STAGES; u += gridDim.x) {
+        const int sp = u / tiles, tile = u % tiles, mb = tile % A.m_tiles, nb = tile / A.m_tiles;
+        const int kb0 = sp * A.kb_per_split, nk = min(A.n_kb, kb0 + A.kb_per_split) - kb0;
+        const int rot = u % nk;
+        for (int i = 0; i < nk && npre < (uint32_t)C::STAGES; ++i, ++npre) {
+          const int kb = kb0 + (i + rot) % nk;
+          mbar_expect_tx(&full[npre], C::STAGE_BYTES);
+          tma_load_2d(smem + npre * C::STAGE_BYTES, &tm_w, &full[npre], kb * TC_BK, nb * TC_BN);
+          pre_kb[npre] = kb;
+          pre_mb[npre] = mb;
+        }
+      }
+      pdl_wait();
+      for (uint32_t j = 0; j < npre; ++j)
+        tma_load_2d(smem + j * C::STAGE_BYTES + C::W_BYTES, &tm_x, &full[j], pre_kb[j] * TC_BK, pre_mb[j] * MT);
       uint32_t it = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < A.units && ok; u += gridDim.x) {
@@ -299,6 +325,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
         // activation slabs (all CTAs on the same slab at once hot-spots L2)
         const int rot = u % nk;
         for (int i = 0; i < nk; ++i, ++it) {
+          if (it < npre) continue;   // issued above
           const int kb = kb0 + (i + rot) % nk;
           const int s = it % C::STAGES;
           const uint32_t ph = (it / C::STAGES) & 1u;
@@ -309,8 +336,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
           tma_load_2d(st + C::W_BYTES, &tm_x, &full[s], kb * TC_BK, mb * MT);
         }
       }
+    } else {
+      pdl_wait();
     }
   } else if (warp == 1) {
+    pdl_wait();
     // MMA issuer: accumulator buffer ui & 1 for the ui-th unit of this CTA
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_bf16(TC_MM, MT);
@@ -348,6 +378,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
   } else {
     // epilogue: warp w reads TMEM lanes 32*(w%4)..+31, i.e. weight rows (output columns n)
     // 128q + 32*(w%4) + lane of accumulator q
+    pdl_wait();
     const int quad = warp & 3;
     uint32_t ui = 0;
     for (int u = blockIdx.x; u < A.units; u += gridDim.x, ++ui) {
@@ -501,25 +532,23 @@ static int launch_tc(const CUtensorMap& mw, const CUtensorMap& mx, const TcArgs&
   aa.n_tiles = p.n_tiles;
   aa.units = units;
   const int grid = std::min(units, sm_count());
-  kern<<<grid, TC_THREADS, TcCfgMT::SMEM, st>>>(mw, mx, aa);
-  int rc = check_launch("qsp_gemm(tcgen05)");
+  int rc = launch_pdl("qsp_gemm(tcgen05)", kern, dim3(grid), dim3(TC_THREADS), TcCfgMT::SMEM, st, mw, mx, aa);
   if (rc || p.splits == 1) return rc;
   const int ldp = p.n_tiles * BN;
   const int64_t split_stride = (int64_t)p.m_tiles * MT * ldp;
-  if (epi.kind == GEMM_EPI_RESNORM) {
-    splitk_residual_rmsnorm_kernel<<<a.m, 256, 0, st>>>(a.partial, p.splits, split_stride, ldp, a.c, a.ldc,
-                                                         epi.norm_w, epi.y, epi.ldy, a.n, epi.eps);
-    return check_launch("qsp_gemm(split-k merge + residual + rmsnorm)");
-  }
+  if (epi.kind == GEMM_EPI_RESNORM)
+    return launch_pdl("qsp_gemm(split-k merge + residual + rmsnorm)", splitk_residual_rmsnorm_kernel, dim3(a.m),
+                      dim3(256), 0, st, (const float*)a.partial, p.splits, split_stride, ldp, a.c, a.ldc,
+                      epi.norm_w, epi.y, epi.ldy, a.n, epi.eps);
   if (epi.kind == GEMM_EPI_SWIGLU) {
     const int inter = a.n / 2;
     dim3 g((unsigned)((inter / 4 + 255) / 256), (unsigned)a.m);
-    splitk_swiglu_kernel<<<g, 256, 0, st>>>(a.partial, p.splits, split_stride, ldp, epi.y, epi.ldy, inter);
-    return check_launch("qsp_gemm(split-k merge + swiglu)");
+    return launch_pdl("qsp_gemm(split-k merge + swiglu)", splitk_swiglu_kernel, g, dim3(256), 0, st,
+                      (const float*)a.partial, p.splits, split_stride, ldp, epi.y, epi.ldy, inter);
   }
   dim3 rgrid((unsigned)((a.n / 4 + 255) / 256 + 1), (unsigned)a.m);
-  splitk_store_kernel<<<rgrid, 256, 0, st>>>(a.partial, p.splits, split_stride, ldp, a.c, a.ldc, a.n, a.accumulate);
-  return check_launch("qsp_gemm(split-k merge)");
+  return launch_pdl("qsp_gemm(split-k merge)", splitk_store_kernel, rgrid, dim3(256), 0, st, (const float*)a.partial,
+                    p.splits, split_stride, ldp, a.c, a.ldc, a.n, a.accumulate);
 }
 
 static size_t ws_need(const TcPlan& p) { return p.partial_bytes; }
@@ -580,6 +609,7 @@ namespace qsp {
 int gdn_device_error(int reset);
 int attn_device_error(int reset);
 int moe_device_error(int reset);
+int gemm_cl_device_error(int reset);
 }
 
 extern "C" int qsp_device_status(int32_t* code, int32_t reset) {
@@ -587,10 +617,11 @@ extern "C" int qsp_device_status(int32_t* code, int32_t reset) {
   const int gdn = qsp::gdn_device_error(reset);
   const int attn = qsp::attn_device_error(reset);
   const int moe = qsp::moe_device_error(reset);
+  const int cl = qsp::gemm_cl_device_error(reset);
   int v = 0;
   cudaError_t e = cudaMemcpyFromSymbol(&v, qsp::g_qsp_dev_error, sizeof(int));
   if (e != cudaSuccess) return qsp::set_error(QSP_ERR_CUDA, "qsp_device_status: %s", cudaGetErrorString(e));
-  *code = v != 0 ? v : (gdn != 0 ? gdn : (attn != 0 ? attn : moe));
+  *code = v != 0 ? v : (gdn != 0 ? gdn : (attn != 0 ? attn : (moe != 0 ? moe : cl)));
   if (reset && v != 0) {
     const int zero = 0;
     e = cudaMemcpyToSymbol(qsp::g_qsp_dev_error, &zero, sizeof(int));

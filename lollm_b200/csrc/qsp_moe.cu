@@ -97,6 +97,8 @@ __global__ void __launch_bounds__(256) moe_route_kernel(const T* __restrict__ R,
                                                         int* __restrict__ idx, float* __restrict__ wts,
                                                         int* __restrict__ rank, int* __restrict__ counts,
                                                         T* __restrict__ act_s, float* __restrict__ sig) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ float route_smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t = blockIdx.x * 8 + warp;
@@ -188,6 +190,8 @@ __global__ void __launch_bounds__(256) moe_gather_kernel(const T* __restrict__ x
                                                          int* __restrict__ pos_of, int* __restrict__ tok_of,
                                                          float* __restrict__ w_of, int* __restrict__ e_of,
                                                          T* __restrict__ xs, int32_t* __restrict__ counts_out) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ int offs[MOE_MAX_EXPERTS + 1];
   __shared__ int wsum[8];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -253,6 +257,8 @@ __global__ void __launch_bounds__(256) moe_gate_up_simt_kernel(const T* __restri
                                                                const T* __restrict__ gu, int I,
                                                                const int* __restrict__ e_of, int P,
                                                                T* __restrict__ as) {
+  pdl_trigger();
+  pdl_wait();
   const int pos = blockIdx.x;
   const int j = blockIdx.y * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (pos >= P || j >= I) return;
@@ -278,6 +284,8 @@ __global__ void __launch_bounds__(256) moe_down_simt_kernel(const T* __restrict_
                                                             const int* __restrict__ e_of,
                                                             const float* __restrict__ w_of, int P,
                                                             T* __restrict__ yw) {
+  pdl_trigger();
+  pdl_wait();
   const int pos = blockIdx.x;
   const int n = blockIdx.y * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (pos >= P || n >= H) return;
@@ -322,6 +330,8 @@ struct MoeTcArgs {
 template <int NA>
 __global__ void __launch_bounds__(192, 1)
 moe_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x, const MoeTcArgs A) {
+  pdl_trigger();
+  pdl_wait();
   using C = MoeTcCfg<NA>;
   using namespace tc;
   extern __shared__ uint8_t smem_raw[];
@@ -486,8 +496,7 @@ static int launch_moe_tc(const CUtensorMap& mw, const CUtensorMap& mx, const Moe
   }
   const int units = a.E * a.RB;
   const int grid = std::min(units, tc::sm_count());
-  kern<<<grid, 192, C::SMEM, st>>>(mw, mx, a);
-  return check_launch("qsp_moe_ffn(tcgen05 experts)");
+  return launch_pdl("qsp_moe_ffn(tcgen05 experts)", kern, dim3(grid), dim3(192), C::SMEM, st, mw, mx, a);
 }
 
 // ------------------------------------------------------------------ 7. combine
@@ -501,6 +510,8 @@ __global__ void __launch_bounds__(256) moe_combine_kernel(const T* __restrict__ 
                                                           T* __restrict__ x, int64_t ldx,
                                                           const T* __restrict__ norm_w, T* __restrict__ y,
                                                           int64_t ldy, float eps) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ float red[32];
   __shared__ int pos[MOE_MAX_TOPK];
   const int t = blockIdx.x;
@@ -593,17 +604,17 @@ extern "C" int qsp_moe_ffn(const qsp_moe_layer* L, void* stream) {
   QSP_DISPATCH_DTYPE(L->dtype, T, {
     // 2. route
     const size_t rsmem = (size_t)8 * E * sizeof(float);
-    moe_route_kernel<T><<<(unsigned)((m + 7) / 8), 256, rsmem, st>>>(
-        (const T*)at(W.r), W.n_in, (int)m, (int)E, (int)k, L->norm_topk_prob ? 1 : 0, (int)Is, (int)W.n_route,
-        (int*)at(W.idx), (float*)at(W.wts), (int*)at(W.rank), counts, (T*)at(W.act_s), (float*)at(W.sig));
-    rc = check_launch("qsp_moe_ffn(route)");
+    rc = launch_pdl("qsp_moe_ffn(route)", moe_route_kernel<T>, dim3((unsigned)((m + 7) / 8)), dim3(256), rsmem, st,
+                    (const T*)at(W.r), (int64_t)W.n_in, (int)m, (int)E, (int)k, L->norm_topk_prob ? 1 : 0, (int)Is,
+                    (int)W.n_route, (int*)at(W.idx), (float*)at(W.wts), (int*)at(W.rank), counts, (T*)at(W.act_s),
+                    (float*)at(W.sig));
     if (rc) return rc;
     // 3. gather
-    moe_gather_kernel<T><<<(unsigned)((P + 7) / 8), 256, 0, st>>>(
-        (const T*)L->xn, L->ld_xn, (int)m, (int)H, (int)E, (int)k, (const int*)at(W.idx), (const float*)at(W.wts),
-        (const int*)at(W.rank), counts, (int*)at(W.offsets), (int*)at(W.pos_of), (int*)at(W.tok_of),
-        (float*)at(W.w_of), (int*)at(W.e_of), (T*)at(W.xs), L->expert_counts);
-    rc = check_launch("qsp_moe_ffn(gather)");
+    rc = launch_pdl("qsp_moe_ffn(gather)", moe_gather_kernel<T>, dim3((unsigned)((P + 7) / 8)), dim3(256), 0, st,
+                    (const T*)L->xn, (int64_t)L->ld_xn, (int)m, (int)H, (int)E, (int)k, (const int*)at(W.idx),
+                    (const float*)at(W.wts), (const int*)at(W.rank), (const int*)counts, (int*)at(W.offsets),
+                    (int*)at(W.pos_of), (int*)at(W.tok_of), (float*)at(W.w_of), (int*)at(W.e_of), (T*)at(W.xs),
+                    L->expert_counts);
     if (rc) return rc;
     // 4-5. routed experts
     // tensor-core path when every operand can go through TMA (16-byte rows and bases)
@@ -633,14 +644,13 @@ extern "C" int qsp_moe_ffn(const qsp_moe_layer* L, void* stream) {
       rc = launch_moe_tc<1>(m_dn, m_as, a, st);
       if (rc) return rc;
     } else {
-      moe_gate_up_simt_kernel<T><<<dim3((unsigned)P, (unsigned)((I + 7) / 8)), 256, 0, st>>>(
-          (const T*)at(W.xs), (int)H, (const T*)L->gate_up, (int)I, (const int*)at(W.e_of), P, (T*)at(W.as));
-      rc = check_launch("qsp_moe_ffn(gate|up simt)");
+      rc = launch_pdl("qsp_moe_ffn(gate|up simt)", moe_gate_up_simt_kernel<T>, dim3((unsigned)P, (unsigned)((I + 7) / 8)),
+                      dim3(256), 0, st, (const T*)at(W.xs), (int)H, (const T*)L->gate_up, (int)I,
+                      (const int*)at(W.e_of), P, (T*)at(W.as));
       if (rc) return rc;
-      moe_down_simt_kernel<T><<<dim3((unsigned)P, (unsigned)((H + 7) / 8)), 256, 0, st>>>(
-          (const T*)at(W.as), (int)I, (const T*)L->down, (int)H, (const int*)at(W.e_of), (const float*)at(W.w_of), P,
-          (T*)at(W.yw));
-      rc = check_launch("qsp_moe_ffn(down simt)");
+      rc = launch_pdl("qsp_moe_ffn(down simt)", moe_down_simt_kernel<T>, dim3((unsigned)P, (unsigned)((H + 7) / 8)),
+                      dim3(256), 0, st, (const T*)at(W.as), (int)I, (const T*)L->down, (int)H, (const int*)at(W.e_of),
+                      (const float*)at(W.w_of), P, (T*)at(W.yw));
       if (rc) return rc;
     }
     // 6. shared expert down projection
@@ -650,10 +660,10 @@ extern "C" int qsp_moe_ffn(const qsp_moe_layer* L, void* stream) {
       if (rc) return rc;
     }
     // 7. combine + residual + next norm
-    moe_combine_kernel<T><<<(unsigned)m, 256, 0, st>>>(
-        (const T*)at(W.yw), (int)H, (int)k, (const int*)at(W.pos_of), Is > 0 ? (const T*)at(W.s) : nullptr,
-        (const float*)at(W.sig), (T*)L->x, L->ld_x, (const T*)L->norm_w, (T*)L->y, L->ld_y, L->eps);
-    rc = check_launch("qsp_moe_ffn(combine)");
+    rc = launch_pdl("qsp_moe_ffn(combine)", moe_combine_kernel<T>, dim3((unsigned)m), dim3(256), 0, st,
+                    (const T*)at(W.yw), (int)H, (int)k, (const int*)at(W.pos_of),
+                    Is > 0 ? (const T*)at(W.s) : (const T*)nullptr, (const float*)at(W.sig), (T*)L->x,
+                    (int64_t)L->ld_x, (const T*)L->norm_w, (T*)L->y, (int64_t)L->ld_y, L->eps);
   });
   (void)es;
   return rc;

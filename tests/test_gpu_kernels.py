@@ -72,6 +72,36 @@ def test_gemm(dt, mnk):
     assert K().device_status() == 0
 
 
+@pytest.mark.parametrize("m", [64, 200, 256])
+def test_gemm_fused_epilogues(m):
+    """The projections' fused tails in bf16 — residual add + next RMSNorm and SwiGLU — at the
+    verify-step row counts (m = 200, 256 take the cluster split-K kernel, m = 64 the persistent
+    one), against a float64 product with the same rounding points."""
+    dt = torch.bfloat16
+    g = gen(11)
+    eps = 1e-6
+    a, w = rn(g, m, 4096, dtype=dt), rn(g, 2048, 4096, scale=0.02, dtype=dt)
+    x0, nw = rn(g, m, 2048, dtype=dt), rn(g, 2048, scale=0.1, dtype=dt)
+    x, y = x0.to(DEV), torch.empty(m, 2048, dtype=dt, device=DEV)
+    K().gemm_residual_rmsnorm(a.to(DEV), w.to(DEV), x, nw.to(DEV), y, eps)
+    xr = (x0.float() + (a.double() @ w.double().T).to(dt).float()).to(dt)
+    close(x, xr, dt)
+    close(y, Q.rms_norm(xr, nw, eps), dt)
+    inter = 1536
+    a2, wgu = rn(g, m, 2048, dtype=dt), rn(g, 2 * inter, 2048, scale=0.02, dtype=dt)
+    act = torch.empty(m, inter, dtype=dt, device=DEV)
+    tmp = torch.empty(m, 2 * inter, dtype=dt, device=DEV)
+    K().gemm_swiglu(a2.to(DEV), wgu.to(DEV), act, tmp)
+    h = (a2.double() @ wgu.double().T).to(dt)
+    close(act, Q.silu_mul(h[:, :inter], h[:, inter:]), dt)
+    # the in_proj shape (12352 columns: a partial last tile) through plain qsp_gemm
+    w3 = rn(g, 12352, 2048, scale=0.02, dtype=dt)
+    c = torch.empty(m, 12352, dtype=dt, device=DEV)
+    K().gemm(a2.to(DEV), w3.to(DEV), c)
+    close(c, (a2.double() @ w3.double().T).to(dt), dt)
+    assert K().device_status() == 0
+
+
 @pytest.mark.parametrize("dt", DTS)
 def test_swiglu_embed_select(dt):
     g = gen(2)
