@@ -212,23 +212,46 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const qsp_attn_layer 
   den = warp_sum(den);
   const T* row = static_cast<const T*>(L.qkv) + (int64_t)m * L.ld_qkv;
   T* o = static_cast<T*>(L.out) + (int64_t)m * L.ld_out + (int64_t)hq * hd;
-  for (int d0 = 2 * lane; d0 < hd; d0 += 64) {
-    float n0 = 0.f, n1 = 0.f;
-    if (M != -INFINITY) {
-      for (int p = 0; p < np; ++p) {
-        const float* q = base + (int64_t)p * (hd + 2);
-        const float mp = q[hd];
+  // lane (2·lane + 64·i, +1) of every partial: the weights e^{m_p − M} are computed once per
+  // partial (lane p of each 32-partial group) and broadcast; all of a partial's columns are
+  // loaded together, so the merge waits on memory once per partial, not once per column pair
+  constexpr int MAXI = 8;   // head_dim ≤ 512
+  float2 n[MAXI];
+#pragma unroll
+  for (int i = 0; i < MAXI; ++i) n[i] = make_float2(0.f, 0.f);
+  if (M != -INFINITY) {
+    for (int p0 = 0; p0 < np; p0 += 32) {
+      const int pl = p0 + lane;
+      const float mpl = pl < np ? base[(int64_t)pl * (hd + 2) + hd] : -INFINITY;
+      const float wl = mpl != -INFINITY ? expf(mpl - M) : 0.f;
+      const int cnt = min(32, np - p0);
+      for (int j = 0; j < cnt; ++j) {
+        const float mp = __shfl_sync(0xffffffffu, mpl, j);
+        const float w = __shfl_sync(0xffffffffu, wl, j);
         if (mp == -INFINITY) continue;
-        const float w = expf(mp - M);
-        const float2 v = *reinterpret_cast<const float2*>(q + d0);
-        n0 = fmaf(w, v.x, n0);
-        n1 = fmaf(w, v.y, n1);
+        const float* q = base + (int64_t)(p0 + j) * (hd + 2);
+        float2 v[MAXI];
+#pragma unroll
+        for (int i = 0; i < MAXI; ++i)
+          if (2 * lane + 64 * i < hd) v[i] = *reinterpret_cast<const float2*>(q + 2 * lane + 64 * i);
+#pragma unroll
+        for (int i = 0; i < MAXI; ++i) {
+          if (2 * lane + 64 * i < hd) {
+            n[i].x = fmaf(w, v[i].x, n[i].x);
+            n[i].y = fmaf(w, v[i].y, n[i].y);
+          }
+        }
       }
     }
+  }
+#pragma unroll
+  for (int i = 0; i < MAXI; ++i) {
+    const int d0 = 2 * lane + 64 * i;
+    if (d0 >= hd) continue;
 #pragma unroll
     for (int k = 0; k < 2; ++k) {
       const int d = d0 + k;
-      const float attn = dt<T>::round(den > 0.f ? (k ? n1 : n0) / den : 0.f);
+      const float attn = dt<T>::round(den > 0.f ? (k ? n[i].y : n[i].x) / den : 0.f);
       const float gate = dt<T>::to_f(row[(int64_t)hq * 2 * hd + hd + d]);
       o[d] = dt<T>::from_f(attn * dt<T>::round(sigmoidf_(gate)));
     }
