@@ -299,12 +299,13 @@ __global__ void __launch_bounds__(256) moe_down_simt_kernel(const T* __restrict_
 }
 
 // ------------------------------------------------------------------ 4/5 on tensor cores
-// Work unit = (expert e, 128 output rows rb). For each tile of ≤ 64 of the expert's sorted
-// token rows, the unit streams the expert's weight rows over K through the ring; the MMA is
-// D[128 weight rows × N tokens] += W[128 × 16] · Xᵀ[16 × N] with N = the tile's rows rounded
-// up to 16. NA = 2 (gate|up): two weight tiles per stage (gate rows and the matching up
-// rows), two accumulators, SwiGLU in the epilogue. NA = 1 (down): one weight tile, one
-// accumulator, times the pair's routing weight in the epilogue.
+// Work unit = (expert e, a block of weight rows). For each tile of ≤ 64 of the expert's
+// sorted token rows, the unit streams the expert's weight rows over K through the ring; the
+// MMA is D[128 weight rows × N tokens] += W[128 × 16] · Xᵀ[16 × N] with N = the tile's rows
+// rounded up to 16, one accumulator per 128-row weight tile (NA of them per stage).
+// SWI (gate|up): the two tiles are gate rows and the matching up rows, SwiGLU in the
+// epilogue. Otherwise (down): NA consecutive 128-row tiles of output rows, each product times
+// the pair's routing weight in the epilogue.
 template <int NA>
 struct MoeTcCfg {
   static constexpr int TN = 64;                   // token rows per tile
@@ -327,7 +328,7 @@ struct MoeTcArgs {
   const float* w_of;       // [P] routing weight per sorted row (down)
 };
 
-template <int NA>
+template <int NA, bool SWI>
 __global__ void __launch_bounds__(192, 1)
 moe_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x, const MoeTcArgs A) {
   pdl_trigger();
@@ -372,7 +373,7 @@ moe_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
       for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
         const int e = u / A.RB, rb = u % A.RB;
         const int off = __ldg(&A.offsets[e]), n_e = __ldg(&A.offsets[e + 1]) - off;
-        const int row0 = e * A.rows_per_expert + rb * 128;
+        const int row0 = e * A.rows_per_expert + rb * (SWI ? 128 : 128 * NA);
         for (int t0 = 0; t0 < n_e && ok; t0 += C::TN) {
           const int nb16 = (min(C::TN, n_e - t0) + 15) / 16;
           const uint32_t bytes = NA * C::A_BYTES + nb16 * 2048;
@@ -386,7 +387,7 @@ moe_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
             uint8_t* st = smem + s * C::STAGE;
             mbar_expect_tx(&full[s], bytes);
             tma_load_2d(st, &tm_w, &full[s], kb * 64, row0);
-            if (NA == 2) tma_load_2d(st + C::A_BYTES, &tm_w, &full[s], kb * 64, row0 + A.out_w);
+            if (NA == 2) tma_load_2d(st + C::A_BYTES, &tm_w, &full[s], kb * 64, row0 + (SWI ? A.out_w : 128));
             for (int q = 0; q < nb16; ++q)
               tma_load_2d(st + NA * C::A_BYTES + q * 2048, &tm_x, &full[s], kb * 64, off + t0 + q * 16);
           }
@@ -436,7 +437,7 @@ moe_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
     for (int u = blockIdx.x; u < units; u += gridDim.x) {
       const int e = u / A.RB, rb = u % A.RB;
       const int off = __ldg(&A.offsets[e]), n_e = __ldg(&A.offsets[e + 1]) - off;
-      const int orow = rb * 128 + quad * 32 + lane;
+      const int orow = rb * (SWI ? 128 : 128 * NA) + quad * 32 + lane;
       for (int t0 = 0; t0 < n_e; t0 += C::TN, ++ti) {
         const int nt = min(C::TN, n_e - t0);
         const uint32_t buf = ti & 1u, use = ti >> 1;
@@ -446,7 +447,7 @@ moe_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
         for (int c0 = 0; c0 < nt; c0 += 32) {
           float v[32];
           tmem_ld32(tb + c0, v);
-          if (NA == 2) {
+          if (SWI) {
             float w[32];
             tmem_ld32(tb + C::ACC_COLS + c0, w);
             if (ok && orow < A.out_w) {
@@ -460,13 +461,21 @@ moe_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
                 }
               }
             }
-          } else if (ok && orow < A.out_w) {
+          } else {
+            // down projection: accumulator q holds output rows orow + 128·q
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              if (c0 + j < nt) {
-                const int pos = off + t0 + c0 + j;
-                const float r = dt<__nv_bfloat16>::round(v[j]);
-                A.out[(int64_t)pos * A.out_w + orow] = __float2bfloat16_rn(r * __ldg(&A.w_of[pos]));
+            for (int q = 0; q < NA; ++q) {
+              if (q > 0) tmem_ld32(tb + q * C::ACC_COLS + c0, v);
+              const int oq = orow + q * 128;
+              if (ok && oq < A.out_w) {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                  if (c0 + j < nt) {
+                    const int pos = off + t0 + c0 + j;
+                    const float r = dt<__nv_bfloat16>::round(v[j]);
+                    A.out[(int64_t)pos * A.out_w + oq] = __float2bfloat16_rn(r * __ldg(&A.w_of[pos]));
+                  }
+                }
               }
             }
           }
@@ -484,10 +493,10 @@ moe_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
   }
 }
 
-template <int NA>
+template <int NA, bool SWI>
 static int launch_moe_tc(const CUtensorMap& mw, const CUtensorMap& mx, const MoeTcArgs& a, cudaStream_t st) {
   using C = MoeTcCfg<NA>;
-  auto kern = moe_tc_kernel<NA>;
+  auto kern = moe_tc_kernel<NA, SWI>;
   static bool attr_set = false;
   if (!attr_set) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM) != cudaSuccess)
@@ -633,15 +642,15 @@ extern "C" int qsp_moe_ffn(const qsp_moe_layer* L, void* stream) {
       a.rows_per_expert = (int)(2 * I);
       a.out_w = (int)I;
       a.out = (__nv_bfloat16*)at(W.as);
-      rc = launch_moe_tc<2>(m_gu, m_xs, a, st);
+      rc = launch_moe_tc<2, true>(m_gu, m_xs, a, st);
       if (rc) return rc;
-      a.RB = (int)((H + 127) / 128);
+      a.RB = (int)((H + 255) / 256);   // 256 output rows (two accumulators) per unit
       a.n_kb = (int)((I + 63) / 64);
       a.rows_per_expert = (int)H;
       a.out_w = (int)H;
       a.out = (__nv_bfloat16*)at(W.yw);
       a.w_of = (const float*)at(W.w_of);
-      rc = launch_moe_tc<1>(m_dn, m_as, a, st);
+      rc = launch_moe_tc<2, false>(m_dn, m_as, a, st);
       if (rc) return rc;
     } else {
       rc = launch_pdl("qsp_moe_ffn(gate|up simt)", moe_gate_up_simt_kernel<T>, dim3((unsigned)P, (unsigned)((I + 7) / 8)),
