@@ -551,15 +551,38 @@ __global__ void __launch_bounds__(256) gdn_prep_kernel(const qsp_gdn_layer L, co
           *reinterpret_cast<const uint4*>(xr + (int64_t)(r0 + i) * nchg + c);
     }
   }
-  // 3. conv + SiLU
-  for (int e = tid; e < nchg * T_; e += blockDim.x) {
-    const int t = e / nchg, c = e % nchg;
-    float acc = 0.f;
-    for (int jj = 0; jj < K; ++jj)
-      acc = fmaf(dt<T>::to_f(cwr[c * K + jj]), dt<T>::to_f(xr[(int64_t)(t + jj) * nchg + c]), acc);
-    const float a = dt<T>::round(siluf_(dt<T>::round(acc)));
-    if (c < 2 * DK) qk[t * 2 * DK + c] = a;
-    else recA(kh * vpk + (c - 2 * DK) / DV, t)->v[(c - 2 * DK) % DV] = dt<T>::from_f(a);
+  // 3. conv + SiLU: a thread takes a pair of adjacent channels for every token (taps read
+  //    once, paired loads and stores); per output the taps accumulate in order jj = 0..K-1
+  for (int cp = tid; cp < nchg / 2; cp += blockDim.x) {
+    const int c = 2 * cp;
+    float w0[GDN_KMAX], w1[GDN_KMAX];
+#pragma unroll
+    for (int jj = 0; jj < GDN_KMAX; ++jj) {
+      w0[jj] = jj < K ? dt<T>::to_f(cwr[c * K + jj]) : 0.f;
+      w1[jj] = jj < K ? dt<T>::to_f(cwr[(c + 1) * K + jj]) : 0.f;
+    }
+    const bool isv = c >= 2 * DK;
+    const int vh = isv ? kh * vpk + (c - 2 * DK) / DV : 0, vc = isv ? (c - 2 * DK) % DV : 0;
+    for (int t = 0; t < T_; ++t) {
+      float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+      for (int jj = 0; jj < GDN_KMAX; ++jj) {
+        if (jj < K) {
+          const T* xp = xr + (int64_t)(t + jj) * nchg + c;
+          a0 = fmaf(w0[jj], dt<T>::to_f(xp[0]), a0);
+          a1 = fmaf(w1[jj], dt<T>::to_f(xp[1]), a1);
+        }
+      }
+      const float s0 = dt<T>::round(siluf_(dt<T>::round(a0)));
+      const float s1 = dt<T>::round(siluf_(dt<T>::round(a1)));
+      if (!isv) {
+        *reinterpret_cast<float2*>(qk + t * 2 * DK + c) = make_float2(s0, s1);
+      } else {
+        T* vp = recA(vh, t)->v + vc;
+        vp[0] = dt<T>::from_f(s0);
+        vp[1] = dt<T>::from_f(s1);
+      }
+    }
   }
   if (gate_t >= 0) recA(gate_h, gate_t)->db = make_float4(gate_d, gate_b, 0.f, 0.f);
   __syncthreads();
