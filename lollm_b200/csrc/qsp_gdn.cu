@@ -673,19 +673,19 @@ struct __align__(128) GdnChunkSmem {
 
 // Column sums over this thread's rows of S·x_v for 4 consecutive vector slots, reduced over
 // the 4 row blocks by a butterfly: on return own[v] = (Sᵀx_v) at column 4cg + rg.
-template <int DK>
+template <int DK, int NV = 4>
 __device__ __forceinline__ void gdn_dots4(const uint64_t (&S)[4][DK / 8], const float* __restrict__ vec0, int rg,
                                           float* own) {
   constexpr int RB = DK / 4;
-  uint64_t acc[4][4];
+  uint64_t acc[NV][4];
 #pragma unroll
-  for (int v = 0; v < 4; ++v)
+  for (int v = 0; v < NV; ++v)
 #pragma unroll
     for (int c = 0; c < 4; ++c) acc[v][c] = 0;
 #pragma unroll
   for (int m = 0; m < RB / 4; ++m) {
 #pragma unroll
-    for (int v = 0; v < 4; ++v) {
+    for (int v = 0; v < NV; ++v) {
       const ulonglong2 kk = *reinterpret_cast<const ulonglong2*>(vec0 + v * DK + RB * rg + 4 * m);
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
@@ -696,7 +696,7 @@ __device__ __forceinline__ void gdn_dots4(const uint64_t (&S)[4][DK / 8], const 
   }
   const bool hi = rg & 2, lo = rg & 1;
 #pragma unroll
-  for (int v = 0; v < 4; ++v) {
+  for (int v = 0; v < NV; ++v) {
     float p[4];
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
@@ -926,8 +926,13 @@ gdn_chunk_kernel(const qsp_gdn_layer L, const GdnRing RG, const int n_new) {
       for (int g = 0; g < ng; ++g) {   // pass 1: Sᵀk_s, then (phase 1) Sᵀq_t, four slots at a time
         const bool isq = g >= ngk;
         const int g4 = isq ? g - ngk : g;
-        float t4[4];
-        gdn_dots4<DK>(S, sm.vec[(isq ? 2 * GDN_TB : kslot) + 4 * g4], rg, t4);
+        float t4[4] = {0.f, 0.f, 0.f, 0.f};
+        // the last group of a call with n % 4 in {1, 2} only needs that many slots
+        const int left = n - 4 * g4;
+        const float* vg = sm.vec[(isq ? 2 * GDN_TB : kslot) + 4 * g4];
+        if (left == 1) gdn_dots4<DK, 1>(S, vg, rg, t4);
+        else if (left == 2) gdn_dots4<DK, 2>(S, vg, rg, t4);
+        else gdn_dots4<DK>(S, vg, rg, t4);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
 #pragma unroll
@@ -964,13 +969,22 @@ gdn_chunk_kernel(const qsp_gdn_layer L, const GdnRing RG, const int n_new) {
     }
     if (N > 0) {
       // 6. RMSNormGated over the dv columns of each token: w·round(x̂)·silu(z), x = round(core)
+      // the per-token sums of squares, their butterflies interleaved (same order per token as
+      // warp_sum)
+      float ssq[GDN_TB];
 #pragma unroll
       for (int t = 0; t < GDN_TB; ++t) {
-        if (t < N) {
-          const float x = dt<T>::round(o[t]);
-          const float ss = warp_sum(x * x);
-          if (lane == 0) sm.red[warp][t] = ss;
-        }
+        const float x = dt<T>::round(o[t]);
+        ssq[t] = x * x;
+      }
+#pragma unroll
+      for (int sh = 16; sh > 0; sh >>= 1)
+#pragma unroll
+        for (int t = 0; t < GDN_TB; ++t) ssq[t] += __shfl_xor_sync(0xffffffffu, ssq[t], sh);
+      if (lane == 0) {
+#pragma unroll
+        for (int t = 0; t < GDN_TB; ++t)
+          if (t < N) sm.red[warp][t] = ssq[t];
       }
       __syncthreads();
 #pragma unroll
