@@ -136,8 +136,35 @@ struct TcArgs {
   int64_t ldc;
   int m, n, n_kb, kb_per_split, splits, accumulate;
   int m_tiles, n_tiles, units;   // work unit u: split u / tiles, tile u % tiles (m-tile fastest)
-  float* partial;  // [splits][m_tiles*MT][n_tiles*128]
+  float* partial;  // [splits][m_tiles*MT][n_tiles*BN]
+  // K-split tail (unsplit plans only): units from full_units on cover tiles full_units.. in
+  // tail_split K slices of tail_kps k-blocks each, written as fp32 partials
+  // [tail_split][MT][(tiles − full_units)·BN] and summed by a merge
+  int full_units, tail_split, tail_kps;
 };
+
+struct TcUnit {
+  int tile, slice, kb0, nk;
+  bool tail;
+};
+__device__ __forceinline__ TcUnit tc_unit(const TcArgs& A, int u, int tiles) {
+  TcUnit r;
+  if (A.tail_split > 0 && u >= A.full_units) {
+    const int v = u - A.full_units;
+    r.tile = A.full_units + v / A.tail_split;
+    r.slice = v % A.tail_split;
+    r.kb0 = r.slice * A.tail_kps;
+    r.nk = min(A.n_kb, r.kb0 + A.tail_kps) - r.kb0;
+    r.tail = true;
+  } else {
+    r.slice = u / tiles;
+    r.tile = u % tiles;
+    r.kb0 = r.slice * A.kb_per_split;
+    r.nk = min(A.n_kb, r.kb0 + A.kb_per_split) - r.kb0;
+    r.tail = false;
+  }
+  return r;
+}
 
 // What happens to the product after the split-K merge (the unsplit kernel always stores c).
 struct GemmEpi {
@@ -302,8 +329,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
       int pre_kb[C::STAGES], pre_mb[C::STAGES];
       uint32_t npre = 0;
       for (int u = blockIdx.x; u < A.units && npre < (uint32_t)C::STAGES; u += gridDim.x) {
-        const int sp = u / tiles, tile = u % tiles, mb = tile % A.m_tiles, nb = tile / A.m_tiles;
-        const int kb0 = sp * A.kb_per_split, nk = min(A.n_kb, kb0 + A.kb_per_split) - kb0;
+        const TcUnit U = tc_unit(A, u, tiles);
+        const int mb = U.tile % A.m_tiles, nb = U.tile / A.m_tiles, kb0 = U.kb0, nk = U.nk;
         const int rot = u % nk;
         for (int i = 0; i < nk && npre < (uint32_t)C::STAGES; ++i, ++npre) {
           const int kb = kb0 + (i + rot) % nk;
@@ -319,8 +346,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
       uint32_t it = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < A.units && ok; u += gridDim.x) {
-        const int sp = u / tiles, tile = u % tiles, mb = tile % A.m_tiles, nb = tile / A.m_tiles;
-        const int kb0 = sp * A.kb_per_split, nk = min(A.n_kb, kb0 + A.kb_per_split) - kb0;
+        const TcUnit U = tc_unit(A, u, tiles);
+        const int mb = U.tile % A.m_tiles, nb = U.tile / A.m_tiles, kb0 = U.kb0, nk = U.nk;
         // units walk their k-blocks from a rotated start so concurrent CTAs read different
         // activation slabs (all CTAs on the same slab at once hot-spots L2)
         const int rot = u % nk;
@@ -347,8 +374,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
       uint32_t it = 0, ui = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < A.units; u += gridDim.x, ++ui) {
-        const int sp = u / tiles;
-        const int kb0 = sp * A.kb_per_split, nk = min(A.n_kb, kb0 + A.kb_per_split) - kb0;
+        const int nk = tc_unit(A, u, tiles).nk;
         const uint32_t buf = (C::ACC_BUFS == 2) ? (ui & 1u) : 0u;
         const uint32_t use = (C::ACC_BUFS == 2) ? (ui >> 1) : ui;   // how often this buffer was used before
         if (ok && use >= 1 && !mbar_wait(&acc_empty[buf], (use - 1) & 1u, 104)) ok = false;
@@ -382,32 +408,48 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
     const int quad = warp & 3;
     uint32_t ui = 0;
     for (int u = blockIdx.x; u < A.units; u += gridDim.x, ++ui) {
-      const int sp = u / tiles, tile = u % tiles, mb = tile % A.m_tiles, nb = tile / A.m_tiles;
+      const TcUnit U = tc_unit(A, u, tiles);
+      const int mb = U.tile % A.m_tiles, nb = U.tile / A.m_tiles;
       const uint32_t buf = (C::ACC_BUFS == 2) ? (ui & 1u) : 0u;
       const uint32_t use = (C::ACC_BUFS == 2) ? (ui >> 1) : ui;
       const bool ok = mbar_wait(&acc_full[buf], use & 1u, 103);
       tc_fence_after();
-      const bool split = A.splits > 1;
-      const int ldp = A.n_tiles * TC_BN;
-      const int64_t prow0 = ((int64_t)sp * A.m_tiles + mb) * MT;
+      const bool split = A.splits > 1 || U.tail;
+      // partial row / column of this unit (the tail has its own compact partial block)
+      const int ldp = U.tail ? (A.n_tiles * A.m_tiles - A.full_units) * TC_BN : A.n_tiles * TC_BN;
+      const int64_t prow0 = ((int64_t)U.slice * A.m_tiles + mb) * MT;
+      const int pcol0 = U.tail ? (U.tile - A.full_units) * TC_BN : nb * TC_BN;
+      if (split) {   // fp32 partial rows, one column per thread (coalesced across the warp)
 #pragma unroll
-      for (int q = 0; q < C::NACC; ++q) {
-        const int n = nb * TC_BN + q * TC_MM + quad * 32 + lane;
-        const uint32_t tbase = tmem + buf * C::UNIT_COLS + q * C::ACC_COLS + ((uint32_t)(quad * 32) << 16);
-        for (int c0 = 0; c0 < MT; c0 += 32) {
-          float v[32];
-          tmem_ld32(tbase + c0, v);
-          if (!ok) continue;
+        for (int q = 0; q < C::NACC; ++q) {
+          float* prow = A.partial + prow0 * ldp + pcol0 + q * TC_MM + quad * 32 + lane;
+          const uint32_t tbase = tmem + buf * C::UNIT_COLS + q * C::ACC_COLS + ((uint32_t)(quad * 32) << 16);
+          for (int c0 = 0; c0 < MT; c0 += 32) {
+            float v[32];
+            tmem_ld32(tbase + c0, v);
+            if (!ok) continue;
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int m = mb * MT + c0 + j;
-            if (split) {
-              A.partial[(prow0 + c0 + j) * ldp + n] = v[j];
-            } else if (m < A.m && n < A.n) {
-              __nv_bfloat16* p = A.c + (int64_t)m * A.ldc + n;
-              float r = dt<__nv_bfloat16>::round(v[j]);
-              if (A.accumulate) r += __bfloat162float(*p);
-              *p = __float2bfloat16_rn(r);
+            for (int j = 0; j < 32; ++j) prow[(c0 + j) * ldp] = v[j];   // < 2^31: MT·ldp floats
+          }
+        }
+      } else {
+#pragma unroll
+        for (int q = 0; q < C::NACC; ++q) {
+          const int n = nb * TC_BN + q * TC_MM + quad * 32 + lane;
+          const uint32_t tbase = tmem + buf * C::UNIT_COLS + q * C::ACC_COLS + ((uint32_t)(quad * 32) << 16);
+          for (int c0 = 0; c0 < MT; c0 += 32) {
+            float v[32];
+            tmem_ld32(tbase + c0, v);
+            if (!ok) continue;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const int m = mb * MT + c0 + j;
+              if (m < A.m && n < A.n) {
+                __nv_bfloat16* p = A.c + (int64_t)m * A.ldc + n;
+                float r = dt<__nv_bfloat16>::round(v[j]);
+                if (A.accumulate) r += __bfloat162float(*p);
+                *p = __float2bfloat16_rn(r);
+              }
             }
           }
         }
@@ -465,6 +507,7 @@ static int pick_mt(int64_t m) {
 
 struct TcPlan {
   int mt, bn, m_tiles, n_tiles, n_kb, splits, kb_per_split;
+  int full_units, tail_split, tail_kps;   // K-split tail of an unsplit plan (0: none)
   size_t partial_bytes;
 };
 
@@ -500,6 +543,25 @@ static TcPlan plan(int64_t m, int64_t n, int64_t k, int sm_count) {
   p.kb_per_split = (p.n_kb + best_s - 1) / best_s;
   p.splits = (p.n_kb + p.kb_per_split - 1) / p.kb_per_split;
   p.partial_bytes = p.splits > 1 ? (size_t)p.splits * p.m_tiles * p.mt * p.n_tiles * p.bn * sizeof(float) : 0;
+  // An unsplit plan whose tiles overrun whole rounds of the SMs by less than half a round
+  // (the vocabulary projection: 1187 tiles on 148 SMs) would finish with a few CTAs computing
+  // whole tiles while the rest idle. Those last tiles are split along K instead, so that
+  // the last round takes a fraction of a tile's time.
+  p.full_units = p.tail_split = p.tail_kps = 0;
+  if (p.splits == 1 && p.m_tiles == 1) {
+    const int grid = std::min(tiles, sm_count);
+    const int full = tiles / grid * grid, r = tiles - full;
+    if (tiles > grid && r > 0 && 2 * r <= grid) {
+      int ts = std::min(std::min(16, p.n_kb / 2), grid / r);
+      if (ts >= 2) {
+        const int kps = (p.n_kb + ts - 1) / ts;
+        p.full_units = full;
+        p.tail_split = (p.n_kb + kps - 1) / kps;
+        p.tail_kps = kps;
+        p.partial_bytes = (size_t)p.tail_split * p.mt * r * p.bn * sizeof(float);
+      }
+    }
+  }
   return p;
 }
 
@@ -526,14 +588,23 @@ static int launch_tc(const CUtensorMap& mw, const CUtensorMap& mx, const TcArgs&
       return set_error(QSP_ERR_CUDA, "qsp_gemm: cannot reserve %zu bytes of shared memory", TcCfgMT::SMEM);
     attr_set = true;
   }
-  const int units = p.m_tiles * p.n_tiles * p.splits;
+  const int tiles = p.m_tiles * p.n_tiles;
+  const int units = a.tail_split > 0 ? a.full_units + (tiles - a.full_units) * a.tail_split : tiles * p.splits;
   TcArgs aa = a;
   aa.m_tiles = p.m_tiles;
   aa.n_tiles = p.n_tiles;
   aa.units = units;
   const int grid = std::min(units, sm_count());
   int rc = launch_pdl("qsp_gemm(tcgen05)", kern, dim3(grid), dim3(TC_THREADS), TcCfgMT::SMEM, st, mw, mx, aa);
-  if (rc || p.splits == 1) return rc;
+  if (rc) return rc;
+  if (a.tail_split > 0) {   // the tail tiles' columns: c[:, full·BN, n)
+    const int col0 = a.full_units * BN, nt = a.n - col0, ldp = (tiles - a.full_units) * BN;
+    dim3 tgrid((unsigned)((nt / 4 + 255) / 256 + 1), (unsigned)a.m);
+    return launch_pdl("qsp_gemm(k-split tail merge)", splitk_store_kernel, tgrid, dim3(256), 0, st,
+                      (const float*)a.partial, a.tail_split, (int64_t)MT * ldp, ldp, a.c + col0, a.ldc, nt,
+                      a.accumulate);
+  }
+  if (p.splits == 1) return rc;
   const int ldp = p.n_tiles * BN;
   const int64_t split_stride = (int64_t)p.m_tiles * MT * ldp;
   if (epi.kind == GEMM_EPI_RESNORM)
@@ -577,6 +648,8 @@ int gemm_tc(const void* a, int64_t lda, const void* w, int64_t ldw, void* c, int
     }
   }
   if (p.splits > 1 && !aligned(workspace, 256)) return QSP_ERR_UNSUPPORTED;
+  if (p.tail_split > 0 && (workspace == nullptr || ws_bytes < ws_need(p) || !aligned(workspace, 256)))
+    p.tail_split = 0;   // no room for the tail partials: whole tiles to the end
   if (p.splits > 1 && epi.kind == GEMM_EPI_RESNORM && n > RN_MAXV * 1024) return QSP_ERR_UNSUPPORTED;
   if (p.splits > 1 && epi.kind != GEMM_EPI_STORE && (n % 8) != 0) return QSP_ERR_UNSUPPORTED;
   CUtensorMap mw, mx;
@@ -590,7 +663,10 @@ int gemm_tc(const void* a, int64_t lda, const void* w, int64_t ldw, void* c, int
   args.kb_per_split = p.kb_per_split;
   args.splits = p.splits;
   args.accumulate = (flags & QSP_GEMM_ACCUMULATE) ? 1 : 0;
-  if (p.splits > 1) args.partial = static_cast<float*>(workspace);
+  if (p.splits > 1 || p.tail_split > 0) args.partial = static_cast<float*>(workspace);
+  args.full_units = p.tail_split > 0 ? p.full_units : 0;
+  args.tail_split = p.tail_split;
+  args.tail_kps = p.tail_kps;
   if (split_out) *split_out = p.splits > 1;
   const bool wide = p.bn == 256;
   switch (p.mt) {

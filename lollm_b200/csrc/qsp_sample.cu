@@ -1,7 +1,10 @@
 // Token selection over the vocabulary: row argmax, greedy exact-match verification, the
 // lossless p/q speculative sampler and inverse-CDF categorical draws. Per-row work is one CTA
-// per row (a vocabulary row is ≤ 1.2 MB, read once or twice from HBM).
+// per row (a vocabulary row is ≤ 1.2 MB, read once or twice from HBM), except the argmax of
+// few rows, which splits each row over a thread-block cluster.
 #include "qsp_common.cuh"
+
+#include <cooperative_groups.h>
 
 namespace qsp {
 
@@ -25,10 +28,11 @@ __device__ __forceinline__ ArgBest warp_argbest(ArgBest best) {
   return best;
 }
 
-// Block argmax of one row (blockDim = SEL_THREADS). A 16-byte-aligned row is read with
-// 16-byte loads, four in flight per thread; the tail (and unaligned rows) element by element.
+// Block argmax of one row (blockDim = SEL_THREADS): the best (value, index), index LLONG_MAX
+// when no element compares (an all-NaN row). A 16-byte-aligned row is read with 16-byte
+// loads, four in flight per thread; the tail (and unaligned rows) element by element.
 template <typename T>
-__device__ long long row_argmax(const T* __restrict__ row, int64_t vocab) {
+__device__ ArgBest row_argbest(const T* __restrict__ row, int64_t vocab) {
   __shared__ float sv[32];
   __shared__ long long si[32];
   ArgBest best{-INFINITY, LLONG_MAX};
@@ -74,10 +78,17 @@ __device__ long long row_argmax(const T* __restrict__ row, int64_t vocab) {
   if (warp == 0) {
     best = lane < nw ? ArgBest{sv[lane], si[lane]} : ArgBest{-INFINITY, LLONG_MAX};
     best = warp_argbest(best);
-    if (lane == 0) si[0] = best.i == LLONG_MAX ? 0 : best.i;
+    if (lane == 0) { sv[0] = best.v; si[0] = best.i; }
   }
   __syncthreads();
-  return si[0];
+  const ArgBest r{sv[0], si[0]};
+  __syncthreads();   // sv/si are reused by the next call
+  return r;
+}
+template <typename T>
+__device__ long long row_argmax(const T* __restrict__ row, int64_t vocab) {
+  const ArgBest b = row_argbest<T>(row, vocab);
+  return b.i == LLONG_MAX ? 0 : b.i;
 }
 
 template <typename T>
@@ -86,6 +97,63 @@ __global__ void __launch_bounds__(SEL_THREADS) argmax_kernel(const T* __restrict
                                                              int64_t out_stride) {
   const long long i = row_argmax<T>(logits + (int64_t)blockIdx.x * ld, vocab);
   if (threadIdx.x == 0) out[(int64_t)blockIdx.x * out_stride] = i;
+}
+
+// Argmax with S CTAs per row (one thread-block cluster per row): CTA r scans the r-th of S
+// 16-byte-aligned chunks and rank 0 combines the S results through distributed shared memory.
+// Ties go to the smaller index, as in the one-CTA kernel.
+template <typename T, int S>
+__global__ void __cluster_dims__(S, 1, 1) __launch_bounds__(SEL_THREADS)
+argmax_split_kernel(const T* __restrict__ logits, int64_t ld, int64_t vocab, int64_t* out, int64_t out_stride) {
+  namespace cg = cooperative_groups;
+  __shared__ float cv;
+  __shared__ long long ci;
+  cg::cluster_group cl = cg::this_cluster();
+  const int rank = (int)cl.block_rank();
+  const int64_t row = blockIdx.x / S;
+  constexpr int EPV = 16 / (int)sizeof(T);
+  const int64_t chunk = ((vocab + S - 1) / S + EPV - 1) / EPV * EPV;
+  const int64_t lo = min(vocab, (int64_t)rank * chunk), hi = min(vocab, lo + chunk);
+  ArgBest b{-INFINITY, LLONG_MAX};
+  if (hi > lo) {
+    b = row_argbest<T>(logits + row * ld + lo, hi - lo);
+    if (b.i != LLONG_MAX) b.i += lo;
+  }
+  if (threadIdx.x == 0) {
+    cv = b.v;
+    ci = b.i;
+  }
+  cl.sync();
+  if (rank == 0 && threadIdx.x == 0) {
+    ArgBest best{cv, ci};
+    for (int r = 1; r < S; ++r) best = arg_better(best, ArgBest{*cl.map_shared_rank(&cv, r), *cl.map_shared_rank(&ci, r)});
+    out[row * out_stride] = best.i == LLONG_MAX ? 0 : best.i;
+  }
+  cl.sync();   // every CTA keeps its shared memory until rank 0 has read it
+}
+
+// rows × S CTAs: S (1, 2, 4 or 8) doubles while the grid is under two CTAs per SM and each
+// chunk keeps at least 4096 elements.
+template <typename T>
+static int launch_argmax(const T* logits, int64_t ld, int64_t rows, int64_t vocab, int64_t* out, int64_t out_stride,
+                         cudaStream_t st) {
+  static int sms = 0;
+  if (sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms <= 0) sms = 148;
+  }
+  int S = 1;
+  while (S < 8 && rows * S < 2 * sms && vocab / (2 * S) >= 4096) S *= 2;
+  const unsigned g = (unsigned)(rows * S);
+  switch (S) {
+    case 1: argmax_kernel<T><<<g, SEL_THREADS, 0, st>>>(logits, ld, vocab, out, out_stride); break;
+    case 2: argmax_split_kernel<T, 2><<<g, SEL_THREADS, 0, st>>>(logits, ld, vocab, out, out_stride); break;
+    case 4: argmax_split_kernel<T, 4><<<g, SEL_THREADS, 0, st>>>(logits, ld, vocab, out, out_stride); break;
+    default: argmax_split_kernel<T, 8><<<g, SEL_THREADS, 0, st>>>(logits, ld, vocab, out, out_stride); break;
+  }
+  return check_launch("qsp_argmax_rows");
 }
 
 __global__ void greedy_accept_kernel(int B, int T, const int64_t* __restrict__ amax,
@@ -484,11 +552,7 @@ int qsp_argmax_rows(const void* logits, int64_t ld, int64_t rows, int64_t vocab,
   QSP_REQUIRE(logits && out && out_stride >= 1, "qsp_argmax_rows: null pointer / bad stride");
   QSP_REQUIRE(rows >= 0 && rows < (1ll << 31) && vocab > 0 && ld >= vocab, "qsp_argmax_rows: bad shape");
   if (rows == 0) return QSP_OK;
-  QSP_DISPATCH_DTYPE(dtype, T, {
-    argmax_kernel<T><<<(unsigned)rows, SEL_THREADS, 0, as_stream(stream)>>>((const T*)logits, ld, vocab, out,
-                                                                            out_stride);
-  });
-  return check_launch("qsp_argmax_rows");
+  QSP_DISPATCH_DTYPE(dtype, T, { return launch_argmax<T>((const T*)logits, ld, rows, vocab, out, out_stride, as_stream(stream)); });
 }
 
 int qsp_greedy_verify(const void* logits, int64_t ld, int32_t batch, int32_t tokens, int64_t vocab,
@@ -505,10 +569,8 @@ int qsp_greedy_verify(const void* logits, int64_t ld, int32_t batch, int32_t tok
   }
   const int64_t rows = (int64_t)batch * tokens;
   cudaStream_t st = as_stream(stream);
-  QSP_DISPATCH_DTYPE(dtype, T, {
-    argmax_kernel<T><<<(unsigned)rows, SEL_THREADS, 0, st>>>((const T*)logits, ld, vocab, amax, 1);
-  });
-  int rc = check_launch("qsp_greedy_verify(argmax)");
+  int rc = QSP_OK;
+  QSP_DISPATCH_DTYPE(dtype, T, { rc = launch_argmax<T>((const T*)logits, ld, rows, vocab, amax, 1, st); });
   if (rc) return rc;
   greedy_accept_kernel<<<(batch + 127) / 128, 128, 0, st>>>(batch, tokens, amax, drafts, drafts_ld,
                                                             accept_n, next_tok);

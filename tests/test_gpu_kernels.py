@@ -55,7 +55,9 @@ def test_rmsnorm_and_add(dt):
 @pytest.mark.parametrize("dt", DTS)
 @pytest.mark.parametrize("mnk", [(1, 64, 64), (7, 129, 100), (64, 384, 512), (256, 1000, 2048), (130, 256, 136),
                                  (256, 2048, 4096), (256, 12352, 2048), (64, 4608, 2048), (300, 256, 512),
-                                 (1024, 384, 256), (16, 256, 64), (33, 200, 6144)])
+                                 (1024, 384, 256), (16, 256, 64), (33, 200, 6144),
+                                 # 149 weight tiles on 148 SMs: the last tile is split along K
+                                 (64, 19000, 1024), (100, 19072, 520)])
 def test_gemm(dt, mnk):
     m, n, k = mnk
     g = gen(1)
@@ -384,6 +386,23 @@ def test_argmax_first_index_and_greedy_verify(dt):
     for b in range(B):
         a, t = S.greedy_accept(want[b * T:(b + 1) * T], drafts[b])
         assert int(acc[b]) == a and int(nxt[b]) == t
+
+
+@pytest.mark.parametrize("rows", [1, 3, 64, 256])
+def test_argmax_vocab_rows_split_over_clusters(rows):
+    """Few rows of a 151936-entry vocabulary are split over 2-8 CTAs per row; the result is
+    torch's first-maximum index, including ties planted across chunk boundaries."""
+    g = gen(16 + rows)
+    V = 151936
+    logits = rn(g, rows, V, dtype=torch.bfloat16)
+    for r in range(rows):
+        a, b = sorted(torch.randint(0, V, (2,), generator=g).tolist())
+        logits[r, a] = logits[r, b] = 30.0 + r % 3           # tie → the smaller index
+    logits[0, V - 1] = 40.0                                   # maximum in the ragged last chunk
+    ld = logits.to(DEV)
+    out = torch.empty(rows, dtype=torch.int64, device=DEV)
+    K().argmax_rows(ld, out)
+    assert torch.equal(out.cpu(), logits.float().argmax(-1))
 
 
 def test_spec_sample_matches_oracle_off_near_ties():
