@@ -195,6 +195,24 @@ __device__ __forceinline__ float4 merge4(const float* __restrict__ p, int splits
   return acc;
 }
 
+// The same sum (same order) with up to eight splits' loads in flight at once.
+__device__ __forceinline__ float4 merge8(const float* __restrict__ p, int splits, int64_t stride) {
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int s = 0; s < splits; s += 8) {
+    float4 v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      v[u] = (s + u < splits) ? __ldcg(reinterpret_cast<const float4*>(p + (s + u) * stride)) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      if (s + u < splits) {
+        acc.x += v[u].x; acc.y += v[u].y; acc.z += v[u].z; acc.w += v[u].w;
+      }
+    }
+  }
+  return acc;
+}
+
 // c = round(Σ partial) (+ c)
 __global__ void __launch_bounds__(256) splitk_store_kernel(const float* __restrict__ partial, int splits,
                                                            int64_t split_stride, int ldp,
@@ -219,8 +237,11 @@ __global__ void __launch_bounds__(256) splitk_store_kernel(const float* __restri
 
 // Residual add + the following RMSNorm, one CTA per row:
 // x := round(x + round(Σ partial)); y = round(x̂·(1 + w)) with x̂ = x·rsqrt(mean(x²) + eps).
-constexpr int RN_MAXV = 8;   // up to 8192 columns (256 threads x 4 x 8)
-__global__ void __launch_bounds__(256) splitk_residual_rmsnorm_kernel(
+// One CTA of 512 threads per row: a 2048-column row is one float4 per thread, so every split
+// of it is in flight at once (the row's latency is one L2 round trip, not one per four splits).
+constexpr int RN_THREADS = 512;
+constexpr int RN_MAXV = 4;   // up to 8192 columns (512 threads x 4 x 4)
+__global__ void __launch_bounds__(RN_THREADS) splitk_residual_rmsnorm_kernel(
     const float* __restrict__ partial, int splits, int64_t split_stride, int ldp, __nv_bfloat16* __restrict__ x,
     int64_t ldx, const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ y, int64_t ldy, int n, float eps) {
   pdl_trigger();
@@ -231,9 +252,9 @@ __global__ void __launch_bounds__(256) splitk_residual_rmsnorm_kernel(
   float ss = 0.f;
 #pragma unroll
   for (int v = 0; v < RN_MAXV; ++v) {
-    const int col = (threadIdx.x + v * 256) * 4;
+    const int col = (threadIdx.x + v * RN_THREADS) * 4;
     if (col < n) {
-      const float4 acc = merge4(partial + (int64_t)row * ldp + col, splits, split_stride);
+      const float4 acc = merge8(partial + (int64_t)row * ldp + col, splits, split_stride);
       const float a4[4] = {acc.x, acc.y, acc.z, acc.w};
       __nv_bfloat16* xo = x + (int64_t)row * ldx + col;
 #pragma unroll
@@ -249,7 +270,7 @@ __global__ void __launch_bounds__(256) splitk_residual_rmsnorm_kernel(
   const float inv = rsqrtf(tot / (float)n + eps);
 #pragma unroll
   for (int v = 0; v < RN_MAXV; ++v) {
-    const int col = (threadIdx.x + v * 256) * 4;
+    const int col = (threadIdx.x + v * RN_THREADS) * 4;
     if (col < n) {
       __nv_bfloat16* yo = y + (int64_t)row * ldy + col;
 #pragma unroll
@@ -609,7 +630,7 @@ static int launch_tc(const CUtensorMap& mw, const CUtensorMap& mx, const TcArgs&
   const int64_t split_stride = (int64_t)p.m_tiles * MT * ldp;
   if (epi.kind == GEMM_EPI_RESNORM)
     return launch_pdl("qsp_gemm(split-k merge + residual + rmsnorm)", splitk_residual_rmsnorm_kernel, dim3(a.m),
-                      dim3(256), 0, st, (const float*)a.partial, p.splits, split_stride, ldp, a.c, a.ldc,
+                      dim3(RN_THREADS), 0, st, (const float*)a.partial, p.splits, split_stride, ldp, a.c, a.ldc,
                       epi.norm_w, epi.y, epi.ldy, a.n, epi.eps);
   if (epi.kind == GEMM_EPI_SWIGLU) {
     const int inter = a.n / 2;
@@ -650,7 +671,7 @@ int gemm_tc(const void* a, int64_t lda, const void* w, int64_t ldw, void* c, int
   if (p.splits > 1 && !aligned(workspace, 256)) return QSP_ERR_UNSUPPORTED;
   if (p.tail_split > 0 && (workspace == nullptr || ws_bytes < ws_need(p) || !aligned(workspace, 256)))
     p.tail_split = 0;   // no room for the tail partials: whole tiles to the end
-  if (p.splits > 1 && epi.kind == GEMM_EPI_RESNORM && n > RN_MAXV * 1024) return QSP_ERR_UNSUPPORTED;
+  if (p.splits > 1 && epi.kind == GEMM_EPI_RESNORM && n > RN_MAXV * RN_THREADS * 4) return QSP_ERR_UNSUPPORTED;
   if (p.splits > 1 && epi.kind != GEMM_EPI_STORE && (n % 8) != 0) return QSP_ERR_UNSUPPORTED;
   CUtensorMap mw, mx;
   if (!make_map(&mw, w, n, k, ldw, p.bn) || !make_map(&mx, a, m, k, lda, p.mt)) return QSP_ERR_UNSUPPORTED;
