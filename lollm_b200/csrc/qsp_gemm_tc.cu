@@ -549,18 +549,24 @@ static TcPlan plan(int64_t m, int64_t n, int64_t k, int sm_count) {
   const int tiles = p.m_tiles * p.n_tiles;
   // µs per k-block per SM: ingest-bound (weight tile + activation tile at ~40 GB/s per SM)
   const double t_kb = (double)(p.bn + p.mt) * TC_BK * 2 / 40.0e3;
+  double est[17] = {};
   double best = 1e30;
-  int best_s = 1;
   for (int s = 1; s <= 16; ++s) {
     const int kps = (p.n_kb + s - 1) / s;
     const int ss = (p.n_kb + kps - 1) / kps;
+    est[s] = 1e30;
     if (ss != s && s > 1) continue;
     const int units = tiles * ss;
     const int per_cta = (units + sm_count - 1) / sm_count;
     double t = per_cta * kps * t_kb + 1.0;
     if (ss > 1) t += 2.0 + (double)ss * p.m_tiles * p.mt * p.n_tiles * p.bn * 4.0 * 2.0 / 6.0e6;   // bytes / (6 TB/s)
-    if (t < best - 1e-9) { best = t; best_s = ss; }
+    est[s] = t;
+    best = std::min(best, t);
   }
+  // the fewest splits within 3 % of the best estimate: fewer fp32 partials to write and merge
+  // (measured: the 2048 × 6144 projection at 256 rows is 0.9 µs faster with 8 splits than 9)
+  int best_s = 1;
+  while (est[best_s] > 1.03 * best) ++best_s;
   p.kb_per_split = (p.n_kb + best_s - 1) / best_s;
   p.splits = (p.n_kb + p.kb_per_split - 1) / p.kb_per_split;
   p.partial_bytes = p.splits > 1 ? (size_t)p.splits * p.m_tiles * p.mt * p.n_tiles * p.bn * sizeof(float) : 0;
