@@ -155,8 +155,8 @@ gemm_cl_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
       for (int i = 0; i < npre; ++i) {
         uint8_t* st = smem + i * C::STAGE;
         mbar_expect_tx(&full[i], C::STAGE);
-        tma_load_2d(st, &tm_w, &full[i], (kb0 + i) * 64, row0);
-        if (NACC == 2) tma_load_2d(st + 128 * 128, &tm_w, &full[i], (kb0 + i) * 64, row0 + A.box1);
+        tma_load_2d_evict_first(st, &tm_w, &full[i], (kb0 + i) * 64, row0);
+        if (NACC == 2) tma_load_2d_evict_first(st + 128 * 128, &tm_w, &full[i], (kb0 + i) * 64, row0 + A.box1);
       }
       pdl_wait();
       for (int i = 0; i < npre; ++i) tma_load_2d(smem + i * C::STAGE + C::W_BYTES, &tm_x, &full[i], (kb0 + i) * 64, 0);
@@ -166,8 +166,8 @@ gemm_cl_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
         if (!mbar_wait(&empty[s], ph ^ 1u, 301, &g_gemm_cl_error, abort)) break;
         uint8_t* st = smem + s * C::STAGE;
         mbar_expect_tx(&full[s], C::STAGE);
-        tma_load_2d(st, &tm_w, &full[s], (kb0 + i) * 64, row0);
-        if (NACC == 2) tma_load_2d(st + 128 * 128, &tm_w, &full[s], (kb0 + i) * 64, row0 + A.box1);
+        tma_load_2d_evict_first(st, &tm_w, &full[s], (kb0 + i) * 64, row0);
+        if (NACC == 2) tma_load_2d_evict_first(st + 128 * 128, &tm_w, &full[s], (kb0 + i) * 64, row0 + A.box1);
         tma_load_2d(st + C::W_BYTES, &tm_x, &full[s], (kb0 + i) * 64, 0);
       }
     } else {

@@ -66,6 +66,18 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y)
       : "memory");
 }
+// Weight tiles are read once per launch: load them with an L2 evict-first policy so that they
+// do not displace the activations, split-K partials and state that the step re-reads.
+__device__ __forceinline__ void tma_load_2d_evict_first(void* dst, const CUtensorMap* map, uint64_t* bar, int x,
+                                                        int y) {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%3, %4}], "
+      "[%2], %5;" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y), "l"(pol)
+      : "memory");
+}
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
@@ -356,7 +368,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
         for (int i = 0; i < nk && npre < (uint32_t)C::STAGES; ++i, ++npre) {
           const int kb = kb0 + (i + rot) % nk;
           mbar_expect_tx(&full[npre], C::STAGE_BYTES);
-          tma_load_2d(smem + npre * C::STAGE_BYTES, &tm_w, &full[npre], kb * TC_BK, nb * TC_BN);
+          tma_load_2d_evict_first(smem + npre * C::STAGE_BYTES, &tm_w, &full[npre], kb * TC_BK, nb * TC_BN);
           pre_kb[npre] = kb;
           pre_mb[npre] = mb;
         }
@@ -380,7 +392,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
           if (it >= (uint32_t)C::STAGES && !mbar_wait(&empty[s], ph ^ 1u, 101)) { ok = false; break; }
           uint8_t* st = smem + s * C::STAGE_BYTES;
           mbar_expect_tx(&full[s], C::STAGE_BYTES);
-          tma_load_2d(st, &tm_w, &full[s], kb * TC_BK, nb * TC_BN);
+          tma_load_2d_evict_first(st, &tm_w, &full[s], kb * TC_BK, nb * TC_BN);
           tma_load_2d(st + C::W_BYTES, &tm_x, &full[s], kb * TC_BK, mb * MT);
         }
       }

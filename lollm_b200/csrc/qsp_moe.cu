@@ -386,8 +386,8 @@ moe_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
             }
             uint8_t* st = smem + s * C::STAGE;
             mbar_expect_tx(&full[s], bytes);
-            tma_load_2d(st, &tm_w, &full[s], kb * 64, row0);
-            if (NA == 2) tma_load_2d(st + C::A_BYTES, &tm_w, &full[s], kb * 64, row0 + (SWI ? A.out_w : 128));
+            tma_load_2d_evict_first(st, &tm_w, &full[s], kb * 64, row0);
+            if (NA == 2) tma_load_2d_evict_first(st + C::A_BYTES, &tm_w, &full[s], kb * 64, row0 + (SWI ? A.out_w : 128));
             for (int q = 0; q < nb16; ++q)
               tma_load_2d(st + NA * C::A_BYTES + q * 2048, &tm_x, &full[s], kb * 64, off + t0 + q * 16);
           }
