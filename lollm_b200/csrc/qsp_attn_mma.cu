@@ -357,11 +357,15 @@ struct At2Smem {
   static constexpr size_t BYTES = 1024 + RING + QBYTES + 128;
 };
 
+// Key/value tiles are read once per call: an L2 evict-first policy keeps them from displacing
+// the split partials that the merge kernel reads next.
 __device__ __forceinline__ void at2_tma(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
   asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(
           su32(dst)),
-      "l"(map), "r"(su32(bar)), "r"(x), "r"(y)
+      "l"(map), "r"(su32(bar)), "r"(x), "r"(y), "l"(pol)
       : "memory");
 }
 

@@ -204,12 +204,15 @@ __device__ __forceinline__ bool gdn_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Prefetch one head's fp32 state (contiguous DK*DV floats) into shared memory with a single
-// bulk copy that completes on `bar`.
+// bulk copy that completes on `bar`. The state is read once per call (the layers' states do not
+// fit L2): it is loaded with an L2 evict-first policy.
 __device__ __forceinline__ void gdn_prefetch_state(float* dst, const float* src, uint64_t* bar, uint32_t bytes) {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(gsm(bar)), "r"(bytes) : "memory");
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(gsm(dst)),
-               "l"(src), "r"(bytes), "r"(gsm(bar))
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(gsm(dst)),
+               "l"(src), "r"(bytes), "r"(gsm(bar)), "l"(pol)
                : "memory");
 }
 

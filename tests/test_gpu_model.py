@@ -193,3 +193,10 @@ def test_micro_filtered_stochastic_spec_runs_in_a_graph():
         prev = dec.n_out.clone()
     for toks in dec.outputs():
         assert all(0 <= t < cfg.vocab_size for t in toks)
+
+
+def test_graft_entry_smoke():
+    """The packaged smoke check (one forward against the oracle, then speculative steps whose
+    committed stream must equal the oracle's greedy stream) runs as a test too."""
+    import __graft_entry__
+    __graft_entry__.smoke()
