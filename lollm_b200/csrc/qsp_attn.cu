@@ -3,6 +3,7 @@
 // output gate.
 #include "qsp_common.cuh"
 
+#include <algorithm>
 #include <atomic>
 
 namespace qsp {
@@ -12,7 +13,8 @@ int launch_attn_tma(const qsp_attn_layer& L, cudaStream_t st);
 int launch_attn_ws(const qsp_attn_layer& L, cudaStream_t st);
 
 // ------------------------------------------------------------------ prep
-// One CTA per token row m = b*T + t; warps loop over the q and k heads.
+// One CTA per token row m = b*T + t; warps loop over the q and k heads (one head per warp
+// when the heads fit in 32 warps).
 template <typename T>
 __global__ void attn_prep_kernel(const qsp_attn_layer L) {
   pdl_trigger();
@@ -348,9 +350,12 @@ int qsp_attn_prep(const qsp_attn_layer* layer, void* stream) {
   int rc = validate_attn(layer, false);
   if (rc) return rc;
   const qsp_attn_layer& L = *layer;
-  const size_t smem = 4 * L.head_dim * sizeof(float);
+  // a warp per q/k head (up to 32): each head's load → norm → RoPE → store chain runs once
+  // per row instead of once per head a warp would otherwise loop over
+  const int warps = std::min(L.n_heads + L.n_kv_heads, 32);
+  const size_t smem = (size_t)warps * L.head_dim * sizeof(float);
   QSP_DISPATCH_DTYPE(L.dtype, T, {
-    return launch_pdl("qsp_attn_prep", attn_prep_kernel<T>, dim3(L.batch * L.tokens), dim3(128), smem,
+    return launch_pdl("qsp_attn_prep", attn_prep_kernel<T>, dim3(L.batch * L.tokens), dim3(32 * warps), smem,
                       as_stream(stream), L);
   });
   return QSP_OK;
