@@ -192,8 +192,8 @@ __global__ void __launch_bounds__(128) attn_simt_kernel(const qsp_attn_layer L, 
 // ------------------------------------------------------------------ merge splits + gate
 // One warp per (token row m, q head): the np partials (o unnormalised, m natural-log max,
 // l) of the row are merged with weights e^{m_p − M}, then σ(gate) is applied.
-template <typename T>
-__global__ void __launch_bounds__(256) attn_combine_kernel(const qsp_attn_layer L, int np) {
+template <typename T, int HD>
+__global__ void __launch_bounds__(256, 2) attn_combine_kernel(const qsp_attn_layer L, int np) {
   pdl_trigger();
   pdl_wait();
   const int lane = threadIdx.x & 31;
@@ -201,7 +201,7 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const qsp_attn_layer 
   if (pair >= L.batch * L.tokens * L.n_heads) return;
   const int m = pair / L.n_heads, hq = pair % L.n_heads;
   const int b = m / L.tokens, t = m % L.tokens;
-  const int hd = L.head_dim;
+  constexpr int hd = HD;
   const float* base = L.partial + ((((int64_t)b * L.n_heads + hq) * L.tokens + t) * np) * (hd + 2);
   float M = -INFINITY;
   for (int p = lane; p < np; p += 32) M = fmaxf(M, base[(int64_t)p * (hd + 2) + hd]);
@@ -215,9 +215,10 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const qsp_attn_layer 
   const T* row = static_cast<const T*>(L.qkv) + (int64_t)m * L.ld_qkv;
   T* o = static_cast<T*>(L.out) + (int64_t)m * L.ld_out + (int64_t)hq * hd;
   // lane (2·lane + 64·i, +1) of every partial: the weights e^{m_p − M} are computed once per
-  // partial (lane p of each 32-partial group) and broadcast; all of a partial's columns are
-  // loaded together, so the merge waits on memory once per partial, not once per column pair
-  constexpr int MAXI = 8;   // head_dim ≤ 512
+  // partial (lane p of each 32-partial group) and broadcast; four partials' columns are
+  // loaded together, so the merge waits on memory once per four partials (the sum keeps the
+  // partial order)
+  constexpr int MAXI = (HD + 63) / 64;
   float2 n[MAXI];
 #pragma unroll
   for (int i = 0; i < MAXI; ++i) n[i] = make_float2(0.f, 0.f);
@@ -227,20 +228,31 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const qsp_attn_layer 
       const float mpl = pl < np ? base[(int64_t)pl * (hd + 2) + hd] : -INFINITY;
       const float wl = mpl != -INFINITY ? expf(mpl - M) : 0.f;
       const int cnt = min(32, np - p0);
-      for (int j = 0; j < cnt; ++j) {
-        const float mp = __shfl_sync(0xffffffffu, mpl, j);
-        const float w = __shfl_sync(0xffffffffu, wl, j);
-        if (mp == -INFINITY) continue;
-        const float* q = base + (int64_t)(p0 + j) * (hd + 2);
-        float2 v[MAXI];
+      for (int j0 = 0; j0 < cnt; j0 += 4) {
+        float2 v[4][MAXI];
+        float w[4];
+        bool use[4];
 #pragma unroll
-        for (int i = 0; i < MAXI; ++i)
-          if (2 * lane + 64 * i < hd) v[i] = *reinterpret_cast<const float2*>(q + 2 * lane + 64 * i);
+        for (int u = 0; u < 4; ++u) {
+          const int j = j0 + u;   // < 32; lanes j ≥ cnt hold an empty partial (m = −∞)
+          const float mp = __shfl_sync(0xffffffffu, mpl, j);
+          w[u] = __shfl_sync(0xffffffffu, wl, j);
+          use[u] = j < cnt && mp != -INFINITY;
+          const float* q = base + (int64_t)(p0 + j) * (hd + 2);
 #pragma unroll
-        for (int i = 0; i < MAXI; ++i) {
-          if (2 * lane + 64 * i < hd) {
-            n[i].x = fmaf(w, v[i].x, n[i].x);
-            n[i].y = fmaf(w, v[i].y, n[i].y);
+          for (int i = 0; i < MAXI; ++i)
+            v[u][i] = (use[u] && 2 * lane + 64 * i < hd) ? *reinterpret_cast<const float2*>(q + 2 * lane + 64 * i)
+                                                        : make_float2(0.f, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          if (!use[u]) continue;
+#pragma unroll
+          for (int i = 0; i < MAXI; ++i) {
+            if (2 * lane + 64 * i < hd) {
+              n[i].x = fmaf(w[u], v[u][i].x, n[i].x);
+              n[i].y = fmaf(w[u], v[u][i].y, n[i].y);
+            }
           }
         }
       }
@@ -270,8 +282,13 @@ static int attn_chunk(const qsp_attn_layer& L) {
 template <typename T>
 static int launch_combine(const qsp_attn_layer& L, int np, cudaStream_t st) {
   const int pairs = L.batch * L.tokens * L.n_heads;
-  return launch_pdl("qsp_attn_verify(combine)", attn_combine_kernel<T>, dim3((pairs + 7) / 8), dim3(256), 0, st, L,
-                    np);
+  const dim3 grid((pairs + 7) / 8);
+  switch (L.head_dim) {   // validated: 32, 64, 128 or 256
+    case 32: return launch_pdl("qsp_attn_verify(combine)", attn_combine_kernel<T, 32>, grid, dim3(256), 0, st, L, np);
+    case 64: return launch_pdl("qsp_attn_verify(combine)", attn_combine_kernel<T, 64>, grid, dim3(256), 0, st, L, np);
+    case 128: return launch_pdl("qsp_attn_verify(combine)", attn_combine_kernel<T, 128>, grid, dim3(256), 0, st, L, np);
+    default: return launch_pdl("qsp_attn_verify(combine)", attn_combine_kernel<T, 256>, grid, dim3(256), 0, st, L, np);
+  }
 }
 
 template <typename T, int HD, int RPW>
