@@ -53,6 +53,7 @@ __global__ void rmsnorm_kernel(T* __restrict__ x, int64_t ld_x, const T* __restr
   const int64_t r = blockIdx.x;
   T* xr = x + r * ld_x;
   float ss = 0.0f;
+#pragma unroll 8   // the row's loads in flight together (a 2048-wide row is 8 per thread)
   for (int64_t j = threadIdx.x; j < dim; j += blockDim.x) {
     float v = dt<T>::to_f(xr[j]);
     if (ADD) {
@@ -65,6 +66,7 @@ __global__ void rmsnorm_kernel(T* __restrict__ x, int64_t ld_x, const T* __restr
   const float tot = block_sum(ss, red);
   const float inv = rsqrtf(tot / (float)dim + eps);
   T* yr = y + r * ld_y;
+#pragma unroll 8
   for (int64_t j = threadIdx.x; j < dim; j += blockDim.x) {
     const float v = srow[j] * inv;
     yr[j] = dt<T>::from_f(v * (dt<T>::to_f(w[j]) + 1.0f));
