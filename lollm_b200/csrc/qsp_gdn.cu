@@ -904,12 +904,20 @@ gdn_chunk_kernel(const qsp_gdn_layer L, const GdnRing RG, const int n_new) {
     }
     __syncthreads();
 
+    // the new state is not read again in this step: stored with an L2 evict-first policy so
+    // its 64 KB per head do not displace the step's re-read data
     auto store_state = [&]() {
+      uint64_t pol;
+      asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
 #pragma unroll
       for (int p = 0; p < RB / 2; ++p) {
         const float2 a = upk2(S[0][p]), bq = upk2(S[1][p]), c2 = upk2(S[2][p]), d2 = upk2(S[3][p]);
-        *reinterpret_cast<float4*>(state + (int64_t)(RB * rg + 2 * p) * DV + 4 * cg) = make_float4(a.x, bq.x, c2.x, d2.x);
-        *reinterpret_cast<float4*>(state + (int64_t)(RB * rg + 2 * p + 1) * DV + 4 * cg) = make_float4(a.y, bq.y, c2.y, d2.y);
+        float* d0 = state + (int64_t)(RB * rg + 2 * p) * DV + 4 * cg;
+        float* d1 = d0 + DV;
+        asm volatile("st.global.L2::cache_hint.v4.f32 [%0], {%1, %2, %3, %4}, %5;" ::"l"(d0), "f"(a.x), "f"(bq.x),
+                     "f"(c2.x), "f"(d2.x), "l"(pol) : "memory");
+        asm volatile("st.global.L2::cache_hint.v4.f32 [%0], {%1, %2, %3, %4}, %5;" ::"l"(d1), "f"(a.y), "f"(bq.y),
+                     "f"(c2.y), "f"(d2.y), "l"(pol) : "memory");
       }
     };
     // 4. phase 0 replays the kept tokens of the previous speculative call; phase 1 applies this
