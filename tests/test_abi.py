@@ -74,3 +74,19 @@ def test_static_attention_scratch_limits_without_gpu():
     assert b"static region" in lib.qsp_last_error()
     d.num_splits = 0
     assert lib.qsp_attn_verify_static(ctypes.byref(d), None) == L.QSP_ERR_INVALID
+
+
+def test_gemm_plans_at_the_step_shapes():
+    """The split-K plans behind the verify step's projections, read through the workspace
+    query (host-side planning only, no launch; the SM count is the B200's 148): the
+    vocabulary projection's last partial round of tiles is split along K into 16 slices of
+    fp32 partials (3 tiles of 128 rows x 256 tokens), the 2048 x 6144 down projection takes the
+    fewest splits within 3 % of the best estimate (8, not 9), gate|up 3 splits."""
+    lib = L.load()
+    f4 = 4
+    assert lib.qsp_gemm_workspace_bytes(256, 151936, 2048, L.QSP_BF16) == 16 * 256 * 3 * 128 * f4
+    assert lib.qsp_gemm_workspace_bytes(64, 151936, 2048, L.QSP_BF16) == 16 * 64 * 3 * 128 * f4
+    assert lib.qsp_gemm_workspace_bytes(256, 2048, 6144, L.QSP_BF16) == 8 * 256 * 2048 * f4
+    assert lib.qsp_gemm_workspace_bytes(256, 2048, 4096, L.QSP_BF16) == 8 * 256 * 2048 * f4
+    assert lib.qsp_gemm_workspace_bytes(256, 12288, 2048, L.QSP_BF16) == 3 * 256 * 12288 * f4
+    assert lib.qsp_gemm_workspace_bytes(256, 2048, 4096, L.QSP_F32) == 0   # fp32 runs unsplit
