@@ -3,7 +3,7 @@ batch 64 per GPU, 2048-token prompts, k=3 recurrent MTP drafts, greedy), and the
 step's fraction of the HBM roofline.
 
     python bench.py [--gpus N --steps K --warmup W]          # this implementation
-    python bench.py --impl reference [...]                   # the reference's algorithm on CPU
+    python bench.py --impl reference [...]                   # the installed reference, host CPU
 
 One step = draft k tokens with the MTP head → verify [pending, d1..dk] through the 24-layer
 hybrid stack → accept → keep a prefix by index → emit, for all sequences of this GPU. The
@@ -12,8 +12,10 @@ CUDA events on its stream. Inputs are far larger than L2 (4 GB of weights, 2.4 G
 state, 1.8 GB of KV per step), so no L2 flush is needed between steps.
 
 Multi-GPU (torchrun): one process per GPU, each its own replica and its own 64 sequences
-(weak scaling; sequences are independent, no collective on the data path). Rank 0 prints
-one JSON line; times are the max over ranks.
+(weak scaling, the headline; sequences are independent, no collective on the data path).
+At N > 1 the same run also times BASELINE's global batch of 64 split over the GPUs (64/N per
+GPU, strong scaling) and reports it under "strong". Rank 0 prints one JSON line; times are
+the max over ranks.
 """
 
 from __future__ import annotations
@@ -149,60 +151,139 @@ def verify_step_bytes(cfg, B, T, ctx_lens):
 
 # ─────────────────────────────────────────── CPU arm ───────────────────────────────────────────
 
-def cpu_reference_sample(cfg, batch, ctx, k, steps, warmup, seed=0, budget_s=None):
-    """The reference's own algorithm on the host cores (the oracle restatement of
-    generate_mtp generalised to k drafts: draft → clone → verify → exact-match accept →
-    restore + recompute on rejection), bf16, on a synthetic prefilled state of `ctx`
-    tokens per sequence. Returns (tok/s, tokens, seconds, steps_run, threads)."""
-    from oracle import loops as OL
-    from oracle import qwen35 as Q
-    from lollm_b200.qwen3_5.weights import load_checkpoint, random_init
+REF_DIR = os.path.join(ROOT, "baseline", "_ref")
+
+
+def stock_reference(cfg, raw_cfg, seed=0):
+    """The installed reference (baseline/_ref): its own `qwen3_5.weights.load` and
+    `qwen3_5.mtp.load_mtp` build the stock `Qwen3_5Model` and `MTP` modules from seeded
+    random-init N(0, 0.02) weights (HF names), bf16 on the CPU. Returns (modules dict)."""
+    if not os.path.isdir(os.path.join(REF_DIR, "qwen3_5")):
+        raise FileNotFoundError(f"the reference is not installed under {REF_DIR}")
+    if REF_DIR not in sys.path:
+        sys.path.insert(0, REF_DIR)
+    from qwen3_5 import mtp as RM
+    from qwen3_5 import weights as RW
+    from qwen3_5.kv import Qwen3_5Cache as RefCache
+    from lollm_b200.qwen3_5.weights import random_init
+    w = random_init(cfg, seed, dtype=torch.bfloat16, generator="torch")
+    model = RW.load(raw_cfg, dict(w), "hf", device="cpu", dtype=torch.bfloat16)
+    mtp = RM.load_mtp(model, dict(w), "hf", device="cpu", dtype=torch.bfloat16)
+    del w
+    return {"model": model, "mtp": mtp, "Cache": RefCache}
+
+
+def stock_prefilled_cache(ref, cfg, batch, ctx, seed=1):
+    """A stock `Qwen3_5Cache` holding `ctx` positions for every sequence: seeded random
+    post-RoPE K/V (B, n_kv, ctx, hd) in bf16 for the attention layers, and (conv (B, C, K-1)
+    bf16, recurrent (B, Hv, dk, dv) fp32 N(0, 0.1)) for the GDN layers. A 2048-token CPU
+    prefill of 64 sequences would take hours; the step's cost does not depend on the values."""
+    g = torch.Generator().manual_seed(seed)
+    dt = torch.bfloat16
+    cache = ref["Cache"](cfg.num_hidden_layers)
+    for i in range(cfg.num_hidden_layers):
+        if cfg.layer_type(i) == "full_attention":
+            shp = (batch, cfg.num_key_value_heads, ctx, cfg.head_dim)
+            cache.layers[i] = (torch.randn(*shp, generator=g).to(dt), torch.randn(*shp, generator=g).to(dt))
+        else:
+            cache.layers[i] = (torch.randn(batch, cfg.conv_dim, cfg.linear_conv_kernel_dim - 1, generator=g).to(dt),
+                               torch.randn(batch, cfg.linear_num_value_heads, cfg.linear_key_head_dim,
+                                           cfg.linear_value_head_dim, generator=g) * 0.1)
+    cache.seen_tokens = ctx
+    return cache
+
+
+def stock_spec_step(ref, past, hidden_last, pending, k):
+    """One greedy speculative step of the reference's `generate_mtp` (src/qwen3_5/mtp.py:
+    127-162) on a batch, through the stock modules: k MTP drafts (mtp(hidden, emb) →
+    lm_head → argmax; depth d > 1 feeds the previous depth's pre-norm MTP output, read off
+    the head's final norm, and its token), `past.clone()` snapshot, one (B, k+1) verify
+    forward, exact-match accept, and on a rejection the snapshot restored and the kept
+    tokens re-run. The stock cache holds one length for the whole batch, so the batch keeps
+    the common accepted prefix (every sequence commits a+1 tokens, a = the smallest
+    acceptance). Returns (past, hidden_last (B,1,H), pending (B,), tokens committed)."""
+    model, mtp = ref["model"], ref["mtp"]
+    pre = {}
+    hook = mtp.norm.register_forward_hook(lambda m, inp, out: pre.__setitem__("x", inp[0]))
+    try:
+        h, tok, drafts = hidden_last, pending, []
+        for _ in range(k):
+            emb = model.model.embed_tokens(tok[:, None])
+            tok = model.lm_head(mtp(h, emb))[:, -1].argmax(-1)
+            drafts.append(tok)
+            h = pre["x"]
+    finally:
+        hook.remove()
+    ids = torch.cat([pending[:, None], torch.stack(drafts, 1)], dim=1)
+    snap = past.clone()
+    logits, past, hidden = model(ids, past, return_hidden=True)
+    tgt = logits.argmax(-1)                                   # (B, k+1)
+    match = (ids[:, 1:] == tgt[:, :k]).int().cumprod(dim=1).sum(dim=1)
+    a = int(match.min())
+    if a == k:
+        return past, hidden[:, k:k + 1], tgt[:, k], ids.shape[0] * (k + 1)
+    _, past, h1 = model(ids[:, :a + 1], snap, return_hidden=True)
+    return past, h1[:, -1:], tgt[:, a], ids.shape[0] * (a + 1)
+
+
+def stock_reference_sample(cfg, batch, ctx, k, steps, warmup, budget_s):
+    """Time the reference's own CPU path: the installed stock modules at `batch` sequences of
+    context `ctx`, greedy, k drafts, with all host threads; at most `steps` timed steps,
+    stopping once `budget_s` seconds have passed. Returns a dict, or None with the reason
+    when the reference cannot be imported."""
+    from lollm_b200.qwen3_5.config import QWEN35_2B
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    torch.manual_seed(seed)
-    P = load_checkpoint(cfg, random_init(cfg, seed, dtype=torch.bfloat16, generator="torch"))
-    g = torch.Generator().manual_seed(seed + 1)
-    dt = torch.bfloat16
-    cache = Q.OracleCache(cfg.num_hidden_layers, lens=[ctx] * batch)
-    for i in cfg.attn_layers:
-        cache.kv[i] = [(torch.randn(cfg.num_key_value_heads, ctx, cfg.head_dim, generator=g).to(dt),
-                        torch.randn(cfg.num_key_value_heads, ctx, cfg.head_dim, generator=g).to(dt))
-                       for _ in range(batch)]
-    for i in cfg.gdn_layers:
-        cache.gdn[i] = ((torch.randn(batch, cfg.conv_dim, cfg.linear_conv_kernel_dim - 1, generator=g)).to(dt),
-                        torch.randn(batch, cfg.linear_num_value_heads, cfg.linear_key_head_dim,
-                                    cfg.linear_value_head_dim, generator=g) * 0.1)
-    hidden = torch.randn(batch, cfg.hidden_size, generator=g).to(dt)
+    torch.set_grad_enabled(False)
+    try:
+        ref = stock_reference(cfg, QWEN35_2B)
+    except Exception as e:  # noqa: BLE001
+        return None, f"reference import failed: {type(e).__name__}: {e}"
+    past = stock_prefilled_cache(ref, cfg, batch, ctx)
+    g = torch.Generator().manual_seed(2)
+    hidden = torch.randn(batch, 1, cfg.hidden_size, generator=g).to(torch.bfloat16)
     pending = torch.randint(0, cfg.vocab_size, (batch,), generator=g)
-    with torch.no_grad():
-        for _ in range(warmup):
-            cache, hidden, pending, committed, acc, _ = OL.spec_step(P, cfg, cache, hidden, pending, k, scan="reference")
-        toks, t0, n = 0, time.perf_counter(), 0
-        for _ in range(steps):
-            cache, hidden, pending, committed, acc, _ = OL.spec_step(P, cfg, cache, hidden, pending, k, scan="reference")
-            toks += sum(len(c) for c in committed)
-            n += 1
-            if budget_s is not None and time.perf_counter() - t0 > budget_s:
-                break
-        dt_s = time.perf_counter() - t0
-    return toks / dt_s, toks, dt_s, n, threads
+    for _ in range(warmup):
+        past, hidden, pending, _ = stock_spec_step(ref, past, hidden, pending, k)
+    toks, n, t0 = 0, 0, time.perf_counter()
+    while n < steps:
+        past, hidden, pending, c = stock_spec_step(ref, past, hidden, pending, k)
+        toks += c
+        n += 1
+        if time.perf_counter() - t0 > budget_s:
+            break
+    secs = time.perf_counter() - t0
+    sample = (f"{n} speculative steps (of {steps} asked, {budget_s:.0f} s budget; {warmup} warm-up) x {batch} "
+              f"sequences at context {ctx}, k={k}, greedy: the installed reference's stock Qwen3_5Model / MTP / "
+              f"Qwen3_5Cache (generate_mtp's draft, clone, verify, restore + recompute) in bf16 on {threads} host threads")
+    return {"value": toks / secs, "unit": UNIT, "cores": threads, "kind": "reference", "sample": sample,
+            "steps": n, "seconds": secs, "tokens": toks}, None
 
 
 def run_reference_arm(args, cfg, ws, rank):
+    """The reference's own CPU path, timed on the host cores: the installed stock modules
+    (baseline/_ref) at the GPU arm's per-GPU batch and context, greedy, k drafts. It has no
+    multi-GPU path: under torchrun only rank 0 runs (one CPU measurement per box) and the other
+    ranks exit without work, so at N > 1 the line still describes one process serving
+    `batch` sequences on the host cores."""
     if rank != 0:
         return
-    batch, ctx = args.cpu_batch, args.prompt
-    tps, toks, secs, n, threads = cpu_reference_sample(cfg, batch, ctx, args.k, args.steps, args.warmup)
+    warm = min(args.warmup, args.ref_warmup)
+    cb, why = stock_reference_sample(cfg, args.batch, args.prompt, args.k, args.steps, warm, args.ref_budget_s)
+    if cb is None:
+        print(json.dumps({"impl": "reference", "unavailable": why}), flush=True)
+        return
+    n, secs, tps = cb.pop("steps"), cb.pop("seconds"), cb["value"]
+    cb.pop("tokens")
     line = {"metric": METRIC, "value": tps, "unit": UNIT, "n_gpus": args.gpus, "steps": n,
-            "warmup": args.warmup, "ms_per_step": 1000 * secs / max(n, 1), "higher_is_better": True,
+            "warmup": warm, "ms_per_step": 1000 * secs / max(n, 1), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded random-init weights, random prefilled state)",
             "impl": "reference",
-            "config": config_block(args, cfg),
-            "cpu_baseline": {"value": tps, "unit": UNIT, "cores": threads, "kind": "port",
-                             "sample": f"{n} speculative steps x {batch} sequences at context {ctx}, "
-                                       f"k={args.k}, the oracle restatement of the reference's generate_mtp "
-                                       f"(clone + verify + restore/recompute) in bf16 on {threads} threads"},
+            "config": dict(config_block(args, cfg), global_batch=args.batch,
+                           parallelism=f"one CPU process on the box's host cores (rank 0 of {args.gpus}; "
+                                       "the reference has no multi-GPU path)"),
+            "cpu_baseline": cb,
             "e2e": {"value": tps, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -248,6 +329,13 @@ def run_gpu_arm(args, cfg, ws, rank, local):
     for _ in range(args.warmup):
         full.replay()
     torch.cuda.synchronize()
+
+    if ws > 1:
+        # every rank reached the timed region: a rank lost during set-up is named here, on the
+        # host, before any rank enters the timed region's collectives
+        from lollm_b200.ranks import PeerGuard
+        PeerGuard(torch.distributed.distributed_c10d._get_default_store(), rank, ws,
+                  timeout_s=300.0).checkpoint("timed")
 
     # ---------------- timed region: device-resident inputs
     n0 = int(dec.n_out.sum())
@@ -350,7 +438,67 @@ def run_gpu_arm(args, cfg, ws, rank, local):
         "acceptance_rate": acc_rate, "tokens_per_step_per_seq": tokens / (args.steps * B),
         "prefill_s": prefill_s, "setup_s": time.perf_counter() - t_setup,
     }
+    if ws > 1 and args.global_batch % ws == 0 and args.global_batch // ws != args.batch:
+        del graphs, full, dec
+        torch.cuda.empty_cache()
+        out["strong"] = strong_scaling(args, cfg, model, mtp, ws, rank, local)
     return out
+
+
+def strong_scaling(args, cfg, model, mtp, ws, rank, local):
+    """The same step at a FIXED global batch (`--global-batch`, BASELINE's 64) split over the
+    ranks: global_batch / N sequences per GPU (8 at N = 8, i.e. 32 verify rows). Timed like
+    the headline (barrier + synchronize around K graph replays, max over ranks); reports the
+    whole-job tok/s, the verify phase against its HBM roofline at that batch, and the live
+    per-class kernel times that name the limiting kernel."""
+    from lollm_b200.qwen3_5 import SpecDecoder
+    dev = torch.device("cuda", local)
+    B = args.global_batch // ws
+    n_steps_total = args.warmup + args.steps + 4
+    max_len = args.prompt + (n_steps_total + 2) * (args.k + 1) + 16
+    dec = SpecDecoder(model, mtp, B, args.k, max_len, out_capacity=n_steps_total * (args.k + 1) + 8)
+    g = torch.Generator(device=dev)
+    g.manual_seed(2000 + rank)
+    dec.prefill(torch.randint(0, cfg.vocab_size, (B, args.prompt), generator=g, device=dev), chunk=args.prefill_chunk)
+    dec.step()
+    graphs = capture_split(dec)
+    full = capture_full(dec, graphs)
+    stream = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        full.replay()
+    n0 = int(dec.n_out.sum())
+    ctx_lens = dec.cache.seq_lens.tolist()
+    barrier(ws)
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(args.steps):
+        full.replay()
+    end.record(stream)
+    torch.cuda.synchronize()
+    barrier(ws)
+    max_ms = reduce_max(start.elapsed_time(end), ws)
+    tokens = reduce_sum(int(dec.n_out.sum()) - n0, ws)
+    n_ph = max(3, min(args.steps, 10))
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(n_ph)]
+    for e in ev:
+        replay_split(graphs, e, stream)
+    torch.cuda.synchronize()
+    verify_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in ev)
+    draft_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in ev)
+    hbm, _, src = peaks()
+    vb = verify_step_bytes(cfg, B, args.k + 1, ctx_lens)
+    live = live_kernel_times(dec, graphs, n_ph)
+    del graphs, full
+    return {"global_batch": args.global_batch, "batch_per_gpu": B, "verify_rows_per_gpu": B * (args.k + 1),
+            "value": tokens / (max_ms / 1000.0), "unit": UNIT, "ms_per_step": max_ms / args.steps,
+            "phases_ms": {"draft": draft_ms, "verify": verify_ms},
+            "verify_roofline": {"bound": "hbm", "achieved": vb["total"] / (verify_ms / 1000) / 1e9, "peak": hbm,
+                                "unit": "GB/s", "frac": vb["total"] / (verify_ms / 1000) / 1e9 / hbm,
+                                "peak_source": src, "algorithmic_bytes": vb["total"]},
+            "live_kernels_ms_per_step": {LIVE_CLASSES[k]: {"launches": v[0], "ms_per_launch": v[1], "ms_per_step": v[2]}
+                                         for k, v in live.items()},
+            "scaling": "strong"}
 
 
 def capture_split(dec):
@@ -653,6 +801,107 @@ def run_attn_workload(args):
                          "traffic": None, "algorithmic_bytes_per_launch": algo}}
 
 
+def run_attn_compare_workload(args):
+    """The verify attention of configs[2] (64 sequences, T=4, 16 q / 2 kv heads, hd 256,
+    scale 1/16, causal over the 4 new rows) at EQUAL context lengths — the reference needs
+    one length per batch — timed three ways on the same GPU:
+      ours      qsp_attn_verify over the paged cache (GQA in the kernel);
+      sdpa      the reference's `attention.torch_attention` (src/attention.py:43-51) on
+                (B, 16, L+4, 256) K/V already expanded from 2 to 16 heads, as the reference's
+                GatedAttention does before the call (src/qwen3_5/blocks.py:229);
+      triton    the reference's `_triton_attn.flash_attention_kv` (src/_triton_attn.py) on
+                the same expanded tensors (autotuned once before timing).
+    The reference's GQA expansion (repeat_interleave of K and V, per call in the reference)
+    is timed separately as `expand_ms` and not included in its attention time. HBM
+    roofline for every impl: the unexpanded K/V bytes, Σ_b (L+T)·2·256·2·2."""
+    from lollm_b200 import _lib as L
+    from lollm_b200 import kernels as K
+    from lollm_b200.qwen3_5.modeling_qwen3_5 import rope_table
+    if REF_DIR not in sys.path:
+        sys.path.insert(0, REF_DIR)
+    dev = torch.device("cuda", 0)
+    B, T, nh, nkv, hd, rd, ps = args.batch, 4, 16, 2, 256, 64, 64
+    hbm, _, src = peaks()
+    rows = []
+    for Lc in (int(x) for x in args.attn_equal.split(",")):
+        g = torch.Generator(device=dev); g.manual_seed(Lc)
+        max_pages = (Lc + T + ps - 1) // ps
+        num_pages = B * max_pages
+        page_table = torch.arange(num_pages, dtype=torch.int32, device=dev).view(B, max_pages)
+        kp = torch.empty(num_pages, nkv, ps, hd, dtype=torch.bfloat16, device=dev).normal_(generator=g)
+        vp = torch.empty_like(kp).normal_(generator=g)
+        qkv = torch.randn(B * T, 2 * nh * hd + 2 * nkv * hd, generator=g, device=dev).to(torch.bfloat16)
+        qn = torch.zeros(hd, dtype=torch.bfloat16, device=dev); kn = torch.zeros_like(qn)
+        cos, sin = rope_table(rd, 1e7, Lc + 8, torch.bfloat16)
+        cos, sin = cos.to(dev), sin.to(dev)
+        lens = torch.full((B,), Lc, dtype=torch.int32, device=dev)
+        splits = max(1, (Lc + 511) // 512)
+        q_buf = torch.empty(B * T, nh * hd, dtype=torch.bfloat16, device=dev)
+        out = torch.empty(B * T, nh * hd, dtype=torch.bfloat16, device=dev)
+        part = torch.empty(K.attn_workspace_bytes(B, T, nh, hd, splits) // 4, device=dev)
+        d = L.AttnLayer()
+        d.batch, d.tokens, d.n_heads, d.n_kv_heads, d.head_dim, d.rotary_dim = B, T, nh, nkv, hd, rd
+        d.page_size, d.max_pages, d.num_pages, d.dtype, d.eps, d.scale = ps, max_pages, num_pages, L.QSP_BF16, 1e-6, 1 / 16
+        d.qkv, d.ld_qkv, d.q_norm_w, d.k_norm_w = qkv.data_ptr(), qkv.stride(0), qn.data_ptr(), kn.data_ptr()
+        d.rope_cos, d.rope_sin, d.rope_rows = cos.data_ptr(), sin.data_ptr(), Lc + 8
+        d.k_pages, d.v_pages, d.page_table, d.seq_lens = kp.data_ptr(), vp.data_ptr(), page_table.data_ptr(), lens.data_ptr()
+        d.q_buf, d.out, d.ld_out, d.partial, d.num_splits, d.bad_index = (q_buf.data_ptr(), out.data_ptr(), out.stride(0),
+                                                                         part.data_ptr(), splits, 0)
+        K.attn_prep(d)                       # appends the T new keys at L..L+T-1, writes q_buf
+        torch.cuda.synchronize()
+        stream = torch.cuda.current_stream()
+        ours = statistics.mean(timed_loop(lambda: K.attn_verify(d), args.steps, args.warmup, stream))
+        # the same tensors in the reference's layout: q (B, nh, T, hd) post-norm/RoPE,
+        # K/V (B, nkv, L+T, hd) contiguous, then expanded to nh heads
+        Lt = Lc + T
+        kc = kp.view(B, max_pages, nkv, ps, hd).permute(0, 2, 1, 3, 4).reshape(B, nkv, max_pages * ps, hd)[:, :, :Lt].contiguous()
+        vc = vp.view(B, max_pages, nkv, ps, hd).permute(0, 2, 1, 3, 4).reshape(B, nkv, max_pages * ps, hd)[:, :, :Lt].contiguous()
+        del kp, vp
+        q = q_buf.view(B, T, nh, hd).transpose(1, 2).contiguous()
+        n_rep = nh // nkv
+        expand = lambda: (kc.repeat_interleave(n_rep, dim=1), vc.repeat_interleave(n_rep, dim=1))
+        ke, ve = expand()
+        del ke, ve
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        ke, ve = expand()                    # eager: a captured loop would hold one copy per call
+        e1.record(stream)
+        torch.cuda.synchronize()
+        exp_ms = e0.elapsed_time(e1)
+        import attention as RA
+        o_ref = RA.torch_attention(q, ke, ve)
+        sdpa = statistics.mean(timed_loop(lambda: RA.torch_attention(q, ke, ve), args.steps, args.warmup, stream))
+        # agreement of ours with the reference's SDPA output (ungated: ours applies σ(gate))
+        gate = torch.sigmoid(qkv[:, :2 * nh * hd].reshape(B, T, nh, 2 * hd)[..., hd:].float())
+        ours_o = out.view(B, T, nh, hd).float()
+        ref_o = o_ref.transpose(1, 2).float() * gate
+        err = float((ours_o - ref_o).abs().max())
+        tri, tri_err = None, None
+        try:
+            from _triton_attn import flash_attention_kv
+            o_tri = flash_attention_kv(q, ke, ve)          # autotune + compile outside the timing
+            torch.cuda.synchronize()
+            tri = statistics.mean(timed_loop(lambda: flash_attention_kv(q, ke, ve), args.steps, args.warmup, stream))
+            tri_err = float((o_tri.float() - o_ref.float()).abs().max())
+        except Exception as e:  # noqa: BLE001
+            tri = f"failed: {type(e).__name__}: {str(e)[:200]}"
+        algo = B * Lt * nkv * hd * 2 * 2
+        gbs = lambda ms: algo / (ms / 1000) / 1e9 if isinstance(ms, float) else None
+        rows.append({"L": Lc, "splits": splits, "ours_ms": ours, "sdpa_ms": sdpa, "triton_ms": tri,
+                     "expand_ms": exp_ms, "ours_frac": gbs(ours) / hbm, "sdpa_frac": gbs(sdpa) / hbm,
+                     "triton_frac": (gbs(tri) / hbm) if isinstance(tri, float) else None,
+                     "max_abs_diff_ours_vs_sdpa": err, "max_abs_diff_triton_vs_sdpa": tri_err,
+                     "algorithmic_bytes": algo})
+        del ke, ve, kc, vc, q, o_ref, part
+        torch.cuda.empty_cache()
+    return {"metric": "verify attention at equal lengths: ours vs the reference's SDPA and Triton kernels",
+            "unit": "ms", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": False,
+            "dtype": "bf16", "data": "synthetic (BASELINE configs[2] shapes, equal lengths per batch)",
+            "config": {"workload": "attn_compare", "batch": B, "T": T, "heads": f"{nh}q/{nkv}kv", "head_dim": hd},
+            "peak_gbs": hbm, "peak_source": src, "rows": rows}
+
+
 def run_gemm_workload(args):
     """One projection of the verify step alone: c = a·wᵀ (bf16, fp32 accumulate) with
     M = batch·(k+1) token rows (default: the GDN in_proj shape 256 x 12352 x 2048)."""
@@ -762,15 +1011,21 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--batch", type=int, default=64, help="sequences per GPU (weak scaling, the headline)")
+    ap.add_argument("--global-batch", type=int, default=64,
+                    help="N > 1: also time the step with this many sequences split over the GPUs (strong scaling)")
     ap.add_argument("--prompt", type=int, default=2048)
     ap.add_argument("--k", type=int, default=3)
     ap.add_argument("--prefill-chunk", type=int, default=128)
-    ap.add_argument("--cpu-batch", type=int, default=2)
-    ap.add_argument("--cpu-steps", type=int, default=3)
+    ap.add_argument("--ref-budget-s", type=float, default=150.0,
+                    help="reference arm: stop the timed CPU steps after this many seconds")
+    ap.add_argument("--ref-warmup", type=int, default=1, help="reference arm: at most this many warm-up steps")
+    ap.add_argument("--cpu-steps", type=int, default=2, help="cpu_baseline: timed reference steps")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--attn-len", default="1024,32768",
                     help="attn workload: per-sequence context lengths ~ U[lo, hi] (configs[2]: 1024,32768)")
+    ap.add_argument("--attn-equal", default="1024,4096,16384,32768",
+                    help="attn_compare workload: the equal context lengths to time")
     ap.add_argument("--profile", action="store_true",
                     help="bracket the timed steps with cudaProfilerStart/Stop (for ncu --profile-from-start off)")
     ap.add_argument("--m", type=int, default=256)
@@ -779,16 +1034,17 @@ def main():
     ap.add_argument("--l2-resident", action="store_true", help="gemm workload: one weight copy (stays in L2)")
     ap.add_argument("--gemm-epi", choices=["store", "resnorm", "swiglu"], default="store",
                     help="gemm workload: plain product, + residual add and RMSNorm, or SwiGLU of [gate; up]")
-    ap.add_argument("--workload", choices=["step", "gdn", "attn", "gemm", "moe"], default="step",
+    ap.add_argument("--workload", choices=["step", "gdn", "attn", "attn_compare", "gemm", "moe"], default="step",
                     help="step: the speculative step (headline); gdn / attn: BASELINE configs[3] / [2] kernels "
-                         "alone; moe: one configs[4] sparse FFN block")
+                         "alone; attn_compare: configs[2] attention at equal lengths against the reference's "
+                         "SDPA and Triton kernels; moe: one configs[4] sparse FFN block")
     args = ap.parse_args()
     from lollm_b200.qwen3_5.config import QWEN35_2B, Qwen3_5Config
     cfg = Qwen3_5Config.from_hf(QWEN35_2B)
     if args.workload != "step":
         torch.cuda.set_device(0)
-        out = {"gdn": run_gdn_workload, "attn": run_attn_workload, "gemm": run_gemm_workload,
-               "moe": run_moe_workload}[args.workload](args)
+        out = {"gdn": run_gdn_workload, "attn": run_attn_workload, "attn_compare": run_attn_compare_workload,
+               "gemm": run_gemm_workload, "moe": run_moe_workload}[args.workload](args)
         print(json.dumps(out), flush=True)
         return
     if args.impl == "reference":
@@ -799,12 +1055,11 @@ def main():
     args.gpus = ws
     out = run_gpu_arm(args, cfg, ws, rank, local)
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
-        tps, toks, secs, n, threads = cpu_reference_sample(cfg, args.cpu_batch, args.prompt, args.k,
-                                                           args.cpu_steps, 1, budget_s=30)
-        out["cpu_baseline"] = {"value": tps, "unit": UNIT, "cores": threads, "kind": "port",
-                               "sample": f"{n} speculative steps x {args.cpu_batch} sequences at context "
-                                         f"{args.prompt}, k={args.k}: the oracle restatement of the "
-                                         f"reference's generate_mtp in bf16 on {threads} host threads"}
+        cb, why = stock_reference_sample(cfg, args.batch, args.prompt, args.k, args.cpu_steps, 1, 30.0)
+        if cb is not None:
+            for key in ("steps", "seconds", "tokens"):
+                cb.pop(key)
+        out["cpu_baseline"] = cb if cb is not None else {"unavailable": why}
     if ws > 1:
         torch.distributed.destroy_process_group()
     if rank == 0:

@@ -88,9 +88,26 @@ int qsp_gemm_swiglu(const void* a, int64_t lda, const void* w_gu, int64_t ldw, v
 /* Workspace bytes qsp_gemm uses for this shape (0 when it never splits). */
 size_t qsp_gemm_workspace_bytes(int64_t m, int64_t n, int64_t k, int dtype);
 
-/* Device error flag: nonzero after a kernel's bounded wait ran out (the kernel returned
- * instead of hanging). Synchronous; `reset` clears it. */
+/* Device status codes (qsp_device_status). 1xx-3xx: a kernel's bounded mbarrier wait ran out
+ * (GEMM, GDN, attention, MoE, cluster GEMM) and the kernel returned instead of hanging. */
+#define QSP_DEV_BAD_ACCEPT 401  /* qsp_cache_accept got an accepted count outside [0, T-1]
+                                   (clamped into range)                                      */
+#define QSP_DEV_NAN_LOGITS 501  /* a sampler or argmax row held a NaN logit (argmax then
+                                   picks the first NaN, as torch.argmax does)                */
+#define QSP_DEV_WAIT_PROBE 901  /* qsp_wait_probe's wait ran out (its expected outcome)      */
+
+/* Device status: the first nonzero code recorded by any kernel since the last reset, else 0.
+ * Synchronous; `reset` clears it. The "hard-fail, never guess" checks of the reference
+ * (src/qwen3_5/weights.py:57-62) have no device side; this is where device-side failures
+ * surface for the host to raise. */
 int qsp_device_status(int32_t* code, int32_t reset);
+
+/* Failure-detection probe (test support, no reference counterpart): one CTA waits on an
+ * mbarrier that is never signalled, through the same bounded wait as the tensor-core kernels
+ * but with a limit of `polls` polls (the kernels use 2^24, about a second). When it runs out
+ * the kernel records QSP_DEV_WAIT_PROBE and returns; `waited_ns` (device, may be NULL)
+ * receives how long it waited. polls in [1, 2^24]. */
+int qsp_wait_probe(uint32_t polls, uint32_t* waited_ns, void* stream);
 
 /* ---------------------------------------------------------------- Gated DeltaNet */
 
@@ -211,6 +228,10 @@ size_t qsp_attn_workspace_bytes(int32_t batch, int32_t tokens, int32_t n_heads,
  *   capture. Later calls only launch kernels.
  * - One region per device: calls that overlap in time on one device (two streams, two host
  *   threads) race on it and must be serialised by the caller.
+ * - The address is looked up once per device ordinal and kept for the life of the process,
+ *   which assumes every call runs in that device's primary context (the CUDA runtime's
+ *   default) and that nothing calls cudaDeviceReset on the device in between; after a reset,
+ *   or from another driver context on the same device, the kept address is not valid.
  * - Nothing in the region has to start at zero: every partial the merge reads is written
  *   earlier in the same call (an empty key split writes an all-masked partial). */
 #define QSP_ATTN_STATIC_SCRATCH_BYTES ((size_t)16 << 20)

@@ -76,6 +76,7 @@ SIGNATURES = {
                                             vp, sz, vp]),
     "qsp_gemm_swiglu": (C.c_int, [vp, i64, vp, i64, vp, i64, vp, i64, i64, i64, i64, C.c_int, vp, sz, vp]),
     "qsp_device_status": (C.c_int, [C.POINTER(i32), i32]),
+    "qsp_wait_probe": (C.c_int, [C.c_uint32, vp, vp]),
     "qsp_gdn_verify": (C.c_int, [C.POINTER(GdnLayer), vp]),
     "qsp_gdn_pending_bytes": (sz, [i32, i32, i32, i32, i32, i32, i32]),
     "qsp_attn_prep": (C.c_int, [C.POINTER(AttnLayer), vp]),

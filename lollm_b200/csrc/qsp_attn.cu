@@ -412,8 +412,12 @@ int qsp_attn_verify_static(const qsp_attn_layer* layer, void* stream) {
   qsp_attn_layer L = *layer;
   QSP_REQUIRE(L.batch > 0 && L.tokens > 0 && L.n_heads > 0 && L.head_dim > 0 && L.num_splits > 0,
               "qsp_attn_verify_static: batch, tokens, heads, head_dim and num_splits must be positive");
-  const size_t need = qsp_attn_workspace_bytes(L.batch, L.tokens, L.n_heads, L.head_dim, L.num_splits);
-  QSP_REQUIRE(need <= QSP_ATTN_STATIC_SCRATCH_BYTES,
+  // the size product in overflow-checked steps: a wrapped product must not pass the limit
+  size_t need = 2 * sizeof(float) * ((size_t)L.head_dim + 2);
+  bool wrapped = false;
+  for (const int32_t f : {L.batch, L.tokens, L.n_heads, L.num_splits})
+    wrapped = wrapped || __builtin_mul_overflow(need, (size_t)f, &need);
+  QSP_REQUIRE(!wrapped && need <= QSP_ATTN_STATIC_SCRATCH_BYTES,
               "qsp_attn_verify_static: this shape needs %zu bytes of split-KV scratch; the static region "
               "holds %zu (use qsp_attn_verify with a caller workspace, or fewer splits)",
               need, (size_t)QSP_ATTN_STATIC_SCRATCH_BYTES);

@@ -129,11 +129,16 @@ __global__ void finalize_kernel(int B, int T, int spec, int32_t* lens, int32_t* 
   if (b == 0) parity[0] ^= 1;
 }
 
+// Set when qsp_cache_accept met an accepted count outside [0, T-1] (read through
+// qsp_device_status); the count is clamped into range so the cache stays consistent.
+__device__ int g_core_error = 0;
+
 __global__ void accept_kernel(int B, int T, const int32_t* acc, int32_t* lens, int32_t* replay,
                               int32_t* conv_off) {
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= B) return;
   int keep = acc[b] + 1;
+  if (keep < 1 || keep > T) atomicExch(&g_core_error, QSP_DEV_BAD_ACCEPT);
   keep = keep < 1 ? 1 : (keep > T ? T : keep);
   lens[b] -= (T - keep);
   replay[b] = keep;
@@ -153,6 +158,16 @@ __global__ void commit_tokens_kernel(int B, int T, int64_t* ids, const int32_t* 
   }
   n_out[b] = (int32_t)(n + keep);
   ids[(int64_t)b * T] = next_tok[b];
+}
+
+int core_device_error(int reset) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_core_error, sizeof(int)) != cudaSuccess) return 0;
+  if (reset && v != 0) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(g_core_error, &zero, sizeof(int));
+  }
+  return v;
 }
 
 }  // namespace qsp

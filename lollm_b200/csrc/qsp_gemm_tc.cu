@@ -725,6 +725,9 @@ int gdn_device_error(int reset);
 int attn_device_error(int reset);
 int moe_device_error(int reset);
 int gemm_cl_device_error(int reset);
+int core_device_error(int reset);
+int sample_device_error(int reset);
+int probe_device_error(int reset);
 }
 
 extern "C" int qsp_device_status(int32_t* code, int32_t reset) {
@@ -733,10 +736,14 @@ extern "C" int qsp_device_status(int32_t* code, int32_t reset) {
   const int attn = qsp::attn_device_error(reset);
   const int moe = qsp::moe_device_error(reset);
   const int cl = qsp::gemm_cl_device_error(reset);
+  const int others[] = {qsp::core_device_error(reset), qsp::sample_device_error(reset),
+                        qsp::probe_device_error(reset)};
   int v = 0;
   cudaError_t e = cudaMemcpyFromSymbol(&v, qsp::g_qsp_dev_error, sizeof(int));
   if (e != cudaSuccess) return qsp::set_error(QSP_ERR_CUDA, "qsp_device_status: %s", cudaGetErrorString(e));
   *code = v != 0 ? v : (gdn != 0 ? gdn : (attn != 0 ? attn : (moe != 0 ? moe : cl)));
+  for (int o : others)
+    if (*code == 0) *code = o;
   if (reset && v != 0) {
     const int zero = 0;
     e = cudaMemcpyToSymbol(qsp::g_qsp_dev_error, &zero, sizeof(int));

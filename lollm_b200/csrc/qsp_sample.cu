@@ -14,8 +14,14 @@ struct ArgBest {
   float v;
   long long i;
 };
+// Set when an argmax met a NaN logit (read through qsp_device_status).
+__device__ int g_sample_error = 0;
+
 __device__ __forceinline__ ArgBest arg_better(ArgBest a, ArgBest b) {
-  // larger value wins; ties → smaller index (torch.argmax returns the first maximum)
+  // larger value wins; ties → smaller index (torch.argmax returns the first maximum). A NaN
+  // ranks above every number, as in torch.argmax, so a row holding NaNs selects its first NaN.
+  const bool an = a.v != a.v, bn = b.v != b.v;
+  if (an || bn) return (bn && (!an || b.i < a.i)) ? b : a;
   if (b.v > a.v || (b.v == a.v && b.i < a.i)) return b;
   return a;
 }
@@ -88,6 +94,7 @@ __device__ ArgBest row_argbest(const T* __restrict__ row, int64_t vocab) {
 template <typename T>
 __device__ long long row_argmax(const T* __restrict__ row, int64_t vocab) {
   const ArgBest b = row_argbest<T>(row, vocab);
+  if (b.v != b.v && threadIdx.x == 0) atomicExch(&g_sample_error, QSP_DEV_NAN_LOGITS);
   return b.i == LLONG_MAX ? 0 : b.i;
 }
 
@@ -127,6 +134,7 @@ argmax_split_kernel(const T* __restrict__ logits, int64_t ld, int64_t vocab, int
   if (rank == 0 && threadIdx.x == 0) {
     ArgBest best{cv, ci};
     for (int r = 1; r < S; ++r) best = arg_better(best, ArgBest{*cl.map_shared_rank(&cv, r), *cl.map_shared_rank(&ci, r)});
+    if (best.v != best.v) atomicExch(&g_sample_error, QSP_DEV_NAN_LOGITS);
     out[row * out_stride] = best.i == LLONG_MAX ? 0 : best.i;
   }
   cl.sync();   // every CTA keeps its shared memory until rank 0 has read it
@@ -189,6 +197,7 @@ __global__ void __launch_bounds__(SEL_THREADS) softmax_stats_kernel(const T* __r
   if (threadIdx.x == 0) {
     stats[2 * blockIdx.x] = m;
     stats[2 * blockIdx.x + 1] = z;
+    if (z != z) atomicExch(&g_sample_error, QSP_DEV_NAN_LOGITS);   // a NaN logit poisons Z
   }
 }
 
@@ -466,7 +475,10 @@ __global__ void __launch_bounds__(SEL_THREADS) filter_rows_kernel(
   for (int64_t j = tid; j < vocab; j += blockDim.x)
     if (w[j] >= thr) z += expf(w[j] - m);
   z = block_sum(z, red);
-  if (tid == 0) stats[r] = FilterRow{m, z, thr, 0.f};
+  if (tid == 0) {
+    stats[r] = FilterRow{m, z, thr, 0.f};
+    if (z != z) atomicExch(&g_sample_error, QSP_DEV_NAN_LOGITS);
+  }
 }
 
 __device__ __forceinline__ float filtered_p(const float* w, const FilterRow& s, int64_t x) {
@@ -534,6 +546,16 @@ __global__ void __launch_bounds__(SEL_THREADS) spec_filtered_kernel(
     accept_n[b] = a;
     next_tok[b] = pick;
   }
+}
+
+int sample_device_error(int reset) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_sample_error, sizeof(int)) != cudaSuccess) return 0;
+  if (reset && v != 0) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(g_sample_error, &zero, sizeof(int));
+  }
+  return v;
 }
 
 }  // namespace qsp

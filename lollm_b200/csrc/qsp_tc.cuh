@@ -41,9 +41,9 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // Bounded wait on one phase. Gives up (false) after WAIT_LIMIT polls, or as soon as another
 // role of the CTA raised `*abort` (shared memory); a timeout records `code` in `*flag` (global)
 // and raises `*abort`, so the other roles stop waiting too and the CTA exits promptly.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int code, int* flag,
-                                          volatile int* abort) {
-  for (uint32_t i = 0; i < WAIT_LIMIT; ++i) {
+__device__ __forceinline__ bool mbar_wait_limit(uint64_t* bar, uint32_t parity, int code, int* flag,
+                                                volatile int* abort, uint32_t limit) {
+  for (uint32_t i = 0; i < limit; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if (i > 256) {
       if (*abort) return false;
@@ -53,6 +53,10 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int co
   atomicExch(flag, code);
   *abort = 1;
   return false;
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int code, int* flag,
+                                          volatile int* abort) {
+  return mbar_wait_limit(bar, parity, code, flag, abort, WAIT_LIMIT);
 }
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
   asm volatile(

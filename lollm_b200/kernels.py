@@ -106,6 +106,21 @@ def device_status(reset=True) -> int:
     return int(v.value)
 
 
+# device status codes (include/qsp.h)
+DEV_BAD_ACCEPT, DEV_NAN_LOGITS, DEV_WAIT_PROBE = 401, 501, 901
+DEVICE_CODES = {DEV_BAD_ACCEPT: "an accepted count outside [0, T-1] (clamped)",
+                DEV_NAN_LOGITS: "a NaN logit in a sampled or argmax row",
+                DEV_WAIT_PROBE: "the wait probe ran out (expected)"}
+
+
+def wait_probe(polls: int, waited_ns: torch.Tensor | None = None):
+    """Launch the bounded-wait probe: a wait that nothing ends, limited to `polls` polls; it
+    records DEV_WAIT_PROBE in the device status and returns (test support)."""
+    if waited_ns is not None:
+        _cuda(waited_ns)
+    L.call("qsp_wait_probe", int(polls), L.ptr(waited_ns), _s())
+
+
 def gdn_verify(desc: L.GdnLayer):
     L.call("qsp_gdn_verify", C.byref(desc), _s())
 

@@ -148,6 +148,21 @@ class Qwen3_5Cache:
         return sum(t.numel() * t.element_size() for t in
                    (self.k_pages, self.v_pages, self.state, self.conv_hist, self.pending))
 
+    def check(self):
+        """Raise RuntimeError if a kernel flagged this cache or the device since the last check:
+        a position outside its sequence's pages (the page pool or the capacity exhausted), an
+        accepted count out of range, a NaN logit, or a bounded wait that ran out. Kernels
+        record these on the device without stopping the stream; this call synchronises and
+        turns them into the reference's hard failure (weights.py:57-62 style RuntimeError)."""
+        bad = int(self.bad_index.item())
+        code = K.device_status(reset=True)
+        if bad:
+            self.bad_index.zero_()
+            raise RuntimeError("qsp cache: a token position fell outside its sequence's pages "
+                               f"(capacity {self.capacity} positions per sequence, {self.num_pages} pages)")
+        if code:
+            raise RuntimeError(f"qsp device status {code}: {K.DEVICE_CODES.get(code, 'a bounded wait ran out')}")
+
     # ------------------------------------------------------------------ speculative support
     def accept(self, accept_n: torch.Tensor):
         """Keep accept_n[b] + 1 of the last speculative forward's tokens (device int32 [B])."""

@@ -74,6 +74,19 @@ def test_static_attention_scratch_limits_without_gpu():
     assert b"static region" in lib.qsp_last_error()
     d.num_splits = 0
     assert lib.qsp_attn_verify_static(ctypes.byref(d), None) == L.QSP_ERR_INVALID
+    # a shape whose byte count wraps 64 bits (2^30 rows x 2^31 heads x 2^31 splits x 2 KB)
+    # is refused, not reduced to a small number that would pass the limit
+    d.batch, d.tokens, d.n_heads, d.num_splits = 1 << 15, 1 << 15, (1 << 31) - 1, (1 << 31) - 1
+    assert lib.qsp_attn_verify_static(ctypes.byref(d), None) == L.QSP_ERR_INVALID
+    assert b"static region" in lib.qsp_last_error()
+
+
+def test_wait_probe_limits_without_gpu():
+    """The failure-detection probe checks its poll limit on the host before any launch."""
+    lib = L.load()
+    assert lib.qsp_wait_probe(0, None, None) == L.QSP_ERR_INVALID
+    assert lib.qsp_wait_probe((1 << 24) + 1, None, None) == L.QSP_ERR_INVALID
+    assert b"polls" in lib.qsp_last_error()
 
 
 def test_gemm_plans_at_the_step_shapes():

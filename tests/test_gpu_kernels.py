@@ -319,6 +319,30 @@ def _attn_case(dt, B, T, nh, nkv, hd, rd, lens, page_size=16, seed=4, shuffle_pa
     return d, D, dict(qkv=qkv, qn=qn, kn=kn, kp=kp, vp=vp, pt=page_table, cos=cos, sin=sin)
 
 
+def _attn_reference(H, b, n, T, nh, nkv, hd, ps):
+    """Oracle gated attention output (T, nh*hd) of sequence b with n cached keys: QK-norm and
+    RoPE of the new rows, the pages' old keys + the new ones, offset-causal softmax, σ(gate);
+    also returns the roped new keys (nkv, T, hd)."""
+    qkv = H["qkv"].view(-1, T, H["qkv"].shape[-1])
+    pos = torch.arange(n, n + T)
+    cos, sin = H["cos"][pos], H["sin"][pos]
+    qg = qkv[b, :, :2 * nh * hd].view(T, nh, 2 * hd)
+    q = Q.rms_norm(qg[..., :hd], H["qn"], 1e-6).transpose(0, 1)      # (nh, T, hd)
+    gate = qg[..., hd:].reshape(T, nh * hd)
+    k = Q.rms_norm(qkv[b, :, 2 * nh * hd:2 * nh * hd + nkv * hd].view(T, nkv, hd), H["kn"], 1e-6).transpose(0, 1)
+    v = qkv[b, :, 2 * nh * hd + nkv * hd:].view(T, nkv, hd).transpose(0, 1)
+    q, k = Q.rope_rotate(q, cos, sin), Q.rope_rotate(k, cos, sin)
+    if n > 0:
+        pages = H["pt"][b, :math.ceil(n / ps)].long()
+        kold = H["kp"][pages].permute(1, 0, 2, 3).reshape(nkv, -1, hd)[:, :n]
+        vold = H["vp"][pages].permute(1, 0, 2, 3).reshape(nkv, -1, hd)[:, :n]
+        kf, vf = torch.cat([kold, k], 1), torch.cat([vold, v], 1)
+    else:
+        kf, vf = k, v
+    o = Q.offset_causal_attention(q, kf.repeat_interleave(nh // nkv, 0), vf.repeat_interleave(nh // nkv, 0))
+    return o.transpose(0, 1).reshape(T, nh * hd) * torch.sigmoid(gate), k
+
+
 @pytest.mark.parametrize("dt", DTS)
 @pytest.mark.parametrize("shape", [(2, 4, 4, 2, 32, 8, [5, 17], 16, 3), (3, 4, 16, 2, 256, 64, [40, 1, 77], 16, 3),
                                    (2, 1, 8, 2, 64, 16, [100, 3], 16, 3), (1, 9, 4, 1, 128, 32, [0], 16, 3),
@@ -332,30 +356,12 @@ def test_attention_matches_oracle(dt, shape):
     assert int(D["bad"]) == 0
     ps = d.page_size
     out = D["out"].cpu().view(B, T, nh * hd)
-    qkv = H["qkv"].view(B, T, -1)
+    kp_dev = D["kp"].cpu()
     for b in range(B):
         n = lens[b]
-        pos = torch.arange(n, n + T)
-        cos, sin = H["cos"][pos], H["sin"][pos]
-        qg = qkv[b, :, :2 * nh * hd].view(T, nh, 2 * hd)
-        q = Q.rms_norm(qg[..., :hd], H["qn"], 1e-6).transpose(0, 1)      # (nh, T, hd)
-        gate = qg[..., hd:].reshape(T, nh * hd)
-        k = Q.rms_norm(qkv[b, :, 2 * nh * hd:2 * nh * hd + nkv * hd].view(T, nkv, hd), H["kn"], 1e-6).transpose(0, 1)
-        v = qkv[b, :, 2 * nh * hd + nkv * hd:].view(T, nkv, hd).transpose(0, 1)
-        q, k = Q.rope_rotate(q, cos, sin), Q.rope_rotate(k, cos, sin)
-        # old keys from the pages
-        if n > 0:
-            pages = H["pt"][b, :math.ceil(n / ps)].long()
-            kold = H["kp"][pages].permute(1, 0, 2, 3).reshape(nkv, -1, hd)[:, :n]
-            vold = H["vp"][pages].permute(1, 0, 2, 3).reshape(nkv, -1, hd)[:, :n]
-            kf, vf = torch.cat([kold, k], 1), torch.cat([vold, v], 1)
-        else:
-            kf, vf = k, v
-        o = Q.offset_causal_attention(q, kf.repeat_interleave(nh // nkv, 0), vf.repeat_interleave(nh // nkv, 0))
-        o = o.transpose(0, 1).reshape(T, nh * hd) * torch.sigmoid(gate)
+        o, k = _attn_reference(H, b, n, T, nh, nkv, hd, ps)
         close(out[b], o, dt)
         # the appended keys/values sit in the pages at positions n..n+T-1
-        kp_dev = D["kp"].cpu()
         for t in range(T):
             p = H["pt"][b, (n + t) // ps]
             close(kp_dev[p, :, (n + t) % ps], k[:, t], dt)

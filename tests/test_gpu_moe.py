@@ -21,7 +21,7 @@ from lollm_b200.qwen3_5.weights import load_checkpoint, random_init
 pytestmark = pytest.mark.gpu
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 SEED = 1234
-TOL = {torch.float32: dict(rtol=1e-4, atol=1e-4), torch.bfloat16: dict(rtol=2e-2, atol=3e-2)}
+TOL = {torch.float32: dict(rtol=1e-4, atol=1e-4), torch.bfloat16: dict(rtol=2e-2, atol=2e-2)}
 MOE_CASES = [
     ("shared", 128, 16, 4, 64, 64, True, 40),
     ("noshared", 128, 16, 4, 64, 0, True, 24),
