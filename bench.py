@@ -768,7 +768,7 @@ def run_attn_workload(args):
     qn = torch.zeros(hd, dtype=torch.bfloat16, device=dev); kn = torch.zeros_like(qn)
     cos, sin = rope_table(rd, 1e7, hi + 8, torch.bfloat16)
     cos, sin = cos.to(dev), sin.to(dev)
-    splits = max(1, (hi + 511) // 512)
+    splits = max(1, (hi + args.attn_split_len - 1) // args.attn_split_len)   # fixed-length key splits
     q_buf = torch.empty(B * T, nh * hd, dtype=torch.bfloat16, device=dev)
     out = torch.empty(B * T, nh * hd, dtype=torch.bfloat16, device=dev)
     part = torch.empty(K.attn_workspace_bytes(B, T, nh, hd, splits) // 4, device=dev)
@@ -902,6 +902,168 @@ def run_attn_compare_workload(args):
             "peak_gbs": hbm, "peak_source": src, "rows": rows}
 
 
+def moe_step_bytes(cfg, model, B, T, ctx_lens, expert_hits):
+    """Algorithmic HBM bytes of one verify forward of the MoE model: the dense weights (every
+    projection, norms, the lm_head once; not the embedding table), the experts hit in each
+    layer (`expert_hits[i]` of them, gate|up + down), the K/V of every visible key plus the T
+    new rows, the GDN state read + written and the conv window read + written."""
+    elt = 2
+    w = 0
+    E = cfg.num_experts
+    per_expert = (2 * cfg.moe_intermediate_size * cfg.hidden_size + cfg.hidden_size * cfg.moe_intermediate_size) * elt
+    from lollm_b200.qwen3_5.weights import param_specs
+    for name, shape in param_specs(cfg, with_mtp=False):
+        if name == "model.embed_tokens.weight" or ".mlp.experts." in name:
+            continue
+        w += math.prod(shape) * elt
+    if cfg.tie_word_embeddings:
+        w += cfg.vocab_size * cfg.hidden_size * elt
+    experts = sum(expert_hits) * per_expert
+    n_attn, n_gdn = len(cfg.attn_layers), len(cfg.gdn_layers)
+    kv_row = n_attn * cfg.num_key_value_heads * cfg.head_dim * 2 * elt
+    kv = sum(kv_row * (L + T) for L in ctx_lens) + kv_row * T * B
+    state = 2 * n_gdn * B * cfg.linear_num_value_heads * cfg.linear_key_head_dim * cfg.linear_value_head_dim * 4
+    conv = 2 * n_gdn * B * cfg.conv_dim * (cfg.linear_conv_kernel_dim - 1) * elt
+    return {"dense_weights": w, "experts": experts, "kv": kv, "gdn_state": state, "conv": conv,
+            "total": w + experts + kv + state + conv}
+
+
+def run_moe_step_workload(args, ws, rank, local):
+    """the qwen3_5_moe shape (48 layers, 512 experts top-10 + a shared
+    expert) in bf16, stochastic speculative decoding at temperature 0.8 with seeded uniforms,
+    k=3, 4096-token prompts, `--moe-batch` (256) sequences sharded over the ranks.
+
+    The ~162 GB of weights are generated on the device one tensor at a time (StreamingParams);
+    what is left of the GPU holds the state of one resident WAVE of sequences (KV, GDN state,
+    conv windows) — about 200 MB per sequence at 4.6k positions — so a rank's sequences run in
+    waves: prefill a wave, run its steps, drop its state, next wave. Each wave's steps are one
+    CUDA graph replayed with fresh uniforms copied in before every replay. Timed: K steps per
+    wave (CUDA events around the replays); value = committed tokens of all waves of all ranks ÷
+    the max over ranks of the summed wave times."""
+    from lollm_b200.qwen3_5 import MTP, Qwen3_5Model, SpecDecoder
+    from lollm_b200.qwen3_5.config import QWEN35_MOE, Qwen3_5Config
+    from lollm_b200.qwen3_5.weights import StreamingParams
+    dev = torch.device("cuda", local)
+    raw = dict(QWEN35_MOE)
+    if args.moe_layers:
+        raw["num_hidden_layers"] = args.moe_layers
+    cfg = Qwen3_5Config.from_hf(raw)
+    t0 = time.perf_counter()
+    k, T = args.k, args.k + 1
+    n_total = args.warmup + args.steps + 2
+    max_len = args.moe_prompt + (n_total + 2) * T + 16
+    model = Qwen3_5Model(cfg, StreamingParams.random(cfg, 0, device=dev), dtype=torch.bfloat16, device=dev,
+                         max_positions=max_len + 64)
+    mtp = MTP(model, StreamingParams.random(cfg, 0, device=dev))
+    torch.cuda.synchronize()
+    build_s = time.perf_counter() - t0
+    weight_gb = torch.cuda.memory_allocated(dev) / 1e9
+    per_rank = args.moe_batch // ws
+    # one sequence's resident state at max_len positions (KV pages, GDN state, conv ring, token
+    # ring), measured on a 1-sequence cache so nothing is estimated
+    probe = model.new_cache(1, max_len, max_spec_tokens=max(T, 2))
+    per_seq = probe.nbytes()
+    del probe
+    free, _ = torch.cuda.mem_get_info(dev)
+    reserve = int(args.moe_reserve_gb * 1e9)
+    fit = max(8, int((free - reserve) // per_seq) // 8 * 8)
+    n_waves = math.ceil(per_rank / min(per_rank, fit))
+    wave = min(fit, math.ceil(per_rank / n_waves / 8) * 8)      # balanced waves
+    stream = torch.cuda.current_stream()
+    tot_tokens, tot_ms, verify_ms, prefill_s, acc_steps = 0, 0.0, [], 0.0, []
+    gen = torch.Generator(device=dev)
+    hits = torch.zeros(cfg.num_experts, dtype=torch.int32, device=dev)
+    bytes_rows = []
+    for wv in range(n_waves):
+        B = min(wave, per_rank - wv * wave)
+        gen.manual_seed(10_000 * rank + wv)
+        dec = SpecDecoder(model, mtp, B, k, max_len, temperature=args.moe_temperature,
+                          out_capacity=n_total * T + 8)
+        U = {"draft": torch.rand(n_total + 2, B, k, generator=gen, device=dev),
+             "accept": torch.rand(n_total + 2, B, k, generator=gen, device=dev),
+             "resample": torch.rand(n_total + 2, B, generator=gen, device=dev)}
+        dec.u = {key: v[0].clone() for key, v in U.items()}
+        prompts = torch.randint(0, cfg.vocab_size, (B, args.moe_prompt), generator=gen, device=dev)
+        torch.cuda.synchronize()
+        tp = time.perf_counter()
+        dec.prefill(prompts, chunk=args.prefill_chunk, u_first=torch.rand(B, generator=gen, device=dev))
+        torch.cuda.synchronize()
+        prefill_s += time.perf_counter() - tp
+        del prompts
+        graph = dec.capture(warmup=1)
+        si = [1]
+
+        def feed():
+            for key, v in U.items():
+                dec.u[key].copy_(v[si[0]])
+            si[0] += 1
+
+        for _ in range(args.warmup):
+            feed()
+            graph.replay()
+        ctx_lens = dec.cache.seq_lens.tolist()
+        n0 = int(dec.n_out.sum())
+        barrier(ws)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            feed()
+            graph.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        tot_ms += e0.elapsed_time(e1)
+        tot_tokens += int(dec.n_out.sum()) - n0
+        acc_steps.append((int(dec.n_out.sum()) - n0) / (args.steps * B))
+        # verify phase alone (same wave state), with the experts each layer hit
+        ws_ = model.workspace(B, T, dec.cache)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        dec.mtp.draft(dec.hidden_last, dec.ids, k, dec.temperature, dec.u["draft"])
+        hits.zero_()
+        counts = []
+        for lw in model.layers:
+            c = torch.zeros(cfg.num_experts, dtype=torch.int32, device=dev)
+            lw["moe"].counts_probe = c
+            counts.append(c)
+        ev[0].record(stream)
+        model._forward_into(dec.ids, dec.cache, B, T, True)
+        ev[1].record(stream)
+        torch.cuda.synchronize()
+        verify_ms.append(ev[0].elapsed_time(ev[1]))
+        for lw in model.layers:
+            lw["moe"].counts_probe = None
+        expert_hits = [int((c > 0).sum()) for c in counts]
+        bytes_rows.append(moe_step_bytes(cfg, model, B, T, ctx_lens, expert_hits))
+        dec.cache.accept(torch.zeros(B, dtype=torch.int32, device=dev))
+        del dec, graph, U, ws_
+        model._ws.clear()
+        mtp._ws.clear()
+        torch.cuda.empty_cache()
+    max_ms = reduce_max(tot_ms, ws)
+    all_tokens = reduce_sum(tot_tokens, ws)
+    hbm, _, src = peaks()
+    vb = bytes_rows[0]
+    v_ms = verify_ms[0]
+    return {"metric": "generated tok/s, qwen3_5_moe 48-layer shape, stochastic spec decode (batch 256, k=3, T=0.8)",
+            "value": all_tokens / (max_ms / 1000.0), "unit": UNIT, "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": max_ms / (args.steps * n_waves), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded random-init N(0,0.02) weights generated on the device, uniform random prompt ids, seeded uniforms)",
+            "config": {"workload": "moe_step (BASELINE configs[4])", "layers": cfg.num_hidden_layers,
+                       "experts": cfg.num_experts, "top_k": cfg.num_experts_per_tok, "global_batch": args.moe_batch,
+                       "batch_per_gpu": per_rank, "wave": wave, "waves_per_gpu": n_waves,
+                       "prompt_len": args.moe_prompt, "k": k, "temperature": args.moe_temperature,
+                       "parallelism": f"replicas x{ws}, sequence-sharded, resident waves",
+                       "weights_gb_per_gpu": weight_gb, "state_bytes_per_sequence": per_seq,
+                       "l2": "inputs larger than L2 (~160 GB of weights per step)"},
+            "acceptance_rate": (statistics.mean(acc_steps) - 1.0) / k,
+            "roofline": {"kernel": "verify phase (48-layer forward, T=k+1, all kernels), first wave", "bound": "hbm",
+                         "achieved": vb["total"] / (v_ms / 1000) / 1e9, "peak": hbm, "unit": "GB/s",
+                         "frac": vb["total"] / (v_ms / 1000) / 1e9 / hbm, "peak_source": src, "traffic": None,
+                         "algorithmic_bytes": vb, "verify_ms": v_ms},
+            "prefill_s": prefill_s, "build_s": build_s, "setup_s": time.perf_counter() - t0}
+
+
 def run_gemm_workload(args):
     """One projection of the verify step alone: c = a·wᵀ (bf16, fp32 accumulate) with
     M = batch·(k+1) token rows (default: the GDN in_proj shape 256 x 12352 x 2048)."""
@@ -1024,6 +1186,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--attn-len", default="1024,32768",
                     help="attn workload: per-sequence context lengths ~ U[lo, hi] (configs[2]: 1024,32768)")
+    ap.add_argument("--attn-split-len", type=int, default=512,
+                    help="attn workload: keys per split (the split count is the longest context over this)")
     ap.add_argument("--attn-equal", default="1024,4096,16384,32768",
                     help="attn_compare workload: the equal context lengths to time")
     ap.add_argument("--profile", action="store_true",
@@ -1034,13 +1198,28 @@ def main():
     ap.add_argument("--l2-resident", action="store_true", help="gemm workload: one weight copy (stays in L2)")
     ap.add_argument("--gemm-epi", choices=["store", "resnorm", "swiglu"], default="store",
                     help="gemm workload: plain product, + residual add and RMSNorm, or SwiGLU of [gate; up]")
-    ap.add_argument("--workload", choices=["step", "gdn", "attn", "attn_compare", "gemm", "moe"], default="step",
+    ap.add_argument("--moe-batch", type=int, default=256, help="moe_step: sequences over all GPUs (configs[4]: 256)")
+    ap.add_argument("--moe-prompt", type=int, default=4096, help="moe_step: prompt length (configs[4]: 4096)")
+    ap.add_argument("--moe-temperature", type=float, default=0.8)
+    ap.add_argument("--moe-layers", type=int, default=0, help="moe_step: fewer layers (0 = the 48 of configs[4])")
+    ap.add_argument("--moe-reserve-gb", type=float, default=6.0,
+                    help="moe_step: device memory kept free of wave state (workspaces)")
+    ap.add_argument("--workload", choices=["step", "gdn", "attn", "attn_compare", "gemm", "moe", "moe_step"],
+                    default="step",
                     help="step: the speculative step (headline); gdn / attn: BASELINE configs[3] / [2] kernels "
                          "alone; attn_compare: configs[2] attention at equal lengths against the reference's "
                          "SDPA and Triton kernels; moe: one configs[4] sparse FFN block")
     args = ap.parse_args()
     from lollm_b200.qwen3_5.config import QWEN35_2B, Qwen3_5Config
     cfg = Qwen3_5Config.from_hf(QWEN35_2B)
+    if args.workload == "moe_step":
+        ws, rank, local = dist_setup()
+        out = run_moe_step_workload(args, ws, rank, local)
+        if ws > 1:
+            torch.distributed.destroy_process_group()
+        if rank == 0:
+            print(json.dumps(out), flush=True)
+        return
     if args.workload != "step":
         torch.cuda.set_device(0)
         out = {"gdn": run_gdn_workload, "attn": run_attn_workload, "attn_compare": run_attn_compare_workload,

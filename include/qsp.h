@@ -233,7 +233,8 @@ size_t qsp_attn_workspace_bytes(int32_t batch, int32_t tokens, int32_t n_heads,
  *   default) and that nothing calls cudaDeviceReset on the device in between; after a reset,
  *   or from another driver context on the same device, the kept address is not valid.
  * - Nothing in the region has to start at zero: every partial the merge reads is written
- *   earlier in the same call (an empty key split writes an all-masked partial). */
+ *   earlier in the same call (a key split past the end of its sequence either writes an
+ *   all-masked partial or is not read by the merge). */
 #define QSP_ATTN_STATIC_SCRATCH_BYTES ((size_t)16 << 20)
 int qsp_attn_verify_static(const qsp_attn_layer* layer, void* stream);
 

@@ -11,6 +11,7 @@ namespace qsp {
 int launch_attn_mma(const qsp_attn_layer& L, cudaStream_t st);
 int launch_attn_tma(const qsp_attn_layer& L, cudaStream_t st);
 int launch_attn_ws(const qsp_attn_layer& L, cudaStream_t st);
+int attn_ws_chunk(const qsp_attn_layer& L);
 
 // ------------------------------------------------------------------ prep
 // One CTA per token row m = b*T + t; warps loop over the q and k heads (one head per warp
@@ -193,7 +194,10 @@ __global__ void __launch_bounds__(128) attn_simt_kernel(const qsp_attn_layer L, 
 // One warp per (token row m, q head): the np partials (o unnormalised, m natural-log max,
 // l) of the row are merged with weights e^{m_p − M}, then σ(gate) is applied.
 template <typename T, int HD>
-__global__ void __launch_bounds__(256, 2) attn_combine_kernel(const qsp_attn_layer L, int np) {
+// np_all partials per row in the workspace; with split_len > 0 (the tensor-core kernel:
+// fixed-length key splits, two partials each) only the 2·ceil(kv_len / split_len) partials of
+// the row's sequence exist and only those are read.
+__global__ void __launch_bounds__(256, 2) attn_combine_kernel(const qsp_attn_layer L, int np_all, int split_len) {
   pdl_trigger();
   pdl_wait();
   const int lane = threadIdx.x & 31;
@@ -202,7 +206,12 @@ __global__ void __launch_bounds__(256, 2) attn_combine_kernel(const qsp_attn_lay
   const int m = pair / L.n_heads, hq = pair % L.n_heads;
   const int b = m / L.tokens, t = m % L.tokens;
   constexpr int hd = HD;
-  const float* base = L.partial + ((((int64_t)b * L.n_heads + hq) * L.tokens + t) * np) * (hd + 2);
+  const float* base = L.partial + ((((int64_t)b * L.n_heads + hq) * L.tokens + t) * np_all) * (hd + 2);
+  int np = np_all;
+  if (split_len > 0) {
+    const int kv_len = max(L.seq_lens[b] + L.tokens, 1);
+    np = min(np_all, 2 * ((kv_len + split_len - 1) / split_len));
+  }
   float M = -INFINITY;
   for (int p = lane; p < np; p += 32) M = fmaxf(M, base[(int64_t)p * (hd + 2) + hd]);
   M = warp_max(M);
@@ -280,14 +289,14 @@ static int attn_chunk(const qsp_attn_layer& L) {
 }
 
 template <typename T>
-static int launch_combine(const qsp_attn_layer& L, int np, cudaStream_t st) {
+static int launch_combine(const qsp_attn_layer& L, int np, cudaStream_t st, int split_len = 0) {
   const int pairs = L.batch * L.tokens * L.n_heads;
   const dim3 grid((pairs + 7) / 8);
   switch (L.head_dim) {   // validated: 32, 64, 128 or 256
-    case 32: return launch_pdl("qsp_attn_verify(combine)", attn_combine_kernel<T, 32>, grid, dim3(256), 0, st, L, np);
-    case 64: return launch_pdl("qsp_attn_verify(combine)", attn_combine_kernel<T, 64>, grid, dim3(256), 0, st, L, np);
-    case 128: return launch_pdl("qsp_attn_verify(combine)", attn_combine_kernel<T, 128>, grid, dim3(256), 0, st, L, np);
-    default: return launch_pdl("qsp_attn_verify(combine)", attn_combine_kernel<T, 256>, grid, dim3(256), 0, st, L, np);
+    case 32: return launch_pdl("qsp_attn_verify(combine)", attn_combine_kernel<T, 32>, grid, dim3(256), 0, st, L, np, split_len);
+    case 64: return launch_pdl("qsp_attn_verify(combine)", attn_combine_kernel<T, 64>, grid, dim3(256), 0, st, L, np, split_len);
+    case 128: return launch_pdl("qsp_attn_verify(combine)", attn_combine_kernel<T, 128>, grid, dim3(256), 0, st, L, np, split_len);
+    default: return launch_pdl("qsp_attn_verify(combine)", attn_combine_kernel<T, 256>, grid, dim3(256), 0, st, L, np, split_len);
   }
 }
 
@@ -386,7 +395,7 @@ int qsp_attn_verify(const qsp_attn_layer* layer, void* stream) {
   if (L.dtype == QSP_BF16) {
     // tensor-core path (head_dim 64/128/256); other shapes use the CUDA-core kernel below
     int rc2 = launch_attn_ws(L, st);
-    if (rc2 == QSP_OK) return launch_combine<__nv_bfloat16>(L, 2 * L.num_splits, st);
+    if (rc2 == QSP_OK) return launch_combine<__nv_bfloat16>(L, 2 * L.num_splits, st, attn_ws_chunk(L));
     if (rc2 == QSP_ERR_UNSUPPORTED) rc2 = launch_attn_mma(L, st);
     if (rc2 == QSP_OK) return launch_combine<__nv_bfloat16>(L, L.num_splits, st);
     if (rc2 != QSP_ERR_UNSUPPORTED) return rc2;

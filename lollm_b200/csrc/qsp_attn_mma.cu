@@ -734,6 +734,12 @@ struct At3Smem {
   static constexpr size_t BYTES = 1024 + RING + 2 * (size_t)QB + 256;
 };
 
+__host__ __device__ __forceinline__ int at3_chunk(const qsp_attn_layer& L) {
+  const int cap = L.max_pages * L.page_size;
+  const int chunk = (cap + L.num_splits - 1) / L.num_splits;
+  return ((chunk + AT2_KT - 1) / AT2_KT) * AT2_KT;
+}
+
 struct At3Item {
   int s, g, b, row0, nrows, k_begin, k_end, base_len;
 };
@@ -751,10 +757,13 @@ __device__ __forceinline__ At3Item at3_item(const qsp_attn_layer& L, int item, i
   w.nrows = min(AM_ROWS, nrep * L.tokens - w.row0);
   w.base_len = L.seq_lens[w.b];
   const int kv_len = w.base_len + L.tokens;
-  int chunk = (kv_len + L.num_splits - 1) / L.num_splits;
-  chunk = ((chunk + AT2_KT - 1) / AT2_KT) * AT2_KT;
+  // splits of a fixed length (the cache capacity over num_splits, whole 32-key tiles): a
+  // sequence uses ceil(kv_len / chunk) of them and the rest of its items are empty, so short
+  // sequences of a ragged batch write few partials; the last split takes any keys past the
+  // capacity (they have no pages and stay masked)
+  const int chunk = at3_chunk(L);
   w.k_begin = w.s * chunk;
-  w.k_end = min(kv_len, w.k_begin + chunk);
+  w.k_end = (w.s == L.num_splits - 1) ? kv_len : min(kv_len, w.k_begin + chunk);
   return w;
 }
 
@@ -856,22 +865,7 @@ attn_ws_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ 
   for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
     const At3Item w = at3_item(L, item, n_rg);
     const int64_t idx0 = ((int64_t)w.b * L.n_heads) * L.tokens;
-    if (w.k_begin >= w.k_end) {   // empty split: all-masked partials for both halves
-      if (kh == 0 && tq == 0) {
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int r = mt * 16 + gq + 8 * h;
-          if (r >= w.nrows) continue;
-          const int rr = w.row0 + r, t = rr / nrep, hq = w.g * nrep + rr % nrep;
-          for (int half = 0; half < 2; ++half) {
-            float* po = L.partial + ((idx0 + (int64_t)hq * L.tokens + t) * NP + 2 * w.s + half) * (HD + 2);
-            po[HD] = -INFINITY;
-            po[HD + 1] = 0.f;
-          }
-        }
-      }
-      continue;
-    }
+    if (w.k_begin >= w.k_end) continue;   // past the sequence's keys: the merge reads no partial of it
     int qpos[2];
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
@@ -1011,6 +1005,8 @@ attn_ws_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ 
 }
 
 int launch_attn_ws(const qsp_attn_layer& L, cudaStream_t st);
+
+int attn_ws_chunk(const qsp_attn_layer& L) { return at3_chunk(L); }
 
 int launch_attn_ws(const qsp_attn_layer& L, cudaStream_t st) {
   if (L.head_dim != 64 && L.head_dim != 128 && L.head_dim != 256) return QSP_ERR_UNSUPPORTED;

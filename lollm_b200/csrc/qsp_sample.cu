@@ -34,21 +34,40 @@ __device__ __forceinline__ ArgBest warp_argbest(ArgBest best) {
   return best;
 }
 
+// NaN-propagating running maxima (PTX max.NaN): they only tell whether a NaN was seen.
+__device__ __forceinline__ float fmax_nan(float a, float b) {
+  float d;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t bmax_nan2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("max.NaN.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
 // Block argmax of one row (blockDim = SEL_THREADS): the best (value, index), index LLONG_MAX
 // when no element compares (an all-NaN row). A 16-byte-aligned row is read with 16-byte
-// loads, four in flight per thread; the tail (and unaligned rows) element by element.
+// loads, four in flight per thread; the tail (and unaligned rows) element by element. Each
+// thread visits its elements in increasing index order, so a strict `>` keeps its first
+// maximum; threads combine with ties going to the smaller index. A NaN-propagating max runs
+// alongside; when the row holds a NaN (rare) the row is scanned again for its first NaN,
+// which is the result (torch.argmax ranks NaN above every number). vocab < 2^31.
 template <typename T>
 __device__ ArgBest row_argbest(const T* __restrict__ row, int64_t vocab) {
   __shared__ float sv[32];
   __shared__ long long si[32];
-  ArgBest best{-INFINITY, LLONG_MAX};
+  float bv = -INFINITY;
+  int bi = INT_MAX;
+  float nanmax = -INFINITY;
+  uint32_t nan2 = 0xff80ff80u;   // two bf16 -inf
   constexpr int EPV = 16 / (int)sizeof(T);
   int64_t done = 0;
   if ((reinterpret_cast<uintptr_t>(row) & 15) == 0) {
-    const int64_t nvec = vocab / EPV;
+    const int nvec = (int)(vocab / EPV);
     const uint4* rv = reinterpret_cast<const uint4*>(row);
-    const int64_t bd = blockDim.x;
-    for (int64_t v0 = threadIdx.x; v0 < nvec; v0 += 4 * bd) {
+    const int bd = blockDim.x;
+    for (int v0 = threadIdx.x; v0 < nvec; v0 += 4 * bd) {
       uint4 x[4];
 #pragma unroll
       for (int u = 0; u < 4; ++u)
@@ -60,23 +79,42 @@ __device__ ArgBest row_argbest(const T* __restrict__ row, int64_t vocab) {
         const uint32_t w[4] = {x[u].x, x[u].y, x[u].z, x[u].w};
         if constexpr (sizeof(T) == 4) {
 #pragma unroll
-          for (int e = 0; e < 4; ++e) f[e] = __uint_as_float(w[e]);
+          for (int e = 0; e < 4; ++e) {
+            f[e] = __uint_as_float(w[e]);
+            nanmax = fmax_nan(nanmax, f[e]);
+          }
         } else {
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             f[2 * e] = __uint_as_float(w[e] << 16);
             f[2 * e + 1] = __uint_as_float(w[e] & 0xffff0000u);
+            nan2 = bmax_nan2(nan2, w[e]);
           }
         }
-        const long long j0 = (v0 + u * bd) * EPV;
+        const int j0 = (v0 + u * bd) * EPV;
 #pragma unroll
-        for (int e = 0; e < EPV; ++e) best = arg_better(best, ArgBest{f[e], j0 + e});
+        for (int e = 0; e < EPV; ++e)
+          if (f[e] > bv) { bv = f[e]; bi = j0 + e; }
       }
     }
-    done = nvec * EPV;
+    done = (int64_t)nvec * EPV;
   }
-  for (int64_t j = done + threadIdx.x; j < vocab; j += blockDim.x)
-    best = arg_better(best, ArgBest{dt<T>::to_f(row[j]), (long long)j});
+  for (int64_t j = done + threadIdx.x; j < vocab; j += blockDim.x) {
+    const float f = dt<T>::to_f(row[j]);
+    nanmax = fmax_nan(nanmax, f);
+    if (f > bv) { bv = f; bi = (int)j; }
+  }
+  const bool has_nan = nanmax != nanmax || __uint_as_float(nan2 << 16) != __uint_as_float(nan2 << 16) ||
+                       __uint_as_float(nan2 & 0xffff0000u) != __uint_as_float(nan2 & 0xffff0000u);
+  ArgBest best{bv, bi == INT_MAX ? LLONG_MAX : (long long)bi};
+  if (__syncthreads_or(has_nan)) {   // rare: the first NaN of the row
+    long long first = LLONG_MAX;
+    for (int64_t j = threadIdx.x; j < vocab; j += blockDim.x) {
+      const float f = dt<T>::to_f(row[j]);
+      if (f != f) { first = j; break; }
+    }
+    best = ArgBest{__int_as_float(0x7fffffff), first};   // NaN, or (NaN, LLONG_MAX): no NaN here
+  }
   best = warp_argbest(best);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   if (lane == 0) { sv[warp] = best.v; si[warp] = best.i; }
@@ -572,7 +610,7 @@ size_t qsp_select_workspace_bytes(int64_t rows, int64_t vocab) {
 int qsp_argmax_rows(const void* logits, int64_t ld, int64_t rows, int64_t vocab, int64_t* out,
                     int64_t out_stride, int dtype, void* stream) {
   QSP_REQUIRE(logits && out && out_stride >= 1, "qsp_argmax_rows: null pointer / bad stride");
-  QSP_REQUIRE(rows >= 0 && rows < (1ll << 31) && vocab > 0 && ld >= vocab, "qsp_argmax_rows: bad shape");
+  QSP_REQUIRE(rows >= 0 && rows < (1ll << 31) && vocab > 0 && vocab < (1ll << 31) && ld >= vocab, "qsp_argmax_rows: bad shape");
   if (rows == 0) return QSP_OK;
   QSP_DISPATCH_DTYPE(dtype, T, { return launch_argmax<T>((const T*)logits, ld, rows, vocab, out, out_stride, as_stream(stream)); });
 }
@@ -582,7 +620,7 @@ int qsp_greedy_verify(const void* logits, int64_t ld, int32_t batch, int32_t tok
                       int64_t* next_tok, int64_t* argmax_out, float* workspace, int dtype,
                       void* stream) {
   QSP_REQUIRE(logits && accept_n && next_tok, "qsp_greedy_verify: null pointer");
-  QSP_REQUIRE(batch > 0 && tokens >= 1 && vocab > 0 && ld >= vocab, "qsp_greedy_verify: bad shape");
+  QSP_REQUIRE(batch > 0 && tokens >= 1 && vocab > 0 && vocab < (1ll << 31) && ld >= vocab, "qsp_greedy_verify: bad shape");
   QSP_REQUIRE(tokens == 1 || drafts != nullptr, "qsp_greedy_verify: drafts required when tokens > 1");
   int64_t* amax = argmax_out;
   if (amax == nullptr) {
@@ -605,7 +643,7 @@ int qsp_spec_sample(const void* target_logits, int64_t ld_t, const void* draft_l
                     int32_t* accept_n, int64_t* next_tok, float* workspace, int dtype,
                     void* stream) {
   QSP_REQUIRE(target_logits && accept_n && next_tok && u_resample && workspace, "qsp_spec_sample: null pointer");
-  QSP_REQUIRE(batch > 0 && k >= 0 && vocab > 0 && ld_t >= vocab, "qsp_spec_sample: bad shape");
+  QSP_REQUIRE(batch > 0 && k >= 0 && vocab > 0 && vocab < (1ll << 31) && ld_t >= vocab, "qsp_spec_sample: bad shape");
   QSP_REQUIRE(k == 0 || (draft_logits && drafts && u_accept && ld_d >= vocab), "qsp_spec_sample: drafts missing");
   QSP_REQUIRE(temperature > 0.f, "qsp_spec_sample: temperature must be > 0 (use qsp_greedy_verify)");
   const float inv_t = 1.0f / temperature;
@@ -631,7 +669,7 @@ int qsp_sample_rows(const void* logits, int64_t ld, int64_t rows, int64_t vocab,
                     const float* u, int64_t* out, int64_t out_stride, float* workspace, int dtype,
                     void* stream) {
   QSP_REQUIRE(logits && out, "qsp_sample_rows: null pointer");
-  QSP_REQUIRE(rows >= 0 && rows < (1ll << 31) && vocab > 0 && ld >= vocab, "qsp_sample_rows: bad shape");
+  QSP_REQUIRE(rows >= 0 && rows < (1ll << 31) && vocab > 0 && vocab < (1ll << 31) && ld >= vocab, "qsp_sample_rows: bad shape");
   if (rows == 0) return QSP_OK;
   if (temperature <= 0.f) return qsp_argmax_rows(logits, ld, rows, vocab, out, out_stride, dtype, stream);
   QSP_REQUIRE(u && workspace, "qsp_sample_rows: uniforms and workspace required");
@@ -688,7 +726,7 @@ int qsp_sample_filtered(const void* logits, int64_t ld, int64_t rows, int32_t ro
   int rc = check_params(params, "qsp_sample_filtered");
   if (rc) return rc;
   QSP_REQUIRE(logits && out && out_stride >= 1 && rows_per_seq >= 1, "qsp_sample_filtered: null pointer / bad stride");
-  QSP_REQUIRE(rows >= 0 && rows < (1ll << 31) && vocab > 0 && ld >= vocab, "qsp_sample_filtered: bad shape");
+  QSP_REQUIRE(rows >= 0 && rows < (1ll << 31) && vocab > 0 && vocab < (1ll << 31) && ld >= vocab, "qsp_sample_filtered: bad shape");
   if (rows == 0) return QSP_OK;
   const bool greedy = !(params->temperature > 0.f);
   QSP_REQUIRE(greedy || u != nullptr, "qsp_sample_filtered: uniforms required");
@@ -719,7 +757,7 @@ int qsp_spec_sample_filtered(const void* target_logits, int64_t ld_t, const void
   int rc = check_params(params, "qsp_spec_sample_filtered");
   if (rc) return rc;
   QSP_REQUIRE(target_logits && accept_n && next_tok, "qsp_spec_sample_filtered: null pointer");
-  QSP_REQUIRE(batch > 0 && k >= 0 && vocab > 0 && ld_t >= vocab, "qsp_spec_sample_filtered: bad shape");
+  QSP_REQUIRE(batch > 0 && k >= 0 && vocab > 0 && vocab < (1ll << 31) && ld_t >= vocab, "qsp_spec_sample_filtered: bad shape");
   QSP_REQUIRE(k == 0 || drafts != nullptr, "qsp_spec_sample_filtered: drafts missing");
   const bool greedy = !(params->temperature > 0.f);
   QSP_REQUIRE(greedy || (u_resample && (k == 0 || (draft_logits && u_accept && ld_d >= vocab))),

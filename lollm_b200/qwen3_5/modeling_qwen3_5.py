@@ -64,7 +64,8 @@ class _Workspace:
         self.act = e(M, max(inter, 1))
         moe_ws = max([lw["moe"].workspace_bytes(M) for lw in model.layers if "moe" in lw] + [0])
         self.moe_ws = torch.empty(moe_ws, dtype=torch.uint8, device=dev) if moe_ws else None
-        self.logits = e(M, cfg.vocab_size)
+        self._logits = None            # [M, vocab]: allocated on first use (a prompt prefill never needs it)
+        self._M, self._V, self._e = M, cfg.vocab_size, e
         self.last_x = e(B, H)
         self.last_xn = e(B, H)
         self.last_logits = e(B, cfg.vocab_size)
@@ -72,6 +73,12 @@ class _Workspace:
         self.num_splits = num_splits
         ws = K.attn_workspace_bytes(B, T, cfg.num_attention_heads, cfg.head_dim, num_splits)
         self.partial = torch.empty(max(ws // 4, 1), dtype=torch.float32, device=dev)
+
+    @property
+    def logits(self):
+        if self._logits is None:
+            self._logits = self._e(self._M, self._V)
+        return self._logits
 
 
 class Qwen3_5Model:
@@ -86,8 +93,9 @@ class Qwen3_5Model:
         dev = self.device
         g = lambda n: params[n].to(device=dev, dtype=dtype).contiguous()
         self.embed = g("model.embed_tokens.weight")
-        self.lm_head = self.embed if params["lm_head.weight"] is params["model.embed_tokens.weight"] \
-            else g("lm_head.weight")
+        tied = params.tied if hasattr(params, "tied") else \
+            params["lm_head.weight"] is params["model.embed_tokens.weight"]
+        self.lm_head = self.embed if tied else g("lm_head.weight")
         self.final_norm = g("model.norm.weight")
         self.layers = []
         for i in range(cfg.num_hidden_layers):

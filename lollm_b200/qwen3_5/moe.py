@@ -43,6 +43,8 @@ class SparseMoeBlock:
         self.w_in = w_in
         self.gate_up = g("mlp.experts.gate_up_proj")
         self.down = g("mlp.experts.down_proj")
+        # when set (a device int32 [E] tensor), every call adds its per-expert token counts to it
+        self.counts_probe = None
 
     def workspace_bytes(self, tokens: int) -> int:
         return int(L.load().qsp_moe_workspace_bytes(tokens, self.H, self.E, self.k, self.I, self.Is,
@@ -76,5 +78,7 @@ class SparseMoeBlock:
 
     def __call__(self, xn, x, norm_w, y, eps, tokens, workspace, expert_counts=None):
         """x[:tokens] += FFN(xn[:tokens]); y = RMSNorm(x)·(1+norm_w) when norm_w is given."""
+        if expert_counts is None:
+            expert_counts = self.counts_probe
         d = self.desc(xn, x, norm_w, y, eps, tokens, workspace, expert_counts)
         L.call("qsp_moe_ffn", C.byref(d), L.stream_handle())

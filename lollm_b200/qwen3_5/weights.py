@@ -127,6 +127,53 @@ def random_init(cfg: Qwen3_5Config, seed: int, *, dtype=torch.float32, device="c
     return out
 
 
+_M64 = (1 << 64) - 1
+
+
+def _s64(v: int) -> int:
+    """An unsigned 64-bit constant as the int64 torch stores (two's complement)."""
+    v &= _M64
+    return v - (1 << 64) if v >= (1 << 63) else v
+
+
+def _shr(x: torch.Tensor, s: int) -> torch.Tensor:
+    """Logical right shift of int64 lanes (torch's >> is arithmetic)."""
+    return (x >> s) & ((1 << (64 - s)) - 1)
+
+
+def counter_uniform(n: int, offset: int, seed: int, device, std: float = 0.02) -> torch.Tensor:
+    """n float32 values uniform in [-a, a) with a = std·√3 (standard deviation `std`), value i
+    from the splitmix64 hash of (seed, offset + i). Integer arithmetic only (int64 products
+    wrap identically everywhere), so the values are bit-identical on any CPU and on the GPU,
+    and any slice can be generated on its own."""
+    i = torch.arange(offset, offset + n, dtype=torch.int64, device=device)
+    x = i * _s64(0x9E3779B97F4A7C15) + _s64(seed * 0xD1B54A32D192ED03 + 0x632BE59BD9B4E019)
+    x = (x ^ _shr(x, 30)) * _s64(0xBF58476D1CE4E5B9)
+    x = (x ^ _shr(x, 27)) * _s64(0x94D049BB133111EB)
+    x = x ^ _shr(x, 31)
+    u = _shr(x, 40).to(torch.float32) * (1.0 / (1 << 24))          # 24 bits: exact in fp32
+    a = torch.tensor(std * (3.0 ** 0.5), dtype=torch.float32, device=device)   # one fp32 rounding, same everywhere
+    return (u * 2.0 - 1.0) * a
+
+
+def counter_init(cfg: Qwen3_5Config, seed: int, *, dtype=torch.float32, device="cpu", std: float = 0.02,
+                 with_mtp: bool = True, chunk: int = 1 << 26) -> dict:
+    """Seeded weights from `counter_uniform` (uniform with standard deviation `std`) as an
+    HF-named dict, every tensor the slice of one global counter stream in `param_specs` order.
+    Bit-identical on CPU and GPU: fixtures for multi-GB shapes are made on the host by running
+    the reference and rebuilt on the GPU in seconds."""
+    out, off = {}, 0
+    for name, shape in param_specs(cfg, with_mtp):
+        n = int(np.prod(shape))
+        t = torch.empty(n, dtype=dtype, device=device)
+        for c0 in range(0, n, chunk):
+            c1 = min(n, c0 + chunk)
+            t[c0:c1] = counter_uniform(c1 - c0, off + c0, seed, device, std).to(dtype)
+        out[to_raw(name)] = t.view(shape)
+        off += n
+    return out
+
+
 def load_checkpoint(cfg: Qwen3_5Config, weights: dict, *, with_mtp: bool = True,
                     device="cpu", dtype=None) -> dict:
     """Strict shape-checked load: {canonical_name: tensor on device}, lm_head re-tied."""
@@ -144,3 +191,108 @@ def load_checkpoint(cfg: Qwen3_5Config, weights: dict, *, with_mtp: bool = True,
     if cfg.tie_word_embeddings or "lm_head.weight" not in params:
         params["lm_head.weight"] = params["model.embed_tokens.weight"]
     return params
+
+
+# ─────────────────────────────────────── streaming load ───────────────────────────────────────
+
+class StreamingParams:
+    """{canonical name: tensor} that produces each tensor only when the model asks for it and
+    keeps no reference afterwards, so building a model holds at most one source tensor beyond
+    the model itself — the reference's meta-build-then-stream load (src/qwen3_5/weights.py:
+    40-70, mtp.py:171-189), for sources that do not fit twice in memory (the 48-layer MoE shape
+    is ~160 GB of bf16).
+
+    `fetch(raw_name) -> tensor` supplies the HF-named tensor. Every tensor is shape-checked
+    against `param_specs` when produced (RuntimeError on a mismatch or a missing name), then
+    cast to `dtype` and moved to `device`. `tied` says whether lm_head shares the embedding
+    (the model then reuses the embedding and never asks for lm_head).
+    """
+
+    def __init__(self, cfg: Qwen3_5Config, fetch, *, tied: bool, device=None, dtype=None,
+                 with_mtp: bool = True):
+        self.cfg, self._fetch, self.tied = cfg, fetch, bool(tied)
+        self.device, self.dtype = device, dtype
+        self._shapes = dict(param_specs(cfg, with_mtp))
+        if not self.tied:
+            self._shapes["lm_head.weight"] = (cfg.vocab_size, cfg.hidden_size)
+
+    def __contains__(self, name):
+        return name in self._shapes
+
+    def keys(self):
+        return self._shapes.keys()
+
+    def __getitem__(self, name: str) -> torch.Tensor:
+        if name == "lm_head.weight" and self.tied:
+            raise RuntimeError("qwen3_5: lm_head is tied to the embedding; use the embedding tensor")
+        if name not in self._shapes:
+            raise RuntimeError(f"qwen3_5: no parameter named {name}")
+        t = self._fetch(to_raw(name))
+        if t is None:
+            raise RuntimeError(f"qwen3_5: missing tensor for {name} (raw {to_raw(name)})")
+        if tuple(t.shape) != tuple(self._shapes[name]):
+            raise RuntimeError(f"qwen3_5: shape mismatch {name}: {tuple(t.shape)} vs {self._shapes[name]}")
+        if self.dtype is not None or self.device is not None:
+            t = t.to(device=self.device if self.device is not None else t.device,
+                      dtype=self.dtype if self.dtype is not None else t.dtype)
+        return t
+
+    # ---------------------------------------------------------------- sources
+    @classmethod
+    def from_dict(cls, cfg, weights: dict, *, consume: bool = True, **kw):
+        """An HF-named dict; with `consume` each tensor is popped as the model takes it (the
+        caller's dict shrinks as the model grows, as the reference's load does)."""
+        tied = cfg.tie_word_embeddings or "lm_head.weight" not in weights
+        fetch = (lambda raw: weights.pop(raw, None)) if consume else (lambda raw: weights.get(raw))
+        return cls(cfg, fetch, tied=tied, **kw)
+
+    @classmethod
+    def from_safetensors(cls, cfg, path: str, **kw):
+        """A safetensors checkpoint: one file, or a directory holding `model.safetensors` or a
+        sharded `model.safetensors.index.json`. Tensors are read one at a time."""
+        import json
+        import os
+        from safetensors import safe_open
+        if os.path.isdir(path):
+            idx = os.path.join(path, "model.safetensors.index.json")
+            if os.path.exists(idx):
+                wmap = json.load(open(idx))["weight_map"]
+                files = {raw: os.path.join(path, f) for raw, f in wmap.items()}
+            else:
+                path = os.path.join(path, "model.safetensors")
+                files = None
+        else:
+            files = None
+        if files is None:
+            with safe_open(path, framework="pt", device="cpu") as f:
+                files = {raw: path for raw in f.keys()}
+        handles = {}
+
+        def fetch(raw):
+            fn = files.get(raw)
+            if fn is None:
+                return None
+            if fn not in handles:
+                handles[fn] = safe_open(fn, framework="pt", device="cpu")
+            return handles[fn].get_tensor(raw)
+
+        tied = cfg.tie_word_embeddings or "lm_head.weight" not in files
+        return cls(cfg, fetch, tied=tied, **kw)
+
+    @classmethod
+    def random(cls, cfg, seed: int, *, device, dtype=torch.bfloat16, std: float = 0.02, **kw):
+        """Seeded N(0, std) tensors generated on `device` when asked for: each name has its own
+        generator seeded from (seed, the name's position in `param_specs`), so a tensor's values
+        do not depend on the order the model asks for them."""
+        order = {to_raw(n): i for i, (n, _) in enumerate(param_specs(cfg, True))}
+        shapes = {to_raw(n): s for n, s in param_specs(cfg, True)}
+
+        def fetch(raw):
+            if raw not in shapes:
+                return None
+            g = torch.Generator(device=device)
+            g.manual_seed(seed * 1_000_003 + order[raw])
+            t = torch.empty(shapes[raw], device=device, dtype=dtype)
+            return t.normal_(0.0, std, generator=g)
+
+        return cls(cfg, fetch, tied=cfg.tie_word_embeddings, device=device, dtype=dtype, **kw)

@@ -1,6 +1,7 @@
 """Whole-step parity on the GPU: the qsp model path (C ABI) against the reference's own
 outputs (golden fixtures) and the CPU oracle. fp32 logits within 1e-4 relative, bf16 within
-2e-2; greedy token streams token-identical; speculative streams equal the greedy stream."""
+2e-2 (tests/tolerance.py); greedy token streams token-identical; speculative streams equal the
+greedy stream."""
 
 import pytest
 import torch
@@ -9,10 +10,10 @@ from oracle import loops as OL
 from oracle import qwen35 as Q
 from lollm_b200.qwen3_5.config import MICRO, TINY, Qwen3_5Config
 from lollm_b200.qwen3_5.weights import load_checkpoint, random_init
+from tolerance import assert_close_dt
 
 pytestmark = pytest.mark.gpu
 SEED = 1234
-TOL = {torch.float32: dict(rtol=1e-4, atol=1e-4), torch.bfloat16: dict(rtol=2e-2, atol=2e-2)}
 
 
 def build(raw, dtype, **kw):
@@ -25,7 +26,7 @@ def build(raw, dtype, **kw):
 
 
 def close(got, want, dt):
-    torch.testing.assert_close(got.float().cpu(), want.float().cpu(), **TOL[dt])
+    assert_close_dt(got, want, dt)
 
 
 @pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16])

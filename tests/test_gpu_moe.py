@@ -17,11 +17,11 @@ from oracle import loops as OL
 from oracle import qwen35 as Q
 from lollm_b200.qwen3_5.config import MICRO_MOE, Qwen3_5Config
 from lollm_b200.qwen3_5.weights import load_checkpoint, random_init
+from tolerance import assert_close_dt
 
 pytestmark = pytest.mark.gpu
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 SEED = 1234
-TOL = {torch.float32: dict(rtol=1e-4, atol=1e-4), torch.bfloat16: dict(rtol=2e-2, atol=2e-2)}
 MOE_CASES = [
     ("shared", 128, 16, 4, 64, 64, True, 40),
     ("noshared", 128, 16, 4, 64, 0, True, 24),
@@ -82,7 +82,7 @@ def test_moe_block_matches_reference(golden_moe, case, dt):
     want = golden_moe[f"moe.{name}.{tag}.y"]
     ok = margins_ok(cfg, P, xn)
     assert int(ok.sum()) >= n - 2
-    torch.testing.assert_close(got[ok].float(), want[ok].float(), **TOL[dt])
+    assert_close_dt(got[ok].float(), want[ok].float(), dt)
     if bool(ok.all()):
         assert torch.equal(counts, oracle_counts(cfg, P, xn))
 
@@ -124,8 +124,8 @@ def test_moe_block_fused_residual_norm_matches_oracle(shape, dt):
     want_y = Q.rms_norm(want_x, nw, eps)
     ok = margins_ok(cfg, P, xn)
     assert int(ok.sum()) >= int(0.85 * m)
-    torch.testing.assert_close(got_x[ok].float(), want_x[ok].float(), **TOL[dt])
-    torch.testing.assert_close(got_y[ok].float(), want_y[ok].float(), **TOL[dt])
+    assert_close_dt(got_x[ok].float(), want_x[ok].float(), dt)
+    assert_close_dt(got_y[ok].float(), want_y[ok].float(), dt)
     if bool(ok.all()):
         assert torch.equal(counts, oracle_counts(cfg, P, xn))
     if skew is not None:
@@ -191,14 +191,14 @@ def test_micro_moe_forward_matches_reference(golden_moe, dt):
         else:
             ok = torch.ones(ids.shape, dtype=torch.bool)
         logits, cache, hidden = model(ids.cuda(), cache, return_hidden=True)
-        torch.testing.assert_close(logits.cpu()[ok].float(), G[f"{name}.logits"][ok].float(), **TOL[dt])
+        assert_close_dt(logits.cpu()[ok].float(), G[f"{name}.logits"][ok].float(), dt)
         n_cmp += int(ok.sum())
     assert n_cmp >= (30 if dt == torch.float32 else 12)
     ids = torch.zeros(2, 2, dtype=torch.int64, device="cuda")
     ids[:, 0] = G["decode.ids"][:, 0].cuda()
     h = G["mtp.draft_hidden"][:, 0].to(device="cuda", dtype=dt).contiguous()
     dl = mtp.draft(h, ids, 1)
-    torch.testing.assert_close(dl[:, 0].cpu().float(), G["mtp.draft_logits"][:, 0].float(), **TOL[dt])
+    assert_close_dt(dl[:, 0].cpu().float(), G["mtp.draft_logits"][:, 0].float(), dt)
 
 
 def test_micro_moe_all_experts_bf16_matches_oracle():
@@ -214,11 +214,11 @@ def test_micro_moe_all_experts_bf16_matches_oracle():
     cache = model.new_cache(3, 64)
     logits, _ = model(prompt.cuda(), cache)
     ol, oc, _ = Q.model_forward(P, cfg, prompt)
-    torch.testing.assert_close(logits.cpu().float(), ol.float(), **TOL[dt])
+    assert_close_dt(logits.cpu().float(), ol.float(), dt)
     ver = torch.randint(0, cfg.vocab_size, (3, 4), generator=g)
     logits, _ = model(ver.cuda(), cache)
     ol, oc, _ = Q.model_forward(P, cfg, ver, oc)
-    torch.testing.assert_close(logits.cpu().float(), ol.float(), **TOL[dt])
+    assert_close_dt(logits.cpu().float(), ol.float(), dt)
 
 
 @pytest.mark.parametrize("k", [1, 3])
