@@ -813,7 +813,14 @@ def run_attn_compare_workload(args):
                 the same expanded tensors (autotuned once before timing).
     The reference's GQA expansion (repeat_interleave of K and V, per call in the reference)
     is timed separately as `expand_ms` and not included in its attention time. HBM
-    roofline for every impl: the unexpanded K/V bytes, Σ_b (L+T)·2·256·2·2."""
+    roofline for every impl: the unexpanded K/V bytes, Σ_b (L+T)·2·256·2·2.
+
+    The reference's Triton kernel forms element offsets in 32-bit integers (b·stride_b with
+    stride_b = H·(L+T)·D, src/_triton_attn.py:64-65): once B·H·(L+T)·D reaches 2^31 they wrap
+    and the kernel reads outside its tensors (an illegal memory access here at L = 16384,
+    B = 64). Both reference paths are therefore called on batch slices that stay below that
+    bound (the reference would have to split the batch the same way), and their time is the
+    sum over the slices."""
     from lollm_b200 import _lib as L
     from lollm_b200 import kernels as K
     from lollm_b200.qwen3_5.modeling_qwen3_5 import rope_table
@@ -870,8 +877,15 @@ def run_attn_compare_workload(args):
         torch.cuda.synchronize()
         exp_ms = e0.elapsed_time(e1)
         import attention as RA
-        o_ref = RA.torch_attention(q, ke, ve)
-        sdpa = statistics.mean(timed_loop(lambda: RA.torch_attention(q, ke, ve), args.steps, args.warmup, stream))
+        per = max(1, min(B, ((1 << 31) - 1) // (nh * Lt * hd)))          # sequences per reference call
+        slices = [(i, min(B, i + per)) for i in range(0, B, per)]
+        print(f"attn_compare L={Lc}: reference calls of {per} sequences", file=sys.stderr, flush=True)
+
+        def sliced(fn):
+            return lambda: [fn(q[i:j], ke[i:j], ve[i:j]) for i, j in slices]
+
+        o_ref = torch.cat(sliced(RA.torch_attention)())
+        sdpa = statistics.mean(timed_loop(sliced(RA.torch_attention), args.steps, args.warmup, stream))
         # agreement of ours with the reference's SDPA output (ungated: ours applies σ(gate))
         gate = torch.sigmoid(qkv[:, :2 * nh * hd].reshape(B, T, nh, 2 * hd)[..., hd:].float())
         ours_o = out.view(B, T, nh, hd).float()
@@ -880,15 +894,16 @@ def run_attn_compare_workload(args):
         tri, tri_err = None, None
         try:
             from _triton_attn import flash_attention_kv
-            o_tri = flash_attention_kv(q, ke, ve)          # autotune + compile outside the timing
+            o_tri = torch.cat(sliced(flash_attention_kv)())   # autotune + compile outside the timing
             torch.cuda.synchronize()
-            tri = statistics.mean(timed_loop(lambda: flash_attention_kv(q, ke, ve), args.steps, args.warmup, stream))
+            tri = statistics.mean(timed_loop(sliced(flash_attention_kv), args.steps, args.warmup, stream))
             tri_err = float((o_tri.float() - o_ref.float()).abs().max())
         except Exception as e:  # noqa: BLE001
             tri = f"failed: {type(e).__name__}: {str(e)[:200]}"
         algo = B * Lt * nkv * hd * 2 * 2
         gbs = lambda ms: algo / (ms / 1000) / 1e9 if isinstance(ms, float) else None
-        rows.append({"L": Lc, "splits": splits, "ours_ms": ours, "sdpa_ms": sdpa, "triton_ms": tri,
+        rows.append({"L": Lc, "splits": splits, "ref_sequences_per_call": per, "ours_ms": ours, "sdpa_ms": sdpa,
+                     "triton_ms": tri,
                      "expand_ms": exp_ms, "ours_frac": gbs(ours) / hbm, "sdpa_frac": gbs(sdpa) / hbm,
                      "triton_frac": (gbs(tri) / hbm) if isinstance(tri, float) else None,
                      "max_abs_diff_ours_vs_sdpa": err, "max_abs_diff_triton_vs_sdpa": tri_err,
@@ -944,9 +959,11 @@ def run_moe_step_workload(args, ws, rank, local):
     from lollm_b200.qwen3_5.config import QWEN35_MOE, Qwen3_5Config
     from lollm_b200.qwen3_5.weights import StreamingParams
     dev = torch.device("cuda", local)
-    raw = dict(QWEN35_MOE)
+    raw = json.loads(json.dumps(QWEN35_MOE))
     if args.moe_layers:
-        raw["num_hidden_layers"] = args.moe_layers
+        tc = raw["text_config"]
+        tc["num_hidden_layers"] = args.moe_layers
+        tc["layer_types"] = tc["layer_types"][:args.moe_layers]
     cfg = Qwen3_5Config.from_hf(raw)
     t0 = time.perf_counter()
     k, T = args.k, args.k + 1
@@ -1062,6 +1079,47 @@ def run_moe_step_workload(args, ws, rank, local):
                          "frac": vb["total"] / (v_ms / 1000) / 1e9 / hbm, "peak_source": src, "traffic": None,
                          "algorithmic_bytes": vb, "verify_ms": v_ms},
             "prefill_s": prefill_s, "build_s": build_s, "setup_s": time.perf_counter() - t0}
+
+
+def run_prefill_workload(args):
+    """Prompt prefill of the 2B shape: `--batch` sequences of `--prompt` tokens
+    through the commit-all forward in chunks of `--prefill-chunk` (logits at each sequence's
+    last position only). Timed with CUDA events over the whole prefill, after one untimed
+    prefill of the same shape; reports prompt tokens per second."""
+    from lollm_b200.qwen3_5 import MTP, Qwen3_5Model, SpecDecoder
+    from lollm_b200.qwen3_5.config import QWEN35_2B, Qwen3_5Config
+    from lollm_b200.qwen3_5.weights import load_checkpoint, random_init
+    dev = torch.device("cuda", 0)
+    cfg = Qwen3_5Config.from_hf(QWEN35_2B)
+    params = load_checkpoint(cfg, random_init(cfg, 0, dtype=torch.bfloat16, device=dev, generator="torch"), device=dev)
+    model = Qwen3_5Model(cfg, params, dtype=torch.bfloat16, device=dev, max_positions=args.prompt + 64)
+    mtp = MTP(model, params)
+    del params
+    g = torch.Generator(device=dev)
+    g.manual_seed(5)
+    prompts = torch.randint(0, cfg.vocab_size, (args.batch, args.prompt), generator=g, device=dev)
+    ms = []
+    stream = torch.cuda.current_stream()
+    for rep in range(2):
+        dec = SpecDecoder(model, mtp, args.batch, args.k, args.prompt + 16, out_capacity=16)
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if args.profile and rep == 1:
+            torch.cuda.profiler.start()
+        a.record(stream)
+        dec.prefill(prompts, chunk=args.prefill_chunk)
+        b.record(stream)
+        torch.cuda.synchronize()
+        if args.profile and rep == 1:
+            torch.cuda.profiler.stop()
+        ms.append(a.elapsed_time(b))
+        del dec
+    toks = args.batch * args.prompt
+    return {"metric": "prompt prefill tok/s (2B shape, bf16)", "value": toks / (ms[-1] / 1000), "unit": "tok/s",
+            "n_gpus": 1, "steps": 1, "warmup": 1, "ms_per_step": ms[-1], "higher_is_better": True, "dtype": "bf16",
+            "data": "synthetic (seeded random-init weights, uniform random prompt ids)",
+            "config": {"workload": "prefill (configs[1] prompts)", "batch": args.batch, "prompt_len": args.prompt,
+                       "chunk": args.prefill_chunk}, "prefill_s": ms[-1] / 1000}
 
 
 def run_gemm_workload(args):
@@ -1204,7 +1262,7 @@ def main():
     ap.add_argument("--moe-layers", type=int, default=0, help="moe_step: fewer layers (0 = the 48 of configs[4])")
     ap.add_argument("--moe-reserve-gb", type=float, default=6.0,
                     help="moe_step: device memory kept free of wave state (workspaces)")
-    ap.add_argument("--workload", choices=["step", "gdn", "attn", "attn_compare", "gemm", "moe", "moe_step"],
+    ap.add_argument("--workload", choices=["step", "gdn", "attn", "attn_compare", "gemm", "moe", "moe_step", "prefill"],
                     default="step",
                     help="step: the speculative step (headline); gdn / attn: BASELINE configs[3] / [2] kernels "
                          "alone; attn_compare: configs[2] attention at equal lengths against the reference's "
@@ -1223,7 +1281,7 @@ def main():
     if args.workload != "step":
         torch.cuda.set_device(0)
         out = {"gdn": run_gdn_workload, "attn": run_attn_workload, "attn_compare": run_attn_compare_workload,
-               "gemm": run_gemm_workload, "moe": run_moe_workload}[args.workload](args)
+               "gemm": run_gemm_workload, "moe": run_moe_workload, "prefill": run_prefill_workload}[args.workload](args)
         print(json.dumps(out), flush=True)
         return
     if args.impl == "reference":

@@ -455,38 +455,45 @@ inline GdnRing gdn_ring(int batch, int Hv, int Ts, int DK, int DV, int esz) {
 
 // ------------------------------------------------------------------ prep
 // One CTA per (sequence b, key head kh): the q and k channels of kh and the v channels of its
-// v_per_k value heads. Every input (conv window, token rows, conv weights) is staged into
-// shared memory with cp.async first, so the CTA waits for global memory once. Arithmetic per
-// element is the reference's: conv accumulated in fp32 and rounded like F.conv1d, SiLU
-// rounded, l2norm x·rsqrt(Σx² + 1e-6) with each op rounded to the model dtype.
-// Dynamic shared memory: xr [K-1+T][nchg] T | cwr [nchg][K] T | qk [T][2·dk] fp32.
+// VPK value heads (a compile-time group shape, so every index below is shifts and adds).
+// Every input (conv window, token rows, conv weights) is staged into shared memory with
+// cp.async first, so the CTA waits for global memory once; results are assembled in shared
+// memory and written to the records with 16-byte stores. Arithmetic per element is the
+// reference's: conv accumulated in fp32 and rounded like F.conv1d, SiLU rounded, l2norm
+// x·rsqrt(Σx² + 1e-6) with each op rounded to the model dtype.
+// Dynamic shared memory: xr [K-1+T][nchg] T | cwr [nchg][K] T | qk [T][2·dk] fp32 |
+// yst [T][2·dk + VPK·dv] T (normalised q, k and the v outputs of each token, record order).
 inline size_t gdn_prep_smem(int nchg, int K, int T, int DK, int esz) {
+  const int Tm = T > 0 ? T : 1;
   size_t a = (size_t)(K - 1 + T) * nchg * esz;
   a = (a + 15) / 16 * 16;
   size_t b = (size_t)nchg * K * esz;
   b = (b + 15) / 16 * 16;
-  return a + b + (size_t)(T > 0 ? T : 1) * 2 * DK * 4;
+  return a + b + (size_t)Tm * 2 * DK * 4 + (size_t)Tm * nchg * esz;
 }
 
-template <typename T, int DK, int DV>
-__global__ void __launch_bounds__(256) gdn_prep_kernel(const qsp_gdn_layer L, const GdnRing RG) {
+template <typename T, int DK, int DV, int VPK>
+__global__ void __launch_bounds__(256, 8) gdn_prep_kernel(const qsp_gdn_layer L, const GdnRing RG) {
   pdl_trigger();
   pdl_wait();
   using RA = GdnRecA<T, DK, DV>;
   using RB = GdnRecB<T, DK, DV>;
   extern __shared__ __align__(16) uint8_t gdn_prep_raw[];
   constexpr int ESZ = (int)sizeof(T), EPV = 16 / ESZ;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
-  const int Hk = L.n_k_heads, Hv = L.n_v_heads, vpk = Hv / Hk;
+  constexpr int NCHG = 2 * DK + VPK * DV;   // q | k | v of the group
+  constexpr int CPR = NCHG / EPV;            // 16-byte chunks per row
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  constexpr int NW = 256 / 32;
+  const int Hk = L.n_k_heads, Hv = L.n_v_heads;
   const int b = blockIdx.x / Hk, kh = blockIdx.x % Hk;
   const int T_ = L.tokens, K = L.conv_kernel, Ts = L.max_spec_tokens;
   const int key_dim = Hk * DK, conv_dim = 2 * key_dim + Hv * DV, value_dim = Hv * DV;
-  const int nchg = 2 * DK + vpk * DV;
   const int nrows = K - 1 + T_;
   const bool spec = L.speculative != 0;
   T* xr = reinterpret_cast<T*>(gdn_prep_raw);
-  T* cwr = reinterpret_cast<T*>(gdn_prep_raw + ((size_t)nrows * nchg * ESZ + 15) / 16 * 16);
-  float* qk = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(cwr) + ((size_t)nchg * K * ESZ + 15) / 16 * 16);
+  T* cwr = reinterpret_cast<T*>(gdn_prep_raw + ((size_t)nrows * NCHG * ESZ + 15) / 16 * 16);
+  float* qk = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(cwr) + ((size_t)NCHG * K * ESZ + 15) / 16 * 16);
+  T* yst = reinterpret_cast<T*>(qk + (size_t)(T_ > 0 ? T_ : 1) * 2 * DK);
   const T* __restrict__ proj = static_cast<const T*>(L.proj);
   const T* __restrict__ cw = static_cast<const T*>(L.conv_w);
   T* hist = static_cast<T*>(L.conv_hist);
@@ -496,50 +503,47 @@ __global__ void __launch_bounds__(256) gdn_prep_kernel(const qsp_gdn_layer L, co
   const T* hin = hist + ((int64_t)par * L.batch + b) * hist_rows * conv_dim;
   T* hout = hist + ((int64_t)(par ^ 1) * L.batch + b) * hist_rows * conv_dim;
   uint8_t* ring = static_cast<uint8_t*>(L.pending);
-  // records of (value head hh, slot t) written by this call
-  auto recA = [&](int hh, int t) {
-    return reinterpret_cast<RA*>(ring + ((((int64_t)(par ^ 1) * L.batch + b) * Hv + hh) * Ts + t) * RG.recA);
-  };
-  auto recB = [&](int hh, int t) {
-    return reinterpret_cast<RB*>(ring + RG.offB + ((((int64_t)(par ^ 1) * L.batch + b) * Hv + hh) * Ts + t) * RG.recB);
-  };
+  // record (value head kh·VPK + g, slot t) written by this call: slot index (g·Ts + t) from
+  // the group's first record
+  const int64_t rec0 = (((int64_t)(par ^ 1) * L.batch + b) * Hv + (int64_t)kh * VPK) * Ts;
+  uint8_t* baseA = ring + rec0 * RG.recA;
+  uint8_t* baseB = ring + RG.offB + rec0 * RG.recB;
+  auto recA = [&](int g, int t) { return reinterpret_cast<RA*>(baseA + (int64_t)(g * Ts + t) * RG.recA); };
+  auto recB = [&](int g, int t) { return reinterpret_cast<RB*>(baseB + (int64_t)(g * Ts + t) * RG.recB); };
   // global channel of local channel c (q of kh | k of kh | v of the group's heads)
   auto gch = [&](int c) -> int {
-    return c < DK ? kh * DK + c : (c < 2 * DK ? key_dim + kh * DK + (c - DK) : 2 * key_dim + kh * vpk * DV + (c - 2 * DK));
+    return c < DK ? kh * DK + c : (c < 2 * DK ? key_dim + kh * DK + (c - DK) : 2 * key_dim + kh * VPK * DV + (c - 2 * DK));
   };
 
   // 1. stage: window rows, token rows, conv weights (16-byte chunks, all in flight)
-  const int cpr = nchg / EPV;   // chunks per row (segments are multiples of 16 bytes)
-  for (int e = tid; e < nrows * cpr; e += blockDim.x) {
-    const int i = e / cpr, c = (e % cpr) * EPV;
+  for (int e = tid; e < nrows * CPR; e += 256) {
+    const int i = e / CPR, c = (e % CPR) * EPV;
     const T* src = i < K - 1 ? hin + (int64_t)(coff + i) * conv_dim + gch(c)
                              : proj + (int64_t)(b * T_ + i - (K - 1)) * L.ld_proj + gch(c);
-    gcp16(xr + (int64_t)i * nchg + c, src);
+    gcp16(xr + i * NCHG + c, src);
   }
-  for (int e = tid; e < nchg * K / EPV; e += blockDim.x) {
+  for (int e = tid; e < NCHG * K / EPV; e += 256) {
     const int c = e * EPV / K;   // first channel of the chunk; a chunk never crosses a segment
-    gcp16(cwr + (int64_t)e * EPV, cw + (int64_t)gch(c) * K + (e * EPV - c * K));
+    gcp16(cwr + e * EPV, cw + (int64_t)gch(c) * K + (e * EPV - c * K));
   }
   asm volatile("cp.async.commit_group;" ::: "memory");
   // gates of the group's value heads (scalar loads, in flight with the copies)
-  float gate_d = 0.f, gate_b = 0.f;
-  int gate_t = -1, gate_h = 0;
-  if (tid < vpk * T_) {
-    gate_t = tid / vpk;
-    gate_h = kh * vpk + tid % vpk;
-    const T* prow = proj + (int64_t)(b * T_ + gate_t) * L.ld_proj + conv_dim + value_dim;
-    const float bb = dt<T>::to_f(prow[gate_h]), aa = dt<T>::to_f(prow[Hv + gate_h]);
-    const float A = -expf(dt<T>::to_f(static_cast<const T*>(L.a_log)[gate_h]));
-    const float dtb = dt<T>::to_f(static_cast<const T*>(L.dt_bias)[gate_h]);
-    gate_d = expf(A * softplusf_(aa + dtb));   // the per-token decay d = e^g
-    gate_b = dt<T>::round(sigmoidf_(bb));
+  if (tid < VPK * T_) {
+    const int t = tid / VPK, g = tid % VPK, hh = kh * VPK + g;
+    const T* prow = proj + (int64_t)(b * T_ + t) * L.ld_proj + conv_dim + value_dim;
+    const float bb = dt<T>::to_f(prow[hh]), aa = dt<T>::to_f(prow[Hv + hh]);
+    const float A = -expf(dt<T>::to_f(static_cast<const T*>(L.a_log)[hh]));
+    const float dtb = dt<T>::to_f(static_cast<const T*>(L.dt_bias)[hh]);
+    // the per-token decay d = e^g and β = σ(b)
+    recA(g, t)->db = make_float4(expf(A * softplusf_(aa + dtb)), dt<T>::round(sigmoidf_(bb)), 0.f, 0.f);
   }
   // output gate z of the group's heads: copied into the B records (16-byte chunks)
-  for (int e = tid; e < T_ * vpk * (DV / EPV); e += blockDim.x) {
-    const int t = e / (vpk * (DV / EPV)), r = e % (vpk * (DV / EPV));
-    const int hh = kh * vpk + r / (DV / EPV), c = (r % (DV / EPV)) * EPV;
-    *reinterpret_cast<uint4*>(recB(hh, t)->z + c) =
-        *reinterpret_cast<const uint4*>(proj + (int64_t)(b * T_ + t) * L.ld_proj + conv_dim + hh * DV + c);
+  constexpr int ZC = DV / EPV;
+  for (int e = tid; e < T_ * VPK * ZC; e += 256) {
+    const int t = e / (VPK * ZC), r = e % (VPK * ZC);
+    const int g = r / ZC, c = (r % ZC) * EPV;
+    *reinterpret_cast<uint4*>(recB(g, t)->z + c) =
+        *reinterpret_cast<const uint4*>(proj + (int64_t)(b * T_ + t) * L.ld_proj + conv_dim + (kh * VPK + g) * DV + c);
   }
   asm volatile("cp.async.wait_all;" ::: "memory");
   __syncthreads();
@@ -548,15 +552,15 @@ __global__ void __launch_bounds__(256) gdn_prep_kernel(const qsp_gdn_layer L, co
   //    commit keeps the window after the last token
   {
     const int r0 = spec ? 0 : T_, nr = spec ? nrows : K - 1;
-    for (int e = tid; e < nr * cpr; e += blockDim.x) {
-      const int i = e / cpr, c = (e % cpr) * EPV;
+    for (int e = tid; e < nr * CPR; e += 256) {
+      const int i = e / CPR, c = (e % CPR) * EPV;
       *reinterpret_cast<uint4*>(hout + (int64_t)i * conv_dim + gch(c)) =
-          *reinterpret_cast<const uint4*>(xr + (int64_t)(r0 + i) * nchg + c);
+          *reinterpret_cast<const uint4*>(xr + (r0 + i) * NCHG + c);
     }
   }
   // 3. conv + SiLU: a thread takes a pair of adjacent channels for every token (taps read
   //    once, paired loads and stores); per output the taps accumulate in order jj = 0..K-1
-  for (int cp = tid; cp < nchg / 2; cp += blockDim.x) {
+  for (int cp = tid; cp < NCHG / 2; cp += 256) {
     const int c = 2 * cp;
     float w0[GDN_KMAX], w1[GDN_KMAX];
 #pragma unroll
@@ -564,56 +568,67 @@ __global__ void __launch_bounds__(256) gdn_prep_kernel(const qsp_gdn_layer L, co
       w0[jj] = jj < K ? dt<T>::to_f(cwr[c * K + jj]) : 0.f;
       w1[jj] = jj < K ? dt<T>::to_f(cwr[(c + 1) * K + jj]) : 0.f;
     }
-    const bool isv = c >= 2 * DK;
-    const int vh = isv ? kh * vpk + (c - 2 * DK) / DV : 0, vc = isv ? (c - 2 * DK) % DV : 0;
     for (int t = 0; t < T_; ++t) {
       float a0 = 0.f, a1 = 0.f;
 #pragma unroll
       for (int jj = 0; jj < GDN_KMAX; ++jj) {
         if (jj < K) {
-          const T* xp = xr + (int64_t)(t + jj) * nchg + c;
+          const T* xp = xr + (t + jj) * NCHG + c;
           a0 = fmaf(w0[jj], dt<T>::to_f(xp[0]), a0);
           a1 = fmaf(w1[jj], dt<T>::to_f(xp[1]), a1);
         }
       }
       const float s0 = dt<T>::round(siluf_(dt<T>::round(a0)));
       const float s1 = dt<T>::round(siluf_(dt<T>::round(a1)));
-      if (!isv) {
+      if (c < 2 * DK) {
         *reinterpret_cast<float2*>(qk + t * 2 * DK + c) = make_float2(s0, s1);
       } else {
-        T* vp = recA(vh, t)->v + vc;
-        vp[0] = dt<T>::from_f(s0);
-        vp[1] = dt<T>::from_f(s1);
+        yst[t * NCHG + c] = dt<T>::from_f(s0);
+        yst[t * NCHG + c + 1] = dt<T>::from_f(s1);
       }
     }
   }
-  if (gate_t >= 0) recA(gate_h, gate_t)->db = make_float4(gate_d, gate_b, 0.f, 0.f);
   __syncthreads();
-  // 4. l2norm of q and k, one warp per vector
+  // 4. l2norm of q and k, one warp per vector; the model-dtype results go to yst (record
+  //    order q | k), the fp32 ones stay in qk for the Gram products (q scaled by dk^-0.5)
   const float qscale = (float)(1.0 / sqrt((double)DK));   // dk^-0.5 rounded once to fp32
-  for (int vi = warp; vi < 2 * T_; vi += nw) {
+  for (int vi = warp; vi < 2 * T_; vi += NW) {
     const int t = vi >> 1;
     const bool isk = vi & 1;
     float* xv = qk + t * 2 * DK + (isk ? DK : 0);
+    T* yv = yst + t * NCHG + (isk ? DK : 0);
     float ss = 0.f;
+#pragma unroll
     for (int i = lane; i < DK; i += 32) ss += dt<T>::round(xv[i] * xv[i]);
     ss = warp_sum(ss);
     const float sq = dt<T>::round(dt<T>::round(ss) + 1e-6f);
     const float r = dt<T>::round(rsqrtf(sq));
+#pragma unroll
     for (int i = lane; i < DK; i += 32) {
       const float y = dt<T>::round(xv[i] * r);
-      const T yt = dt<T>::from_f(y);
-      for (int g = 0; g < vpk; ++g) {
-        if (isk) recA(kh * vpk + g, t)->k[i] = yt;
-        else recB(kh * vpk + g, t)->q[i] = yt;
-      }
+      yv[i] = dt<T>::from_f(y);
       xv[i] = isk ? y : y * qscale;
     }
   }
   __syncthreads();
-  // 5. Gram products of the call's tokens (fixed summation order: they are replayed later)
+  // 5. records: k̂ and v into the A records, q̂ into the B records (16-byte chunks; k̂ and q̂
+  //    belong to the key head and are repeated in each of its value heads' records)
+  {
+    constexpr int QC = DK / EPV, VC = DV / EPV, PER = 2 * QC + VC;   // chunks per (head, token)
+    for (int e = tid; e < T_ * VPK * PER; e += 256) {
+      const int t = e / (VPK * PER), r = e % (VPK * PER);
+      const int g = r / PER, j = r % PER;
+      const T* src;
+      T* dst;
+      if (j < QC) { src = yst + t * NCHG + j * EPV; dst = recB(g, t)->q + j * EPV; }
+      else if (j < 2 * QC) { src = yst + t * NCHG + DK + (j - QC) * EPV; dst = recA(g, t)->k + (j - QC) * EPV; }
+      else { src = yst + t * NCHG + 2 * DK + g * DV + (j - 2 * QC) * EPV; dst = recA(g, t)->v + (j - 2 * QC) * EPV; }
+      *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
+    }
+  }
+  // 6. Gram products of the call's tokens (fixed summation order: they are replayed later)
   const int nkk = T_ * (T_ - 1) / 2, nkq = T_ * (T_ + 1) / 2;
-  for (int e = warp; e < nkk + nkq; e += nw) {
+  for (int e = warp; e < nkk + nkq; e += NW) {
     int s, t;
     const bool isq = e >= nkk;
     if (!isq) {   // pairs s < t, t = 1..T-1
@@ -630,11 +645,12 @@ __global__ void __launch_bounds__(256) gdn_prep_kernel(const qsp_gdn_layer L, co
     const float* ks = qk + s * 2 * DK + DK;
     const float* o = qk + t * 2 * DK + (isq ? 0 : DK);
     float acc = 0.f;
+#pragma unroll
     for (int i = lane; i < DK; i += 32) acc = fmaf(ks[i], o[i], acc);
     acc = warp_sum(acc);
-    if (lane < vpk) {
-      if (isq) recB(kh * vpk + lane, t)->gkq[s] = acc;
-      else recA(kh * vpk + lane, t)->gkk[s] = acc;
+    if (lane < VPK) {
+      if (isq) recB(lane, t)->gkq[s] = acc;
+      else recA(lane, t)->gkk[s] = acc;
     }
   }
 }
@@ -1048,12 +1064,15 @@ static int launch_gdn_dims(const qsp_gdn_layer& L, cudaStream_t st) {
   if (L.tokens <= L.max_spec_tokens) {
     const int nchg = 2 * DK + (L.n_v_heads / L.n_k_heads) * DV;
     const size_t psmem = gdn_prep_smem(nchg, L.conv_kernel, L.tokens, DK, (int)sizeof(T));
-    auto prep = gdn_prep_kernel<T, DK, DV>;
-    static size_t prep_set = 0;
-    if (psmem > prep_set) {
+    const int vpk = L.n_v_heads / L.n_k_heads;
+    auto prep = vpk == 1 ? gdn_prep_kernel<T, DK, DV, 1> : (vpk == 2 ? gdn_prep_kernel<T, DK, DV, 2> : gdn_prep_kernel<T, DK, DV, 4>);
+    if (vpk != 1 && vpk != 2 && vpk != 4)
+      return set_error(QSP_ERR_UNSUPPORTED, "qsp_gdn_verify: %d value heads per key head not built (1, 2 or 4)", vpk);
+    static size_t prep_set[5] = {0, 0, 0, 0, 0};
+    if (psmem > prep_set[vpk]) {
       if (cudaFuncSetAttribute(prep, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)psmem) != cudaSuccess)
         return set_error(QSP_ERR_CUDA, "qsp_gdn_verify: cannot reserve %zu bytes of shared memory", psmem);
-      prep_set = psmem;
+      prep_set[vpk] = psmem;
     }
     rc = launch_pdl("qsp_gdn_verify(prep)", prep, dim3(L.batch * L.n_k_heads), dim3(256), psmem, st, L, RG);
     if (rc) return rc;
