@@ -203,13 +203,17 @@ class Qwen3_5Model:
         return ws.last_logits, ws.last_x
 
     def _forward_into(self, ids, cache: Qwen3_5Cache, B: int, T: int, speculative: bool,
-                      last_only: bool = False):
+                      last_only: bool = False, trace: list | None = None):
+        """The forward's launches into the workspace. `trace` (tests): a list that receives a
+        copy of the residual stream after the embedding and after every mixer and FFN."""
         cfg = self.cfg
         ws = self.workspace(B, T, cache)
         M = B * T
         eps = cfg.rms_norm_eps
         K.embed(ids, self.embed, ws.x, rows=M, bad=cache.bad_index)
         K.rmsnorm(ws.x, self.layers[0]["in_norm"], ws.xn, eps, rows=M)
+        if trace is not None:
+            trace.append(ws.x[:M].clone())
         n_layers = len(self.layers)
         for i, lw in enumerate(self.layers):
             # ws.xn holds input_layernorm(x) of this layer (fused into the previous residual add)
@@ -227,16 +231,20 @@ class Qwen3_5Model:
                                    lw["dt_bias"], lw["norm_w"], None, ws.core, speculative)
                 K.gdn_verify(d)
                 K.gemm_residual_rmsnorm(ws.core, lw["out_proj"], ws.x, lw["post_norm"], ws.xn, eps, m=M)
+            if trace is not None:
+                trace.append(ws.x[:M].clone())
             # residual add + the next norm: next layer's input_layernorm, or the final norm
             nxt = self.layers[i + 1]["in_norm"] if i + 1 < n_layers else (None if last_only else self.final_norm)
             if "moe" in lw:
                 lw["moe"](ws.xn, ws.x, nxt, ws.xn, eps, M, ws.moe_ws)
-                continue
-            K.gemm_swiglu(ws.xn, lw["w_gu"], ws.act, ws.gu, m=M)
-            if nxt is not None:
-                K.gemm_residual_rmsnorm(ws.act, lw["down"], ws.x, nxt, ws.xn, eps, m=M)
             else:
-                K.gemm(ws.act, lw["down"], ws.x, accumulate=True, m=M)
+                K.gemm_swiglu(ws.xn, lw["w_gu"], ws.act, ws.gu, m=M)
+                if nxt is not None:
+                    K.gemm_residual_rmsnorm(ws.act, lw["down"], ws.x, nxt, ws.xn, eps, m=M)
+                else:
+                    K.gemm(ws.act, lw["down"], ws.x, accumulate=True, m=M)
+            if trace is not None:
+                trace.append(ws.x[:M].clone())
         if last_only:
             K.select_rows(ws.x, B, T, ws.last_idx, ws.last_x)
             K.rmsnorm(ws.last_x, self.final_norm, ws.last_xn, eps, rows=B)

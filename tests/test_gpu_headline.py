@@ -4,9 +4,12 @@ grids the benchmark times, checked against the CPU oracle.
 * One speculative step of the full 24-layer 2B-shape model in bf16 at batch 64 with ragged
   contexts around 2048 (the bench's 296-CTA GDN grid over 64x32 heads, its attention split
   count and the vocabulary K-split tail at 151936). The oracle recomputes 8 of the 64
-  sequences (they are independent): MTP draft logits at every depth, verify logits,
-  greedy acceptance with drafts planted to be accepted 0..3 times, the cache after the
-  index rollback, and the logits of the next decode.
+  sequences (they are independent): MTP draft logits at every depth; every mixer and FFN of
+  the verify forward on the GPU's own inputs (bf16 rounding differences of one step per
+  block add up over 24 layers to ~3 % of the largest logit at random init, so blocks are
+  compared one at a time and the end-to-end drift only bounded); greedy acceptance of drafts
+  planted to be accepted 0..3 times; the committed GDN states after the index rollback; and
+  the decode after it, block by block from the kept-token state.
 * The verify attention at configs[2] lengths (up to 32768 keys) at the bench's split count.
 * The GDN update at configs[3] shape (64 sequences, 16 key / 32 value heads of 128) with a
   ragged rollback checked bit for bit against fresh forwards over the kept tokens.
@@ -89,8 +92,52 @@ def filled_cache(cfg, model, B, lens, seed):
     return cache, oc
 
 
+def _teacher_forced(P, cfg, trace, rows, T, oc, what, keep=None):
+    """Check one traced GPU forward block by block against the oracle fed the GPU's own
+    inputs: layer i's mixer runs on the GPU's residual stream entering layer i, its FFN on the
+    GPU's stream after the mixer, the logits on the GPU's final stream. Every block must then
+    match to bf16 rounding, whatever the drift accumulated over the layers before it. `oc`
+    (the oracle cache of the SUBSET, updated in place) supplies the K/V and GDN state the
+    blocks start from; with `keep` the GDN states and K/V are left as after only the first
+    keep[j] tokens of sequence j (the rollback). Returns the last stream (S, T, H)."""
+    eps = cfg.rms_norm_eps
+    S = len(rows)
+    xs = [t.view(-1, T, t.shape[-1])[rows].cpu() for t in trace]
+    positions = torch.stack([torch.arange(n, n + T) for n in oc.lens])
+    for i in range(cfg.num_hidden_layers):
+        pre = f"model.layers.{i}."
+        x_in, x_mid, x_out = xs[2 * i], xs[2 * i + 1], xs[2 * i + 2]
+        h = Q.rms_norm(x_in, P[pre + "input_layernorm.weight"], eps)
+        if cfg.layer_type(i) == "full_attention":
+            o, kv = Q.attn_mixer(P, pre + "self_attn.", cfg, h, positions, oc.kv.get(i))
+            oc.kv[i] = kv if keep is None else [(k_[:, :n + keep[j]], v_[:, :n + keep[j]])
+                                                for j, ((k_, v_), n) in enumerate(zip(kv, oc.lens))]
+        else:
+            o, st = Q.gdn_mixer(P, pre + "linear_attn.", cfg, h, oc.gdn.get(i))
+            if keep is None:
+                oc.gdn[i] = st
+            else:   # the state after only the kept tokens of each sequence
+                convs, recs = [], []
+                for j in range(S):
+                    _, (cv, rc) = Q.gdn_mixer(P, pre + "linear_attn.", cfg, h[j:j + 1, :keep[j]],
+                                              (oc.gdn[i][0][j:j + 1], oc.gdn[i][1][j:j + 1]))
+                    convs.append(cv)
+                    recs.append(rc)
+                oc.gdn[i] = (torch.cat(convs), torch.cat(recs))
+        assert_bf16_close(x_mid, x_in + o, what=f"{what}: layer {i} mixer")
+        f = Q.ffn(P, pre, cfg, Q.rms_norm(x_mid, P[pre + "post_attention_layernorm.weight"], eps))
+        assert_bf16_close(x_out, x_mid + f, what=f"{what}: layer {i} FFN")
+    oc.lens = [n + (T if keep is None else keep[j]) for j, n in enumerate(oc.lens)]
+    return xs[-1]
+
+
 def test_two_b_speculative_step_matches_oracle(two_b):
+    """One speculative step of the production configuration, checked block by block (each
+    mixer and FFN of all 24 layers on the GPU's own inputs, so bf16 rounding differences do
+    not compound into the comparison), plus the end-to-end drift, the greedy acceptance of
+    drafts planted to be accepted 0..3 times, the index rollback and the decode after it."""
     cfg, model, mtp, P = two_b
+    from lollm_b200 import kernels as K
     B, k = 64, 3
     T = k + 1
     g = torch.Generator().manual_seed(11)
@@ -101,7 +148,7 @@ def test_two_b_speculative_step_matches_oracle(two_b):
     ids = torch.zeros(B, T, dtype=torch.int64, device=DEV)
     ids[:, 0] = pending.to(DEV)
     sub = torch.tensor(SUBSET)
-    flagged = []
+    rows = sub.to(DEV)
 
     # ---- MTP drafts (depth 1..k): logits per depth, the oracle fed the GPU's drafted tokens
     dl = mtp.draft(hidden_last.to(DEV).contiguous(), ids, k).cpu()
@@ -111,83 +158,75 @@ def test_two_b_speculative_step_matches_oracle(two_b):
         post, pre = Q.mtp_forward(P, cfg, h, emb)
         want = Q.lm_head(P, post)[:, 0]
         assert_bf16_close(dl[sub, d], want, what=f"draft logits depth {d + 1}")
-        got_tok = ids[sub.to(DEV), d + 1].cpu()
+        got_tok = ids[rows, d + 1].cpu()
         for j, b in enumerate(SUBSET):
             if not near_tie(want[j]):
                 assert int(got_tok[j]) == int(want[j].float().argmax()), f"draft depth {d + 1}, sequence {b}"
         h, tok = pre, got_tok
 
-    # ---- plant drafts the target accepts a_b times (a_b = 0..3) for the SUBSET sequences
-    plan = [j % (k + 1) for j in range(len(SUBSET))]
-    chain = oc.clone()
-    cur = pending[sub]
-    planted = torch.zeros(len(SUBSET), k, dtype=torch.int64)
+    # ---- plant drafts accepted a_b = 0..3 times: the target's own pick at the accepted
+    #      positions (found by verify passes on copies of the cache; the kernels are
+    #      deterministic, so the real pass repeats those picks), a different token after
+    plan = [j % (k + 1) for j in range(B)]
+    planv = torch.tensor(plan, device=DEV)
     for d in range(k):
-        lg, chain, _ = Q.model_forward(P, cfg, cur[:, None], chain)
-        best = lg[:, 0].float().argmax(-1)
-        for j in range(len(SUBSET)):
-            if near_tie(lg[j, 0]):
-                flagged.append(("plant", SUBSET[j], d))
-        # accepted positions carry the target's pick; the first rejected one a different token
-        planted[:, d] = torch.where(torch.tensor(plan) > d, best, (best + 1) % cfg.vocab_size)
-        cur = planted[:, d]
-    ids[sub.to(DEV), 1:] = planted.to(DEV)
+        c2 = cache.clone()
+        ws = model._forward_into(ids, c2, B, T, True)
+        best = ws.logits.view(B, T, -1)[:, d].float().argmax(-1)
+        ids[:, d + 1] = torch.where(planv > d, best, (best + 1) % cfg.vocab_size)
+        del c2
+        torch.cuda.empty_cache()
 
-    # ---- the speculative verify forward (all 64 sequences) against the oracle
-    ws = model._forward_into(ids, cache, B, T, True)
+    # ---- the speculative verify forward, traced, checked block by block
+    trace = []
+    ws = model._forward_into(ids, cache, B, T, True, trace=trace)
     logits = ws.logits.view(B, T, -1)
-    ol, _, _ = Q.model_forward(P, cfg, ids[sub.to(DEV)].cpu(), oc.clone())
-    assert_bf16_close(logits[sub.to(DEV)], ol, what="verify logits")
+    oc_v = oc.clone()
+    x_last = _teacher_forced(P, cfg, trace, rows, T, oc_v, "verify")
+    lg_tf = Q.lm_head(P, Q.rms_norm(x_last, P["model.norm.weight"], cfg.rms_norm_eps))
+    assert_bf16_close(logits[rows], lg_tf, what="verify logits (final stream)")
+    # end to end: the oracle's own 24 layers from the same cache. bf16 rounding differences
+    # of one step per block accumulate over the residual stream (measured: ~3 % of the
+    # largest logit after 24 layers at random init), so this bound only catches gross errors
+    ol, _, _ = Q.model_forward(P, cfg, ids[rows].cpu(), oc.clone())
+    drift = float((logits[rows].float().cpu() - ol.float()).abs().max() / ol.float().abs().max())
+    assert drift < 0.1, f"end-to-end logits drift {drift:.3f} of the largest logit"
 
     # ---- greedy acceptance (exact match) and the next token
     accept_n = torch.zeros(B, dtype=torch.int32, device=DEV)
     next_tok = torch.zeros(B, dtype=torch.int64, device=DEV)
     amax = torch.zeros(B * T, dtype=torch.int64, device=DEV)
-    from lollm_b200 import kernels as K
     K.greedy_verify(ws.logits, B, T, ids[:, 1:], T, accept_n, next_tok, amax)
     acc = accept_n.cpu()
     nxt = next_tok.cpu()
-    clean = []
+    assert acc.tolist() == plan, "accepted counts differ from the planted drafts"
+    am = logits.float().argmax(-1).cpu()            # torch's argmax of the same logits
+    assert torch.equal(am.flatten(), amax.cpu())
+    assert nxt.tolist() == [int(am[b, plan[b]]) for b in range(B)]
+    # and the reference's picks from the same final stream (off near-ties)
     for j, b in enumerate(SUBSET):
-        tie = any(near_tie(ol[j, t]) for t in range(plan[j] + 1))
-        if tie or any(f[1] == b for f in flagged):
-            flagged.append(("verify", b))
-            continue
-        clean.append(j)
-        assert int(acc[b]) == plan[j], f"sequence {b}: accepted {int(acc[b])}, planted {plan[j]}"
-        assert int(nxt[b]) == int(ol[j, plan[j]].float().argmax())
-    assert len(clean) >= len(SUBSET) - 2, f"too many near-ties: {flagged}"
-    # every sequence: the accepted count is the matched prefix of its own argmax row
-    am = amax.view(B, T).cpu()
-    idc = ids.cpu()
-    for b in range(B):
-        a = 0
-        while a < k and int(idc[b, a + 1]) == int(am[b, a]):
-            a += 1
-        assert int(acc[b]) == a and int(nxt[b]) == int(am[b, a])
+        for t in range(plan[b] + 1):
+            if not near_tie(lg_tf[j, t]):
+                assert int(am[b, t]) == int(lg_tf[j, t].float().argmax()), f"sequence {b} position {t}"
 
     # ---- rollback by index, then one decode step from the kept tokens
     cache.accept(accept_n)
     keep = (acc + 1).tolist()
     assert cache.seq_lens.cpu().tolist() == [lens[b] + keep[b] for b in range(B)]
-    per = []
-    for j, b in enumerate(SUBSET):
-        s1 = OL._select(oc, j)
-        _, s1, _ = Q.model_forward(P, cfg, idc[b:b + 1, :keep[b]], s1)
-        per.append(s1)
-    oc2 = OL._merge(per, cfg.num_hidden_layers)
-    dec = nxt[:, None].to(DEV)
-    logits2, _ = model(dec, cache)
-    ol2, oc2, _ = Q.model_forward(P, cfg, nxt[sub][:, None], oc2)
-    # (the oracle keeps exactly the GPU's accepted prefix, so every SUBSET row compares)
-    assert_bf16_close(logits2[sub.to(DEV)], ol2, what="decode logits after rollback")
-    # the committed GDN state (pending updates flushed) of the first and last GDN layers
-    for i in (cfg.gdn_layers[0], cfg.gdn_layers[-1]):
+    oc_r = oc.clone()
+    _teacher_forced(P, cfg, trace, rows, T, oc_r, "verify (kept tokens)", keep=[keep[b] for b in SUBSET])
+    # the committed GDN states (pending updates flushed) equal the kept-token states
+    for i in cfg.gdn_layers:
         conv, rec = cache.linear_state(i)
-        assert_bf16_close(rec[sub.to(DEV)], oc2.gdn[i][1], what=f"GDN state layer {i}")
-        assert_bf16_close(conv[sub.to(DEV)], oc2.gdn[i][0], what=f"conv window layer {i}")
+        assert_bf16_close(rec[rows], oc_r.gdn[i][1], what=f"GDN state layer {i}")
+        assert_bf16_close(conv[rows], oc_r.gdn[i][0], what=f"conv window layer {i}")
+    trace2 = []
+    ws2 = model._forward_into(nxt[:, None].to(DEV).contiguous(), cache, B, 1, False, trace=trace2)
+    x2 = _teacher_forced(P, cfg, trace2, rows, 1, oc_r, "decode after rollback")
+    lg2 = Q.lm_head(P, Q.rms_norm(x2, P["model.norm.weight"], cfg.rms_norm_eps))
+    assert_bf16_close(ws2.logits.view(B, 1, -1)[rows], lg2, what="decode logits after rollback")
     assert int(cache.bad_index) == 0 and K.device_status() == 0
-    print(f"near-ties flagged: {flagged}")
+    print(f"end-to-end verify logits drift: {drift:.4f} of the largest logit")
 
 
 @pytest.mark.parametrize("splits", [64, 5])
