@@ -15,7 +15,8 @@
 //                     delta rule, so nothing is reduced across threads except the gated
 //                     RMSNorm of the output.
 // Longer commit calls (prefill) replay the kept tokens with gdn_chunk_kernel, then run
-// gdn_seq_kernel, which steps token by token through blocks of 8.
+// gdn_prefill_kernel, which applies the tokens in blocks of 8 with the same chunked update,
+// computing each block's conv, gates, l2norm and Gram products itself.
 //
 // HBM traffic is one state read plus (when the state changes) one write per head and call —
 // the algorithmic minimum of the recurrence. Rollback by index: see include/qsp.h.
@@ -50,103 +51,6 @@ __device__ __forceinline__ uint64_t fmul2(uint64_t a, uint64_t b) {
   asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
 }
-__device__ __forceinline__ float2 shfl_add2(float2 v, int o) {
-  v.x = __fadd_rn(v.x, __shfl_xor_sync(0xffffffffu, v.x, o));
-  v.y = __fadd_rn(v.y, __shfl_xor_sync(0xffffffffu, v.y, o));
-  return v;
-}
-
-// One state update S ← S·e^g; δ = (v − Sᵀk)·β; S ← S + k δᵀ, on packed column pairs. The
-// thread's state is S2[2i] = columns (4cg, 4cg+1), S2[2i+1] = (4cg+2, 4cg+3) of row 4i+rg.
-// kd holds k duplicated as (k, k) pairs. Every operation is an explicitly rounded IEEE op, so
-// the arithmetic is identical wherever this is inlined (the replay of kept tokens reproduces
-// the original forward bit for bit).
-template <int RPT>
-__device__ __forceinline__ void gdn_update(uint64_t (&S2)[2 * RPT], const float2* __restrict__ kd,
-                                           const float* __restrict__ vvec, float g, float beta, int rg, int cg) {
-  const float d = expf(g);
-  const uint64_t dd = pk2(d, d);
-  uint64_t a0 = 0, a1 = 0, b0 = 0, b1 = 0;   // (0.f, 0.f); even rows → a, odd rows → b
-#pragma unroll
-  for (int i = 0; i < RPT; ++i) {
-    const float2 kr = kd[4 * i + rg];
-    const uint64_t kk = *reinterpret_cast<const uint64_t*>(&kr);
-    S2[2 * i] = fmul2(S2[2 * i], dd);
-    S2[2 * i + 1] = fmul2(S2[2 * i + 1], dd);
-    if (i & 1) {
-      b0 = ffma2(S2[2 * i], kk, b0);
-      b1 = ffma2(S2[2 * i + 1], kk, b1);
-    } else {
-      a0 = ffma2(S2[2 * i], kk, a0);
-      a1 = ffma2(S2[2 * i + 1], kk, a1);
-    }
-  }
-  float2 kv0 = upk2(a0), kv1 = upk2(a1);
-  {
-    const float2 o0 = upk2(b0), o1 = upk2(b1);
-    kv0 = make_float2(__fadd_rn(kv0.x, o0.x), __fadd_rn(kv0.y, o0.y));
-    kv1 = make_float2(__fadd_rn(kv1.x, o1.x), __fadd_rn(kv1.y, o1.y));
-  }
-  kv0 = shfl_add2(kv0, 8);
-  kv1 = shfl_add2(kv1, 8);
-  kv0 = shfl_add2(kv0, 16);
-  kv1 = shfl_add2(kv1, 16);
-  const float4 vv = *reinterpret_cast<const float4*>(vvec + 4 * cg);
-  const uint64_t dl0 = pk2(__fmul_rn(__fsub_rn(vv.x, kv0.x), beta), __fmul_rn(__fsub_rn(vv.y, kv0.y), beta));
-  const uint64_t dl1 = pk2(__fmul_rn(__fsub_rn(vv.z, kv1.x), beta), __fmul_rn(__fsub_rn(vv.w, kv1.y), beta));
-#pragma unroll
-  for (int i = 0; i < RPT; ++i) {
-    const float2 kr = kd[4 * i + rg];
-    const uint64_t kk = *reinterpret_cast<const uint64_t*>(&kr);
-    S2[2 * i] = ffma2(kk, dl0, S2[2 * i]);
-    S2[2 * i + 1] = ffma2(kk, dl1, S2[2 * i + 1]);
-  }
-}
-
-// o = Sᵀq for the thread's 4 columns (q duplicated as (q, q) pairs in qd).
-template <int RPT>
-__device__ __forceinline__ float4 gdn_readout(const uint64_t (&S2)[2 * RPT], const float2* __restrict__ qd, int rg) {
-  uint64_t a0 = 0, a1 = 0, b0 = 0, b1 = 0;
-#pragma unroll
-  for (int i = 0; i < RPT; ++i) {
-    const float2 qr = qd[4 * i + rg];
-    const uint64_t qq = *reinterpret_cast<const uint64_t*>(&qr);
-    if (i & 1) {
-      b0 = ffma2(S2[2 * i], qq, b0);
-      b1 = ffma2(S2[2 * i + 1], qq, b1);
-    } else {
-      a0 = ffma2(S2[2 * i], qq, a0);
-      a1 = ffma2(S2[2 * i + 1], qq, a1);
-    }
-  }
-  float2 o0 = upk2(a0), o1 = upk2(a1);
-  {
-    const float2 e0 = upk2(b0), e1 = upk2(b1);
-    o0 = make_float2(__fadd_rn(o0.x, e0.x), __fadd_rn(o0.y, e0.y));
-    o1 = make_float2(__fadd_rn(o1.x, e1.x), __fadd_rn(o1.y, e1.y));
-  }
-  o0 = shfl_add2(o0, 8);
-  o1 = shfl_add2(o1, 8);
-  o0 = shfl_add2(o0, 16);
-  o1 = shfl_add2(o1, 16);
-  return make_float4(o0.x, o0.y, o1.x, o1.y);
-}
-
-// l2norm in the reference's arithmetic: x·rsqrt(Σx² + 1e-6) evaluated in the model dtype
-// (each op rounded for bf16; plain fp32 otherwise). `x` is DK floats in shared memory,
-// normalised in place by one warp.
-template <typename T, int DK>
-__device__ __forceinline__ void warp_l2norm(float2* x, float post_scale, int lane) {
-  float ss = 0.f;
-  for (int i = lane; i < DK; i += 32) ss += dt<T>::round(x[i].x * x[i].x);
-  ss = warp_sum(ss);
-  const float s = dt<T>::round(dt<T>::round(ss) + 1e-6f);
-  const float r = dt<T>::round(rsqrtf(s));
-  for (int i = lane; i < DK; i += 32) {
-    const float y = dt<T>::round(x[i].x * r) * post_scale;
-    x[i] = make_float2(y, y);
-  }
-}
 
 // 16-byte vector of T converted to floats
 template <typename T>
@@ -164,23 +68,6 @@ __device__ __forceinline__ void load16_as_float(const T* src, float* dst) {
     }
   }
 }
-
-template <typename T, int DK, int DV>
-struct __align__(128) GdnSmem {
-  static constexpr int NCH = 2 * DK + DV;   // q, k, v conv channels of one value head
-  float sst[DK * DV];                       // next head's state (TMA bulk prefetch target)
-  T xr[GDN_KMAX - 1 + GDN_TB][NCH];         // raw conv inputs: window rows, then tokens
-  T zr[GDN_TB][DV];                         // raw output gate z
-  T cwr[NCH][GDN_KMAX];                     // conv weights of this head's channels
-  float2 q[GDN_TB][DK];                     // q, k duplicated as (x, x) pairs (packed FMA operands)
-  float2 k[GDN_TB][DK];
-  float v[GDN_TB][DV];
-  float o[GDN_TB][DV];
-  float g[GDN_TB];
-  float beta[GDN_TB];
-  float ab[GDN_TB][2];                      // a, b of this head
-  uint64_t bar;                             // state prefetch barrier
-};
 
 __device__ int g_gdn_error = 0;
 
@@ -214,207 +101,6 @@ __device__ __forceinline__ void gdn_prefetch_state(float* dst, const float* src,
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(gsm(dst)),
                "l"(src), "r"(bytes), "r"(gsm(bar)), "l"(pol)
                : "memory");
-}
-
-// Sequential commit of T > max_spec_tokens tokens (prefill chunks); any kept tokens of a
-// previous speculative call were replayed into the state before this launch.
-// Persistent: CTA c handles (sequence, value head) units c, c+G, c+2G, ... . While a unit is
-// computed from registers, the next unit's state streams into shared memory. A unit's small
-// inputs (conv window, token rows, z, weights) are staged with cp.async.
-// Thread (warp w, lane l) owns columns 4*cg..4*cg+3 with cg = 8w + (l&7) and rows rg, rg+4, ...
-// with rg = l>>3, so every reduction over rows is an in-thread sum plus two xor-shuffles.
-template <typename T, int DK, int DV>
-__global__ void __launch_bounds__(DV, 2)
-gdn_seq_kernel(const qsp_gdn_layer L) {
-  pdl_trigger();
-  pdl_wait();
-  using SMT = GdnSmem<T, DK, DV>;
-  constexpr int RPT = DK / 4;
-  constexpr int NT = DV;
-  constexpr int NCH = SMT::NCH;
-  constexpr int EPV = 16 / (int)sizeof(T);   // elements per 16-byte vector
-  extern __shared__ __align__(128) uint8_t gdn_smem_raw[];
-  SMT& sm = *reinterpret_cast<SMT*>(gdn_smem_raw);
-
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int cg = warp * 8 + (lane & 7), rg = lane >> 3;
-  const int T_ = L.tokens, K = L.conv_kernel, Ts = L.max_spec_tokens;
-  const int Hv = L.n_v_heads, Hk = L.n_k_heads, vpk = Hv / Hk;
-  const int key_dim = Hk * DK, conv_dim = 2 * key_dim + Hv * DV, value_dim = Hv * DV;
-  const T* proj = static_cast<const T*>(L.proj);
-  const T* cw = static_cast<const T*>(L.conv_w);
-  T* hist = static_cast<T*>(L.conv_hist);
-  T* out = static_cast<T*>(L.out);
-  const int par = L.parity[0];
-  const int hist_rows = K - 1 + Ts;
-  const int units = L.batch * Hv;
-  const float qscale = (float)(1.0 / sqrt((double)DK));  // dk^-0.5 rounded once to fp32
-  const T* normw = static_cast<const T*>(L.norm_w);
-  constexpr uint32_t SBYTES = DK * DV * 4;
-
-  if (tid == 0) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(gsm(&sm.bar)) : "memory");
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-  }
-  __syncthreads();
-  if (tid == 0 && blockIdx.x < units)
-    gdn_prefetch_state(sm.sst, L.state + (int64_t)blockIdx.x * DK * DV, &sm.bar, SBYTES);
-
-  uint32_t it = 0;
-  for (int u = blockIdx.x; u < units; u += gridDim.x, ++it) {
-    const int b = u / Hv, h = u % Hv, kh = h / vpk;
-    // device-side counters are clamped to the buffers they index (they are produced by
-    // qsp_cache_finalize / qsp_cache_accept and never exceed max_spec_tokens)
-    const int coff = min(max(L.conv_off[b], 0), Ts);
-    const T* hist_in = hist + ((int64_t)par * L.batch + b) * hist_rows * conv_dim;
-    T* hist_out = hist + ((int64_t)(par ^ 1) * L.batch + b) * hist_rows * conv_dim;
-    float* state = L.state + ((int64_t)b * Hv + h) * DK * DV;
-    // global channel of local conv channel c (q | k | v segments of this head)
-    const int seg0 = kh * DK, seg1 = key_dim + kh * DK - DK, seg2 = 2 * key_dim + h * DV - 2 * DK;
-    auto gch = [&](int c) -> int { return c + (c < DK ? seg0 : (c < 2 * DK ? seg1 : seg2)); };
-
-    // 1. stage this unit's inputs (cp.async: every copy in flight at once)
-    for (int e = tid; e < NCH * GDN_KMAX * (int)sizeof(T) / 16 && K == GDN_KMAX; e += NT) {
-      const int c = (e * 16 / (int)sizeof(T)) / GDN_KMAX;   // first channel of this 16-byte chunk
-      const int within = (e * 16 / (int)sizeof(T)) % GDN_KMAX;
-      gcp16(&sm.cwr[c][within], cw + (int64_t)gch(c) * GDN_KMAX + within);
-    }
-    if (K != GDN_KMAX) {   // narrower conv kernels: element loads
-      for (int e = tid; e < NCH * K; e += NT) sm.cwr[e / K][e % K] = cw[(int64_t)gch(e / K) * K + e % K];
-    }
-    auto stage_tokens = [&](int t0, int nt) {
-      for (int t = 0; t < nt; ++t) {
-        const T* prow = proj + (int64_t)(b * T_ + t0 + t) * L.ld_proj;
-        for (int c = tid * EPV; c < NCH; c += NT * EPV) gcp16(&sm.xr[K - 1 + t][c], prow + gch(c));
-        for (int c = tid * EPV; c < DV; c += NT * EPV) gcp16(&sm.zr[t][c], prow + conv_dim + h * DV + c);
-      }
-      if (tid < 2 * nt) {
-        const int t = tid >> 1, w = tid & 1;   // w = 0: b, 1: a
-        sm.ab[t][w] = dt<T>::to_f(proj[(int64_t)(b * T_ + t0 + t) * L.ld_proj + conv_dim + value_dim + w * Hv + h]);
-      }
-    };
-    for (int i = 0; i < K - 1; ++i)
-      for (int c = tid * EPV; c < NCH; c += NT * EPV) gcp16(&sm.xr[i][c], hist_in + (int64_t)(coff + i) * conv_dim + gch(c));
-    stage_tokens(0, min(GDN_TB, T_));
-    asm volatile("cp.async.commit_group;" ::: "memory");
-
-    // 2. this unit's state: prefetched into shared memory → registers
-    gdn_wait(&sm.bar, it & 1u);
-    uint64_t S[2 * RPT];
-#pragma unroll
-    for (int i = 0; i < RPT; ++i) {
-      const float4 v4 = *reinterpret_cast<const float4*>(&sm.sst[(4 * i + rg) * DV + 4 * cg]);
-      S[2 * i] = pk2(v4.x, v4.y);
-      S[2 * i + 1] = pk2(v4.z, v4.w);
-    }
-    asm volatile("cp.async.wait_all;" ::: "memory");
-    __syncthreads();   // inputs staged; every thread holds its state slice
-    // 3. prefetch the next unit's state while this one computes
-    if (tid == 0 && u + (int)gridDim.x < units)
-      gdn_prefetch_state(sm.sst, L.state + (int64_t)(u + gridDim.x) * DK * DV, &sm.bar, SBYTES);
-
-    auto store_state = [&]() {
-#pragma unroll
-      for (int i = 0; i < RPT; ++i) {
-        const float2 lo = upk2(S[2 * i]), hi = upk2(S[2 * i + 1]);
-        *reinterpret_cast<float4*>(state + (int64_t)(4 * i + rg) * DV + 4 * cg) = make_float4(lo.x, lo.y, hi.x, hi.y);
-      }
-    };
-
-    // conv-history ownership: every head writes its v channels; the first v head of a k-head
-    // group also writes that group's q and k channels
-    const int c_first = ((h % vpk) == 0) ? 0 : 2 * DK;
-    auto write_hist_rows = [&](int src_row0, int n_rows) {
-      for (int i = 0; i < n_rows; ++i)
-        for (int c = c_first + tid * EPV; c < NCH; c += NT * EPV)
-          *reinterpret_cast<uint4*>(hist_out + (int64_t)i * conv_dim + gch(c)) =
-              *reinterpret_cast<const uint4*>(&sm.xr[src_row0 + i][c]);
-    };
-
-    const float A = -expf(dt<T>::to_f(static_cast<const T*>(L.a_log)[h]));
-    const float dtb = dt<T>::to_f(static_cast<const T*>(L.dt_bias)[h]);
-
-    for (int t0 = 0; t0 < T_; t0 += GDN_TB) {
-      const int nt = min(GDN_TB, T_ - t0);
-      __syncthreads();   // the previous block is done with the token buffers
-      // 5. conv + SiLU (fp32 accumulate, rounded like F.conv1d then F.silu), gates
-      for (int c = tid; c < NCH; c += NT) {
-        float w[GDN_KMAX];
-#pragma unroll
-        for (int j = 0; j < GDN_KMAX; ++j) w[j] = j < K ? dt<T>::to_f(sm.cwr[c][j]) : 0.f;
-        for (int t = 0; t < nt; ++t) {
-          float acc = 0.f;
-          for (int j = 0; j < K; ++j) acc = fmaf(w[j], dt<T>::to_f(sm.xr[t + j][c]), acc);
-          const float a = dt<T>::round(siluf_(dt<T>::round(acc)));
-          if (c < DK) sm.q[t][c] = make_float2(a, a);
-          else if (c < 2 * DK) sm.k[t][c - DK] = make_float2(a, a);
-          else sm.v[t][c - 2 * DK] = a;
-        }
-      }
-      if (tid < nt) {
-        sm.beta[tid] = dt<T>::round(sigmoidf_(sm.ab[tid][0]));
-        sm.g[tid] = A * softplusf_(sm.ab[tid][1] + dtb);
-      }
-      __syncthreads();
-      for (int vidx = warp; vidx < 2 * nt; vidx += NT / 32) {
-        const int t = vidx >> 1;
-        if (vidx & 1) warp_l2norm<T, DK>(sm.k[t], 1.0f, lane);
-        else warp_l2norm<T, DK>(sm.q[t], qscale, lane);
-      }
-      __syncthreads();
-      // 6. recurrence + readout
-      for (int t = 0; t < nt; ++t) {
-        gdn_update<RPT>(S, sm.k[t], sm.v[t], sm.g[t], sm.beta[t], rg, cg);
-        const float4 o = gdn_readout<RPT>(S, sm.q[t], rg);
-        if (rg == 0) *reinterpret_cast<float4*>(&sm.o[t][4 * cg]) = o;
-      }
-      __syncthreads();
-      // 7. RMSNormGated over dv per token: w·round(x̂) · silu(z), x = round(core)
-      for (int t = warp; t < nt; t += NT / 32) {
-        float ss = 0.f;
-        for (int c = lane; c < DV; c += 32) {
-          const float x = dt<T>::round(sm.o[t][c]);
-          ss = fmaf(x, x, ss);
-        }
-        ss = warp_sum(ss);
-        const float inv = rsqrtf(ss / (float)DV + L.eps);
-        T* orow = out + (int64_t)(b * T_ + t0 + t) * L.ld_out + h * DV;
-        for (int c = lane; c < DV; c += 32) {
-          const float xh = dt<T>::round(dt<T>::round(sm.o[t][c]) * inv);
-          const float wx = dt<T>::round(dt<T>::to_f(normw[c]) * xh);
-          orow[c] = dt<T>::from_f(wx * siluf_(dt<T>::to_f(sm.zr[t][c])));
-        }
-      }
-      const bool last = t0 + nt >= T_;
-      if (last) {
-        write_hist_rows(nt, K - 1);   // the window after the last token
-      } else {
-        // slide the window (last K-1 combined rows to the front) and stage the next block;
-        // source and destination rows may overlap: read everything, barrier, then write
-        constexpr int SLIDE = ((GDN_KMAX - 1) * NCH + NT - 1) / NT;
-        T keep[SLIDE];
-        __syncthreads();
-#pragma unroll
-        for (int q4 = 0; q4 < SLIDE; ++q4) {
-          const int e = tid + q4 * NT;
-          keep[q4] = e < (K - 1) * NCH ? sm.xr[nt + e / NCH][e % NCH] : T{};
-        }
-        __syncthreads();
-#pragma unroll
-        for (int q4 = 0; q4 < SLIDE; ++q4) {
-          const int e = tid + q4 * NT;
-          if (e < (K - 1) * NCH) sm.xr[e / NCH][e % NCH] = keep[q4];
-        }
-        stage_tokens(t0 + nt, min(GDN_TB, T_ - t0 - nt));
-        asm volatile("cp.async.commit_group;" ::: "memory");
-        asm volatile("cp.async.wait_all;" ::: "memory");
-        __syncthreads();
-      }
-    }
-
-    store_state();
-    __syncthreads();   // the next unit's staging overwrites the inputs
-  }
 }
 
 // ------------------------------------------------------------------ token ring
@@ -1030,6 +716,329 @@ gdn_chunk_kernel(const qsp_gdn_layer L, const GdnRing RG, const int n_new) {
   }
 }
 
+// ------------------------------------------------------------------ chunked prefill
+// A commit of T > max_spec_tokens tokens (prompt prefill), in blocks of GDN_TB tokens: each
+// block does the conv + SiLU, gates, l2norm and Gram products of the prep kernel for this unit
+// in shared memory, then the chunk kernel's block update — one pass over the state for Sᵀk_s
+// and Sᵀq_t, the per-column triangular recursion for δ_s and o_t, one rank-n update — instead
+// of a state pass per token. Arithmetic per quantity is the prep and chunk kernels' (the same
+// roundings; the block form is the reference's chunked delta rule, blocks.py:59-113, with
+// 8-token chunks). Any kept tokens of a previous speculative call were replayed into the
+// state before this launch. Persistent: CTA c handles (sequence, value head) units c, c+G, ...;
+// the next unit's state streams into shared memory while the current one computes.
+template <typename T, int DK, int DV>
+struct __align__(128) GdnPrefillSmem {
+  static constexpr int NCH = 2 * DK + DV;   // q, k, v conv channels of one value head
+  float sst[DK * DV];                       // next unit's state (bulk prefetch target)
+  float vec[2 * GDN_TB][DK];                // k̂ slots 0..7, dk^-1/2·q̂ slots 8..15 (fp32)
+  float vv[GDN_TB][DV];                     // v (model-dtype values)
+  T xr[GDN_KMAX - 1 + GDN_TB][NCH];         // raw conv inputs: window rows, then tokens
+  T zr[GDN_TB][DV];                         // raw output gate z
+  T cwr[NCH][GDN_KMAX];                     // conv weights of this head's channels
+  float ab[GDN_TB][2];                      // b, a of this head
+  float beta[GDN_TB], dcy[GDN_TB];          // β_s, d_s = e^{g_s}
+  float tabA[GDN_TB][GDN_TB];               // Γ(r, s)·k_r·k_s
+  float tabB[GDN_TB][GDN_TB];               // Γ(r, t)·k_r·q_t
+  float gam[GDN_TB], tail[GDN_TB];          // Γ(−1, s), Γ(s, n−1)
+  float red[(DV + 31) / 32][GDN_TB];
+  uint64_t bar;
+};
+
+template <typename T, int DK, int DV>
+__global__ void __launch_bounds__(DV, 2)
+gdn_prefill_kernel(const qsp_gdn_layer L) {
+  pdl_trigger();
+  pdl_wait();
+  using SMT = GdnPrefillSmem<T, DK, DV>;
+  constexpr int NCH = SMT::NCH;
+  constexpr int RB = DK / 4;            // rows per thread
+  constexpr int NT = DV;
+  constexpr int EPV = 16 / (int)sizeof(T);
+  extern __shared__ __align__(128) uint8_t gdn_pf_raw[];
+  SMT& sm = *reinterpret_cast<SMT*>(gdn_pf_raw);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int rg = lane >> 3, cg = warp * 8 + (lane & 7);
+  const int col = 4 * cg + rg;          // the column this lane owns after a butterfly
+  const int T_ = L.tokens, K = L.conv_kernel, Ts = L.max_spec_tokens;
+  const int Hv = L.n_v_heads, Hk = L.n_k_heads, vpk = Hv / Hk;
+  const int key_dim = Hk * DK, conv_dim = 2 * key_dim + Hv * DV, value_dim = Hv * DV;
+  const T* proj = static_cast<const T*>(L.proj);
+  const T* cw = static_cast<const T*>(L.conv_w);
+  T* hist = static_cast<T*>(L.conv_hist);
+  T* out = static_cast<T*>(L.out);
+  const int par = L.parity[0];
+  const int hist_rows = K - 1 + Ts;
+  const int units = L.batch * Hv;
+  const float qscale = (float)(1.0 / sqrt((double)DK));   // dk^-0.5 rounded once to fp32
+  const float wn = dt<T>::to_f(static_cast<const T*>(L.norm_w)[col]);
+  constexpr uint32_t SBYTES = DK * DV * 4;
+
+  if (tid == 0) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(gsm(&sm.bar)) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  if (tid == 0 && (int)blockIdx.x < units)
+    gdn_prefetch_state(sm.sst, L.state + (int64_t)blockIdx.x * DK * DV, &sm.bar, SBYTES);
+
+  uint32_t it = 0;
+  for (int u = blockIdx.x; u < units; u += gridDim.x, ++it) {
+    const int b = u / Hv, h = u % Hv, kh = h / vpk;
+    const int coff = min(max(L.conv_off[b], 0), Ts);
+    const T* hist_in = hist + ((int64_t)par * L.batch + b) * hist_rows * conv_dim;
+    T* hist_out = hist + ((int64_t)(par ^ 1) * L.batch + b) * hist_rows * conv_dim;
+    float* state = L.state + ((int64_t)b * Hv + h) * DK * DV;
+    const int seg0 = kh * DK, seg1 = key_dim + kh * DK - DK, seg2 = 2 * key_dim + h * DV - 2 * DK;
+    auto gch = [&](int c) -> int { return c + (c < DK ? seg0 : (c < 2 * DK ? seg1 : seg2)); };
+
+    // 1. stage this unit's conv weights, window and first token block (cp.async)
+    for (int e = tid; e < NCH * GDN_KMAX / EPV && K == GDN_KMAX; e += NT) {
+      const int c = e * EPV / GDN_KMAX, within = e * EPV % GDN_KMAX;
+      gcp16(&sm.cwr[c][within], cw + (int64_t)gch(c) * GDN_KMAX + within);
+    }
+    if (K != GDN_KMAX) {
+      for (int e = tid; e < NCH * K; e += NT) sm.cwr[e / K][e % K] = cw[(int64_t)gch(e / K) * K + e % K];
+    }
+    auto stage_tokens = [&](int t0, int nt) {
+      for (int t = 0; t < nt; ++t) {
+        const T* prow = proj + (int64_t)(b * T_ + t0 + t) * L.ld_proj;
+        for (int c = tid * EPV; c < NCH; c += NT * EPV) gcp16(&sm.xr[K - 1 + t][c], prow + gch(c));
+        for (int c = tid * EPV; c < DV; c += NT * EPV) gcp16(&sm.zr[t][c], prow + conv_dim + h * DV + c);
+      }
+      if (tid < 2 * nt) {
+        const int t = tid >> 1, w = tid & 1;   // w = 0: b, 1: a
+        sm.ab[t][w] = dt<T>::to_f(proj[(int64_t)(b * T_ + t0 + t) * L.ld_proj + conv_dim + value_dim + w * Hv + h]);
+      }
+    };
+    for (int i = 0; i < K - 1; ++i)
+      for (int c = tid * EPV; c < NCH; c += NT * EPV) gcp16(&sm.xr[i][c], hist_in + (int64_t)(coff + i) * conv_dim + gch(c));
+    stage_tokens(0, min(GDN_TB, T_));
+    asm volatile("cp.async.commit_group;" ::: "memory");
+
+    // 2. this unit's state: shared memory → registers (thread (rg, cg) holds rows
+    //    RB·rg .. RB·rg+RB-1 of columns 4cg..4cg+3 as packed row pairs), then the next
+    //    unit's prefetch
+    gdn_wait(&sm.bar, it & 1u);
+    uint64_t S[4][RB / 2];
+#pragma unroll
+    for (int p = 0; p < RB / 2; ++p) {
+      const float4 r0 = *reinterpret_cast<const float4*>(&sm.sst[(RB * rg + 2 * p) * DV + 4 * cg]);
+      const float4 r1 = *reinterpret_cast<const float4*>(&sm.sst[(RB * rg + 2 * p + 1) * DV + 4 * cg]);
+      S[0][p] = pk2(r0.x, r1.x);
+      S[1][p] = pk2(r0.y, r1.y);
+      S[2][p] = pk2(r0.z, r1.z);
+      S[3][p] = pk2(r0.w, r1.w);
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    __syncthreads();   // sst consumed; inputs staged
+    if (tid == 0 && u + (int)gridDim.x < units)
+      gdn_prefetch_state(sm.sst, L.state + (int64_t)(u + gridDim.x) * DK * DV, &sm.bar, SBYTES);
+
+    const float A = -expf(dt<T>::to_f(static_cast<const T*>(L.a_log)[h]));
+    const float dtb = dt<T>::to_f(static_cast<const T*>(L.dt_bias)[h]);
+    const int c_first = ((h % vpk) == 0) ? 0 : 2 * DK;   // conv-history ownership (seq kernel)
+
+    for (int t0 = 0; t0 < T_; t0 += GDN_TB) {
+      const int n = min(GDN_TB, T_ - t0);
+      // 3. conv + SiLU (the prep kernel's arithmetic), gates
+      for (int c = tid; c < NCH; c += NT) {
+        float w[GDN_KMAX];
+#pragma unroll
+        for (int j = 0; j < GDN_KMAX; ++j) w[j] = j < K ? dt<T>::to_f(sm.cwr[c][j]) : 0.f;
+        for (int t = 0; t < n; ++t) {
+          float acc = 0.f;
+#pragma unroll
+          for (int j = 0; j < GDN_KMAX; ++j)
+            if (j < K) acc = fmaf(w[j], dt<T>::to_f(sm.xr[t + j][c]), acc);
+          const float a = dt<T>::round(siluf_(dt<T>::round(acc)));
+          if (c < DK) sm.vec[GDN_TB + t][c] = a;
+          else if (c < 2 * DK) sm.vec[t][c - DK] = a;
+          else sm.vv[t][c - 2 * DK] = a;
+        }
+      }
+      if (tid < n) {
+        sm.beta[tid] = dt<T>::round(sigmoidf_(sm.ab[tid][0]));
+        sm.dcy[tid] = expf(A * softplusf_(sm.ab[tid][1] + dtb));
+      }
+      __syncthreads();
+      // 4. l2norm of q and k (warp per vector; x·round(rsqrt(round(Σ round(x²)) + 1e-6)))
+      for (int vi = warp; vi < 2 * n; vi += NT / 32) {
+        const int t = vi >> 1;
+        const bool isk = vi & 1;
+        float* xv = sm.vec[isk ? t : GDN_TB + t];
+        float ss = 0.f;
+#pragma unroll
+        for (int i = lane; i < DK; i += 32) ss += dt<T>::round(xv[i] * xv[i]);
+        ss = warp_sum(ss);
+        const float sq = dt<T>::round(dt<T>::round(ss) + 1e-6f);
+        const float r = dt<T>::round(rsqrtf(sq));
+#pragma unroll
+        for (int i = lane; i < DK; i += 32) {
+          const float y = dt<T>::round(xv[i] * r);
+          xv[i] = isk ? y : y * qscale;
+        }
+      }
+      __syncthreads();
+      // 5. Gram products in the prep kernel's order, straight into the coefficient tables
+      //    (Γ(r, s) = d_{r+1}···d_s), and Γ(−1, s), Γ(s, n−1)
+      const int nkk = n * (n - 1) / 2, nkq = n * (n + 1) / 2;
+      for (int e = warp; e < nkk + nkq; e += NT / 32) {
+        int s, t;
+        const bool isq = e >= nkk;
+        if (!isq) {   // pairs s < t
+          int rem = e;
+          t = 1;
+          while (rem >= t) { rem -= t; ++t; }
+          s = rem;
+        } else {      // pairs s <= t
+          int rem = e - nkk;
+          t = 0;
+          while (rem >= t + 1) { rem -= t + 1; ++t; }
+          s = rem;
+        }
+        const float* ks = sm.vec[s];
+        const float* o = sm.vec[isq ? GDN_TB + t : t];
+        float acc = 0.f;
+#pragma unroll
+        for (int i = lane; i < DK; i += 32) acc = fmaf(ks[i], o[i], acc);
+        acc = warp_sum(acc);
+        if (lane == 0) {
+          float ratio = 1.f;
+          for (int i = s + 1; i <= t; ++i) ratio = __fmul_rn(ratio, sm.dcy[i]);
+          if (isq) sm.tabB[s][t] = __fmul_rn(ratio, acc);
+          else sm.tabA[s][t] = __fmul_rn(ratio, acc);
+        }
+      }
+      if (tid < n) {
+        float ratio = 1.f;
+        for (int i = 0; i <= tid; ++i) ratio = __fmul_rn(ratio, sm.dcy[i]);
+        sm.gam[tid] = ratio;
+        float tl = 1.f;
+        for (int i = tid + 1; i <= n - 1; ++i) tl = __fmul_rn(tl, sm.dcy[i]);
+        sm.tail[tid] = tl;
+      }
+      __syncthreads();
+      // 6. Sᵀk_s and Sᵀq_t (four slots per pass), δ_s and o_t of this lane's column
+      float Pk[GDN_TB], Pq[GDN_TB], dl[GDN_TB], o[GDN_TB];
+#pragma unroll
+      for (int i = 0; i < GDN_TB; ++i) Pk[i] = Pq[i] = 0.f;
+      const int ng = (n + 3) >> 2;
+#pragma unroll 1
+      for (int g = 0; g < 2 * ng; ++g) {
+        const bool isq = g >= ng;
+        const int g4 = isq ? g - ng : g;
+        float t4[4] = {0.f, 0.f, 0.f, 0.f};
+        const int left = n - 4 * g4;
+        const float* vg = sm.vec[(isq ? GDN_TB : 0) + 4 * g4];
+        if (left == 1) gdn_dots4<DK, 1>(S, vg, rg, t4);
+        else if (left == 2) gdn_dots4<DK, 2>(S, vg, rg, t4);
+        else gdn_dots4<DK>(S, vg, rg, t4);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+#pragma unroll
+          for (int jj = 0; jj < GDN_TB / 4; ++jj) {
+            if (g4 == jj) {
+              if (isq) Pq[4 * jj + i] = t4[i];
+              else Pk[4 * jj + i] = t4[i];
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int s = 0; s < GDN_TB; ++s) {
+        dl[s] = 0.f;
+        if (s < n) {
+          float acc = __fmul_rn(sm.gam[s], Pk[s]);
+#pragma unroll
+          for (int r = 0; r < s; ++r) acc = __fmaf_rn(sm.tabA[r][s], dl[r], acc);
+          dl[s] = __fmul_rn(__fsub_rn(sm.vv[s][col], acc), sm.beta[s]);
+        }
+      }
+#pragma unroll
+      for (int t = 0; t < GDN_TB; ++t) {
+        o[t] = 0.f;
+        if (t < n) {
+          float acc = __fmul_rn(sm.gam[t], Pq[t]);
+#pragma unroll
+          for (int r = 0; r <= t; ++r) acc = __fmaf_rn(sm.tabB[r][t], dl[r], acc);
+          o[t] = acc;
+        }
+      }
+      // 7. S ← Γ(−1, n−1)·S + Σ_s Γ(s, n−1)·k_s δ_sᵀ
+      {
+        float c[GDN_TB];
+#pragma unroll
+        for (int s2 = 0; s2 < GDN_TB; ++s2) c[s2] = s2 < n ? __fmul_rn(sm.tail[s2], dl[s2]) : 0.f;
+        gdn_rank<DK>(S, sm.vec[0], sm.gam[n - 1], c, n, rg, lane);
+      }
+      // 8. RMSNormGated over the dv columns of each token (the chunk kernel's step 6)
+      float ssq[GDN_TB];
+#pragma unroll
+      for (int t = 0; t < GDN_TB; ++t) {
+        const float x = dt<T>::round(o[t]);
+        ssq[t] = x * x;
+      }
+#pragma unroll
+      for (int sh = 16; sh > 0; sh >>= 1)
+#pragma unroll
+        for (int t = 0; t < GDN_TB; ++t) ssq[t] += __shfl_xor_sync(0xffffffffu, ssq[t], sh);
+      if (lane == 0) {
+#pragma unroll
+        for (int t = 0; t < GDN_TB; ++t)
+          if (t < n) sm.red[warp][t] = ssq[t];
+      }
+      __syncthreads();
+#pragma unroll
+      for (int t = 0; t < GDN_TB; ++t) {
+        if (t < n) {
+          float ss = 0.f;
+          for (int w2 = 0; w2 < (DV + 31) / 32; ++w2) ss += sm.red[w2][t];
+          const float inv = rsqrtf(ss / (float)DV + L.eps);
+          const float xh = dt<T>::round(dt<T>::round(o[t]) * inv);
+          const float wx = dt<T>::round(wn * xh);
+          out[(int64_t)(b * T_ + t0 + t) * L.ld_out + h * DV + col] = dt<T>::from_f(wx * siluf_(dt<T>::to_f(sm.zr[t][col])));
+        }
+      }
+      // 9. the conv window: after the last block, written to the other parity; otherwise
+      //    slid (its last K-1 combined rows to the front) and the next block staged
+      const bool last = t0 + n >= T_;
+      if (last) {
+        for (int i = 0; i < K - 1; ++i)
+          for (int cc = c_first + tid * EPV; cc < NCH; cc += NT * EPV)
+            *reinterpret_cast<uint4*>(hist_out + (int64_t)i * conv_dim + gch(cc)) =
+                *reinterpret_cast<const uint4*>(&sm.xr[n + i][cc]);
+      } else {
+        constexpr int SLIDE = ((GDN_KMAX - 1) * NCH + NT - 1) / NT;
+        T keep[SLIDE];
+        __syncthreads();   // every thread is done with this block's rows
+#pragma unroll
+        for (int q4 = 0; q4 < SLIDE; ++q4) {
+          const int e = tid + q4 * NT;
+          keep[q4] = e < (K - 1) * NCH ? sm.xr[n + e / NCH][e % NCH] : T{};
+        }
+        __syncthreads();
+#pragma unroll
+        for (int q4 = 0; q4 < SLIDE; ++q4) {
+          const int e = tid + q4 * NT;
+          if (e < (K - 1) * NCH) sm.xr[e / NCH][e % NCH] = keep[q4];
+        }
+        stage_tokens(t0 + n, min(GDN_TB, T_ - t0 - n));
+        asm volatile("cp.async.commit_group;" ::: "memory");
+        asm volatile("cp.async.wait_all;" ::: "memory");
+      }
+      __syncthreads();   // the next block (or unit) overwrites the vector slots and tables
+    }
+    // 10. the committed state
+#pragma unroll
+    for (int p = 0; p < RB / 2; ++p) {
+      const float2 a = upk2(S[0][p]), bq = upk2(S[1][p]), c2 = upk2(S[2][p]), d2 = upk2(S[3][p]);
+      float* d0 = state + (int64_t)(RB * rg + 2 * p) * DV + 4 * cg;
+      *reinterpret_cast<float4*>(d0) = make_float4(a.x, bq.x, c2.x, d2.x);
+      *reinterpret_cast<float4*>(d0 + DV) = make_float4(a.y, bq.y, c2.y, d2.y);
+    }
+  }
+}
+
 static int sm_count_gdn() {
   static int n = 0;
   if (n == 0) {
@@ -1078,15 +1087,15 @@ static int launch_gdn_dims(const qsp_gdn_layer& L, cudaStream_t st) {
     if (rc) return rc;
     return launch_pdl("qsp_gdn_verify(chunk)", chunk, dim3(grid), dim3(DV), csmem, st, L, RG, (int)L.tokens);
   }
-  // long commit call: replay kept tokens into the state, then step through the tokens
+  // long commit call: replay kept tokens into the state, then the tokens in 8-token blocks
   rc = launch_pdl("qsp_gdn_verify(replay)", chunk, dim3(grid), dim3(DV), csmem, st, L, RG, 0);
   if (rc) return rc;
-  auto seq = gdn_seq_kernel<T, DK, DV>;
-  const size_t ssmem = sizeof(GdnSmem<T, DK, DV>);
-  static bool seq_set = false;
-  rc = reserve_smem(seq, ssmem, seq_set);
+  auto pf = gdn_prefill_kernel<T, DK, DV>;
+  const size_t pfsmem = sizeof(GdnPrefillSmem<T, DK, DV>);
+  static bool pf_set = false;
+  rc = reserve_smem(pf, pfsmem, pf_set);
   if (rc) return rc;
-  return launch_pdl("qsp_gdn_verify(seq)", seq, dim3(grid), dim3(DV), ssmem, st, L);
+  return launch_pdl("qsp_gdn_verify(prefill)", pf, dim3(grid), dim3(DV), pfsmem, st, L);
 }
 
 template <typename T>
