@@ -434,6 +434,8 @@ def run_gpu_arm(args, cfg, ws, rank, local):
                           "algorithmic_bytes": vb},
         "live_kernels_ms_per_step": {LIVE_CLASSES[k]: {"launches": v[0], "ms_per_launch": v[1], "ms_per_step": v[2]}
                                      for k, v in live.items()},
+        "live_kernels_note": LIVE_NOTE,
+        "live_kernels_sum_ms": sum(v[2] for v in live.values()),
         "phases_ms": {k: statistics.mean(v) for k, v in phase.items()},
         "acceptance_rate": acc_rate, "tokens_per_step_per_seq": tokens / (args.steps * B),
         "prefill_s": prefill_s, "setup_s": time.perf_counter() - t_setup,
@@ -573,6 +575,11 @@ def graph_kernel_nodes(graphs) -> int:
 LIVE_CLASSES = {"gdn_verify": "gdn_prep_kernel + gdn_chunk_kernel", "attn_verify": "attn_ws_kernel + attn_combine_kernel",
                 "gemm": "gemm_tc_kernel", "gemm_residual_rmsnorm": "gemm_tc_kernel (+ residual/RMSNorm merge)",
                 "gemm_swiglu": "gemm_tc_kernel (+ SwiGLU merge)"}
+
+
+LIVE_NOTE = ("each class is timed between two events recorded around its launches inside the captured verify "
+             "forward; an event between two kernels stops the next kernel from starting early (programmatic "
+             "dependent launch), so these per-launch times are upper bounds and their sum exceeds phases_ms.verify")
 
 
 def live_kernel_times(dec, graphs, steps):

@@ -7,6 +7,10 @@
 // variants apply the op that follows a projection in the decoder layer (residual add + next
 // RMSNorm, or SwiGLU) inside its split-K merge when it splits, and with the standalone kernels
 // otherwise: same results either way.
+#include <stdlib.h>
+
+#include <algorithm>
+
 #include "qsp_common.cuh"
 
 namespace qsp {
@@ -25,13 +29,29 @@ int gemm_tc(const void* a, int64_t lda, const void* w, int64_t ldw, void* c, int
 size_t gemm_tc_workspace(int64_t m, int64_t n, int64_t k);
 int gemm_cl(const void* a, int64_t lda, const void* w, int64_t ldw, void* c, int64_t ldc, int64_t m, int64_t n,
             int64_t k, int mode, cudaStream_t st);
+int gemm_pair(const void* a, int64_t lda, const void* w, int64_t ldw, void* c, int64_t ldc, int64_t m, int64_t n,
+              int64_t k, int mode, const void* norm_w, void* y, int64_t ldy, float eps, void* workspace,
+              size_t ws_bytes, cudaStream_t st);
+size_t gemm_pair_workspace(int64_t m, int64_t n, int64_t k);
+
+// Which products take the CTA-pair kernel (bit 0: plain, bit 1: SwiGLU, bit 2: residual +
+// RMSNorm); QSP_GEMM_PAIR overrides the default, for comparisons with the other kernels.
+static int pair_modes() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("QSP_GEMM_PAIR");
+    v = e != nullptr ? atoi(e) : 0;
+  }
+  return v;
+}
+
 }  // namespace qsp
 
 using namespace qsp;
 
 extern "C" size_t qsp_gemm_workspace_bytes(int64_t m, int64_t n, int64_t k, int dtype) {
   if (dtype != QSP_BF16 || m <= 0 || n <= 0 || k <= 0) return 0;
-  return gemm_tc_workspace(m, n, k);
+  return std::max(gemm_tc_workspace(m, n, k), gemm_pair_workspace(m, n, k));
 }
 
 static int check_gemm_args(const void* a, const void* w, const void* c, int64_t m, int64_t n, int64_t k,
@@ -54,6 +74,27 @@ static int gemm_any(const void* a, int64_t lda, const void* w, int64_t ldw, void
     // on chip. (Measured on B200: faster than the persistent kernel + merge for the wide
     // projections — qkv 16.3 vs 20.6 µs, in_proj 23.9 vs 24.6 µs — and slower for the
     // residual and SwiGLU tails, which therefore keep the persistent kernel.)
+    // verify-sized rows: one CTA pair per tile of weight rows, whole K, epilogue in place
+    if (flags == 0 && epi == nullptr && (pair_modes() & 1)) {
+      const int rp = gemm_pair(a, lda, w, ldw, c, ldc, m, n, k, 0, nullptr, nullptr, 0, 0.f, ws, ws_bytes, st);
+      if (rp != QSP_ERR_UNSUPPORTED) return rp;
+    }
+    if (epi != nullptr && epi->kind == 2 && flags == 0 && (pair_modes() & 2)) {
+      const int rp = gemm_pair(a, lda, w, ldw, epi->y, epi->ldy, m, n / 2, k, 1, nullptr, nullptr, 0, 0.f, ws,
+                               ws_bytes, st);
+      if (rp != QSP_ERR_UNSUPPORTED) {
+        *fused = rp == QSP_OK;
+        return rp;
+      }
+    }
+    if (epi != nullptr && epi->kind == 1 && flags == QSP_GEMM_ACCUMULATE && (pair_modes() & 4)) {
+      const int rp = gemm_pair(a, lda, w, ldw, c, ldc, m, n, k, 2, epi->norm_w, epi->y, epi->ldy, epi->eps, ws,
+                               ws_bytes, st);
+      if (rp != QSP_ERR_UNSUPPORTED) {
+        *fused = rp == QSP_OK;
+        return rp;
+      }
+    }
     if (flags == 0 && epi == nullptr) {
       const int rcl = gemm_cl(a, lda, w, ldw, c, ldc, m, n, k, 0, st);
       if (rcl != QSP_ERR_UNSUPPORTED) return rcl;

@@ -147,57 +147,52 @@ gemm_cl_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
   const int row0 = tile * (NACC == 2 && MODE != CL_SWIGLU ? 256 : 128);
 
   if (warp == 0) {
+    // producer: the whole warp runs the loop, one elected lane issues (qsp_tc.cuh)
     if (lane == 0) {
       asm volatile("prefetch.tensormap [%0];" ::"l"(&tm_w) : "memory");
       asm volatile("prefetch.tensormap [%0];" ::"l"(&tm_x) : "memory");
-      // weights of the first ring pass before the dependency wait, activations after it
-      const int npre = min(nk, C::STAGES);
-      for (int i = 0; i < npre; ++i) {
-        uint8_t* st = smem + i * C::STAGE;
-        mbar_expect_tx(&full[i], C::STAGE);
-        tma_load_2d_evict_first(st, &tm_w, &full[i], (kb0 + i) * 64, row0);
-        if (NACC == 2) tma_load_2d_evict_first(st + 128 * 128, &tm_w, &full[i], (kb0 + i) * 64, row0 + A.box1);
-      }
-      pdl_wait();
-      for (int i = 0; i < npre; ++i) tma_load_2d(smem + i * C::STAGE + C::W_BYTES, &tm_x, &full[i], (kb0 + i) * 64, 0);
-      for (int i = npre; i < nk; ++i) {
-        const int s = i % C::STAGES;
-        const uint32_t ph = (i / C::STAGES) & 1u;
-        if (!mbar_wait(&empty[s], ph ^ 1u, 301, &g_gemm_cl_error, abort)) break;
-        uint8_t* st = smem + s * C::STAGE;
-        mbar_expect_tx(&full[s], C::STAGE);
-        tma_load_2d_evict_first(st, &tm_w, &full[s], (kb0 + i) * 64, row0);
-        if (NACC == 2) tma_load_2d_evict_first(st + 128 * 128, &tm_w, &full[s], (kb0 + i) * 64, row0 + A.box1);
-        tma_load_2d(st + C::W_BYTES, &tm_x, &full[s], (kb0 + i) * 64, 0);
-      }
-    } else {
-      pdl_wait();
+    }
+    __syncwarp();
+    // weights of the first ring pass before the dependency wait, activations after it
+    const int npre = min(nk, C::STAGES);
+    for (int i = 0; i < npre; ++i) {
+      uint8_t* st = smem + i * C::STAGE;
+      mbar_expect_tx_warp(&full[i], C::STAGE);
+      tma_load_2d_evict_first_warp(st, &tm_w, &full[i], (kb0 + i) * 64, row0);
+      if (NACC == 2) tma_load_2d_evict_first_warp(st + 128 * 128, &tm_w, &full[i], (kb0 + i) * 64, row0 + A.box1);
+    }
+    pdl_wait();
+    for (int i = 0; i < npre; ++i) tma_load_2d_warp(smem + i * C::STAGE + C::W_BYTES, &tm_x, &full[i], (kb0 + i) * 64, 0);
+    for (int i = npre; i < nk; ++i) {
+      const int s = i % C::STAGES;
+      const uint32_t ph = (i / C::STAGES) & 1u;
+      if (!mbar_wait_warp(&empty[s], ph ^ 1u, 301, &g_gemm_cl_error, abort)) break;
+      uint8_t* st = smem + s * C::STAGE;
+      mbar_expect_tx_warp(&full[s], C::STAGE);
+      tma_load_2d_evict_first_warp(st, &tm_w, &full[s], (kb0 + i) * 64, row0);
+      if (NACC == 2) tma_load_2d_evict_first_warp(st + 128 * 128, &tm_w, &full[s], (kb0 + i) * 64, row0 + A.box1);
+      tma_load_2d_warp(st + C::W_BYTES, &tm_x, &full[s], (kb0 + i) * 64, 0);
     }
   } else if (warp == 1) {
     pdl_wait();
-    if (lane == 0) {
-      constexpr uint32_t idesc = idesc_bf16(128, CL_MT);
-      bool ok = true;
-      for (int i = 0; i < nk; ++i) {
-        const int s = i % C::STAGES;
-        const uint32_t ph = (i / C::STAGES) & 1u;
-        if (ok && !mbar_wait(&full[s], ph, 302, &g_gemm_cl_error, abort)) ok = false;
-        fence_after();
-        if (ok) {
-          const uint32_t a0 = smem_u32(smem + s * C::STAGE);
-          const uint32_t b0 = a0 + C::W_BYTES;
+    // MMA issuer: the whole warp runs the loop, one elected lane issues
+    constexpr uint32_t idesc = idesc_bf16(128, CL_MT);
+    bool ok = true;
+    for (int i = 0; i < nk; ++i) {
+      const int s = i % C::STAGES;
+      const uint32_t ph = (i / C::STAGES) & 1u;
+      if (ok && !mbar_wait_warp(&full[s], ph, 302, &g_gemm_cl_error, abort)) ok = false;
+      fence_after();
+      if (ok) {
+        const uint32_t a0 = smem_u32(smem + s * C::STAGE);
+        const uint32_t b0 = a0 + C::W_BYTES;
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-#pragma unroll
-            for (int q = 0; q < NACC; ++q)
-              umma_bf16(tmem + q * CL_MT, sdesc_sw128(a0 + q * 128 * 128 + kk * 32), sdesc_sw128(b0 + kk * 32), idesc,
-                        (i > 0 || kk > 0) ? 1u : 0u);
-          }
-        }
-        umma_commit(&empty[s]);
+        for (int q = 0; q < NACC; ++q)
+          umma4_bf16_warp(tmem + q * CL_MT, sdesc_sw128(a0 + q * 128 * 128), sdesc_sw128(b0), idesc, i > 0 ? 1u : 0u);
       }
-      umma_commit(acc_full);
+      umma_commit_warp(&empty[s]);
     }
+    umma_commit_warp(acc_full);
   } else {
     // ---------------------------------------------------------------- exchange + epilogue
     pdl_wait();

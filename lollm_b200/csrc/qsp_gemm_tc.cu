@@ -13,6 +13,7 @@
 // Every mbarrier wait is bounded; a wait that runs out records an error code in a device
 // flag (read by qsp_device_status) and the CTA finishes without hanging the GPU.
 #include "qsp_common.cuh"
+#include "qsp_tc.cuh"
 
 #include <cuda.h>
 
@@ -58,6 +59,10 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int co
   }
   atomicExch(&g_qsp_dev_error, code);
   return false;
+}
+// mbar_wait by all lanes of a converged warp (same result in every lane)
+__device__ __forceinline__ bool mbar_wait_w(uint64_t* bar, uint32_t parity, int code) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity, code));
 }
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
   asm volatile(
@@ -353,56 +358,58 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
   const uint32_t tmem = *tslot;
 
   if (warp == 0) {
-    // TMA producer: one continuous ring across every k-block of every unit of this CTA
+    // TMA producer: one continuous ring across every k-block of every unit of this CTA. The
+    // whole warp runs the loop; one elected lane issues (tcgen05/TMA issue from a lone lane of
+    // a diverged warp is several times slower).
     if (lane == 0) {
       asm volatile("prefetch.tensormap [%0];" ::"l"(&tm_w) : "memory");
       asm volatile("prefetch.tensormap [%0];" ::"l"(&tm_x) : "memory");
-      // The weights do not depend on the previous kernel: the first ring pass issues its
-      // weight tiles before the dependency wait, and its activation tiles after it.
-      int pre_kb[C::STAGES], pre_mb[C::STAGES];
-      uint32_t npre = 0;
-      for (int u = blockIdx.x; u < A.units && npre < (uint32_t)C::STAGES; u += gridDim.x) {
-        const TcUnit U = tc_unit(A, u, tiles);
-        const int mb = U.tile % A.m_tiles, nb = U.tile / A.m_tiles, kb0 = U.kb0, nk = U.nk;
-        const int rot = u % nk;
-        for (int i = 0; i < nk && npre < (uint32_t)C::STAGES; ++i, ++npre) {
-          const int kb = kb0 + (i + rot) % nk;
-          mbar_expect_tx(&full[npre], C::STAGE_BYTES);
-          tma_load_2d_evict_first(smem + npre * C::STAGE_BYTES, &tm_w, &full[npre], kb * TC_BK, nb * TC_BN);
-          pre_kb[npre] = kb;
-          pre_mb[npre] = mb;
-        }
+    }
+    __syncwarp();
+    // The weights do not depend on the previous kernel: the first ring pass issues its
+    // weight tiles before the dependency wait, and its activation tiles after it.
+    int pre_kb[C::STAGES], pre_mb[C::STAGES];
+    uint32_t npre = 0;
+    for (int u = blockIdx.x; u < A.units && npre < (uint32_t)C::STAGES; u += gridDim.x) {
+      const TcUnit U = tc_unit(A, u, tiles);
+      const int mb = U.tile % A.m_tiles, nb = U.tile / A.m_tiles, kb0 = U.kb0, nk = U.nk;
+      const int rot = u % nk;
+      for (int i = 0; i < nk && npre < (uint32_t)C::STAGES; ++i, ++npre) {
+        const int kb = kb0 + (i + rot) % nk;
+        tc::mbar_expect_tx_warp(&full[npre], C::STAGE_BYTES);
+        tc::tma_load_2d_evict_first_warp(smem + npre * C::STAGE_BYTES, &tm_w, &full[npre], kb * TC_BK, nb * TC_BN);
+        pre_kb[npre] = kb;
+        pre_mb[npre] = mb;
       }
-      pdl_wait();
-      for (uint32_t j = 0; j < npre; ++j)
-        tma_load_2d(smem + j * C::STAGE_BYTES + C::W_BYTES, &tm_x, &full[j], pre_kb[j] * TC_BK, pre_mb[j] * MT);
-      uint32_t it = 0;
-      bool ok = true;
-      for (int u = blockIdx.x; u < A.units && ok; u += gridDim.x) {
-        const TcUnit U = tc_unit(A, u, tiles);
-        const int mb = U.tile % A.m_tiles, nb = U.tile / A.m_tiles, kb0 = U.kb0, nk = U.nk;
-        // units walk their k-blocks from a rotated start so concurrent CTAs read different
-        // activation slabs (all CTAs on the same slab at once hot-spots L2)
-        const int rot = u % nk;
-        for (int i = 0; i < nk; ++i, ++it) {
-          if (it < npre) continue;   // issued above
-          const int kb = kb0 + (i + rot) % nk;
-          const int s = it % C::STAGES;
-          const uint32_t ph = (it / C::STAGES) & 1u;
-          if (it >= (uint32_t)C::STAGES && !mbar_wait(&empty[s], ph ^ 1u, 101)) { ok = false; break; }
-          uint8_t* st = smem + s * C::STAGE_BYTES;
-          mbar_expect_tx(&full[s], C::STAGE_BYTES);
-          tma_load_2d_evict_first(st, &tm_w, &full[s], kb * TC_BK, nb * TC_BN);
-          tma_load_2d(st + C::W_BYTES, &tm_x, &full[s], kb * TC_BK, mb * MT);
-        }
+    }
+    pdl_wait();
+    for (uint32_t j = 0; j < npre; ++j)
+      tc::tma_load_2d_warp(smem + j * C::STAGE_BYTES + C::W_BYTES, &tm_x, &full[j], pre_kb[j] * TC_BK, pre_mb[j] * MT);
+    uint32_t it = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < A.units && ok; u += gridDim.x) {
+      const TcUnit U = tc_unit(A, u, tiles);
+      const int mb = U.tile % A.m_tiles, nb = U.tile / A.m_tiles, kb0 = U.kb0, nk = U.nk;
+      // units walk their k-blocks from a rotated start so concurrent CTAs read different
+      // activation slabs
+      const int rot = u % nk;
+      for (int i = 0; i < nk; ++i, ++it) {
+        if (it < npre) continue;   // issued above
+        const int kb = kb0 + (i + rot) % nk;
+        const int s = it % C::STAGES;
+        const uint32_t ph = (it / C::STAGES) & 1u;
+        if (it >= (uint32_t)C::STAGES && !mbar_wait_w(&empty[s], ph ^ 1u, 101)) { ok = false; break; }
+        uint8_t* st = smem + s * C::STAGE_BYTES;
+        tc::mbar_expect_tx_warp(&full[s], C::STAGE_BYTES);
+        tc::tma_load_2d_evict_first_warp(st, &tm_w, &full[s], kb * TC_BK, nb * TC_BN);
+        tc::tma_load_2d_warp(st + C::W_BYTES, &tm_x, &full[s], kb * TC_BK, mb * MT);
       }
-    } else {
-      pdl_wait();
     }
   } else if (warp == 1) {
     pdl_wait();
-    // MMA issuer: accumulator buffer ui & 1 for the ui-th unit of this CTA
-    if (lane == 0) {
+    // MMA issuer (whole warp, one elected lane issues): accumulator buffer ui & 1 for the
+    // ui-th unit of this CTA
+    {
       constexpr uint32_t idesc = idesc_bf16(TC_MM, MT);
       uint32_t it = 0, ui = 0;
       bool ok = true;
@@ -410,28 +417,25 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
         const int nk = tc_unit(A, u, tiles).nk;
         const uint32_t buf = (C::ACC_BUFS == 2) ? (ui & 1u) : 0u;
         const uint32_t use = (C::ACC_BUFS == 2) ? (ui >> 1) : ui;   // how often this buffer was used before
-        if (ok && use >= 1 && !mbar_wait(&acc_empty[buf], (use - 1) & 1u, 104)) ok = false;
+        if (ok && use >= 1 && !mbar_wait_w(&acc_empty[buf], (use - 1) & 1u, 104)) ok = false;
         tc_fence_after();
         const uint32_t d = tmem + buf * C::UNIT_COLS;
         for (int i = 0; i < nk; ++i, ++it) {
           const int s = it % C::STAGES;
           const uint32_t ph = (it / C::STAGES) & 1u;
-          if (ok && !mbar_wait(&full[s], ph, 102)) ok = false;
+          if (ok && !mbar_wait_w(&full[s], ph, 102)) ok = false;
           tc_fence_after();
           if (ok) {
             const uint32_t a0 = smem_u32(smem + s * C::STAGE_BYTES);
             const uint32_t b0 = a0 + C::W_BYTES;
 #pragma unroll
-            for (int kk = 0; kk < TC_BK / 16; ++kk) {
-#pragma unroll
-              for (int q = 0; q < C::NACC; ++q)   // weight rows 128q..128q+127 → accumulator q
-                umma_bf16(d + q * C::ACC_COLS, sdesc_sw128(a0 + q * TC_MM * 128 + kk * 32), sdesc_sw128(b0 + kk * 32),
-                          idesc, (i > 0 || kk > 0) ? 1u : 0u);
-            }
+            for (int q = 0; q < C::NACC; ++q)   // weight rows 128q..128q+127 → accumulator q
+              tc::umma4_bf16_warp(d + q * C::ACC_COLS, sdesc_sw128(a0 + q * TC_MM * 128), sdesc_sw128(b0), idesc,
+                                  i > 0 ? 1u : 0u);
           }
-          umma_commit(&empty[s]);
+          tc::umma_commit_warp(&empty[s]);
         }
-        umma_commit(&acc_full[buf]);
+        tc::umma_commit_warp(&acc_full[buf]);
       }
     }
   } else {
@@ -616,6 +620,26 @@ static int sm_count() {
   return n;
 }
 
+// Sums `splits` fp32 partials [m, ldp] (split_stride floats apart, in split order) and applies
+// the epilogue: c (+)= round(Σ); x += round(Σ) then RMSNorm into epi.y; or SwiGLU of the
+// [gate | up] halves into epi.y.
+int gemm_merge(const float* partial, int splits, int64_t split_stride, int ldp, __nv_bfloat16* c, int64_t ldc, int m,
+               int n, int accumulate, const GemmEpi& epi, cudaStream_t st) {
+  if (epi.kind == GEMM_EPI_RESNORM)
+    return launch_pdl("qsp_gemm(split-k merge + residual + rmsnorm)", splitk_residual_rmsnorm_kernel, dim3(m),
+                      dim3(RN_THREADS), 0, st, partial, splits, split_stride, ldp, c, ldc, epi.norm_w, epi.y, epi.ldy,
+                      n, epi.eps);
+  if (epi.kind == GEMM_EPI_SWIGLU) {
+    const int inter = n / 2;
+    dim3 g((unsigned)((inter / 4 + 255) / 256), (unsigned)m);
+    return launch_pdl("qsp_gemm(split-k merge + swiglu)", splitk_swiglu_kernel, g, dim3(256), 0, st, partial, splits,
+                      split_stride, ldp, epi.y, epi.ldy, inter);
+  }
+  dim3 rgrid((unsigned)((n / 4 + 255) / 256 + 1), (unsigned)m);
+  return launch_pdl("qsp_gemm(split-k merge)", splitk_store_kernel, rgrid, dim3(256), 0, st, partial, splits,
+                    split_stride, ldp, c, ldc, n, accumulate);
+}
+
 template <int MT, int BN>
 static int launch_tc(const CUtensorMap& mw, const CUtensorMap& mx, const TcArgs& a, const TcPlan& p,
                      const GemmEpi& epi, cudaStream_t st) {
@@ -645,20 +669,8 @@ static int launch_tc(const CUtensorMap& mw, const CUtensorMap& mx, const TcArgs&
   }
   if (p.splits == 1) return rc;
   const int ldp = p.n_tiles * BN;
-  const int64_t split_stride = (int64_t)p.m_tiles * MT * ldp;
-  if (epi.kind == GEMM_EPI_RESNORM)
-    return launch_pdl("qsp_gemm(split-k merge + residual + rmsnorm)", splitk_residual_rmsnorm_kernel, dim3(a.m),
-                      dim3(RN_THREADS), 0, st, (const float*)a.partial, p.splits, split_stride, ldp, a.c, a.ldc,
-                      epi.norm_w, epi.y, epi.ldy, a.n, epi.eps);
-  if (epi.kind == GEMM_EPI_SWIGLU) {
-    const int inter = a.n / 2;
-    dim3 g((unsigned)((inter / 4 + 255) / 256), (unsigned)a.m);
-    return launch_pdl("qsp_gemm(split-k merge + swiglu)", splitk_swiglu_kernel, g, dim3(256), 0, st,
-                      (const float*)a.partial, p.splits, split_stride, ldp, epi.y, epi.ldy, inter);
-  }
-  dim3 rgrid((unsigned)((a.n / 4 + 255) / 256 + 1), (unsigned)a.m);
-  return launch_pdl("qsp_gemm(split-k merge)", splitk_store_kernel, rgrid, dim3(256), 0, st, (const float*)a.partial,
-                    p.splits, split_stride, ldp, a.c, a.ldc, a.n, a.accumulate);
+  return gemm_merge(a.partial, p.splits, (int64_t)p.m_tiles * MT * ldp, ldp, a.c, a.ldc, a.m, a.n, a.accumulate, epi,
+                    st);
 }
 
 static size_t ws_need(const TcPlan& p) { return p.partial_bytes; }
@@ -725,6 +737,7 @@ int gdn_device_error(int reset);
 int attn_device_error(int reset);
 int moe_device_error(int reset);
 int gemm_cl_device_error(int reset);
+int gemm_pair_device_error(int reset);
 int core_device_error(int reset);
 int sample_device_error(int reset);
 int probe_device_error(int reset);
@@ -736,8 +749,8 @@ extern "C" int qsp_device_status(int32_t* code, int32_t reset) {
   const int attn = qsp::attn_device_error(reset);
   const int moe = qsp::moe_device_error(reset);
   const int cl = qsp::gemm_cl_device_error(reset);
-  const int others[] = {qsp::core_device_error(reset), qsp::sample_device_error(reset),
-                        qsp::probe_device_error(reset)};
+  const int others[] = {qsp::gemm_pair_device_error(reset), qsp::core_device_error(reset),
+                        qsp::sample_device_error(reset), qsp::probe_device_error(reset)};
   int v = 0;
   cudaError_t e = cudaMemcpyFromSymbol(&v, qsp::g_qsp_dev_error, sizeof(int));
   if (e != cudaSuccess) return qsp::set_error(QSP_ERR_CUDA, "qsp_device_status: %s", cudaGetErrorString(e));

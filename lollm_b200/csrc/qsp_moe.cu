@@ -365,69 +365,68 @@ moe_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
   const uint32_t tmem = *tslot;
 
   if (warp == 0) {
+    // producer: the whole warp runs the loop, one elected lane issues (qsp_tc.cuh)
     if (lane == 0) {
       asm volatile("prefetch.tensormap [%0];" ::"l"(&tm_w) : "memory");
       asm volatile("prefetch.tensormap [%0];" ::"l"(&tm_x) : "memory");
-      uint32_t it = 0;
-      bool ok = true;
-      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
-        const int e = u / A.RB, rb = u % A.RB;
-        const int off = __ldg(&A.offsets[e]), n_e = __ldg(&A.offsets[e + 1]) - off;
-        const int row0 = e * A.rows_per_expert + rb * (SWI ? 128 : 128 * NA);
-        for (int t0 = 0; t0 < n_e && ok; t0 += C::TN) {
-          const int nb16 = (min(C::TN, n_e - t0) + 15) / 16;
-          const uint32_t bytes = NA * C::A_BYTES + nb16 * 2048;
-          for (int kb = 0; kb < A.n_kb; ++kb, ++it) {
-            const int s = it % C::STAGES;
-            const uint32_t ph = (it / C::STAGES) & 1u;
-            if (it >= (uint32_t)C::STAGES && !mbar_wait(&empty[s], ph ^ 1u, 201, &g_moe_dev_error, abort)) {
-              ok = false;
-              break;
-            }
-            uint8_t* st = smem + s * C::STAGE;
-            mbar_expect_tx(&full[s], bytes);
-            tma_load_2d_evict_first(st, &tm_w, &full[s], kb * 64, row0);
-            if (NA == 2) tma_load_2d_evict_first(st + C::A_BYTES, &tm_w, &full[s], kb * 64, row0 + (SWI ? A.out_w : 128));
-            for (int q = 0; q < nb16; ++q)
-              tma_load_2d(st + NA * C::A_BYTES + q * 2048, &tm_x, &full[s], kb * 64, off + t0 + q * 16);
+    }
+    __syncwarp();
+    uint32_t it = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+      const int e = u / A.RB, rb = u % A.RB;
+      const int off = __ldg(&A.offsets[e]), n_e = __ldg(&A.offsets[e + 1]) - off;
+      const int row0 = e * A.rows_per_expert + rb * (SWI ? 128 : 128 * NA);
+      for (int t0 = 0; t0 < n_e && ok; t0 += C::TN) {
+        const int nb16 = (min(C::TN, n_e - t0) + 15) / 16;
+        const uint32_t bytes = NA * C::A_BYTES + nb16 * 2048;
+        for (int kb = 0; kb < A.n_kb; ++kb, ++it) {
+          const int s = it % C::STAGES;
+          const uint32_t ph = (it / C::STAGES) & 1u;
+          if (it >= (uint32_t)C::STAGES && !mbar_wait_warp(&empty[s], ph ^ 1u, 201, &g_moe_dev_error, abort)) {
+            ok = false;
+            break;
           }
+          uint8_t* st = smem + s * C::STAGE;
+          mbar_expect_tx_warp(&full[s], bytes);
+          tma_load_2d_evict_first_warp(st, &tm_w, &full[s], kb * 64, row0);
+          if (NA == 2)
+            tma_load_2d_evict_first_warp(st + C::A_BYTES, &tm_w, &full[s], kb * 64, row0 + (SWI ? A.out_w : 128));
+          for (int q = 0; q < nb16; ++q)
+            tma_load_2d_warp(st + NA * C::A_BYTES + q * 2048, &tm_x, &full[s], kb * 64, off + t0 + q * 16);
         }
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      uint32_t it = 0, ti = 0;
-      bool ok = true;
-      for (int u = blockIdx.x; u < units; u += gridDim.x) {
-        const int e = u / A.RB;
-        const int off = __ldg(&A.offsets[e]), n_e = __ldg(&A.offsets[e + 1]) - off;
-        for (int t0 = 0; t0 < n_e; t0 += C::TN, ++ti) {
-          const int nt = min(C::TN, n_e - t0);
-          const uint32_t idesc = idesc_bf16(128, max(16, (nt + 15) & ~15));
-          const uint32_t buf = ti & 1u, use = ti >> 1;
-          if (ok && use >= 1 && !mbar_wait(&acc_empty[buf], (use - 1) & 1u, 204, &g_moe_dev_error, abort)) ok = false;
+    // MMA issuer: the whole warp runs the loop, one elected lane issues
+    uint32_t it = 0, ti = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < units; u += gridDim.x) {
+      const int e = u / A.RB;
+      const int off = __ldg(&A.offsets[e]), n_e = __ldg(&A.offsets[e + 1]) - off;
+      for (int t0 = 0; t0 < n_e; t0 += C::TN, ++ti) {
+        const int nt = min(C::TN, n_e - t0);
+        const uint32_t idesc = idesc_bf16(128, max(16, (nt + 15) & ~15));
+        const uint32_t buf = ti & 1u, use = ti >> 1;
+        if (ok && use >= 1 && !mbar_wait_warp(&acc_empty[buf], (use - 1) & 1u, 204, &g_moe_dev_error, abort)) ok = false;
+        fence_after();
+        const uint32_t d = tmem + buf * C::BUF_COLS;
+        for (int kb = 0; kb < A.n_kb; ++kb, ++it) {
+          const int s = it % C::STAGES;
+          const uint32_t ph = (it / C::STAGES) & 1u;
+          if (ok && !mbar_wait_warp(&full[s], ph, 202, &g_moe_dev_error, abort)) ok = false;
           fence_after();
-          const uint32_t d = tmem + buf * C::BUF_COLS;
-          for (int kb = 0; kb < A.n_kb; ++kb, ++it) {
-            const int s = it % C::STAGES;
-            const uint32_t ph = (it / C::STAGES) & 1u;
-            if (ok && !mbar_wait(&full[s], ph, 202, &g_moe_dev_error, abort)) ok = false;
-            fence_after();
-            if (ok) {
-              const uint32_t a0 = smem_u32(smem + s * C::STAGE);
-              const uint32_t b0 = a0 + NA * C::A_BYTES;
+          if (ok) {
+            const uint32_t a0 = smem_u32(smem + s * C::STAGE);
+            const uint32_t b0 = a0 + NA * C::A_BYTES;
 #pragma unroll
-              for (int kk = 0; kk < 4; ++kk) {
-#pragma unroll
-                for (int q = 0; q < NA; ++q)
-                  umma_bf16(d + q * C::ACC_COLS, sdesc_sw128(a0 + q * C::A_BYTES + kk * 32), sdesc_sw128(b0 + kk * 32),
-                            idesc, (kb > 0 || kk > 0) ? 1u : 0u);
-              }
-            }
-            umma_commit(&empty[s]);
+            for (int q = 0; q < NA; ++q)
+              umma4_bf16_warp(d + q * C::ACC_COLS, sdesc_sw128(a0 + q * C::A_BYTES), sdesc_sw128(b0), idesc,
+                              kb > 0 ? 1u : 0u);
           }
-          umma_commit(&acc_full[buf]);
+          umma_commit_warp(&empty[s]);
         }
+        umma_commit_warp(&acc_full[buf]);
       }
     }
   } else {

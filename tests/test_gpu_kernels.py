@@ -104,6 +104,37 @@ def test_gemm_fused_epilogues(m):
     assert K().device_status() == 0
 
 
+@pytest.mark.parametrize("m", [136, 256])
+def test_gemm_fused_epilogues_ragged(m):
+    """Products whose column count is not a whole number of weight tiles and whose depth is not
+    a whole number of 64-wide k-blocks, at verify row counts (the CTA-pair kernel writes only
+    columns < n and rows < m; its last tile is partial)."""
+    dt = torch.bfloat16
+    g = gen(12)
+    eps = 1e-6
+    n, k = 2032, 1000
+    a, w = rn(g, m, k, dtype=dt), rn(g, n, k, scale=0.03, dtype=dt)
+    x0, nw = rn(g, m, n, dtype=dt), rn(g, n, scale=0.1, dtype=dt)
+    x, y = x0.to(DEV), torch.empty(m, n, dtype=dt, device=DEV)
+    K().gemm_residual_rmsnorm(a.to(DEV), w.to(DEV), x, nw.to(DEV), y, eps)
+    xr = (x0.float() + (a.double() @ w.double().T).to(dt).float()).to(dt)
+    close(x, xr, dt)
+    close(y, Q.rms_norm(xr, nw, eps), dt)
+    inter, k2 = 1000, 2056
+    a2, wgu = rn(g, m, k2, dtype=dt), rn(g, 2 * inter, k2, scale=0.02, dtype=dt)
+    act = torch.empty(m, inter, dtype=dt, device=DEV)
+    tmp = torch.empty(m, 2 * inter, dtype=dt, device=DEV)
+    K().gemm_swiglu(a2.to(DEV), wgu.to(DEV), act, tmp)
+    h = (a2.double() @ wgu.double().T).to(dt)
+    close(act, Q.silu_mul(h[:, :inter], h[:, inter:]), dt)
+    for n3 in (1000, 4104):
+        w3 = rn(g, n3, k2, scale=0.02, dtype=dt)
+        c = torch.empty(m, n3, dtype=dt, device=DEV)
+        K().gemm(a2.to(DEV), w3.to(DEV), c)
+        close(c, (a2.double() @ w3.double().T).to(dt), dt)
+    assert K().device_status() == 0
+
+
 @pytest.mark.parametrize("dt", DTS)
 def test_swiglu_embed_select(dt):
     g = gen(2)
