@@ -35,14 +35,23 @@ int gemm_pair(const void* a, int64_t lda, const void* w, int64_t ldw, void* c, i
 size_t gemm_pair_workspace(int64_t m, int64_t n, int64_t k);
 
 // Which products take the CTA-pair kernel (bit 0: plain, bit 1: SwiGLU, bit 2: residual +
-// RMSNorm); QSP_GEMM_PAIR overrides the default, for comparisons with the other kernels.
+// RMSNorm). By default only plain products at least PAIR_WIDE_N columns wide do (measured on
+// B200 at 256 rows: the 12352-column GDN input projection 19.5 µs against 24.0 µs on the
+// cluster kernel; the 9216-column attention projection 19.6 against 15.8, the SwiGLU and
+// residual tails slower too). QSP_GEMM_PAIR=<bits> applies the pair kernel to every product of
+// those kinds instead, for comparisons with the other kernels.
+constexpr int64_t PAIR_WIDE_N = 10240;
 static int pair_modes() {
-  static int v = -1;
-  if (v < 0) {
+  static int v = -2;
+  if (v == -2) {
     const char* e = getenv("QSP_GEMM_PAIR");
-    v = e != nullptr ? atoi(e) : 0;
+    v = e != nullptr ? atoi(e) : -1;
   }
   return v;
+}
+static bool pair_for(int bit, int64_t n) {
+  const int v = pair_modes();
+  return v < 0 ? (bit == 1 && n >= PAIR_WIDE_N) : (v & bit) != 0;
 }
 
 }  // namespace qsp
@@ -75,11 +84,11 @@ static int gemm_any(const void* a, int64_t lda, const void* w, int64_t ldw, void
     // projections — qkv 16.3 vs 20.6 µs, in_proj 23.9 vs 24.6 µs — and slower for the
     // residual and SwiGLU tails, which therefore keep the persistent kernel.)
     // verify-sized rows: one CTA pair per tile of weight rows, whole K, epilogue in place
-    if (flags == 0 && epi == nullptr && (pair_modes() & 1)) {
+    if (flags == 0 && epi == nullptr && pair_for(1, n)) {
       const int rp = gemm_pair(a, lda, w, ldw, c, ldc, m, n, k, 0, nullptr, nullptr, 0, 0.f, ws, ws_bytes, st);
       if (rp != QSP_ERR_UNSUPPORTED) return rp;
     }
-    if (epi != nullptr && epi->kind == 2 && flags == 0 && (pair_modes() & 2)) {
+    if (epi != nullptr && epi->kind == 2 && flags == 0 && pair_for(2, n)) {
       const int rp = gemm_pair(a, lda, w, ldw, epi->y, epi->ldy, m, n / 2, k, 1, nullptr, nullptr, 0, 0.f, ws,
                                ws_bytes, st);
       if (rp != QSP_ERR_UNSUPPORTED) {
@@ -87,7 +96,7 @@ static int gemm_any(const void* a, int64_t lda, const void* w, int64_t ldw, void
         return rp;
       }
     }
-    if (epi != nullptr && epi->kind == 1 && flags == QSP_GEMM_ACCUMULATE && (pair_modes() & 4)) {
+    if (epi != nullptr && epi->kind == 1 && flags == QSP_GEMM_ACCUMULATE && pair_for(4, n)) {
       const int rp = gemm_pair(a, lda, w, ldw, c, ldc, m, n, k, 2, epi->norm_w, epi->y, epi->ldy, epi->eps, ws,
                                ws_bytes, st);
       if (rp != QSP_ERR_UNSUPPORTED) {
