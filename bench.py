@@ -364,25 +364,35 @@ def run_gpu_arm(args, cfg, ws, rank, local):
     value = tot_tokens / (max_ms / 1000.0)
 
     # ---------------- e2e: public API with host buffers (H2D pending ids, D2H committed tokens)
+    # Every step: H2D of the pending ids from pinned host memory, D2H of the step's token block
+    # and accepted counts into pinned host memory, D2H of the next pending ids (the next step's
+    # H2D reads them back: stream order carries the round trip through host memory). The host
+    # reads step s's counts once step s's copies have landed, while step s+1 runs (two pinned
+    # buffers), so it never leaves the GPU idle waiting for the host.
     B, T = args.batch, args.k + 1
     h_ids = torch.empty(B, T, dtype=torch.int64, pin_memory=True)
-    h_acc = torch.empty(B, dtype=torch.int32, pin_memory=True)
-    h_tok = torch.empty(B, T, dtype=torch.int64, pin_memory=True)
+    h_acc = [torch.empty(B, dtype=torch.int32, pin_memory=True) for _ in range(2)]
+    h_tok = [torch.empty(B, T, dtype=torch.int64, pin_memory=True) for _ in range(2)]
+    landed = [torch.cuda.Event() for _ in range(2)]
     h_ids.copy_(dec.ids.cpu())
     barrier(ws)
     torch.cuda.synchronize()
     e2e_tokens = 0
     es, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     es.record(stream)
-    for _ in range(args.steps):
+    for s in range(args.steps):
+        j = s & 1
         dec.ids[:, :1].copy_(h_ids[:, :1], non_blocking=True)
-        ids_before = dec.ids.clone()
+        h_tok[j].copy_(dec.ids, non_blocking=True)          # the token block this step verifies
         full.replay()
-        h_acc.copy_(dec.accept_n, non_blocking=True)
-        h_tok.copy_(ids_before, non_blocking=True)
+        h_acc[j].copy_(dec.accept_n, non_blocking=True)
         h_ids[:, :1].copy_(dec.ids[:, :1], non_blocking=True)
-        stream.synchronize()                      # the host now holds this step's tokens
-        e2e_tokens += int(h_acc.sum()) + B
+        landed[j].record(stream)
+        if s > 0:                                         # the previous step's result, on the host
+            landed[j ^ 1].synchronize()
+            e2e_tokens += int(h_acc[j ^ 1].sum()) + B
+    landed[(args.steps - 1) & 1].synchronize()
+    e2e_tokens += int(h_acc[(args.steps - 1) & 1].sum()) + B
     ee.record(stream)
     torch.cuda.synchronize()
     barrier(ws)
