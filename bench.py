@@ -369,12 +369,14 @@ def run_gpu_arm(args, cfg, ws, rank, local):
     # H2D reads them back: stream order carries the round trip through host memory). The host
     # reads step s's counts once step s's copies have landed, while step s+1 runs (two pinned
     # buffers), so it never leaves the GPU idle waiting for the host.
+    # (Host buffers are contiguous: a strided pinned view would make torch stage the copy
+    # through pageable memory synchronously.)
     B, T = args.batch, args.k + 1
-    h_ids = torch.empty(B, T, dtype=torch.int64, pin_memory=True)
+    h_ids = torch.empty(B, 1, dtype=torch.int64, pin_memory=True)
     h_acc = [torch.empty(B, dtype=torch.int32, pin_memory=True) for _ in range(2)]
     h_tok = [torch.empty(B, T, dtype=torch.int64, pin_memory=True) for _ in range(2)]
     landed = [torch.cuda.Event() for _ in range(2)]
-    h_ids.copy_(dec.ids.cpu())
+    h_ids.copy_(dec.ids[:, :1].cpu())
     barrier(ws)
     torch.cuda.synchronize()
     e2e_tokens = 0
@@ -382,11 +384,11 @@ def run_gpu_arm(args, cfg, ws, rank, local):
     es.record(stream)
     for s in range(args.steps):
         j = s & 1
-        dec.ids[:, :1].copy_(h_ids[:, :1], non_blocking=True)
+        dec.ids[:, :1].copy_(h_ids, non_blocking=True)
         h_tok[j].copy_(dec.ids, non_blocking=True)          # the token block this step verifies
         full.replay()
         h_acc[j].copy_(dec.accept_n, non_blocking=True)
-        h_ids[:, :1].copy_(dec.ids[:, :1], non_blocking=True)
+        h_ids.copy_(dec.ids[:, :1], non_blocking=True)
         landed[j].record(stream)
         if s > 0:                                         # the previous step's result, on the host
             landed[j ^ 1].synchronize()

@@ -154,12 +154,15 @@ gemm_cl_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
     }
     __syncwarp();
     // weights of the first ring pass before the dependency wait, activations after it
+    // NACC = 2 outside SWIGLU: the two accumulators' 256 weight rows are contiguous and come as
+    // one 256-row box (fewer, larger TMA requests); SWIGLU's gate and up rows are two boxes
+    constexpr bool ONE_BOX = NACC == 1 || MODE != CL_SWIGLU;
     const int npre = min(nk, C::STAGES);
     for (int i = 0; i < npre; ++i) {
       uint8_t* st = smem + i * C::STAGE;
       mbar_expect_tx_warp(&full[i], C::STAGE);
       tma_load_2d_evict_first_warp(st, &tm_w, &full[i], (kb0 + i) * 64, row0);
-      if (NACC == 2) tma_load_2d_evict_first_warp(st + 128 * 128, &tm_w, &full[i], (kb0 + i) * 64, row0 + A.box1);
+      if (!ONE_BOX) tma_load_2d_evict_first_warp(st + 128 * 128, &tm_w, &full[i], (kb0 + i) * 64, row0 + A.box1);
     }
     pdl_wait();
     for (int i = 0; i < npre; ++i) tma_load_2d_warp(smem + i * C::STAGE + C::W_BYTES, &tm_x, &full[i], (kb0 + i) * 64, 0);
@@ -170,7 +173,7 @@ gemm_cl_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
       uint8_t* st = smem + s * C::STAGE;
       mbar_expect_tx_warp(&full[s], C::STAGE);
       tma_load_2d_evict_first_warp(st, &tm_w, &full[s], (kb0 + i) * 64, row0);
-      if (NACC == 2) tma_load_2d_evict_first_warp(st + 128 * 128, &tm_w, &full[s], (kb0 + i) * 64, row0 + A.box1);
+      if (!ONE_BOX) tma_load_2d_evict_first_warp(st + 128 * 128, &tm_w, &full[s], (kb0 + i) * 64, row0 + A.box1);
       tma_load_2d_warp(st + C::W_BYTES, &tm_x, &full[s], (kb0 + i) * 64, 0);
     }
   } else if (warp == 1) {
@@ -401,7 +404,8 @@ static int launch_cl(const void* a, int64_t lda, const void* w, int64_t ldw, int
                      ClArgs args, cudaStream_t st) {
   using C = ClCfg<NACC>;
   CUtensorMap mw, mx;
-  if (!tc::make_map_bf16(&mw, w, w_rows, k, ldw, 128) || !tc::make_map_bf16(&mx, a, args.m, k, lda, CL_MT))
+  const int w_box = (NACC == 2 && MODE != CL_SWIGLU) ? 256 : 128;
+  if (!tc::make_map_bf16(&mw, w, w_rows, k, ldw, w_box) || !tc::make_map_bf16(&mx, a, args.m, k, lda, CL_MT))
     return QSP_ERR_UNSUPPORTED;
   auto kern = gemm_cl_kernel<NACC, MODE>;
   static bool attr_set = false;

@@ -16,6 +16,7 @@
 #include "qsp_tc.cuh"
 
 #include <cuda.h>
+#include <stdlib.h>
 
 #include <mutex>
 #include <unordered_map>
@@ -129,13 +130,18 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 }
 
 // BN weight rows per work unit: 128 (one accumulator) or 256 (two M=128 MMAs share each
-// activation tile, halving the activation re-reads of a wide projection)
-template <int MT, int BN>
+// activation tile, halving the activation re-reads of a wide projection). KPS k-blocks per ring
+// stage: with KPS = 2 each operand of a stage arrives as ONE 3-D TMA box spanning two k-blocks
+// ([k-block][rows][128 B] in shared memory). A TMA unit moves a bounded number of boxes per
+// microsecond (about 3.4 per SM on B200, whatever their size up to 32 KB), so small boxes —
+// 16 KB weight tiles, 4–8 KB activation tiles of few token rows — cap an SM's ingest well
+// below its ~110 GB/s port; two k-blocks per box double the bytes per box.
+template <int MT, int BN, int KPS = 1>
 struct TcCfg {
   static constexpr int TC_BN = BN;
-  static constexpr int W_BYTES = BN * TC_BK * 2;
+  static constexpr int W_BYTES = KPS * BN * TC_BK * 2;
   static constexpr int NACC = BN / TC_MM;   // accumulators per unit
-  static constexpr int X_BYTES = MT * TC_BK * 2;
+  static constexpr int X_BYTES = KPS * MT * TC_BK * 2;
   static constexpr int STAGE_BYTES = W_BYTES + X_BYTES;
   // one persistent CTA per SM: the ring fills ~192 KB of shared memory
   static constexpr int STAGES = (192 * 1024) / STAGE_BYTES > 8 ? 8 : (192 * 1024) / STAGE_BYTES;
@@ -318,10 +324,41 @@ __global__ void __launch_bounds__(256) splitk_swiglu_kernel(const float* __restr
   }
 }
 
-template <int MT, int BN>
+// Operand loads of one ring stage: k-blocks kb .. kb+KPS-1 of rows [row, row + box rows).
+// KPS = 1: a 2-D box at (kb·64, row); KPS = 2: a 3-D box at (0, row, kb) over the view
+// [k-blocks][rows][64 elements] of the same row-major matrix (K a multiple of 64).
+template <int KPS>
+__device__ __forceinline__ void tc_load_w(void* dst, const CUtensorMap* map, uint64_t* bar, int kb, int row) {
+  if (KPS == 1) {
+    tc::tma_load_2d_evict_first_warp(dst, map, bar, kb * TC_BK, row);
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred e;\n\t.reg .b64 pol;\n\telect.sync _|e, 0xffffffff;\n\t"
+        "createpolicy.fractional.L2::evict_first.b64 pol, 1.0;\n\t"
+        "@e cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%3, %4, "
+        "%5}], [%2], pol;\n\t}" ::"r"(smem_u32(dst)),
+        "l"(map), "r"(smem_u32(bar)), "r"(0), "r"(row), "r"(kb)
+        : "memory");
+  }
+}
+template <int KPS>
+__device__ __forceinline__ void tc_load_x(void* dst, const CUtensorMap* map, uint64_t* bar, int kb, int row) {
+  if (KPS == 1) {
+    tc::tma_load_2d_warp(dst, map, bar, kb * TC_BK, row);
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\t"
+        "@e cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];\n\t}" ::"r"(
+            smem_u32(dst)),
+        "l"(map), "r"(smem_u32(bar)), "r"(0), "r"(row), "r"(kb)
+        : "memory");
+  }
+}
+
+template <int MT, int BN, int KPS>
 __global__ void __launch_bounds__(TC_THREADS, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x, const TcArgs A) {
-  using C = TcCfg<MT, BN>;
+  using C = TcCfg<MT, BN, KPS>;
   constexpr int TC_BN = BN;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -368,41 +405,44 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
     __syncwarp();
     // The weights do not depend on the previous kernel: the first ring pass issues its
     // weight tiles before the dependency wait, and its activation tiles after it.
+    // a unit's k-blocks go in steps of KPS; step i covers k-blocks kb0 + KPS·((i + rot) % ns)
     int pre_kb[C::STAGES], pre_mb[C::STAGES];
     uint32_t npre = 0;
     for (int u = blockIdx.x; u < A.units && npre < (uint32_t)C::STAGES; u += gridDim.x) {
       const TcUnit U = tc_unit(A, u, tiles);
-      const int mb = U.tile % A.m_tiles, nb = U.tile / A.m_tiles, kb0 = U.kb0, nk = U.nk;
-      const int rot = u % nk;
-      for (int i = 0; i < nk && npre < (uint32_t)C::STAGES; ++i, ++npre) {
-        const int kb = kb0 + (i + rot) % nk;
+      const int mb = U.tile % A.m_tiles, nb = U.tile / A.m_tiles, kb0 = U.kb0;
+      const int ns = (U.nk + KPS - 1) / KPS;
+      const int rot = u % ns;
+      for (int i = 0; i < ns && npre < (uint32_t)C::STAGES; ++i, ++npre) {
+        const int kb = kb0 + KPS * ((i + rot) % ns);
         tc::mbar_expect_tx_warp(&full[npre], C::STAGE_BYTES);
-        tc::tma_load_2d_evict_first_warp(smem + npre * C::STAGE_BYTES, &tm_w, &full[npre], kb * TC_BK, nb * TC_BN);
+        tc_load_w<KPS>(smem + npre * C::STAGE_BYTES, &tm_w, &full[npre], kb, nb * TC_BN);
         pre_kb[npre] = kb;
         pre_mb[npre] = mb;
       }
     }
     pdl_wait();
     for (uint32_t j = 0; j < npre; ++j)
-      tc::tma_load_2d_warp(smem + j * C::STAGE_BYTES + C::W_BYTES, &tm_x, &full[j], pre_kb[j] * TC_BK, pre_mb[j] * MT);
+      tc_load_x<KPS>(smem + j * C::STAGE_BYTES + C::W_BYTES, &tm_x, &full[j], pre_kb[j], pre_mb[j] * MT);
     uint32_t it = 0;
     bool ok = true;
     for (int u = blockIdx.x; u < A.units && ok; u += gridDim.x) {
       const TcUnit U = tc_unit(A, u, tiles);
-      const int mb = U.tile % A.m_tiles, nb = U.tile / A.m_tiles, kb0 = U.kb0, nk = U.nk;
+      const int mb = U.tile % A.m_tiles, nb = U.tile / A.m_tiles, kb0 = U.kb0;
       // units walk their k-blocks from a rotated start so concurrent CTAs read different
       // activation slabs
-      const int rot = u % nk;
-      for (int i = 0; i < nk; ++i, ++it) {
+      const int ns = (U.nk + KPS - 1) / KPS;
+      const int rot = u % ns;
+      for (int i = 0; i < ns; ++i, ++it) {
         if (it < npre) continue;   // issued above
-        const int kb = kb0 + (i + rot) % nk;
+        const int kb = kb0 + KPS * ((i + rot) % ns);
         const int s = it % C::STAGES;
         const uint32_t ph = (it / C::STAGES) & 1u;
         if (it >= (uint32_t)C::STAGES && !mbar_wait_w(&empty[s], ph ^ 1u, 101)) { ok = false; break; }
         uint8_t* st = smem + s * C::STAGE_BYTES;
         tc::mbar_expect_tx_warp(&full[s], C::STAGE_BYTES);
-        tc::tma_load_2d_evict_first_warp(st, &tm_w, &full[s], kb * TC_BK, nb * TC_BN);
-        tc::tma_load_2d_warp(st + C::W_BYTES, &tm_x, &full[s], kb * TC_BK, mb * MT);
+        tc_load_w<KPS>(st, &tm_w, &full[s], kb, nb * TC_BN);
+        tc_load_x<KPS>(st + C::W_BYTES, &tm_x, &full[s], kb, mb * MT);
       }
     }
   } else if (warp == 1) {
@@ -415,12 +455,13 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
       bool ok = true;
       for (int u = blockIdx.x; u < A.units; u += gridDim.x, ++ui) {
         const int nk = tc_unit(A, u, tiles).nk;
+        const int ns = (nk + KPS - 1) / KPS, rot = u % ns;
         const uint32_t buf = (C::ACC_BUFS == 2) ? (ui & 1u) : 0u;
         const uint32_t use = (C::ACC_BUFS == 2) ? (ui >> 1) : ui;   // how often this buffer was used before
         if (ok && use >= 1 && !mbar_wait_w(&acc_empty[buf], (use - 1) & 1u, 104)) ok = false;
         tc_fence_after();
         const uint32_t d = tmem + buf * C::UNIT_COLS;
-        for (int i = 0; i < nk; ++i, ++it) {
+        for (int i = 0; i < ns; ++i, ++it) {
           const int s = it % C::STAGES;
           const uint32_t ph = (it / C::STAGES) & 1u;
           if (ok && !mbar_wait_w(&full[s], ph, 102)) ok = false;
@@ -428,10 +469,19 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
           if (ok) {
             const uint32_t a0 = smem_u32(smem + s * C::STAGE_BYTES);
             const uint32_t b0 = a0 + C::W_BYTES;
+            // k-blocks of this step that belong to the unit (the last step of an odd range
+            // carries one k-block of the next range, or the zero fill past K: not multiplied)
+            const int kv = min(KPS, nk - KPS * ((i + rot) % ns));
 #pragma unroll
-            for (int q = 0; q < C::NACC; ++q)   // weight rows 128q..128q+127 → accumulator q
-              tc::umma4_bf16_warp(d + q * C::ACC_COLS, sdesc_sw128(a0 + q * TC_MM * 128), sdesc_sw128(b0), idesc,
-                                  i > 0 ? 1u : 0u);
+            for (int kk = 0; kk < KPS; ++kk) {
+              if (kk < kv) {
+#pragma unroll
+                for (int q = 0; q < C::NACC; ++q)   // weight rows 128q..128q+127 → accumulator q
+                  tc::umma4_bf16_warp(d + q * C::ACC_COLS,
+                                      sdesc_sw128(a0 + kk * TC_BN * 128 + q * TC_MM * 128),
+                                      sdesc_sw128(b0 + kk * MT * 128), idesc, (i > 0 || kk > 0) ? 1u : 0u);
+              }
+            }
           }
           tc::umma_commit_warp(&empty[s]);
         }
@@ -523,6 +573,22 @@ static EncodeTiled get_encode() {
 }
 
 // 2-D bf16 row-major [rows, cols] with row stride ld (elements); box = [box_rows, 64 cols].
+// The same row-major bf16 matrix viewed as [cols/64 k-blocks][rows][64 elements] (strides
+// 128 B and ld·2 B; cols a multiple of 64): box = kps k-blocks × box_rows rows × 64 elements,
+// laid out in shared memory k-block after k-block, each as 128B-swizzled K-major rows.
+static bool make_map3(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int64_t ld, int box_rows,
+                      int kps) {
+  EncodeTiled enc = get_encode();
+  if (!enc || cols % TC_BK != 0) return false;
+  cuuint64_t dims[3] = {(cuuint64_t)TC_BK, (cuuint64_t)rows, (cuuint64_t)(cols / TC_BK)};
+  cuuint64_t strides[2] = {(cuuint64_t)(ld * 2), (cuuint64_t)(TC_BK * 2)};
+  cuuint32_t box[3] = {(cuuint32_t)TC_BK, (cuuint32_t)box_rows, (cuuint32_t)kps};
+  cuuint32_t es[3] = {1, 1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 static bool make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
   EncodeTiled enc = get_encode();
   if (!enc) return false;
@@ -543,10 +609,27 @@ static int pick_mt(int64_t m) {
 }
 
 struct TcPlan {
-  int mt, bn, m_tiles, n_tiles, n_kb, splits, kb_per_split;
+  int mt, bn, kps, m_tiles, n_tiles, n_kb, splits, kb_per_split;
   int full_units, tail_split, tail_kps;   // K-split tail of an unsplit plan (0: none)
   size_t partial_bytes;
 };
+
+// k-blocks per ring stage (TcCfg): 2 for 128-row units whose depth is a whole number of
+// k-blocks (the 3-D TMA view needs K % 64 == 0) over at most 128 token rows, or over one tile
+// of 256 token rows when the units take several rounds of the SMs (the vocabulary projection;
+// with 256 rows a two-k-block stage is 96 KB, so the ring has two stages, which costs the split
+// projections more than the larger boxes gain: measured 13.4 against 12.8 µs on 2048 × 4096,
+// 170.8 against 174.5 µs on the vocabulary). 1 otherwise. QSP_GEMM_KPS=1 keeps one k-block per stage
+// everywhere, =2 uses two wherever K allows (comparisons).
+static int kps_for(int mt, int bn, int64_t k, bool multi_round) {
+  static int mode = -1;
+  if (mode < 0) {
+    const char* e = getenv("QSP_GEMM_KPS");
+    mode = e != nullptr ? atoi(e) : 0;
+  }
+  if (mode == 1 || bn != 128 || k % TC_BK != 0) return 1;
+  return (mt <= 128 || mode == 2 || multi_round) ? 2 : 1;
+}
 
 // Split count: smallest estimated time over s in [1, 16], where one persistent CTA per SM
 // walks ceil(units / SMs) units of ceil(k_blocks / s) k-blocks each, and a split pays for
@@ -563,6 +646,7 @@ static TcPlan plan(int64_t m, int64_t n, int64_t k, int sm_count) {
   p.n_tiles = (int)((n + p.bn - 1) / p.bn);
   p.n_kb = (int)((k + TC_BK - 1) / TC_BK);
   const int tiles = p.m_tiles * p.n_tiles;
+  p.kps = kps_for(p.mt, p.bn, k, p.m_tiles == 1 && tiles > sm_count);
   // µs per k-block per SM: ingest-bound (weight tile + activation tile at ~40 GB/s per SM)
   const double t_kb = (double)(p.bn + p.mt) * TC_BK * 2 / 40.0e3;
   double est[17] = {};
@@ -584,6 +668,7 @@ static TcPlan plan(int64_t m, int64_t n, int64_t k, int sm_count) {
   int best_s = 1;
   while (est[best_s] > 1.03 * best) ++best_s;
   p.kb_per_split = (p.n_kb + best_s - 1) / best_s;
+  p.kb_per_split = (p.kb_per_split + p.kps - 1) / p.kps * p.kps;   // whole stages per split
   p.splits = (p.n_kb + p.kb_per_split - 1) / p.kb_per_split;
   p.partial_bytes = p.splits > 1 ? (size_t)p.splits * p.m_tiles * p.mt * p.n_tiles * p.bn * sizeof(float) : 0;
   // An unsplit plan whose tiles overrun whole rounds of the SMs by less than half a round
@@ -597,7 +682,7 @@ static TcPlan plan(int64_t m, int64_t n, int64_t k, int sm_count) {
     if (tiles > grid && r > 0 && 2 * r <= grid) {
       int ts = std::min(std::min(16, p.n_kb / 2), grid / r);
       if (ts >= 2) {
-        const int kps = (p.n_kb + ts - 1) / ts;
+        const int kps = ((p.n_kb + ts - 1) / ts + p.kps - 1) / p.kps * p.kps;
         p.full_units = full;
         p.tail_split = (p.n_kb + kps - 1) / kps;
         p.tail_kps = kps;
@@ -640,11 +725,11 @@ int gemm_merge(const float* partial, int splits, int64_t split_stride, int ldp, 
                     split_stride, ldp, c, ldc, n, accumulate);
 }
 
-template <int MT, int BN>
+template <int MT, int BN, int KPS = 1>
 static int launch_tc(const CUtensorMap& mw, const CUtensorMap& mx, const TcArgs& a, const TcPlan& p,
                      const GemmEpi& epi, cudaStream_t st) {
-  auto kern = gemm_tc_kernel<MT, BN>;
-  using TcCfgMT = TcCfg<MT, BN>;
+  auto kern = gemm_tc_kernel<MT, BN, KPS>;
+  using TcCfgMT = TcCfg<MT, BN, KPS>;
   static bool attr_set = false;
   if (!attr_set) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)TcCfgMT::SMEM) != cudaSuccess)
@@ -704,7 +789,11 @@ int gemm_tc(const void* a, int64_t lda, const void* w, int64_t ldw, void* c, int
   if (p.splits > 1 && epi.kind == GEMM_EPI_RESNORM && n > RN_MAXV * RN_THREADS * 4) return QSP_ERR_UNSUPPORTED;
   if (p.splits > 1 && epi.kind != GEMM_EPI_STORE && (n % 8) != 0) return QSP_ERR_UNSUPPORTED;
   CUtensorMap mw, mx;
-  if (!make_map(&mw, w, n, k, ldw, p.bn) || !make_map(&mx, a, m, k, lda, p.mt)) return QSP_ERR_UNSUPPORTED;
+  if (p.kps == 2) {
+    if (!make_map3(&mw, w, n, k, ldw, p.bn, 2) || !make_map3(&mx, a, m, k, lda, p.mt, 2)) return QSP_ERR_UNSUPPORTED;
+  } else if (!make_map(&mw, w, n, k, ldw, p.bn) || !make_map(&mx, a, m, k, lda, p.mt)) {
+    return QSP_ERR_UNSUPPORTED;
+  }
   TcArgs args{};
   args.c = static_cast<__nv_bfloat16*>(c);
   args.ldc = ldc;
@@ -720,6 +809,14 @@ int gemm_tc(const void* a, int64_t lda, const void* w, int64_t ldw, void* c, int
   args.tail_kps = p.tail_kps;
   if (split_out) *split_out = p.splits > 1;
   const bool wide = p.bn == 256;
+  if (p.kps == 2) {
+    switch (p.mt) {
+      case 32: return launch_tc<32, 128, 2>(mw, mx, args, p, epi, st);
+      case 64: return launch_tc<64, 128, 2>(mw, mx, args, p, epi, st);
+      case 128: return launch_tc<128, 128, 2>(mw, mx, args, p, epi, st);
+      default: return launch_tc<256, 128, 2>(mw, mx, args, p, epi, st);
+    }
+  }
   switch (p.mt) {
     case 32: return wide ? launch_tc<32, 256>(mw, mx, args, p, epi, st) : launch_tc<32, 128>(mw, mx, args, p, epi, st);
     case 64: return wide ? launch_tc<64, 256>(mw, mx, args, p, epi, st) : launch_tc<64, 128>(mw, mx, args, p, epi, st);
