@@ -787,7 +787,11 @@ def run_attn_workload(args):
     qn = torch.zeros(hd, dtype=torch.bfloat16, device=dev); kn = torch.zeros_like(qn)
     cos, sin = rope_table(rd, 1e7, hi + 8, torch.bfloat16)
     cos, sin = cos.to(dev), sin.to(dev)
-    splits = max(1, (hi + args.attn_split_len - 1) // args.attn_split_len)   # fixed-length key splits
+    if args.attn_split_len > 0:                  # fixed-length key splits of this many keys
+        splits = max(1, (hi + args.attn_split_len - 1) // args.attn_split_len)
+    else:                                        # the model's choice for this capacity and batch
+        from lollm_b200.qwen3_5.modeling_qwen3_5 import attn_num_splits
+        splits = attn_num_splits(max_pages * ps, B * nkv)
     q_buf = torch.empty(B * T, nh * hd, dtype=torch.bfloat16, device=dev)
     out = torch.empty(B * T, nh * hd, dtype=torch.bfloat16, device=dev)
     part = torch.empty(K.attn_workspace_bytes(B, T, nh, hd, splits) // 4, device=dev)
@@ -1263,8 +1267,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--attn-len", default="1024,32768",
                     help="attn workload: per-sequence context lengths ~ U[lo, hi] (configs[2]: 1024,32768)")
-    ap.add_argument("--attn-split-len", type=int, default=512,
-                    help="attn workload: keys per split (the split count is the longest context over this)")
+    ap.add_argument("--attn-split-len", type=int, default=0,
+                    help="attn workload: keys per split (the split count is the longest context over this); "
+                         "0: the model's split count for this capacity and batch")
     ap.add_argument("--attn-equal", default="1024,4096,16384,32768",
                     help="attn_compare workload: the equal context lengths to time")
     ap.add_argument("--profile", action="store_true",

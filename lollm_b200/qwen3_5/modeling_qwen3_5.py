@@ -81,6 +81,18 @@ class _Workspace:
         return self._logits
 
 
+def attn_num_splits(capacity: int, n_seq_heads: int, sms: int = 148) -> int:
+    """Key splits per (sequence, kv head) of the verify attention; the splits have a fixed
+    length of capacity / splits keys, so short sequences of a ragged batch use fewer of them.
+    Measured on B200 (64 sequences, 2 kv heads, head dim 256, T = 4): at 2–2.5k keys two
+    splits are fastest (81.9 µs per call, against 86.1 with three and 96.0 with five); over
+    configs[2]'s 1k–32k keys, 1024-key splits (0.593 of measured HBM, against 0.546 with 512
+    and 1536). Small batches take enough splits to give every SM an item."""
+    by_len = 2 if capacity <= 4096 else math.ceil(capacity / 1024)
+    by_fill = math.ceil(sms / max(n_seq_heads, 1))
+    return max(1, min(max(by_len, by_fill), math.ceil(capacity / 32)))
+
+
 class Qwen3_5Model:
     def __init__(self, cfg: Qwen3_5Config, params: dict, *, dtype=torch.bfloat16, device="cuda",
                  max_positions: int = 8192, page_size: int = 64, max_spec_tokens: int = 8):
@@ -135,12 +147,8 @@ class Qwen3_5Model:
                             max_spec_tokens=kw.pop("max_spec_tokens", self.max_spec_tokens), **kw)
 
     def default_splits(self, B: int, cache: Qwen3_5Cache) -> int:
-        """Key splits per (sequence, kv head): ~512 keys per split, and enough CTAs to fill
-        the SMs twice over."""
-        n_seq_heads = B * self.cfg.num_key_value_heads
-        by_len = math.ceil(cache.capacity / 512)
-        by_fill = math.ceil(2 * 148 / max(n_seq_heads, 1))
-        return max(1, min(max(by_len, by_fill), math.ceil(cache.capacity / 32)))
+        """Key splits per (sequence, kv head) of the verify attention: `attn_num_splits`."""
+        return attn_num_splits(cache.capacity, B * self.cfg.num_key_value_heads)
 
     def workspace(self, B: int, T: int, cache: Qwen3_5Cache) -> _Workspace:
         key = (B, T, cache.capacity)
