@@ -33,6 +33,19 @@ int gemm_pair(const void* a, int64_t lda, const void* w, int64_t ldw, void* c, i
               int64_t k, int mode, const void* norm_w, void* y, int64_t ldy, float eps, void* workspace,
               size_t ws_bytes, cudaStream_t st);
 size_t gemm_pair_workspace(int64_t m, int64_t n, int64_t k);
+int gemm_pair_persistent(const void* a, int64_t lda, const void* w, int64_t ldw, void* c, int64_t ldc, int64_t m,
+                         int64_t n, int64_t k, cudaStream_t st);
+
+// Plain verify-row products whose tiles take several rounds (the vocabulary projection) take
+// the persistent CTA-pair kernel unless QSP_GEMM_PAIRP=0 (comparisons).
+static bool pairp_on() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("QSP_GEMM_PAIRP");
+    v = e != nullptr ? atoi(e) : 1;
+  }
+  return v != 0;
+}
 
 // Which products take the CTA-pair kernel (bit 0: plain, bit 1: SwiGLU, bit 2: residual +
 // RMSNorm). By default only plain products at least PAIR_WIDE_N columns wide do (measured on
@@ -84,6 +97,10 @@ static int gemm_any(const void* a, int64_t lda, const void* w, int64_t ldw, void
     // projections — qkv 16.3 vs 20.6 µs, in_proj 23.9 vs 24.6 µs — and slower for the
     // residual and SwiGLU tails, which therefore keep the persistent kernel.)
     // verify-sized rows: one CTA pair per tile of weight rows, whole K, epilogue in place
+    if (flags == 0 && epi == nullptr && pairp_on()) {
+      const int rp = gemm_pair_persistent(a, lda, w, ldw, c, ldc, m, n, k, st);
+      if (rp != QSP_ERR_UNSUPPORTED) return rp;
+    }
     if (flags == 0 && epi == nullptr && pair_for(1, n)) {
       const int rp = gemm_pair(a, lda, w, ldw, c, ldc, m, n, k, 0, nullptr, nullptr, 0, 0.f, ws, ws_bytes, st);
       if (rp != QSP_ERR_UNSUPPORTED) return rp;

@@ -409,4 +409,249 @@ int gemm_pair(const void* a, int64_t lda, const void* w, int64_t ldw, void* c, i
                     static_cast<const __nv_bfloat16*>(norm_w), static_cast<__nv_bfloat16*>(y), ldy, (int)n, eps);
 }
 
+
+// ------------------------------------------------------------------ persistent pair (STORE)
+// For plain products whose tiles take several rounds of the pairs (the vocabulary projection
+// over the verify rows): pair p computes tiles p, p + P, p + 2P, ... of N weight rows × all
+// 256 token rows, whole K each. Both CTAs stream their halves through one continuous ring
+// across tiles; rank 0 issues the MMAs into one of two TMEM accumulator buffers (N ≤ 256
+// columns each), so a tile's epilogue overlaps the next tile's MMAs. Each epilogue thread owns
+// one token row of its CTA's accumulator and writes its bf16 outputs with 16-byte stores, then
+// its warp releases the buffer on rank 0's barrier (8 arrivals: 4 warps in each CTA).
+// Per SM and k-block the ring takes 16 KB of activations and N/2·128 B of weights, against
+// 32 KB + 16 KB for a 128-row unit of the persistent single-CTA kernel.
+struct PairPArgs {
+  __nv_bfloat16* c;
+  int64_t ldc;
+  int m, n;           // token rows, output columns
+  int N;              // weight rows per tile (MMA N, a multiple of 16, ≤ 256)
+  int tiles, n_kb, stages, w_bytes;
+};
+
+__global__ void __launch_bounds__(192, 1)
+gemm_pairp_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
+                  const PairPArgs A) {
+  using namespace tc;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int S = A.stages;
+  const uint32_t stage_bytes = PAIR_X_BYTES + A.w_bytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)S * stage_bytes);   // used in rank 0
+  uint64_t* empty = full + S;
+  uint64_t* acc_full = empty + S;    // [2], both CTAs (MMA commits are multicast)
+  uint64_t* acc_empty = acc_full + 2;  // [2], rank 0 (arrivals from both CTAs' epilogue warps)
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  volatile int* abort = reinterpret_cast<volatile int*>(tslot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int pair = blockIdx.x >> 1, P = gridDim.x >> 1;
+  const int half = A.N >> 1;
+  const int trow = (int)rank * 128;
+  const int my_tiles = pair < A.tiles ? (A.tiles - 1 - pair) / P + 1 : 0;
+  const int total = my_tiles * A.n_kb;   // ring iterations of this CTA
+  pdl_trigger();
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 8);
+    }
+    *abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) tmem_alloc_pair(tslot, 512u);
+  fence_before();
+  cluster_sync_all();   // both CTAs' barriers are initialised before any cross-CTA arrival
+  fence_after();
+  const uint32_t tmem = *tslot;
+
+  if (warp == 0) {
+    // producer: the whole warp runs the loop, one elected lane issues; both CTAs' bytes of a
+    // stage complete on rank 0's full barrier, which rank 0 arms for both
+    if (lane == 0) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(&tm_w) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(&tm_x) : "memory");
+    }
+    __syncwarp();
+    const int npre = min(total, S);
+    for (int i = 0; i < npre; ++i) {   // weights of the first ring pass before the dependency wait
+      const int tile = pair + (i / A.n_kb) * P, kb = i % A.n_kb;
+      if (rank == 0) mbar_expect_tx_warp(&full[i], 2 * stage_bytes);
+      tma_load_2d_pair_evict_first_warp(smem + i * stage_bytes + PAIR_X_BYTES, &tm_w,
+                                        cluster_addr(smem_u32(&full[i]), 0), kb * 64, tile * A.N + (int)rank * half);
+    }
+    pdl_wait();   // activations are the previous kernel's output
+    for (int i = 0; i < npre; ++i)
+      tma_load_2d_pair_warp(smem + i * stage_bytes, &tm_x, cluster_addr(smem_u32(&full[i]), 0), (i % A.n_kb) * 64,
+                            trow);
+    bool ok = true;
+    for (int i = npre; i < total; ++i) {
+      const int s = i % S;
+      const uint32_t ph = (i / S) & 1u;
+      ok = mbar_wait_warp(&empty[s], ph ^ 1u, 611, &g_gemm_pair_error, abort);
+      if (!ok) break;
+      const int tile = pair + (i / A.n_kb) * P, kb = i % A.n_kb;
+      const uint32_t fb = cluster_addr(smem_u32(&full[s]), 0);
+      uint8_t* st = smem + s * stage_bytes;
+      if (rank == 0) mbar_expect_tx_warp(&full[s], 2 * stage_bytes);
+      tma_load_2d_pair_evict_first_warp(st + PAIR_X_BYTES, &tm_w, fb, kb * 64, tile * A.N + (int)rank * half);
+      tma_load_2d_pair_warp(st, &tm_x, fb, kb * 64, trow);
+    }
+    // the last release of every stage (an MMA-completion arrival from rank 0) has landed
+    for (int s = 0; ok && s < npre; ++s) {
+      const int last = (total - 1 - s) / S;
+      ok = mbar_wait_warp(&empty[s], (uint32_t)last & 1u, 612, &g_gemm_pair_error, abort);
+    }
+  } else if (warp == 1) {
+    pdl_wait();
+    if (rank == 0) {   // MMA issuer: the whole warp, one elected lane issues
+      const uint32_t idesc = idesc_bf16(256, A.N);
+      bool ok = true;
+      int i = 0;
+      for (int ti = 0; ti < my_tiles; ++ti) {
+        const uint32_t b = ti & 1, use = ti >> 1;
+        if (ok && use >= 1) ok = mbar_wait_warp(&acc_empty[b], (use - 1) & 1u, 613, &g_gemm_pair_error, abort);
+        fence_after();
+        for (int kb = 0; kb < A.n_kb; ++kb, ++i) {
+          const int s = i % S;
+          const uint32_t ph = (i / S) & 1u;
+          if (ok) ok = mbar_wait_warp(&full[s], ph, 614, &g_gemm_pair_error, abort);
+          fence_after();
+          if (ok) {
+            const uint32_t xa = smem_u32(smem + s * stage_bytes);
+            umma4_bf16_pair_warp(tmem + b * 256, sdesc_sw128(xa), sdesc_sw128(xa + PAIR_X_BYTES), idesc,
+                                 kb > 0 ? 1u : 0u);
+          }
+          umma_commit_pair_warp(&empty[s]);
+        }
+        umma_commit_pair_warp(&acc_full[b]);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue
+    pdl_wait();
+    const int quad = warp & 3;
+    const int t = trow + quad * 32 + lane;
+    const uint32_t release = cluster_addr(smem_u32(&acc_empty[0]), 0);
+    for (int ti = 0; ti < my_tiles; ++ti) {
+      const uint32_t b = ti & 1;
+      const bool ok = mbar_wait(&acc_full[b], (ti >> 1) & 1u, 615, &g_gemm_pair_error, abort);
+      fence_after();
+      const int n0 = (pair + ti * P) * A.N;
+      const uint32_t tbase = tmem + b * 256 + ((uint32_t)(quad * 32) << 16);
+      __nv_bfloat16* crow = A.c + (int64_t)t * A.ldc;
+      for (int c0 = 0; c0 < A.N; c0 += 16) {
+        float v[16];
+        tmem_ld16(tbase + c0, v);
+        if (!ok || t >= A.m) continue;
+        const int col = n0 + c0;
+        if (col + 16 <= A.n) {
+          uint4 ov[2];
+          __nv_bfloat16* oh = reinterpret_cast<__nv_bfloat16*>(ov);
+#pragma unroll
+          for (int e = 0; e < 16; ++e) oh[e] = __float2bfloat16_rn(v[e]);
+          reinterpret_cast<uint4*>(crow + col)[0] = ov[0];
+          reinterpret_cast<uint4*>(crow + col)[1] = ov[1];
+        } else {
+#pragma unroll
+          for (int e = 0; e < 16; ++e)
+            if (col + e < A.n) crow[col + e] = __float2bfloat16_rn(v[e]);
+        }
+      }
+      fence_before();
+      __syncwarp();
+      if (lane == 0)
+        asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(release + b * 8u)
+                     : "memory");
+    }
+  }
+  fence_before();
+  __syncthreads();
+  cluster_sync_all();   // the partner's arrivals have landed; it is done with this CTA's memory
+  if (warp == 1) {
+    fence_after();
+    tmem_dealloc_pair(tmem, 512u);
+  }
+}
+
+// Tile width of the persistent pair kernel: the multiple of 16 in [128, 256] that minimises
+// the per-CTA ingest (rounds of tiles × the bytes of one k-block: 16 KB of activations + N/2
+// weight rows), ties to the wider tile. Returns false when one round covers the output (the
+// one-shot kernel's case) or the shape does not fit.
+static bool pairp_plan(int64_t m, int64_t n, int64_t k, int pairs, int* N_out, int* tiles_out) {
+  if (m <= 128 || m > 256 || pairs <= 0 || n <= 256 * (int64_t)pairs) return false;
+  double best = 1e300;
+  for (int N = 256; N >= 128; N -= 16) {
+    const int64_t tiles = (n + N - 1) / N;
+    const int64_t rounds = (tiles + pairs - 1) / pairs;
+    const double cost = (double)rounds * (PAIR_X_BYTES + (N / 2) * 128);
+    if (cost < best) {
+      best = cost;
+      *N_out = N;
+      *tiles_out = (int)tiles;
+    }
+  }
+  (void)k;
+  return true;
+}
+
+// c[m, n] = a · wᵀ through the persistent pair kernel; QSP_ERR_UNSUPPORTED when the shape or
+// alignment does not fit (the caller then takes another kernel).
+int gemm_pair_persistent(const void* a, int64_t lda, const void* w, int64_t ldw, void* c, int64_t ldc, int64_t m,
+                         int64_t n, int64_t k, cudaStream_t st) {
+  if (!aligned(a, 16) || !aligned(w, 16) || !aligned(c, 16) || (lda * 2) % 16 != 0 || (ldw * 2) % 16 != 0 ||
+      (ldc * 2) % 16 != 0 || k % 8 != 0)
+    return QSP_ERR_UNSUPPORTED;
+  const int pairs = resident_pairs();
+  int N = 0, tiles = 0;
+  if (!pairp_plan(m, n, k, pairs, &N, &tiles)) return QSP_ERR_UNSUPPORTED;
+  PairPArgs args{};
+  args.c = static_cast<__nv_bfloat16*>(c);
+  args.ldc = ldc;
+  args.m = (int)m;
+  args.n = (int)n;
+  args.N = N;
+  args.tiles = tiles;
+  args.n_kb = ceil_div(k, 64);
+  args.w_bytes = (N / 2) * 128;
+  args.stages = std::min(PAIR_MAX_STAGES, (PAIR_SMEM_MAX - PAIR_AUX) / (PAIR_X_BYTES + args.w_bytes));
+  CUtensorMap mw, mx;
+  if (!tc::make_map_bf16(&mw, w, n, k, ldw, N / 2) || !tc::make_map_bf16(&mx, a, m, k, lda, 128))
+    return QSP_ERR_UNSUPPORTED;
+  auto kern = gemm_pairp_kernel;
+  const size_t smem = (size_t)args.stages * (PAIR_X_BYTES + args.w_bytes) + PAIR_AUX;
+  static bool attr_set = false;
+  if (!attr_set) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, PAIR_SMEM_MAX) != cudaSuccess)
+      return set_error(QSP_ERR_CUDA, "qsp_gemm(pair, persistent): cannot reserve %d bytes of shared memory",
+                       PAIR_SMEM_MAX);
+    attr_set = true;
+  }
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(2 * std::min(pairs, tiles));
+  cfg.blockDim = dim3(192);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[2];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = 2;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 2;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, mw, mx, args);
+  if (e != cudaSuccess) {
+    (void)cudaGetLastError();
+    return set_error(QSP_ERR_CUDA, "qsp_gemm(pair, persistent): %s", cudaGetErrorString(e));
+  }
+  return check_launch("qsp_gemm(pair, persistent)");
+}
+
 }  // namespace qsp

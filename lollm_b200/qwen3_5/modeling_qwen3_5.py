@@ -84,12 +84,15 @@ class _Workspace:
 def attn_num_splits(capacity: int, n_seq_heads: int, sms: int = 148) -> int:
     """Key splits per (sequence, kv head) of the verify attention; the splits have a fixed
     length of capacity / splits keys, so short sequences of a ragged batch use fewer of them.
-    Measured on B200 (64 sequences, 2 kv heads, head dim 256, T = 4): at 2–2.5k keys two
-    splits are fastest (81.9 µs per call, against 86.1 with three and 96.0 with five); over
-    configs[2]'s 1k–32k keys, 1024-key splits (0.593 of measured HBM, against 0.546 with 512
-    and 1536). Small batches take enough splits to give every SM an item."""
-    by_len = 2 if capacity <= 4096 else math.ceil(capacity / 1024)
-    by_fill = math.ceil(sms / max(n_seq_heads, 1))
+    Every work item (split × sequence × kv head) costs a fixed overhead, and one round of items
+    over the SMs already balances the load when the sequences are about equally long, so a
+    short context takes as many splits as fill the SMs once. Measured on B200 (64 sequences,
+    2 kv heads, head dim 256, T = 4, L ~ U[2048, 2560]): 1 split 75.2 µs per call, 2 splits 81.5,
+    3 splits 86.1, 5 splits 96.0. Long ragged contexts need more splits to balance: over
+    configs[2]'s 1k–32k keys, 1024-key splits measured best (0.593 of measured HBM, against
+    0.546 with 512 and 1536)."""
+    by_len = 1 if capacity <= 4096 else math.ceil(capacity / 1024)
+    by_fill = max(1, sms // max(n_seq_heads, 1))
     return max(1, min(max(by_len, by_fill), math.ceil(capacity / 32)))
 
 

@@ -229,11 +229,11 @@ def test_two_b_speculative_step_matches_oracle(two_b):
     print(f"end-to-end verify logits drift: {drift:.4f} of the largest logit")
 
 
-@pytest.mark.parametrize("splits", [64, 32, 2])
+@pytest.mark.parametrize("splits", [64, 32, 1])
 def test_attention_at_configs2_lengths(splits):
     """16 q / 2 kv heads of 256, T=4, contexts spanning [1024, 32768], page size
     64 (the tensor-core kernel), at 64 splits, at the split count the model and the isolated
-    bench take at a 32k capacity (32) and at the step's 2.3k capacity (2), against the
+    bench take at a 32k capacity (32) and at the step's 2.3k capacity (1), against the
     oracle's offset-causal attention."""
     from test_gpu_kernels import _attn_case, _attn_reference
     from lollm_b200 import kernels as K

@@ -57,7 +57,10 @@ def test_rmsnorm_and_add(dt):
                                  (256, 2048, 4096), (256, 12352, 2048), (64, 4608, 2048), (300, 256, 512),
                                  (1024, 384, 256), (16, 256, 64), (33, 200, 6144),
                                  # 149 weight tiles on 148 SMs: the last tile is split along K
-                                 (64, 19000, 1024), (100, 19072, 520)])
+                                 (64, 19000, 1024), (100, 19072, 520),
+                                 # several rounds of tiles over the CTA pairs (the persistent pair
+                                 # kernel), one with a partial last 16-column chunk
+                                 (256, 40000, 512), (136, 19016, 256)])
 def test_gemm(dt, mnk):
     m, n, k = mnk
     g = gen(1)
