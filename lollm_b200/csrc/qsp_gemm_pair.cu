@@ -410,6 +410,44 @@ int gemm_pair(const void* a, int64_t lda, const void* w, int64_t ldw, void* c, i
 }
 
 
+// 3-D TMA load (k-blocks kb, kb+1 of rows [y, y + box rows) over the view [k-blocks][rows][64])
+// into this CTA's shared memory, completing on the pair leader's barrier; weights evict-first.
+__device__ __forceinline__ void tma_load_3d_pair_warp(void* dst, const CUtensorMap* map, uint32_t bar_cluster, int y,
+                                                      int kb, bool evict_first) {
+  if (evict_first) {
+    asm volatile(
+        "{\n\t.reg .pred e;\n\t.reg .b64 pol;\n\telect.sync _|e, 0xffffffff;\n\t"
+        "createpolicy.fractional.L2::evict_first.b64 pol, 1.0;\n\t"
+        "@e cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
+        "[%0], [%1, {%3, %4, %5}], [%2], pol;\n\t}" ::"r"(tc::smem_u32(dst)),
+        "l"(map), "r"(bar_cluster), "r"(0), "r"(y), "r"(kb)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\t"
+        "@e cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, "
+        "%4, %5}], [%2];\n\t}" ::"r"(tc::smem_u32(dst)),
+        "l"(map), "r"(bar_cluster), "r"(0), "r"(y), "r"(kb)
+        : "memory");
+  }
+}
+
+// bf16 row-major [rows, cols] viewed as [cols/64 k-blocks][rows][64 elements] (cols a multiple
+// of 64): a box of kps k-blocks × box_rows rows lands k-block after k-block in shared memory,
+// each as 128B-swizzled K-major rows.
+static bool make_map3_bf16(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int64_t ld, int box_rows,
+                           int kps) {
+  tc::EncodeTiled enc = tc::get_encode();
+  if (!enc || cols % 64 != 0) return false;
+  cuuint64_t dims[3] = {64, (cuuint64_t)rows, (cuuint64_t)(cols / 64)};
+  cuuint64_t strides[2] = {(cuuint64_t)(ld * 2), 128};
+  cuuint32_t box[3] = {64, (cuuint32_t)box_rows, (cuuint32_t)kps};
+  cuuint32_t es[3] = {1, 1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // ------------------------------------------------------------------ persistent pair (STORE)
 // For plain products whose tiles take several rounds of the pairs (the vocabulary projection
 // over the verify rows): pair p computes tiles p, p + P, p + 2P, ... of N weight rows × all
@@ -419,14 +457,17 @@ int gemm_pair(const void* a, int64_t lda, const void* w, int64_t ldw, void* c, i
 // one token row of its CTA's accumulator and writes its bf16 outputs with 16-byte stores, then
 // its warp releases the buffer on rank 0's barrier (8 arrivals: 4 warps in each CTA).
 // Per SM and k-block the ring takes 16 KB of activations and N/2·128 B of weights, against
-// 32 KB + 16 KB for a 128-row unit of the persistent single-CTA kernel.
+// 32 KB + 16 KB for a 128-row unit of the persistent single-CTA kernel. A ring stage holds
+// two k-blocks, each operand loaded as one 3-D TMA box: an SM's TMA moves a bounded number of
+// boxes per microsecond, and 16 KB boxes would cap its ingest near 55 GB/s.
 struct PairPArgs {
   __nv_bfloat16* c;
   int64_t ldc;
   int m, n;           // token rows, output columns
   int N;              // weight rows per tile (MMA N, a multiple of 16, ≤ 256)
-  int tiles, n_kb, stages, w_bytes;
+  int tiles, n_kb, stages, w_bytes;   // n_kb: k-blocks (even); w_bytes: weights of one k-block
 };
+constexpr int PAIRP_KPS = 2;         // k-blocks per ring stage
 
 __global__ void __launch_bounds__(192, 1)
 gemm_pairp_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
@@ -435,7 +476,9 @@ gemm_pairp_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constan
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int S = A.stages;
-  const uint32_t stage_bytes = PAIR_X_BYTES + A.w_bytes;
+  constexpr int KP = PAIRP_KPS;
+  const uint32_t x_bytes = KP * PAIR_X_BYTES;               // [k-block][128 token rows][128 B]
+  const uint32_t stage_bytes = x_bytes + KP * A.w_bytes;    // then [k-block][N/2 rows][128 B]
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)S * stage_bytes);   // used in rank 0
   uint64_t* empty = full + S;
   uint64_t* acc_full = empty + S;    // [2], both CTAs (MMA commits are multicast)
@@ -449,7 +492,8 @@ gemm_pairp_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constan
   const int half = A.N >> 1;
   const int trow = (int)rank * 128;
   const int my_tiles = pair < A.tiles ? (A.tiles - 1 - pair) / P + 1 : 0;
-  const int total = my_tiles * A.n_kb;   // ring iterations of this CTA
+  const int steps = A.n_kb / KP;          // ring stages per tile
+  const int total = my_tiles * steps;     // ring iterations of this CTA
   pdl_trigger();
 
   if (threadIdx.x == 0) {
@@ -480,27 +524,27 @@ gemm_pairp_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constan
     __syncwarp();
     const int npre = min(total, S);
     for (int i = 0; i < npre; ++i) {   // weights of the first ring pass before the dependency wait
-      const int tile = pair + (i / A.n_kb) * P, kb = i % A.n_kb;
+      const int tile = pair + (i / steps) * P, kb = (i % steps) * KP;
       if (rank == 0) mbar_expect_tx_warp(&full[i], 2 * stage_bytes);
-      tma_load_2d_pair_evict_first_warp(smem + i * stage_bytes + PAIR_X_BYTES, &tm_w,
-                                        cluster_addr(smem_u32(&full[i]), 0), kb * 64, tile * A.N + (int)rank * half);
+      tma_load_3d_pair_warp(smem + i * stage_bytes + x_bytes, &tm_w, cluster_addr(smem_u32(&full[i]), 0),
+                            tile * A.N + (int)rank * half, kb, true);
     }
     pdl_wait();   // activations are the previous kernel's output
     for (int i = 0; i < npre; ++i)
-      tma_load_2d_pair_warp(smem + i * stage_bytes, &tm_x, cluster_addr(smem_u32(&full[i]), 0), (i % A.n_kb) * 64,
-                            trow);
+      tma_load_3d_pair_warp(smem + i * stage_bytes, &tm_x, cluster_addr(smem_u32(&full[i]), 0), trow,
+                            (i % steps) * KP, false);
     bool ok = true;
     for (int i = npre; i < total; ++i) {
       const int s = i % S;
       const uint32_t ph = (i / S) & 1u;
       ok = mbar_wait_warp(&empty[s], ph ^ 1u, 611, &g_gemm_pair_error, abort);
       if (!ok) break;
-      const int tile = pair + (i / A.n_kb) * P, kb = i % A.n_kb;
+      const int tile = pair + (i / steps) * P, kb = (i % steps) * KP;
       const uint32_t fb = cluster_addr(smem_u32(&full[s]), 0);
       uint8_t* st = smem + s * stage_bytes;
       if (rank == 0) mbar_expect_tx_warp(&full[s], 2 * stage_bytes);
-      tma_load_2d_pair_evict_first_warp(st + PAIR_X_BYTES, &tm_w, fb, kb * 64, tile * A.N + (int)rank * half);
-      tma_load_2d_pair_warp(st, &tm_x, fb, kb * 64, trow);
+      tma_load_3d_pair_warp(st + x_bytes, &tm_w, fb, tile * A.N + (int)rank * half, kb, true);
+      tma_load_3d_pair_warp(st, &tm_x, fb, trow, kb, false);
     }
     // the last release of every stage (an MMA-completion arrival from rank 0) has landed
     for (int s = 0; ok && s < npre; ++s) {
@@ -517,15 +561,17 @@ gemm_pairp_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constan
         const uint32_t b = ti & 1, use = ti >> 1;
         if (ok && use >= 1) ok = mbar_wait_warp(&acc_empty[b], (use - 1) & 1u, 613, &g_gemm_pair_error, abort);
         fence_after();
-        for (int kb = 0; kb < A.n_kb; ++kb, ++i) {
+        for (int j = 0; j < steps; ++j, ++i) {
           const int s = i % S;
           const uint32_t ph = (i / S) & 1u;
           if (ok) ok = mbar_wait_warp(&full[s], ph, 614, &g_gemm_pair_error, abort);
           fence_after();
           if (ok) {
             const uint32_t xa = smem_u32(smem + s * stage_bytes);
-            umma4_bf16_pair_warp(tmem + b * 256, sdesc_sw128(xa), sdesc_sw128(xa + PAIR_X_BYTES), idesc,
-                                 kb > 0 ? 1u : 0u);
+#pragma unroll
+            for (int kk = 0; kk < KP; ++kk)
+              umma4_bf16_pair_warp(tmem + b * 256, sdesc_sw128(xa + kk * PAIR_X_BYTES),
+                                   sdesc_sw128(xa + x_bytes + kk * A.w_bytes), idesc, (j > 0 || kk > 0) ? 1u : 0u);
           }
           umma_commit_pair_warp(&empty[s]);
         }
@@ -609,7 +655,7 @@ int gemm_pair_persistent(const void* a, int64_t lda, const void* w, int64_t ldw,
     return QSP_ERR_UNSUPPORTED;
   const int pairs = resident_pairs();
   int N = 0, tiles = 0;
-  if (!pairp_plan(m, n, k, pairs, &N, &tiles)) return QSP_ERR_UNSUPPORTED;
+  if (k % (64 * PAIRP_KPS) != 0 || !pairp_plan(m, n, k, pairs, &N, &tiles)) return QSP_ERR_UNSUPPORTED;
   PairPArgs args{};
   args.c = static_cast<__nv_bfloat16*>(c);
   args.ldc = ldc;
@@ -619,12 +665,14 @@ int gemm_pair_persistent(const void* a, int64_t lda, const void* w, int64_t ldw,
   args.tiles = tiles;
   args.n_kb = ceil_div(k, 64);
   args.w_bytes = (N / 2) * 128;
-  args.stages = std::min(PAIR_MAX_STAGES, (PAIR_SMEM_MAX - PAIR_AUX) / (PAIR_X_BYTES + args.w_bytes));
+  const int stage = PAIRP_KPS * (PAIR_X_BYTES + args.w_bytes);
+  args.stages = std::min(PAIR_MAX_STAGES, (PAIR_SMEM_MAX - PAIR_AUX) / stage);
+  if (args.stages < 2) return QSP_ERR_UNSUPPORTED;
   CUtensorMap mw, mx;
-  if (!tc::make_map_bf16(&mw, w, n, k, ldw, N / 2) || !tc::make_map_bf16(&mx, a, m, k, lda, 128))
+  if (!make_map3_bf16(&mw, w, n, k, ldw, N / 2, PAIRP_KPS) || !make_map3_bf16(&mx, a, m, k, lda, 128, PAIRP_KPS))
     return QSP_ERR_UNSUPPORTED;
   auto kern = gemm_pairp_kernel;
-  const size_t smem = (size_t)args.stages * (PAIR_X_BYTES + args.w_bytes) + PAIR_AUX;
+  const size_t smem = (size_t)args.stages * stage + PAIR_AUX;
   static bool attr_set = false;
   if (!attr_set) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, PAIR_SMEM_MAX) != cudaSuccess)
