@@ -369,6 +369,20 @@ __device__ __forceinline__ void at2_tma(void* dst, const CUtensorMap* map, uint6
       : "memory");
 }
 
+// The whole head-dim width of a 32-key tile as ONE 3-D box over the view
+// [hd/64 column blocks][rows][64 elements] (strides hd·2 B and 128 B): it lands column block
+// after column block, each 32 rows × 128 B swizzled — the layout of hd/64 separate 2-D boxes —
+// in one TMA request instead of hd/64 (an SM's TMA moves a bounded number of boxes per µs).
+__device__ __forceinline__ void at3_tma(void* dst, const CUtensorMap* map, uint64_t* bar, int y) {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%3, %4, %5}], "
+      "[%2], %6;" ::"r"(su32(dst)),
+      "l"(map), "r"(su32(bar)), "r"(0), "r"(y), "r"(0), "l"(pol)
+      : "memory");
+}
+
 __device__ __forceinline__ void at2_wait(uint64_t* bar, uint32_t parity) {
   for (uint32_t i = 0; i < (1u << 24); ++i) {
     uint32_t ok;
@@ -664,6 +678,19 @@ static At2Encode at2_encode() {
 
 // Paged K or V of one layer as a 2-D bf16 tensor [num_pages·n_kv·page_size rows, hd], box of
 // 32 rows x 64 head dims, 128-byte swizzle.
+// [rows, hd] bf16 viewed as [hd/64][rows][64] for at3_tma: box = 64 × AT2_KT rows × hd/64.
+static bool at3_map(CUtensorMap* m, const void* base, int64_t rows, int hd) {
+  At2Encode enc = at2_encode();
+  if (!enc || hd % 64 != 0) return false;
+  cuuint64_t dims[3] = {64, (cuuint64_t)rows, (cuuint64_t)(hd / 64)};
+  cuuint64_t strides[2] = {(cuuint64_t)hd * 2, 128};
+  cuuint32_t box[3] = {64, (cuuint32_t)AT2_KT, (cuuint32_t)(hd / 64)};
+  cuuint32_t es[3] = {1, 1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 static bool at2_map(CUtensorMap* m, const void* base, int64_t rows, int hd) {
   At2Encode enc = at2_encode();
   if (!enc) return false;
@@ -842,11 +869,8 @@ attn_ws_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ 
         asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(&full[st])), "r"(SM::STAGE)
                      : "memory");
         uint8_t* kd = ring + st * SM::STAGE;
-#pragma unroll
-        for (int nb = 0; nb < SM::NB; ++nb) {
-          at2_tma(kd + nb * SM::BOX, &tmK, &full[st], nb * 64, row);
-          at2_tma(kd + SM::KV + nb * SM::BOX, &tmV, &full[st], nb * 64, row);
-        }
+        at3_tma(kd, &tmK, &full[st], row);
+        at3_tma(kd + SM::KV, &tmV, &full[st], row);
       }
     }
     return;
@@ -1015,7 +1039,7 @@ int launch_attn_ws(const qsp_attn_layer& L, cudaStream_t st) {
   if (rows >= (1ll << 31) || !aligned(L.k_pages, 16) || !aligned(L.v_pages, 16) || !aligned(L.q_buf, 16))
     return QSP_ERR_UNSUPPORTED;
   CUtensorMap mk, mv;
-  if (!at2_map(&mk, L.k_pages, rows, L.head_dim) || !at2_map(&mv, L.v_pages, rows, L.head_dim))
+  if (!at3_map(&mk, L.k_pages, rows, L.head_dim) || !at3_map(&mv, L.v_pages, rows, L.head_dim))
     return QSP_ERR_UNSUPPORTED;
   const int rows_total = (L.n_heads / L.n_kv_heads) * L.tokens;
   const int n_rg = (rows_total + AM_ROWS - 1) / AM_ROWS;

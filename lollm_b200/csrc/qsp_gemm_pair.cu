@@ -43,6 +43,44 @@ constexpr int PAIR_SMEM_MAX = 232448;                   // 227 KB opt-in per CTA
 constexpr int PAIR_AUX = 1024 + 512;                    // alignment slack + barriers
 constexpr int PAIR_MAX_STAGES = 16;
 
+// 3-D TMA load (k-blocks kb, kb+1 of rows [y, y + box rows) over the view [k-blocks][rows][64])
+// into this CTA's shared memory, completing on the pair leader's barrier; weights evict-first.
+__device__ __forceinline__ void tma_load_3d_pair_warp(void* dst, const CUtensorMap* map, uint32_t bar_cluster, int y,
+                                                      int kb, bool evict_first) {
+  if (evict_first) {
+    asm volatile(
+        "{\n\t.reg .pred e;\n\t.reg .b64 pol;\n\telect.sync _|e, 0xffffffff;\n\t"
+        "createpolicy.fractional.L2::evict_first.b64 pol, 1.0;\n\t"
+        "@e cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
+        "[%0], [%1, {%3, %4, %5}], [%2], pol;\n\t}" ::"r"(tc::smem_u32(dst)),
+        "l"(map), "r"(bar_cluster), "r"(0), "r"(y), "r"(kb)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\t"
+        "@e cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, "
+        "%4, %5}], [%2];\n\t}" ::"r"(tc::smem_u32(dst)),
+        "l"(map), "r"(bar_cluster), "r"(0), "r"(y), "r"(kb)
+        : "memory");
+  }
+}
+
+// bf16 row-major [rows, cols] viewed as [cols/64 k-blocks][rows][64 elements] (cols a multiple
+// of 64): a box of kps k-blocks × box_rows rows lands k-block after k-block in shared memory,
+// each as 128B-swizzled K-major rows.
+static bool make_map3_bf16(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int64_t ld, int box_rows,
+                           int kps) {
+  tc::EncodeTiled enc = tc::get_encode();
+  if (!enc || cols % 64 != 0) return false;
+  cuuint64_t dims[3] = {64, (cuuint64_t)rows, (cuuint64_t)(cols / 64)};
+  cuuint64_t strides[2] = {(cuuint64_t)(ld * 2), 128};
+  cuuint32_t box[3] = {64, (cuuint32_t)box_rows, (cuuint32_t)kps};
+  cuuint32_t es[3] = {1, 1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 struct PairArgs {
   __nv_bfloat16* c;   // STORE: product; SWIGLU: activation; RESNORM: residual stream x
   int64_t ldc;
@@ -53,7 +91,7 @@ struct PairArgs {
   int up_off;         // SWIGLU: first up row of the [gate; up] weight (= inter)
 };
 
-template <int MODE>
+template <int MODE, int KP>
 __global__ void __launch_bounds__(192, 1)
 gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
                  const __grid_constant__ CUtensorMap tm_c, const PairArgs A) {
@@ -61,7 +99,11 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int S = A.stages;
-  const uint32_t stage_bytes = PAIR_X_BYTES + A.w_bytes;
+  // a stage holds KP k-blocks: [k-block][128 token rows][128 B], then [k-block][N/2 rows][128 B]
+  // (KP = 2: each operand one 3-D TMA box)
+  const uint32_t x_bytes = KP * PAIR_X_BYTES;
+  const uint32_t stage_bytes = x_bytes + KP * A.w_bytes;
+  const int steps = A.n_kb / KP;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)S * stage_bytes);   // used in rank 0
   uint64_t* empty = full + S;
   uint64_t* acc_full = empty + S;
@@ -100,17 +142,24 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant
     }
     __syncwarp();
     // both CTAs' bytes of a stage complete on rank 0's full barrier, which rank 0 arms for both
-    const int npre = min(A.n_kb, S);
+    auto load_w = [&](uint8_t* st, uint32_t fb, int i) {
+      if (KP == 1) tma_load_2d_pair_evict_first_warp(st + x_bytes, &tm_w, fb, i * 64, wrow);
+      else tma_load_3d_pair_warp(st + x_bytes, &tm_w, fb, wrow, i * KP, true);
+    };
+    auto load_x = [&](uint8_t* st, uint32_t fb, int i) {
+      if (KP == 1) tma_load_2d_pair_warp(st, &tm_x, fb, i * 64, trow);
+      else tma_load_3d_pair_warp(st, &tm_x, fb, trow, i * KP, false);
+    };
+    const int npre = min(steps, S);
     for (int i = 0; i < npre; ++i) {
       const uint32_t fb = cluster_addr(smem_u32(&full[i]), 0);
       if (rank == 0) mbar_expect_tx_warp(&full[i], 2 * stage_bytes);
-      tma_load_2d_pair_evict_first_warp(smem + i * stage_bytes + PAIR_X_BYTES, &tm_w, fb, i * 64, wrow);
+      load_w(smem + i * stage_bytes, fb, i);
     }
     pdl_wait();   // activations are the previous kernel's output
-    for (int i = 0; i < npre; ++i)
-      tma_load_2d_pair_warp(smem + i * stage_bytes, &tm_x, cluster_addr(smem_u32(&full[i]), 0), i * 64, trow);
+    for (int i = 0; i < npre; ++i) load_x(smem + i * stage_bytes, cluster_addr(smem_u32(&full[i]), 0), i);
     bool ok = true;
-    for (int i = npre; i < A.n_kb; ++i) {
+    for (int i = npre; i < steps; ++i) {
       const int s = i % S;
       const uint32_t ph = (i / S) & 1u;
       ok = mbar_wait_warp(&empty[s], ph ^ 1u, 601, &g_gemm_pair_error, abort);
@@ -118,12 +167,12 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant
       const uint32_t fb = cluster_addr(smem_u32(&full[s]), 0);
       uint8_t* st = smem + s * stage_bytes;
       if (rank == 0) mbar_expect_tx_warp(&full[s], 2 * stage_bytes);
-      tma_load_2d_pair_evict_first_warp(st + PAIR_X_BYTES, &tm_w, fb, i * 64, wrow);
-      tma_load_2d_pair_warp(st, &tm_x, fb, i * 64, trow);
+      load_w(st, fb, i);
+      load_x(st, fb, i);
     }
     // the last release of every stage (an MMA-completion arrival from rank 0) has landed
     for (int s = 0; ok && s < npre; ++s) {
-      const int last = (A.n_kb - 1 - s) / S;
+      const int last = (steps - 1 - s) / S;
       ok = mbar_wait_warp(&empty[s], (uint32_t)last & 1u, 602, &g_gemm_pair_error, abort);
     }
   } else if (warp == 1) {
@@ -131,14 +180,17 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant
     if (rank == 0) {   // MMA issuer: the whole warp, one elected lane issues
       const uint32_t idesc = idesc_bf16(256, A.N);
       bool ok = true;
-      for (int i = 0; i < A.n_kb; ++i) {
+      for (int i = 0; i < steps; ++i) {
         const int s = i % S;
         const uint32_t ph = (i / S) & 1u;
         if (ok) ok = mbar_wait_warp(&full[s], ph, 603, &g_gemm_pair_error, abort);
         fence_after();
         if (ok) {
           const uint32_t xa = smem_u32(smem + s * stage_bytes);
-          umma4_bf16_pair_warp(tmem, sdesc_sw128(xa), sdesc_sw128(xa + PAIR_X_BYTES), idesc, i > 0 ? 1u : 0u);
+#pragma unroll
+          for (int kk = 0; kk < KP; ++kk)
+            umma4_bf16_pair_warp(tmem, sdesc_sw128(xa + kk * PAIR_X_BYTES), sdesc_sw128(xa + x_bytes + kk * A.w_bytes),
+                                 idesc, (i > 0 || kk > 0) ? 1u : 0u);
         }
         umma_commit_pair_warp(&empty[s]);
       }
@@ -260,7 +312,7 @@ __global__ void __launch_bounds__(256) pair_rmsnorm_kernel(const __nv_bfloat16* 
 
 // ------------------------------------------------------------------ host side
 struct PairPlan {
-  int N, tiles, stages, w_bytes, tmem_cols, n_kb;
+  int N, tiles, stages, w_bytes, tmem_cols, n_kb, kp;
 };
 
 static int ceil_div(int64_t a, int64_t b) { return (int)((a + b - 1) / b); }
@@ -270,7 +322,7 @@ static int ceil_div(int64_t a, int64_t b) { return (int)((a + b - 1) / b); }
 static int resident_pairs() {
   static int n = 0;
   if (n != 0) return n;
-  auto kern = gemm_pair_kernel<PAIR_STORE>;   // every mode has the same resources
+  auto kern = gemm_pair_kernel<PAIR_STORE, 1>;   // every mode has the same resources
   n = tc::sm_count() / 2;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, PAIR_SMEM_MAX) != cudaSuccess) {
     (void)cudaGetLastError();
@@ -316,12 +368,14 @@ static bool pair_plan(int64_t m, int64_t n_out, int64_t k, int mode, PairPlan* p
   p->N = N;
   p->tiles = tiles;
   p->w_bytes = (N / 2) * 128;
-  const int stage = PAIR_X_BYTES + p->w_bytes;
+  // two k-blocks per stage (one 3-D box per operand) when K allows and three stages still fit
+  p->n_kb = ceil_div(k, 64);
+  p->kp = (k % 128 == 0 && (PAIR_SMEM_MAX - PAIR_AUX) / (2 * (PAIR_X_BYTES + p->w_bytes)) >= 3) ? 2 : 1;
+  const int stage = p->kp * (PAIR_X_BYTES + p->w_bytes);
   p->stages = std::min(PAIR_MAX_STAGES, (PAIR_SMEM_MAX - PAIR_AUX) / stage);
   int cols = 32;
   while (cols < N) cols *= 2;
   p->tmem_cols = cols;
-  p->n_kb = ceil_div(k, 64);
   return true;
 }
 
@@ -331,12 +385,12 @@ size_t gemm_pair_workspace(int64_t m, int64_t n, int64_t k) {
   return (size_t)p.tiles * (size_t)m * sizeof(float);
 }
 
-template <int MODE>
+template <int MODE, int KP>
 static int launch_pair(const CUtensorMap& mw, const CUtensorMap& mx, const CUtensorMap& mc, const PairPlan& p,
                        const PairArgs& args,
                        cudaStream_t st) {
-  auto kern = gemm_pair_kernel<MODE>;
-  const size_t smem = (size_t)p.stages * (PAIR_X_BYTES + p.w_bytes) + PAIR_AUX;
+  auto kern = gemm_pair_kernel<MODE, KP>;
+  const size_t smem = (size_t)p.stages * KP * (PAIR_X_BYTES + p.w_bytes) + PAIR_AUX;
   static bool attr_set = false;
   if (!attr_set) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, PAIR_SMEM_MAX) != cudaSuccess)
@@ -384,8 +438,9 @@ int gemm_pair(const void* a, int64_t lda, const void* w, int64_t ldw, void* c, i
   }
   const int64_t w_rows = mode == PAIR_SWIGLU ? 2 * n : n;
   CUtensorMap mw, mx, mc;
-  if (!tc::make_map_bf16(&mw, w, w_rows, k, ldw, p.N / 2) || !tc::make_map_bf16(&mx, a, m, k, lda, 128) ||
-      !tc::make_store_map_bf16(&mc, c, m, n, ldc, 32, mode == PAIR_SWIGLU ? p.N / 2 : p.N))
+  const bool maps = p.kp == 2 ? make_map3_bf16(&mw, w, w_rows, k, ldw, p.N / 2, 2) && make_map3_bf16(&mx, a, m, k, lda, 128, 2)
+                              : tc::make_map_bf16(&mw, w, w_rows, k, ldw, p.N / 2) && tc::make_map_bf16(&mx, a, m, k, lda, 128);
+  if (!maps || !tc::make_store_map_bf16(&mc, c, m, n, ldc, 32, mode == PAIR_SWIGLU ? p.N / 2 : p.N))
     return QSP_ERR_UNSUPPORTED;
   PairArgs args{};
   args.c = static_cast<__nv_bfloat16*>(c);
@@ -400,53 +455,21 @@ int gemm_pair(const void* a, int64_t lda, const void* w, int64_t ldw, void* c, i
   args.tmem_cols = p.tmem_cols;
   args.up_off = (int)n;
   int rc;
-  if (mode == PAIR_SWIGLU) rc = launch_pair<PAIR_SWIGLU>(mw, mx, mc, p, args, st);
-  else if (mode == PAIR_RESNORM) rc = launch_pair<PAIR_RESNORM>(mw, mx, mc, p, args, st);
-  else rc = launch_pair<PAIR_STORE>(mw, mx, mc, p, args, st);
+  if (p.kp == 2) {
+    if (mode == PAIR_SWIGLU) rc = launch_pair<PAIR_SWIGLU, 2>(mw, mx, mc, p, args, st);
+    else if (mode == PAIR_RESNORM) rc = launch_pair<PAIR_RESNORM, 2>(mw, mx, mc, p, args, st);
+    else rc = launch_pair<PAIR_STORE, 2>(mw, mx, mc, p, args, st);
+  } else {
+    if (mode == PAIR_SWIGLU) rc = launch_pair<PAIR_SWIGLU, 1>(mw, mx, mc, p, args, st);
+    else if (mode == PAIR_RESNORM) rc = launch_pair<PAIR_RESNORM, 1>(mw, mx, mc, p, args, st);
+    else rc = launch_pair<PAIR_STORE, 1>(mw, mx, mc, p, args, st);
+  }
   if (rc || mode != PAIR_RESNORM) return rc;
   return launch_pdl("qsp_gemm(pair rmsnorm)", pair_rmsnorm_kernel, dim3((unsigned)m), dim3(256), 0, st,
                     static_cast<const __nv_bfloat16*>(c), ldc, static_cast<const float*>(workspace), p.tiles, (int)m,
                     static_cast<const __nv_bfloat16*>(norm_w), static_cast<__nv_bfloat16*>(y), ldy, (int)n, eps);
 }
 
-
-// 3-D TMA load (k-blocks kb, kb+1 of rows [y, y + box rows) over the view [k-blocks][rows][64])
-// into this CTA's shared memory, completing on the pair leader's barrier; weights evict-first.
-__device__ __forceinline__ void tma_load_3d_pair_warp(void* dst, const CUtensorMap* map, uint32_t bar_cluster, int y,
-                                                      int kb, bool evict_first) {
-  if (evict_first) {
-    asm volatile(
-        "{\n\t.reg .pred e;\n\t.reg .b64 pol;\n\telect.sync _|e, 0xffffffff;\n\t"
-        "createpolicy.fractional.L2::evict_first.b64 pol, 1.0;\n\t"
-        "@e cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
-        "[%0], [%1, {%3, %4, %5}], [%2], pol;\n\t}" ::"r"(tc::smem_u32(dst)),
-        "l"(map), "r"(bar_cluster), "r"(0), "r"(y), "r"(kb)
-        : "memory");
-  } else {
-    asm volatile(
-        "{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\t"
-        "@e cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, "
-        "%4, %5}], [%2];\n\t}" ::"r"(tc::smem_u32(dst)),
-        "l"(map), "r"(bar_cluster), "r"(0), "r"(y), "r"(kb)
-        : "memory");
-  }
-}
-
-// bf16 row-major [rows, cols] viewed as [cols/64 k-blocks][rows][64 elements] (cols a multiple
-// of 64): a box of kps k-blocks × box_rows rows lands k-block after k-block in shared memory,
-// each as 128B-swizzled K-major rows.
-static bool make_map3_bf16(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int64_t ld, int box_rows,
-                           int kps) {
-  tc::EncodeTiled enc = tc::get_encode();
-  if (!enc || cols % 64 != 0) return false;
-  cuuint64_t dims[3] = {64, (cuuint64_t)rows, (cuuint64_t)(cols / 64)};
-  cuuint64_t strides[2] = {(cuuint64_t)(ld * 2), 128};
-  cuuint32_t box[3] = {64, (cuuint32_t)box_rows, (cuuint32_t)kps};
-  cuuint32_t es[3] = {1, 1, 1};
-  return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, es,
-             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
 
 // ------------------------------------------------------------------ persistent pair (STORE)
 // For plain products whose tiles take several rounds of the pairs (the vocabulary projection
