@@ -48,12 +48,15 @@ static bool pairp_on() {
 }
 
 // Which products take the CTA-pair kernel (bit 0: plain, bit 1: SwiGLU, bit 2: residual +
-// RMSNorm). By default only plain products at least PAIR_WIDE_N columns wide do (measured on
-// B200 at 256 rows: the 12352-column GDN input projection 19.5 µs against 24.0 µs on the
-// cluster kernel; the 9216-column attention projection 19.6 against 15.8, the SwiGLU and
-// residual tails slower too). QSP_GEMM_PAIR=<bits> applies the pair kernel to every product of
-// those kinds instead, for comparisons with the other kernels.
-constexpr int64_t PAIR_WIDE_N = 10240;
+// RMSNorm). By default plain products at least PAIR_WIDE_N columns wide and the SwiGLU
+// projections do. Measured on B200 at 256 rows, with two k-blocks per TMA box:
+//   GDN input projection (12352 × 2048): 13.7 µs, against 24.0 on the cluster kernel;
+//   attention q|k|v (9216 × 2048): 13.5 µs, against 15.7 on the cluster kernel;
+//   MLP gate|up + SwiGLU (12288 × 2048): 19.2 µs, against 23.1 on the split-K kernel + merge.
+// The residual + RMSNorm tails stay on the split-K kernel (2048 columns give the pairs too few
+// tiles: 21.9 against 12.6 µs, 28.8 against 14.3 µs). QSP_GEMM_PAIR=<bits> applies the pair
+// kernel to exactly the products of those kinds instead, for comparisons.
+constexpr int64_t PAIR_WIDE_N = 8192;
 static int pair_modes() {
   static int v = -2;
   if (v == -2) {
@@ -64,7 +67,7 @@ static int pair_modes() {
 }
 static bool pair_for(int bit, int64_t n) {
   const int v = pair_modes();
-  return v < 0 ? (bit == 1 && n >= PAIR_WIDE_N) : (v & bit) != 0;
+  return v < 0 ? ((bit == 1 && n >= PAIR_WIDE_N) || bit == 2) : (v & bit) != 0;
 }
 
 }  // namespace qsp

@@ -378,8 +378,12 @@ moe_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
       const int off = __ldg(&A.offsets[e]), n_e = __ldg(&A.offsets[e + 1]) - off;
       const int row0 = e * A.rows_per_expert + rb * (SWI ? 128 : 128 * NA);
       for (int t0 = 0; t0 < n_e && ok; t0 += C::TN) {
-        const int nb16 = (min(C::TN, n_e - t0) + 15) / 16;
-        const uint32_t bytes = NA * C::A_BYTES + nb16 * 2048;
+        // one TMA box per operand and stage (an SM's TMA moves a bounded number of boxes per
+        // µs): both weight tiles as one box (SWI: a 3-D box over [gate, up] halves; otherwise
+        // NA·128 consecutive rows), the expert's token rows as one TN-row box (rows past the
+        // expert's belong to the next expert or read as zeros past the last row; the MMA's N
+        // covers only the expert's own)
+        const uint32_t bytes = NA * C::A_BYTES + C::B_BYTES;
         for (int kb = 0; kb < A.n_kb; ++kb, ++it) {
           const int s = it % C::STAGES;
           const uint32_t ph = (it / C::STAGES) & 1u;
@@ -389,11 +393,18 @@ moe_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
           }
           uint8_t* st = smem + s * C::STAGE;
           mbar_expect_tx_warp(&full[s], bytes);
-          tma_load_2d_evict_first_warp(st, &tm_w, &full[s], kb * 64, row0);
-          if (NA == 2)
-            tma_load_2d_evict_first_warp(st + C::A_BYTES, &tm_w, &full[s], kb * 64, row0 + (SWI ? A.out_w : 128));
-          for (int q = 0; q < nb16; ++q)
-            tma_load_2d_warp(st + NA * C::A_BYTES + q * 2048, &tm_x, &full[s], kb * 64, off + t0 + q * 16);
+          if (SWI) {
+            asm volatile(
+                "{\n\t.reg .pred e;\n\t.reg .b64 pol;\n\telect.sync _|e, 0xffffffff;\n\t"
+                "createpolicy.fractional.L2::evict_first.b64 pol, 1.0;\n\t"
+                "@e cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, "
+                "{%3, %4, %5}], [%2], pol;\n\t}" ::"r"(smem_u32(st)),
+                "l"(&tm_w), "r"(smem_u32(&full[s])), "r"(kb * 64), "r"(row0), "r"(0)
+                : "memory");
+          } else {
+            tma_load_2d_evict_first_warp(st, &tm_w, &full[s], kb * 64, row0);
+          }
+          tma_load_2d_warp(st + NA * C::A_BYTES, &tm_x, &full[s], kb * 64, off + t0);
         }
       }
     }
@@ -490,6 +501,23 @@ moe_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
     fence_after();
     tmem_dealloc(tmem, C::TMEM_COLS);
   }
+}
+
+// The stacked [E·2I, H] gate|up weight viewed as [2 halves (gate, up; I rows apart)][E·2I − I
+// rows][H]: a box of 64 columns × 128 rows × both halves brings a unit's 128 gate rows and the
+// matching 128 up rows in one request, laid out as the two 128-row tiles one after the other
+// (the same rows two 2-D boxes at row0 and row0 + I would bring; rows of the first half past
+// E·2I − I read as zeros, so no address leaves the weight).
+static bool make_map_gate_up(CUtensorMap* m, const void* base, int64_t E, int64_t I, int64_t H) {
+  tc::EncodeTiled enc = tc::get_encode();
+  if (!enc) return false;
+  cuuint64_t dims[3] = {(cuuint64_t)H, (cuuint64_t)(E * 2 * I - I), 2};
+  cuuint64_t strides[2] = {(cuuint64_t)(H * 2), (cuuint64_t)(I * H * 2)};
+  cuuint32_t box[3] = {64u, 128u, 2u};
+  cuuint32_t es[3] = {1, 1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 template <int NA, bool SWI>
@@ -628,10 +656,10 @@ extern "C" int qsp_moe_ffn(const qsp_moe_layer* L, void* stream) {
     // tensor-core path when every operand can go through TMA (16-byte rows and bases)
     CUtensorMap m_gu, m_xs, m_dn, m_as;
     const bool tc_ok = L->dtype == QSP_BF16 && (H % 8) == 0 && (I % 8) == 0 && aligned(L->gate_up, 16) &&
-                       aligned(L->down, 16) && tc::make_map_bf16(&m_gu, L->gate_up, E * 2 * I, H, H, 128) &&
-                       tc::make_map_bf16(&m_xs, at(W.xs), P, H, H, 16) &&
-                       tc::make_map_bf16(&m_dn, L->down, E * H, I, I, 128) &&
-                       tc::make_map_bf16(&m_as, at(W.as), P, I, I, 16);
+                       aligned(L->down, 16) && make_map_gate_up(&m_gu, L->gate_up, E, I, H) &&
+                       tc::make_map_bf16(&m_xs, at(W.xs), P, H, H, MoeTcCfg<2>::TN) &&
+                       tc::make_map_bf16(&m_dn, L->down, E * H, I, I, 256) &&
+                       tc::make_map_bf16(&m_as, at(W.as), P, I, I, MoeTcCfg<2>::TN);
     if (tc_ok) {
       MoeTcArgs a{};
       a.offsets = (const int*)at(W.offsets);
