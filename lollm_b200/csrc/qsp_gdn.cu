@@ -53,6 +53,16 @@ __device__ __forceinline__ uint64_t fmul2(uint64_t a, uint64_t b) {
 }
 
 // 16-byte vector of T converted to floats
+// two adjacent elements (4- or 8-byte aligned) as floats, and the reverse
+__device__ __forceinline__ float2 gdn_ld2f(const float* p) { return *reinterpret_cast<const float2*>(p); }
+__device__ __forceinline__ float2 gdn_ld2f(const __nv_bfloat16* p) {
+  return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p));
+}
+__device__ __forceinline__ void gdn_st2(float* p, float a, float b) { *reinterpret_cast<float2*>(p) = make_float2(a, b); }
+__device__ __forceinline__ void gdn_st2(__nv_bfloat16* p, float a, float b) {
+  *reinterpret_cast<__nv_bfloat162*>(p) = __halves2bfloat162(__float2bfloat16_rn(a), __float2bfloat16_rn(b));
+}
+
 template <typename T>
 __device__ __forceinline__ void load16_as_float(const T* src, float* dst) {
   const uint4 u = *reinterpret_cast<const uint4*>(src);
@@ -158,7 +168,10 @@ inline size_t gdn_prep_smem(int nchg, int K, int T, int DK, int esz) {
   return a + b + (size_t)Tm * 2 * DK * 4 + (size_t)Tm * nchg * esz;
 }
 
-template <typename T, int DK, int DV, int VPK>
+// KT / TT > 0 fix the conv kernel width and the call's token count at compile time (the
+// verify step's 4 and 4), so every loop over taps and tokens unrolls without run-time bounds;
+// 0 reads them from the layer.
+template <typename T, int DK, int DV, int VPK, int KT = 0, int TT = 0>
 __global__ void __launch_bounds__(256, 8) gdn_prep_kernel(const qsp_gdn_layer L, const GdnRing RG) {
   pdl_trigger();
   pdl_wait();
@@ -172,7 +185,7 @@ __global__ void __launch_bounds__(256, 8) gdn_prep_kernel(const qsp_gdn_layer L,
   constexpr int NW = 256 / 32;
   const int Hk = L.n_k_heads, Hv = L.n_v_heads;
   const int b = blockIdx.x / Hk, kh = blockIdx.x % Hk;
-  const int T_ = L.tokens, K = L.conv_kernel, Ts = L.max_spec_tokens;
+  const int T_ = TT > 0 ? TT : L.tokens, K = KT > 0 ? KT : L.conv_kernel, Ts = L.max_spec_tokens;
   const int key_dim = Hk * DK, conv_dim = 2 * key_dim + Hv * DV, value_dim = Hv * DV;
   const int nrows = K - 1 + T_;
   const bool spec = L.speculative != 0;
@@ -259,9 +272,9 @@ __global__ void __launch_bounds__(256, 8) gdn_prep_kernel(const qsp_gdn_layer L,
 #pragma unroll
       for (int jj = 0; jj < GDN_KMAX; ++jj) {
         if (jj < K) {
-          const T* xp = xr + (t + jj) * NCHG + c;
-          a0 = fmaf(w0[jj], dt<T>::to_f(xp[0]), a0);
-          a1 = fmaf(w1[jj], dt<T>::to_f(xp[1]), a1);
+          const float2 xv = gdn_ld2f(xr + (t + jj) * NCHG + c);   // the channel pair in one load
+          a0 = fmaf(w0[jj], xv.x, a0);
+          a1 = fmaf(w1[jj], xv.y, a1);
         }
       }
       const float s0 = dt<T>::round(siluf_(dt<T>::round(a0)));
@@ -269,8 +282,7 @@ __global__ void __launch_bounds__(256, 8) gdn_prep_kernel(const qsp_gdn_layer L,
       if (c < 2 * DK) {
         *reinterpret_cast<float2*>(qk + t * 2 * DK + c) = make_float2(s0, s1);
       } else {
-        yst[t * NCHG + c] = dt<T>::from_f(s0);
-        yst[t * NCHG + c + 1] = dt<T>::from_f(s1);
+        gdn_st2(yst + t * NCHG + c, s0, s1);
       }
     }
   }
@@ -1074,14 +1086,19 @@ static int launch_gdn_dims(const qsp_gdn_layer& L, cudaStream_t st) {
     const int nchg = 2 * DK + (L.n_v_heads / L.n_k_heads) * DV;
     const size_t psmem = gdn_prep_smem(nchg, L.conv_kernel, L.tokens, DK, (int)sizeof(T));
     const int vpk = L.n_v_heads / L.n_k_heads;
-    auto prep = vpk == 1 ? gdn_prep_kernel<T, DK, DV, 1> : (vpk == 2 ? gdn_prep_kernel<T, DK, DV, 2> : gdn_prep_kernel<T, DK, DV, 4>);
     if (vpk != 1 && vpk != 2 && vpk != 4)
       return set_error(QSP_ERR_UNSUPPORTED, "qsp_gdn_verify: %d value heads per key head not built (1, 2 or 4)", vpk);
-    static size_t prep_set[5] = {0, 0, 0, 0, 0};
-    if (psmem > prep_set[vpk]) {
+    // the verify step's shape (conv width 4, 4 tokens) runs a specialised instance
+    const bool fixed = L.conv_kernel == 4 && L.tokens == 4;
+    auto prep = fixed ? (vpk == 1 ? gdn_prep_kernel<T, DK, DV, 1, 4, 4>
+                                  : (vpk == 2 ? gdn_prep_kernel<T, DK, DV, 2, 4, 4> : gdn_prep_kernel<T, DK, DV, 4, 4, 4>))
+                      : (vpk == 1 ? gdn_prep_kernel<T, DK, DV, 1>
+                                  : (vpk == 2 ? gdn_prep_kernel<T, DK, DV, 2> : gdn_prep_kernel<T, DK, DV, 4>));
+    static size_t prep_set[2][5] = {{0, 0, 0, 0, 0}, {0, 0, 0, 0, 0}};
+    if (psmem > prep_set[fixed][vpk]) {
       if (cudaFuncSetAttribute(prep, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)psmem) != cudaSuccess)
         return set_error(QSP_ERR_CUDA, "qsp_gdn_verify: cannot reserve %zu bytes of shared memory", psmem);
-      prep_set[vpk] = psmem;
+      prep_set[fixed][vpk] = psmem;
     }
     rc = launch_pdl("qsp_gdn_verify(prep)", prep, dim3(L.batch * L.n_k_heads), dim3(256), psmem, st, L, RG);
     if (rc) return rc;
