@@ -367,23 +367,25 @@ __global__ void __launch_bounds__(256, 8) gdn_prep_kernel(const qsp_gdn_layer L,
 // cg = 8w + (l&7), as packed pairs of adjacent rows. A pass over the state reads each vector
 // with 16-byte loads shared by the 8 lanes of a row block; the 4 row blocks are combined by a
 // butterfly after which lane l owns column 4cg + rg for the per-column recursion.
-template <typename T, int DK, int DV>
+// TB: token slots per call processed by the update kernel (4 when max_spec_tokens ≤ 4, the
+// verify step's k + 1, else GDN_TB); the records keep GDN_TB Gram slots either way.
+template <typename T, int DK, int DV, int TB>
 struct __align__(16) GdnChunkIn {     // one unit's token records (filled by bulk copies)
-  GdnRecA<T, DK, DV> rep[GDN_TB];     // the previous call's tokens (replay)
-  GdnRecA<T, DK, DV> na[GDN_TB];      // this call's tokens
-  GdnRecB<T, DK, DV> nb[GDN_TB];
+  GdnRecA<T, DK, DV> rep[TB];         // the previous call's tokens (replay)
+  GdnRecA<T, DK, DV> na[TB];          // this call's tokens
+  GdnRecB<T, DK, DV> nb[TB];
 };
 
-template <typename T, int DK, int DV>
+template <typename T, int DK, int DV, int TB>
 struct __align__(128) GdnChunkSmem {
   float sst[DK * DV];                 // state of the next unit (TMA bulk prefetch target)
-  float vec[3 * GDN_TB][DK];          // fp32 slots: replay k 0..7, new k 8..15, scaled new q 16..23
-  GdnChunkIn<T, DK, DV> in[2];        // double-buffered token records
-  float tabA[2][GDN_TB][GDN_TB];      // Γ(r, s)·k_r·k_s   (replay, new)
-  float tabB[GDN_TB][GDN_TB];         // Γ(r, t)·k_r·q_t   (new)
-  float gam[2][GDN_TB];               // Γ(−1, s)
-  float tail[2][GDN_TB];              // Γ(s, n−1)
-  float red[(DV + 31) / 32][GDN_TB];
+  float vec[3 * TB][DK];          // fp32 slots: replay k 0..7, new k 8..15, scaled new q 16..23
+  GdnChunkIn<T, DK, DV, TB> in[2];        // double-buffered token records
+  float tabA[2][TB][TB];      // Γ(r, s)·k_r·k_s   (replay, new)
+  float tabB[TB][TB];         // Γ(r, t)·k_r·q_t   (new)
+  float gam[2][TB];               // Γ(−1, s)
+  float tail[2][TB];              // Γ(s, n−1)
+  float red[(DV + 31) / 32][TB];
   uint64_t bar;                       // state prefetch
   uint64_t ibar[2];                   // token records
 };
@@ -432,9 +434,9 @@ __device__ __forceinline__ void gdn_dots4(const uint64_t (&S)[4][DK / 8], const 
 
 // S ← γ·S + Σ_{s<n} c_s·x_s (terms in order of s); c_s of column 4cg+c comes from lane
 // (c, cg), which owns that column's recursion.
-template <int DK>
+template <int DK, int TB>
 __device__ __forceinline__ void gdn_rank(uint64_t (&S)[4][DK / 8], const float* __restrict__ vec0, float gamma,
-                                         const float (&cown)[GDN_TB], int n, int rg, int lane) {
+                                         const float (&cown)[TB], int n, int rg, int lane) {
   constexpr int RB = DK / 4;
   const uint64_t gg = pk2(gamma, gamma);
 #pragma unroll
@@ -445,7 +447,7 @@ __device__ __forceinline__ void gdn_rank(uint64_t (&S)[4][DK / 8], const float* 
   for (int s = 0; s < n; ++s) {
     float cs = cown[0];
 #pragma unroll
-    for (int i = 1; i < GDN_TB; ++i) cs = s == i ? cown[i] : cs;
+    for (int i = 1; i < TB; ++i) cs = s == i ? cown[i] : cs;
     uint64_t cc[4];
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
@@ -466,11 +468,11 @@ __device__ __forceinline__ void gdn_rank(uint64_t (&S)[4][DK / 8], const float* 
 }
 
 // δ_s of this lane's column over n tokens (P = Sᵀk_s of the column, v_s from the records)
-template <typename T, int DK, int DV>
-__device__ __forceinline__ void gdn_deltas(const float (&P)[GDN_TB], const GdnRecA<T, DK, DV>* rec, int col,
-                                           const float (*A)[GDN_TB], const float* gam, int n, float (&dl)[GDN_TB]) {
+template <typename T, int DK, int DV, int TB>
+__device__ __forceinline__ void gdn_deltas(const float (&P)[TB], const GdnRecA<T, DK, DV>* rec, int col,
+                                           const float (*A)[TB], const float* gam, int n, float (&dl)[TB]) {
 #pragma unroll
-  for (int s = 0; s < GDN_TB; ++s) {
+  for (int s = 0; s < TB; ++s) {
     dl[s] = 0.f;
     if (s < n) {
       float acc = __fmul_rn(gam[s], P[s]);
@@ -490,8 +492,8 @@ __device__ __forceinline__ void gdn_bulk(void* dst, const void* src, uint32_t by
 // Warp 0 stages unit u's records into `in` with three bulk copies completing on `bar`: the A
 // records of all Ts replay slots (parity par; the unit uses the first replay_n of them) and
 // this call's N A and B records (parity par^1).
-template <typename T, int DK, int DV>
-__device__ __forceinline__ void gdn_stage(GdnChunkIn<T, DK, DV>& in, uint64_t* bar, const qsp_gdn_layer& L,
+template <typename T, int DK, int DV, int TB>
+__device__ __forceinline__ void gdn_stage(GdnChunkIn<T, DK, DV, TB>& in, uint64_t* bar, const qsp_gdn_layer& L,
                                           const GdnRing& RG, int u, int N, int par, int lane) {
   const int Ts = L.max_spec_tokens;
   const uint8_t* ring = static_cast<const uint8_t*>(L.pending);
@@ -510,12 +512,12 @@ __device__ __forceinline__ void gdn_stage(GdnChunkIn<T, DK, DV>& in, uint64_t* b
 
 // Persistent: CTA c handles (sequence, value head) units c, c+G, ... . While a unit computes,
 // the next unit's state and token records stream into shared memory.
-template <typename T, int DK, int DV>
+template <typename T, int DK, int DV, int TB>
 __global__ void __launch_bounds__(DV, 2)
 gdn_chunk_kernel(const qsp_gdn_layer L, const GdnRing RG, const int n_new) {
   pdl_trigger();
   pdl_wait();
-  using SM = GdnChunkSmem<T, DK, DV>;
+  using SM = GdnChunkSmem<T, DK, DV, TB>;
   extern __shared__ __align__(128) uint8_t gdn_chunk_raw[];
   SM& sm = *reinterpret_cast<SM*>(gdn_chunk_raw);
   constexpr int RB = DK / 4;          // rows per thread
@@ -546,7 +548,7 @@ gdn_chunk_kernel(const qsp_gdn_layer L, const GdnRing RG, const int n_new) {
   __syncthreads();
   if ((int)blockIdx.x < units) {
     if (tid == 0) gdn_prefetch_state(sm.sst, L.state + (int64_t)blockIdx.x * DK * DV, &sm.bar, SBYTES);
-    if (warp == 0) gdn_stage<T, DK, DV>(sm.in[0], &sm.ibar[0], L, RG, blockIdx.x, N, par, lane);
+    if (warp == 0) gdn_stage<T, DK, DV, TB>(sm.in[0], &sm.ibar[0], L, RG, blockIdx.x, N, par, lane);
   }
   int r_next = (int)blockIdx.x < units ? L.replay_n[blockIdx.x / Hv] : 0;
 
@@ -557,10 +559,10 @@ gdn_chunk_kernel(const qsp_gdn_layer L, const GdnRing RG, const int n_new) {
     // qsp_cache_finalize / qsp_cache_accept and never exceed max_spec_tokens)
     const int R = min(max(r_next, 0), Ts);
     const int buf = it & 1;
-    GdnChunkIn<T, DK, DV>& in = sm.in[buf];
+    GdnChunkIn<T, DK, DV, TB>& in = sm.in[buf];
     // 1. the next unit's records go into the other buffer (free since the last unit ended)
     if (u + G < units) {
-      if (warp == 0) gdn_stage<T, DK, DV>(sm.in[buf ^ 1], &sm.ibar[buf ^ 1], L, RG, u + G, N, par, lane);
+      if (warp == 0) gdn_stage<T, DK, DV, TB>(sm.in[buf ^ 1], &sm.ibar[buf ^ 1], L, RG, u + G, N, par, lane);
       r_next = L.replay_n[(u + G) / Hv];
     }
     float* state = L.state + (int64_t)u * DK * DV;
@@ -583,19 +585,19 @@ gdn_chunk_kernel(const qsp_gdn_layer L, const GdnRing RG, const int n_new) {
       gdn_prefetch_state(sm.sst, L.state + (int64_t)(u + G) * DK * DV, &sm.bar, SBYTES);
 
     // 3. fp32 vector slots and the coefficient tables
-    for (int e = tid; e < 3 * GDN_TB * CK; e += DV) {
+    for (int e = tid; e < 3 * TB * CK; e += DV) {
       const int v = e / CK, c = e % CK;   // vector slot, 16-byte chunk of it
       const T* src;
       float sc = 1.f;
-      if (v < GDN_TB) {
+      if (v < TB) {
         if (v >= R) continue;
         src = in.rep[v].k;
-      } else if (v < 2 * GDN_TB) {
-        if (v - GDN_TB >= N) continue;
-        src = in.na[v - GDN_TB].k;
+      } else if (v < 2 * TB) {
+        if (v - TB >= N) continue;
+        src = in.na[v - TB].k;
       } else {
-        if (v - 2 * GDN_TB >= N) continue;
-        src = in.nb[v - 2 * GDN_TB].q;
+        if (v - 2 * TB >= N) continue;
+        src = in.nb[v - 2 * TB].q;
         sc = qscale;
       }
       float x[EPV];
@@ -603,9 +605,9 @@ gdn_chunk_kernel(const qsp_gdn_layer L, const GdnRing RG, const int n_new) {
 #pragma unroll
       for (int i = 0; i < EPV; ++i) sm.vec[v][c * EPV + i] = x[i] * sc;
     }
-    for (int e = tid; e < 2 * (GDN_TB + 1) * GDN_TB; e += DV) {
-      const int ch = e / ((GDN_TB + 1) * GDN_TB);           // 0 replay, 1 new
-      const int r = (e / GDN_TB) % (GDN_TB + 1) - 1, s = e % GDN_TB;
+    for (int e = tid; e < 2 * (TB + 1) * TB; e += DV) {
+      const int ch = e / ((TB + 1) * TB);           // 0 replay, 1 new
+      const int r = (e / TB) % (TB + 1) - 1, s = e % TB;
       const int n = ch ? N : R;
       const GdnRecA<T, DK, DV>* ra = ch ? in.na : in.rep;
       if (s >= n || r > s) continue;
@@ -637,16 +639,16 @@ gdn_chunk_kernel(const qsp_gdn_layer L, const GdnRing RG, const int n_new) {
     // 4. phase 0 replays the kept tokens of the previous speculative call; phase 1 applies this
     //    call's tokens. One copy of the pass code serves both (and keeps the replay's
     //    arithmetic identical to a fresh forward over the same tokens).
-    float o[GDN_TB];
+    float o[TB];
 #pragma unroll 1
     for (int ph = 0; ph < 2; ++ph) {
       const int n = ph ? N : R;
       if (n == 0) continue;
-      const int kslot = ph ? GDN_TB : 0;
+      const int kslot = ph ? TB : 0;
       const int ngk = (n + 3) >> 2, ng = ph ? 2 * ngk : ngk;
-      float Pk[GDN_TB], Pq[GDN_TB], dl[GDN_TB];
+      float Pk[TB], Pq[TB], dl[TB];
 #pragma unroll
-      for (int i = 0; i < GDN_TB; ++i) Pk[i] = Pq[i] = 0.f;
+      for (int i = 0; i < TB; ++i) Pk[i] = Pq[i] = 0.f;
 #pragma unroll 1
       for (int g = 0; g < ng; ++g) {   // pass 1: Sᵀk_s, then (phase 1) Sᵀq_t, four slots at a time
         const bool isq = g >= ngk;
@@ -654,14 +656,14 @@ gdn_chunk_kernel(const qsp_gdn_layer L, const GdnRing RG, const int n_new) {
         float t4[4] = {0.f, 0.f, 0.f, 0.f};
         // the last group of a call with n % 4 in {1, 2} only needs that many slots
         const int left = n - 4 * g4;
-        const float* vg = sm.vec[(isq ? 2 * GDN_TB : kslot) + 4 * g4];
+        const float* vg = sm.vec[(isq ? 2 * TB : kslot) + 4 * g4];
         if (left == 1) gdn_dots4<DK, 1>(S, vg, rg, t4);
         else if (left == 2) gdn_dots4<DK, 2>(S, vg, rg, t4);
         else gdn_dots4<DK>(S, vg, rg, t4);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
 #pragma unroll
-          for (int jj = 0; jj < GDN_TB / 4; ++jj) {
+          for (int jj = 0; jj < TB / 4; ++jj) {
             if (g4 == jj) {
               if (isq) Pq[4 * jj + i] = t4[i];
               else Pk[4 * jj + i] = t4[i];
@@ -669,10 +671,10 @@ gdn_chunk_kernel(const qsp_gdn_layer L, const GdnRing RG, const int n_new) {
           }
         }
       }
-      gdn_deltas<T, DK, DV>(Pk, ph ? in.na : in.rep, col, sm.tabA[ph], sm.gam[ph], n, dl);
+      gdn_deltas<T, DK, DV, TB>(Pk, ph ? in.na : in.rep, col, sm.tabA[ph], sm.gam[ph], n, dl);
       if (ph) {
 #pragma unroll
-        for (int t = 0; t < GDN_TB; ++t) {
+        for (int t = 0; t < TB; ++t) {
           o[t] = 0.f;
           if (t < N) {
             float acc = __fmul_rn(sm.gam[1][t], Pq[t]);
@@ -685,9 +687,9 @@ gdn_chunk_kernel(const qsp_gdn_layer L, const GdnRing RG, const int n_new) {
       // the state after these tokens: needed by phase 1 after a replay, and stored when it is
       // committed (the replay always; this call's tokens only when not speculative)
       if (ph == 0 || !spec) {
-        float c[GDN_TB];
+        float c[TB];
 #pragma unroll
-        for (int s = 0; s < GDN_TB; ++s) c[s] = s < n ? __fmul_rn(sm.tail[ph][s], dl[s]) : 0.f;
+        for (int s = 0; s < TB; ++s) c[s] = s < n ? __fmul_rn(sm.tail[ph][s], dl[s]) : 0.f;
         gdn_rank<DK>(S, sm.vec[kslot], sm.gam[ph][n - 1], c, n, rg, lane);
         if (ph == 1 || spec || N == 0) store_state();
       }
@@ -696,24 +698,24 @@ gdn_chunk_kernel(const qsp_gdn_layer L, const GdnRing RG, const int n_new) {
       // 6. RMSNormGated over the dv columns of each token: w·round(x̂)·silu(z), x = round(core)
       // the per-token sums of squares, their butterflies interleaved (same order per token as
       // warp_sum)
-      float ssq[GDN_TB];
+      float ssq[TB];
 #pragma unroll
-      for (int t = 0; t < GDN_TB; ++t) {
+      for (int t = 0; t < TB; ++t) {
         const float x = dt<T>::round(o[t]);
         ssq[t] = x * x;
       }
 #pragma unroll
       for (int sh = 16; sh > 0; sh >>= 1)
 #pragma unroll
-        for (int t = 0; t < GDN_TB; ++t) ssq[t] += __shfl_xor_sync(0xffffffffu, ssq[t], sh);
+        for (int t = 0; t < TB; ++t) ssq[t] += __shfl_xor_sync(0xffffffffu, ssq[t], sh);
       if (lane == 0) {
 #pragma unroll
-        for (int t = 0; t < GDN_TB; ++t)
+        for (int t = 0; t < TB; ++t)
           if (t < N) sm.red[warp][t] = ssq[t];
       }
       __syncthreads();
 #pragma unroll
-      for (int t = 0; t < GDN_TB; ++t) {
+      for (int t = 0; t < TB; ++t) {
         if (t < N) {
           float ss = 0.f;
           for (int w = 0; w < (DV + 31) / 32; ++w) ss += sm.red[w][t];
@@ -1077,10 +1079,12 @@ static int launch_gdn_dims(const qsp_gdn_layer& L, cudaStream_t st) {
   const GdnRing RG = gdn_ring(L.batch, L.n_v_heads, L.max_spec_tokens, DK, DV, (int)sizeof(T));
   const int units = L.batch * L.n_v_heads;
   const int grid = std::min(units, 2 * sm_count_gdn());
-  auto chunk = gdn_chunk_kernel<T, DK, DV>;
-  const size_t csmem = sizeof(GdnChunkSmem<T, DK, DV>);
-  static bool chunk_set = false;
-  int rc = reserve_smem(chunk, csmem, chunk_set);
+  // the update kernel sizes its per-call token loops by max_spec_tokens (4 in the verify step)
+  const bool tb4 = L.max_spec_tokens <= 4;
+  auto chunk = tb4 ? gdn_chunk_kernel<T, DK, DV, 4> : gdn_chunk_kernel<T, DK, DV, GDN_TB>;
+  const size_t csmem = tb4 ? sizeof(GdnChunkSmem<T, DK, DV, 4>) : sizeof(GdnChunkSmem<T, DK, DV, GDN_TB>);
+  static bool chunk_set[2] = {false, false};
+  int rc = reserve_smem(chunk, csmem, chunk_set[tb4]);
   if (rc) return rc;
   if (L.tokens <= L.max_spec_tokens) {
     const int nchg = 2 * DK + (L.n_v_heads / L.n_k_heads) * DV;
