@@ -708,8 +708,9 @@ def run_gdn_workload(args):
     g = torch.Generator(device=dev); g.manual_seed(0)
     rnd = lambda *s: torch.randn(*s, generator=g, device=dev)
     state = rnd(B, Hv, d, d) * 0.1
-    hist = torch.zeros(2, B, Kc - 1 + 8, C, dtype=torch.bfloat16, device=dev)
-    pending = torch.zeros(K.gdn_pending_bytes(B, Hk, Hv, d, d, 8, torch.bfloat16), dtype=torch.uint8, device=dev)
+    Ts = T                                   # max_spec_tokens as the model sets it: k + 1
+    hist = torch.zeros(2, B, Kc - 1 + Ts, C, dtype=torch.bfloat16, device=dev)
+    pending = torch.zeros(K.gdn_pending_bytes(B, Hk, Hv, d, d, Ts, torch.bfloat16), dtype=torch.uint8, device=dev)
     replay = torch.zeros(B, dtype=torch.int32, device=dev)
     coff = torch.zeros(B, dtype=torch.int32, device=dev)
     parity = torch.zeros(1, dtype=torch.int32, device=dev)
@@ -723,7 +724,7 @@ def run_gdn_workload(args):
     out = torch.empty(B * T, Vd, dtype=torch.bfloat16, device=dev)
     desc = L.GdnLayer()
     desc.batch, desc.tokens, desc.n_k_heads, desc.n_v_heads, desc.head_k, desc.head_v = B, T, Hk, Hv, d, d
-    desc.conv_kernel, desc.max_spec_tokens, desc.speculative, desc.dtype, desc.eps = Kc, 8, 1, L.QSP_BF16, 1e-6
+    desc.conv_kernel, desc.max_spec_tokens, desc.speculative, desc.dtype, desc.eps = Kc, Ts, 1, L.QSP_BF16, 1e-6
     desc.proj, desc.ld_proj = proj.data_ptr(), proj.stride(0)
     desc.conv_w, desc.a_log, desc.dt_bias, desc.norm_w = conv_w.data_ptr(), a_log.data_ptr(), dt_bias.data_ptr(), norm_w.data_ptr()
     desc.state, desc.conv_hist, desc.pending = state.data_ptr(), hist.data_ptr(), pending.data_ptr()
