@@ -39,9 +39,9 @@ METRIC = "generated tok/s (batch 64, k=3) at 1/2/4/8 B200; verify-step HBM % of 
 UNIT = "tok/s"
 # DRAM bytes (read + write) of one GDN layer update at the step's shape (64 sequences, 32 value
 # heads of 128x128, T=4): gdn_chunk_kernel from an ncu capture of `bench.py --workload gdn`,
-# which runs exactly that launch (152.65 MB read + 77.90 MB written; some state write-back is
+# which runs exactly that launch (147.91 MB read + 76.97 MB written; some state write-back is
 # still in L2 when the kernel ends). gdn_prep_kernel's few MB are not included.
-GDN_TRAFFIC_PER_LAUNCH = 230_550_528
+GDN_TRAFFIC_PER_LAUNCH = 224_875_008
 GDN_TRAFFIC_SOURCE = "ncu dram__bytes_read.sum + dram__bytes_write.sum of gdn_chunk_kernel, bench.py --workload gdn"
 
 
