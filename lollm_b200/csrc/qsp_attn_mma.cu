@@ -743,11 +743,14 @@ int launch_attn_tma(const qsp_attn_layer& L, cudaStream_t st) {
 
 // ------------------------------------------------------------------ persistent, warp-specialised
 // Warp 4 produces: for every work item (split s, kv head g, sequence b x row group) of this CTA
-// it brings the item's Q rows (bulk copies) and its key tiles (TMA, as above) into a 5-stage
+// it brings the item's Q rows (bulk copies) and its key tiles (TMA, as above) into a 4-stage
 // ring, running ahead across item boundaries. Warps 0-3 consume as in attn_tma_kernel, and
 // each key-half warp writes its own partial (o, m, l), so a split yields two partials that
 // the merge kernel combines with the rest. Empty/full barriers per stage; no CTA-wide sync.
-constexpr int AT3_NST = 5;
+// Ring depth measured on B200 (µs per call at the step's lengths / over configs[2]): 2 stages
+// 86.6 / 610.7, 3 stages 76.5 / 534.3, 4 stages 73.1 / 507.2, 5 stages 76.2 / 529.6,
+// 6 stages 76.2 / 553.6.
+constexpr int AT3_NST = 4;
 constexpr int AT3_THREADS = 160;
 
 template <int HD>
