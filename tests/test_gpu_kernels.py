@@ -381,7 +381,12 @@ def _attn_reference(H, b, n, T, nh, nkv, hd, ps):
 @pytest.mark.parametrize("shape", [(2, 4, 4, 2, 32, 8, [5, 17], 16, 3), (3, 4, 16, 2, 256, 64, [40, 1, 77], 16, 3),
                                    (2, 1, 8, 2, 64, 16, [100, 3], 16, 3), (1, 9, 4, 1, 128, 32, [0], 16, 3),
                                    (3, 4, 16, 2, 256, 64, [700, 1500, 64], 64, 4),
-                                   (2, 16, 4, 2, 64, 16, [300, 129], 64, 2)])
+                                   (2, 16, 4, 2, 64, 16, [300, 129], 64, 2),
+                                   # one split: the tensor-core kernel merges its key halves itself
+                                   (3, 4, 16, 2, 256, 64, [700, 1500, 64], 64, 1),
+                                   (2, 16, 4, 2, 64, 16, [300, 129], 64, 1),
+                                   (1, 9, 4, 1, 128, 32, [0], 64, 1),
+                                   (2, 1, 8, 2, 64, 16, [100, 3], 64, 1)])
 def test_attention_matches_oracle(dt, shape):
     B, T, nh, nkv, hd, rd, lens, ps, splits = shape
     d, D, H = _attn_case(dt, B, T, nh, nkv, hd, rd, lens, page_size=ps, splits=splits)
