@@ -585,13 +585,17 @@ def graph_kernel_nodes(graphs) -> int:
 
 
 LIVE_CLASSES = {"gdn_verify": "gdn_prep_kernel + gdn_chunk_kernel", "attn_verify": "attn_ws_kernel + attn_combine_kernel",
-                "gemm": "gemm_tc_kernel", "gemm_residual_rmsnorm": "gemm_tc_kernel (+ residual/RMSNorm merge)",
-                "gemm_swiglu": "gemm_tc_kernel (+ SwiGLU merge)"}
+                "gemm": "qsp_gemm plain (in_proj, q|k|v, vocabulary)",
+                "gemm_residual_rmsnorm": "qsp_gemm + residual/RMSNorm (out, o, down)",
+                "gemm_swiglu": "qsp_gemm + SwiGLU (gate|up)"}
 
 
 LIVE_NOTE = ("each class is timed between two events recorded around its launches inside the captured verify "
              "forward; an event between two kernels stops the next kernel from starting early (programmatic "
-             "dependent launch), so these per-launch times are upper bounds and their sum exceeds phases_ms.verify")
+             "dependent launch), so these per-launch times are upper bounds and their sum exceeds phases_ms.verify. "
+             "The qsp_gemm kernels are the planner's: at 256 rows gemm_pair_kernel (in_proj, q|k|v; gate|up with "
+             "SwiGLU in its epilogue), gemm_pairp_kernel (vocabulary), gemm_tc_kernel split-K + "
+             "splitk_residual_rmsnorm_kernel (out, o, down)")
 
 
 def live_kernel_times(dec, graphs, steps):
